@@ -1,0 +1,150 @@
+/*
+ * pesq_cuda.h -- C ABI of the B200 PESQ loss engine (libpesq_cuda.so).
+ *
+ * The reference exposes this path only as the Python module
+ * `PesqLossTriton` (torch_pesq/triton_ops/loss.py:18-215); there is no native
+ * FFI in the reference.  The entry points below are the boundary a binding of
+ * that module needs: a plan replaces the module constructor
+ * (triton_ops/loss.py:60-92, which builds the stage modules and their host
+ * float64 tables), pesq_forward replaces `raw` / `mos` / `forward`
+ * (triton_ops/loss.py:104-147 and 203-215) and pesq_backward replaces the
+ * autograd backward of the whole chain (the `backward` methods of
+ * triton_ops/elementwise.py, resample.py, iir.py, spectral.py and chain.py).
+ *
+ * Conventions
+ *   - every function returns a pesq_status (0 = success); no exception crosses
+ *     the ABI; pesq_last_error() returns a message for the calling thread;
+ *   - plain pointers and sizes only; all device pointers are CUDA device
+ *     memory of the plan's device, all arrays row-major float32;
+ *   - `stream` is a cudaStream_t (CUstream); every launch is stream-ordered,
+ *     nothing synchronises and nothing allocates inside pesq_forward /
+ *     pesq_backward, so both can be captured in a CUDA graph;
+ *   - calls on distinct plans are thread safe; a plan is read only after
+ *     creation and can be shared by concurrent calls with distinct workspaces.
+ */
+#ifndef PESQ_CUDA_H_
+#define PESQ_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PESQ_CUDA_ABI_VERSION 1
+
+typedef enum pesq_status {
+  PESQ_OK = 0,
+  PESQ_ERR_INVALID_ARGUMENT = 1, /* bad shape, pointer or flag; ValueError in Python */
+  PESQ_ERR_UNSUPPORTED = 2,      /* configuration outside what the kernels implement */
+  PESQ_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  PESQ_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+  PESQ_ERR_DEVICE = 5            /* a kernel reported an error flag */
+} pesq_status;
+
+/* flags of a forward / backward pair */
+#define PESQ_GRAD_REF 1u /* the backward will be asked for dL/dref */
+#define PESQ_GRAD_DEG 2u /* the backward will be asked for dL/ddeg */
+
+typedef struct pesq_plan pesq_plan;
+
+/* Constant tables of one causal LTI filter for the chunked scan, float64.
+ * Built by triton_pesq_b200/tables.py (ScanTables); the state space is a
+ * series of balanced second order sections, s[n+1] = A s[n] + B x[n],
+ * y[n] = C s[n] + D x[n]. */
+typedef struct pesq_scan_desc {
+  int32_t states;        /* P: 10 for the level-alignment band pass, 2 for pre-emphasis */
+  int32_t chunk;         /* samples per thread chunk, must be 33 */
+  int32_t levels;        /* Kogge-Stone doubling levels, must be 5 */
+  const double* impulse; /* [chunk]            h[t] */
+  const double* carry;   /* [chunk * states]   C A^t */
+  const double* drive;   /* [chunk * states]   A^(chunk-1-k) B */
+  const double* power;   /* [levels * states * states]  A^(chunk 2^i) */
+  const double* trans;   /* [states * states]  A */
+  const double* input;   /* [states]           B */
+  const double* output;  /* [states]           C */
+  double feed;           /* D */
+} pesq_scan_desc;
+
+/* Everything `PesqLoss.__init__` (torch_pesq/loss.py:61-108) derives from its
+ * arguments, as float64 host arrays.  Only read during pesq_plan_create. */
+typedef struct pesq_plan_desc {
+  int32_t abi_version; /* PESQ_CUDA_ABI_VERSION */
+  int32_t sample_rate; /* input rate; 16000 skips the resampler */
+  int32_t n_fft;       /* 512 */
+  int32_t hop_length;  /* 256 */
+  int32_t nbarks;      /* 1 .. 64 (49 for P.862) */
+  int32_t reserved0;
+  double factor;       /* loss = factor * (0.1 d_symm + 0.0309 d_asymm) */
+  const double* window;      /* [n_fft] analysis window, centred, zero padded */
+  const int32_t* band_start; /* [nbarks] first bin of each Bark band */
+  const int32_t* band_end;   /* [nbarks] one past the last bin */
+  const double* band_corr;   /* [nbarks] power density correction */
+  const double* threshold;   /* [nbarks] absolute hearing threshold */
+  const double* exponent;    /* [nbarks] Zwicker loudness exponent */
+  const double* width;       /* [nbarks] band width in Bark */
+  double total_width;        /* sum of width[1:] */
+  double loudness_sl;        /* Sl calibration, 0.1866055 */
+  pesq_scan_desc power_filter; /* level alignment band pass (states = 10) */
+  pesq_scan_desc pre_filter;   /* pre-emphasis (states = 2) */
+  int32_t rs_orig_step;  /* resampler: orig_freq / gcd      (sample_rate != 16000) */
+  int32_t rs_new_step;   /*            16000 / gcd */
+  int32_t rs_width;      /*            left zero padding */
+  int32_t rs_width_total;/*            taps per phase */
+  const double* rs_taps; /* [new_step * width_total] float32-valued taps */
+} pesq_plan_desc;
+
+/* Shape of one call. */
+typedef struct pesq_shape {
+  int64_t n16;     /* samples per row after resampling to 16 kHz */
+  int32_t frames;  /* STFT frames (loss.py:191-196) */
+  int32_t windows; /* 20-frame overlapping windows (loss.py:258-266) */
+} pesq_shape;
+
+int pesq_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* pesq_last_error(void);
+
+/* Build a plan on the current CUDA device (uploads the constant tables).
+ * Replaces PesqLossTriton.__init__ (triton_ops/loss.py:60-92). */
+int pesq_plan_create(const pesq_plan_desc* desc, pesq_plan** plan);
+
+int pesq_plan_destroy(pesq_plan* plan);
+
+/* CUDA device ordinal the plan lives on. */
+int pesq_plan_device(const pesq_plan* plan, int* device);
+
+/* Shape of a call with `n_src` input samples per row.  Fails with
+ * PESQ_ERR_INVALID_ARGUMENT below 20 frames (triton_ops/chain.py:775-779). */
+int pesq_query_shape(const pesq_plan* plan, int64_t n_src, pesq_shape* shape);
+
+/* Bytes of device workspace a forward/backward pair needs.  The forward
+ * stores the state its backward reads in this workspace, so a pair must use
+ * the same buffer and it must not be reused in between. */
+int pesq_workspace_size(const pesq_plan* plan, int64_t batch, int64_t n_src, uint32_t flags, size_t* bytes);
+
+/* Forward pass of `batch` utterance pairs.  ref / deg: [batch, n_src] rows
+ * with row strides ld_ref / ld_deg (elements, >= n_src).  Any of the four
+ * outputs ([batch] each) may be NULL.  Replaces PesqLossTriton.raw / mos /
+ * forward (triton_ops/loss.py:104-147, 203-215). */
+int pesq_forward(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                 int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
+                 size_t workspace_bytes, float* d_symm, float* d_asymm, float* mos, float* loss);
+
+/* Backward of the preceding pesq_forward with the same inputs, flags and
+ * workspace.  Upstream gradients g_loss / g_mos / g_dsymm / g_dasymm ([batch],
+ * any may be NULL = zero) are summed.  Writes dL/dref into g_ref (row stride
+ * ld_gref) if flags has PESQ_GRAD_REF and dL/ddeg into g_deg if it has
+ * PESQ_GRAD_DEG.  Replaces the autograd backward of PesqLossTriton. */
+int pesq_backward(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
+                  size_t workspace_bytes, const float* g_loss, const float* g_mos, const float* g_dsymm,
+                  const float* g_dasymm, float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PESQ_CUDA_H_ */

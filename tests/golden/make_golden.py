@@ -1,0 +1,147 @@
+"""Generate the golden fixtures from the reference implementation itself.
+
+Runs only where the reference checkout is present (it imports ``torch_pesq``
+from ``REFERENCE_ROOT``, default ``/root/reference``); the ``.npz`` files it
+writes are committed so that the tests never need the reference at run time.
+
+Two shims make the reference importable with this image's packages:
+``torchtyping`` is absent (``TensorType[...]`` is replaced by ``torch.Tensor``)
+and the installed typeguard 4.x cannot evaluate the reference's string
+dimensions, so ``typeguard.typechecked`` is replaced by the identity.  Neither
+changes any computation.
+
+Per case the fixture holds the float32 inputs and
+
+* ``ref32_*``: ``PesqLoss.raw/mos/forward`` and the gradients of
+  ``forward(...).sum()`` w.r.t. both inputs, as the reference computes them on
+  the CPU (float32 signal path, float64 chain);
+* ``f64_*``: ``ref_pipeline`` on ``copy.deepcopy(model).double()`` with float64
+  inputs -- the float64 evaluation of the same pipeline -- and its gradients.
+
+``constants.npz`` holds the reference's constant tensors (filterbank,
+thresholds, exponents, correction, widths, window, filter coefficients and the
+resampling kernels of several rates).
+
+Usage: ``python tests/golden/make_golden.py`` from the repository root.
+"""
+
+import copy
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
+
+
+def _import_reference():
+    shim = types.ModuleType("torchtyping")
+
+    class _TensorType:
+        def __class_getitem__(cls, item):
+            return torch.Tensor
+
+    shim.TensorType = _TensorType
+    sys.modules["torchtyping"] = shim
+    import typeguard
+
+    typeguard.typechecked = lambda fn: fn
+    sys.path.insert(0, REFERENCE_ROOT)
+    from torch_pesq import PesqLoss
+    from torch_pesq.triton_ops.reference import ref_pipeline
+
+    return PesqLoss, ref_pipeline
+
+
+def speech_pair(batch, n, sr, seed, snr_db):
+    """Seeded speech-like reference and a noisy degraded copy (float32)."""
+
+    rng = np.random.default_rng(seed)
+    t = np.arange(n) / sr
+    ref = np.zeros((batch, n))
+    for b in range(batch):
+        f0 = rng.uniform(90, 250)
+        sig = sum(
+            np.sin(2 * np.pi * f0 * k * t + rng.uniform(0, 2 * np.pi)) / k
+            for k in range(1, 31)
+            if f0 * k < sr / 2
+        )
+        sig = sig * 0.5 * (1 + np.sin(2 * np.pi * 4 * t))
+        sig = sig + 0.3 * rng.standard_normal(n) * 0.5 * (1 + np.sin(2 * np.pi * 3 * t))
+        ref[b] = 0.3 * sig / np.abs(sig).max()
+    noise = rng.standard_normal((batch, n))
+    power = (ref**2).mean(axis=1, keepdims=True)
+    deg = ref + noise * np.sqrt(power / 10 ** (snr_db / 10))
+    return ref.astype(np.float32), deg.astype(np.float32)
+
+
+CASES = [
+    # name, batch, samples, sample_rate, seed, snr_db, factor
+    ("sr16k_b2_n6000", 2, 6000, 16000, 1, 10.0, 0.5),
+    ("sr16k_b1_n8192", 1, 8192, 16000, 2, 3.0, 1.0),
+    ("sr16k_b3_n7001", 3, 7001, 16000, 3, 20.0, 1.0),
+    ("sr48k_b1_n18000", 1, 18000, 48000, 4, 10.0, 1.0),
+    ("sr44k_b1_n16540", 1, 16540, 44100, 5, 10.0, 1.0),
+    ("sr8k_b1_n3200", 1, 3200, 8000, 6, 15.0, 1.0),
+]
+
+
+def main():
+    PesqLoss, ref_pipeline = _import_reference()
+    torch.manual_seed(0)
+
+    for name, batch, n, sr, seed, snr, factor in CASES:
+        model = PesqLoss(factor, sample_rate=sr)
+        ref_np, deg_np = speech_pair(batch, n, sr, seed, snr)
+        out = {"ref": ref_np, "deg": deg_np, "factor": np.float64(factor), "sample_rate": np.int64(sr)}
+
+        ref = torch.from_numpy(ref_np).requires_grad_(True)
+        deg = torch.from_numpy(deg_np).requires_grad_(True)
+        d_symm, d_asymm = model.raw(ref, deg)
+        out["ref32_d_symm"] = d_symm.detach().double().numpy()
+        out["ref32_d_asymm"] = d_asymm.detach().double().numpy()
+        out["ref32_mos"] = model.mos(ref, deg).detach().double().numpy()
+        loss = model(ref, deg)
+        out["ref32_loss"] = loss.detach().double().numpy()
+        g_ref, g_deg = torch.autograd.grad(loss.sum(), [ref, deg])
+        out["ref32_grad_ref"] = g_ref.numpy()
+        out["ref32_grad_deg"] = g_deg.numpy()
+
+        model64 = copy.deepcopy(model).double()
+        ref64 = torch.from_numpy(ref_np).double().requires_grad_(True)
+        deg64 = torch.from_numpy(deg_np).double().requires_grad_(True)
+        ds, da = ref_pipeline(ref64, deg64, model64)
+        out["f64_d_symm"] = ds.detach().numpy()
+        out["f64_d_asymm"] = da.detach().numpy()
+        loss64 = factor * (0.1 * ds + 0.0309 * da)
+        g_ref64, g_deg64 = torch.autograd.grad(loss64.sum(), [ref64, deg64])
+        out["f64_grad_ref"] = g_ref64.numpy()
+        out["f64_grad_deg"] = g_deg64.numpy()
+
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+        print(name, out["f64_d_symm"], out["f64_d_asymm"], out["ref32_d_symm"])
+
+    model = PesqLoss(1.0, sample_rate=16000)
+    const = {
+        "fbank": model.fbank.fbank.detach().numpy(),
+        "pow_dens_correction": model.fbank.pow_dens_correction.detach().numpy(),
+        "width_bark": model.fbank.width_bark.detach().numpy(),
+        "total_width": np.float64(model.fbank.total_width),
+        "threshs": model.loudness.threshs.detach().numpy().reshape(-1),
+        "exps": model.loudness.exp.detach().numpy(),
+        "window": model.to_spec.window.detach().numpy(),
+        "power_filter": model.power_filter.detach().numpy(),
+        "pre_filter": model.pre_filter.detach().numpy(),
+    }
+    for sr in (8000, 22050, 44100, 48000):
+        res = PesqLoss(1.0, sample_rate=sr).resampler
+        const[f"resample_{sr}_kernel"] = res.kernel.detach().numpy().reshape(res.kernel.shape[0], -1)
+        const[f"resample_{sr}_width"] = np.int64(res.width)
+    np.savez_compressed(os.path.join(HERE, "constants.npz"), **const)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+"""End-to-end parity of PesqLossCuda on the GPU against the float64 oracle
+and the golden vectors of the reference (mirrors the reference's
+tests/test_triton_loss.py)."""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from gpu_helpers import F64_RTOL, GRAD_RTOL, oracle_grads, peak_rel_err, rel_err
+from triton_pesq_b200 import PesqLossCuda
+from triton_pesq_b200.signals import add_noise, speech_like
+
+pytestmark = pytest.mark.gpu
+
+CASES = sorted(glob.glob(os.path.join(GOLDEN, "sr*.npz")))
+
+
+def _grads(model, ref, deg, which=(True, True)):
+    r = ref.detach().clone().requires_grad_(which[0])
+    d = deg.detach().clone().requires_grad_(which[1])
+    loss = model(r, d)
+    inputs = [t for t in (r, d) if t.requires_grad]
+    grads = torch.autograd.grad(loss.sum(), inputs)
+    return loss, grads
+
+
+@pytest.mark.parametrize("path", CASES, ids=[os.path.basename(c)[:-4] for c in CASES])
+def test_golden_vectors(cuda_device, path):
+    """Distances and gradients against the reference's own float64 pipeline."""
+
+    z = np.load(path)
+    factor, sr = float(z["factor"]), int(z["sample_rate"])
+    model = PesqLossCuda(factor, sample_rate=sr)
+    ref = torch.from_numpy(z["ref"]).to(cuda_device)
+    deg = torch.from_numpy(z["deg"]).to(cuda_device)
+    ds, da = model.raw(ref, deg)
+    assert rel_err(ds.cpu(), z["f64_d_symm"]) < F64_RTOL
+    assert rel_err(da.cpu(), z["f64_d_asymm"]) < F64_RTOL
+    _, (g_ref, g_deg) = _grads(model, ref, deg)
+    assert peak_rel_err(g_ref.cpu(), z["f64_grad_ref"]) < GRAD_RTOL
+    assert peak_rel_err(g_deg.cpu(), z["f64_grad_deg"]) < GRAD_RTOL
+
+
+@pytest.mark.parametrize(
+    "batch,samples,sample_rate,snr",
+    [(1, 16000, 16000, 10.0), (4, 16000, 16000, 0.0), (3, 20000, 16000, 20.0), (2, 48000, 48000, 10.0),
+     (2, 44100, 44100, 5.0), (8, 32000, 16000, 15.0), (2, 24000, 22050, 10.0), (2, 8000, 8000, 10.0)],
+)
+def test_matches_float64(cuda_device, batch, samples, sample_rate, snr):
+    ref = speech_like(batch, samples, sample_rate, seed=batch + samples)
+    deg = add_noise(ref, snr, seed=samples)
+    ds64, da64, gr64, gd64 = oracle_grads(ref, deg, 1.0, sample_rate)
+    model = PesqLossCuda(1.0, sample_rate=sample_rate)
+    ref, deg = ref.to(cuda_device), deg.to(cuda_device)
+    ds, da = model.raw(ref, deg)
+    assert rel_err(ds.cpu(), ds64) < F64_RTOL
+    assert rel_err(da.cpu(), da64) < F64_RTOL
+    _, (g_ref, g_deg) = _grads(model, ref, deg)
+    assert peak_rel_err(g_ref.cpu(), gr64) < GRAD_RTOL
+    assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL
+
+
+def test_outputs_are_consistent(cuda_device):
+    ref = speech_like(3, 16000, 16000, seed=3).to(cuda_device)
+    deg = add_noise(ref.cpu(), 8.0, seed=4).to(cuda_device)
+    model = PesqLossCuda(0.5, sample_rate=16000)
+    ds, da = model.raw(ref, deg)
+    loss = model(ref, deg)
+    mos = model.mos(ref, deg)
+    torch.testing.assert_close(loss, 0.5 * (0.1 * ds + 0.0309 * da), rtol=1e-6, atol=1e-7)
+    m = 4.5 - 0.1 * ds - 0.0309 * da
+    torch.testing.assert_close(mos, 0.999 + 4 / (1 + torch.exp(-1.3669 * m + 3.8224)), rtol=1e-6, atol=1e-6)
+    assert torch.all(loss > 0) and torch.all(mos > 1.0) and torch.all(mos < 5.0)
+
+
+def test_identical_signals(cuda_device):
+    ref = speech_like(3, 16000, 16000, seed=11).to(cuda_device)
+    loss = PesqLossCuda(1.0, sample_rate=16000)(ref, ref)
+    assert torch.all(loss >= 0.0) and torch.all(loss <= 1e-6)
+
+
+def test_deterministic(cuda_device):
+    ref = speech_like(4, 16000, 16000, seed=19).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=20).to(cuda_device)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    l1, g1 = _grads(model, ref, deg)
+    l2, g2 = _grads(model, ref, deg)
+    assert torch.equal(l1, l2)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+
+
+def test_batch_independence(cuda_device):
+    ref = speech_like(4, 16000, 16000, seed=23).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=24).to(cuda_device)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    batched = model(ref, deg)
+    single = torch.cat([model(ref[i : i + 1], deg[i : i + 1]) for i in range(4)])
+    torch.testing.assert_close(batched, single, rtol=0, atol=0)
+
+
+def test_non_contiguous_input(cuda_device):
+    ref = speech_like(4, 32000, 16000, seed=29).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=30).to(cuda_device)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    sr, sd = ref[:, ::2], deg[:, ::2]
+    assert not sr.is_contiguous()
+    torch.testing.assert_close(model(sr, sd), model(sr.contiguous(), sd.contiguous()))
+    # strided rows (a column slice) go straight through the row stride
+    torch.testing.assert_close(model(ref[:, :20000], deg[:, :20000]),
+                               model(ref[:, :20000].contiguous(), deg[:, :20000].contiguous()))
+
+
+def test_one_dimensional_input(cuda_device):
+    ref = speech_like(1, 16000, 16000, seed=31).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=32).to(cuda_device)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    torch.testing.assert_close(model(ref[0], deg[0]), model(ref, deg))
+
+
+def test_errors(cuda_device):
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    ref = torch.randn(2, 16000, device=cuda_device)
+    with pytest.raises(ValueError):
+        model(ref, torch.randn(2, 15000, device=cuda_device))
+    with pytest.raises(ValueError):  # fewer than 20 frames
+        model(ref[:, :4000], ref[:, :4000])
+    with pytest.raises(RuntimeError):
+        model(ref.cpu(), ref.cpu())
+    with pytest.raises(RuntimeError):
+        model(ref.double(), ref.double())
+
+
+def test_gradient_only_for_requested_inputs(cuda_device):
+    ref = speech_like(2, 16000, 16000, seed=5).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=6).to(cuda_device)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    _, (g_deg_only,) = _grads(model, ref, deg, (False, True))
+    _, (g_ref_only,) = _grads(model, ref, deg, (True, False))
+    _, (g_ref, g_deg) = _grads(model, ref, deg)
+    assert torch.equal(g_deg_only, g_deg)
+    assert torch.equal(g_ref_only, g_ref)
+
+
+def test_cuda_graph_is_bit_exact(cuda_device):
+    ref = speech_like(2, 16000, 16000, seed=43).to(cuda_device).requires_grad_(True)
+    deg = add_noise(ref.detach().cpu(), 5.0, seed=44).to(cuda_device).requires_grad_(True)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    eager = model(ref, deg)
+    eager_grads = torch.autograd.grad(eager.sum(), [ref, deg])
+    graphed = model.graphed(ref, deg)
+    captured = graphed(ref, deg)
+    captured_grads = torch.autograd.grad(captured.sum(), [ref, deg])
+    assert torch.equal(captured, eager)
+    for want, got in zip(eager_grads, captured_grads):
+        assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("sample_rate,seconds", [(48000, 12.0), (16000, 30.0)])
+def test_long_signal(cuda_device, sample_rate, seconds):
+    n = int(sample_rate * seconds)
+    ref = speech_like(1, n, sample_rate, seed=41)
+    deg = add_noise(ref, 8.0, seed=42)
+    ds64, da64, _, gd64 = oracle_grads(ref, deg, 1.0, sample_rate)
+    model = PesqLossCuda(1.0, sample_rate=sample_rate)
+    ds, da = model.raw(ref.to(cuda_device), deg.to(cuda_device))
+    assert rel_err(ds.cpu(), ds64) < F64_RTOL
+    assert rel_err(da.cpu(), da64) < F64_RTOL
+    _, (g_deg,) = _grads(model, ref.to(cuda_device), deg.to(cuda_device), (False, True))
+    assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL

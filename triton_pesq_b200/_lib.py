@@ -1,0 +1,244 @@
+"""Loading of the native libraries and plan creation through the C ABI.
+
+``libpesq_cuda.so`` carries every kernel and the C ABI of
+``include/pesq_cuda.h``; ``_pesq_torch_ops.so`` registers the
+``torch.ops.pesq_cuda`` custom ops on top of it.  Both are built in-tree by
+``triton_pesq_b200.build``.  There is no fallback: if they are missing the
+import of the ops fails with an explicit error.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpesq_cuda.so")
+OPS_PATH = os.path.join(HERE, "_pesq_torch_ops.so")
+
+ABI_VERSION = 1
+GRAD_REF = 1
+GRAD_DEG = 2
+
+PESQ_OK = 0
+PESQ_ERR_INVALID_ARGUMENT = 1
+
+_lock = threading.Lock()
+_lib = None
+_ops_loaded = False
+
+
+class ScanDesc(ctypes.Structure):
+    _fields_ = [
+        ("states", ctypes.c_int32),
+        ("chunk", ctypes.c_int32),
+        ("levels", ctypes.c_int32),
+        ("impulse", ctypes.POINTER(ctypes.c_double)),
+        ("carry", ctypes.POINTER(ctypes.c_double)),
+        ("drive", ctypes.POINTER(ctypes.c_double)),
+        ("power", ctypes.POINTER(ctypes.c_double)),
+        ("trans", ctypes.POINTER(ctypes.c_double)),
+        ("input", ctypes.POINTER(ctypes.c_double)),
+        ("output", ctypes.POINTER(ctypes.c_double)),
+        ("feed", ctypes.c_double),
+    ]
+
+
+class PlanDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("sample_rate", ctypes.c_int32),
+        ("n_fft", ctypes.c_int32),
+        ("hop_length", ctypes.c_int32),
+        ("nbarks", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("factor", ctypes.c_double),
+        ("window", ctypes.POINTER(ctypes.c_double)),
+        ("band_start", ctypes.POINTER(ctypes.c_int32)),
+        ("band_end", ctypes.POINTER(ctypes.c_int32)),
+        ("band_corr", ctypes.POINTER(ctypes.c_double)),
+        ("threshold", ctypes.POINTER(ctypes.c_double)),
+        ("exponent", ctypes.POINTER(ctypes.c_double)),
+        ("width", ctypes.POINTER(ctypes.c_double)),
+        ("total_width", ctypes.c_double),
+        ("loudness_sl", ctypes.c_double),
+        ("power_filter", ScanDesc),
+        ("pre_filter", ScanDesc),
+        ("rs_orig_step", ctypes.c_int32),
+        ("rs_new_step", ctypes.c_int32),
+        ("rs_width", ctypes.c_int32),
+        ("rs_width_total", ctypes.c_int32),
+        ("rs_taps", ctypes.POINTER(ctypes.c_double)),
+    ]
+
+
+class Shape(ctypes.Structure):
+    _fields_ = [("n16", ctypes.c_int64), ("frames", ctypes.c_int32), ("windows", ctypes.c_int32)]
+
+
+#: every function of include/pesq_cuda.h with its ctypes signature
+SIGNATURES = {
+    "pesq_abi_version": (ctypes.c_int, []),
+    "pesq_last_error": (ctypes.c_char_p, []),
+    "pesq_plan_create": (ctypes.c_int, [ctypes.POINTER(PlanDesc), ctypes.POINTER(ctypes.c_void_p)]),
+    "pesq_plan_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "pesq_plan_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "pesq_query_shape": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(Shape)]),
+    "pesq_workspace_size": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "pesq_forward": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "pesq_backward": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t,
+         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64],
+    ),
+}
+
+
+def library() -> ctypes.CDLL:
+    """The C ABI library, loaded once (RTLD_GLOBAL so the ops library binds to it)."""
+
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"The CUDA PESQ engine is not built ({LIB_PATH} is missing); run "
+                    "`python -m triton_pesq_b200.build` first."
+                )
+            lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            if lib.pesq_abi_version() != ABI_VERSION:
+                raise RuntimeError("libpesq_cuda.so has an incompatible ABI version")
+            _lib = lib
+        return _lib
+
+
+def load_ops() -> None:
+    """Register ``torch.ops.pesq_cuda`` (idempotent)."""
+
+    global _ops_loaded
+    library()
+    with _lock:
+        if not _ops_loaded:
+            if not os.path.exists(OPS_PATH):
+                raise RuntimeError(
+                    f"The CUDA PESQ torch ops are not built ({OPS_PATH} is missing); run "
+                    "`python -m triton_pesq_b200.build` first."
+                )
+            import torch
+
+            torch.ops.load_library(OPS_PATH)
+            _ops_loaded = True
+
+
+def last_error() -> str:
+    msg = library().pesq_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status == PESQ_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status == PESQ_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise RuntimeError(f"{msg} (status {status})")
+
+
+def _dptr(arr: np.ndarray):
+    return arr.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+
+
+def _scan_desc(tab, keep: list) -> ScanDesc:
+    arrays = [
+        np.ascontiguousarray(tab.impulse, dtype=np.float64),
+        np.ascontiguousarray(tab.carry, dtype=np.float64),
+        np.ascontiguousarray(tab.drive, dtype=np.float64),
+        np.ascontiguousarray(tab.power, dtype=np.float64),
+        np.ascontiguousarray(tab.trans, dtype=np.float64),
+        np.ascontiguousarray(tab.input, dtype=np.float64),
+        np.ascontiguousarray(tab.output, dtype=np.float64),
+    ]
+    keep.extend(arrays)
+    return ScanDesc(
+        states=tab.states, chunk=tab.chunk, levels=tab.levels,
+        impulse=_dptr(arrays[0]), carry=_dptr(arrays[1]), drive=_dptr(arrays[2]), power=_dptr(arrays[3]),
+        trans=_dptr(arrays[4]), input=_dptr(arrays[5]), output=_dptr(arrays[6]), feed=float(tab.feed),
+    )
+
+
+def create_plan(cfg) -> int:
+    """Build a plan on the current CUDA device from a :class:`PlanConfig`."""
+
+    lib = library()
+    keep: list = []
+
+    def arr(values, dtype=np.float64):
+        a = np.ascontiguousarray(values, dtype=dtype)
+        keep.append(a)
+        return a
+
+    window = arr(cfg.window)
+    starts = arr(cfg.layout.starts, np.int32)
+    ends = arr(cfg.layout.ends, np.int32)
+    corr = arr(cfg.layout.pow_dens_correction)
+    thr = arr(cfg.thresholds)
+    expo = arr(cfg.exponents)
+    width = arr(cfg.layout.width_bark)
+
+    desc = PlanDesc()
+    desc.abi_version = ABI_VERSION
+    desc.sample_rate = int(cfg.sample_rate)
+    desc.n_fft = int(cfg.n_fft)
+    desc.hop_length = int(cfg.hop_length)
+    desc.nbarks = int(cfg.layout.nbarks)
+    desc.factor = float(cfg.factor)
+    desc.window = _dptr(window)
+    desc.band_start = starts.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+    desc.band_end = ends.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+    desc.band_corr = _dptr(corr)
+    desc.threshold = _dptr(thr)
+    desc.exponent = _dptr(expo)
+    desc.width = _dptr(width)
+    desc.total_width = float(cfg.layout.total_width)
+    desc.loudness_sl = float(cfg.loudness_sl)
+    desc.power_filter = _scan_desc(cfg.power_scan, keep)
+    desc.pre_filter = _scan_desc(cfg.pre_scan, keep)
+    if cfg.kernel is not None:
+        taps = arr(cfg.kernel.taps)
+        desc.rs_orig_step = cfg.kernel.orig_step
+        desc.rs_new_step = cfg.kernel.new_step
+        desc.rs_width = cfg.kernel.width
+        desc.rs_width_total = cfg.kernel.width_total
+        desc.rs_taps = _dptr(taps)
+
+    handle = ctypes.c_void_p()
+    check(lib.pesq_plan_create(ctypes.byref(desc), ctypes.byref(handle)), "pesq_plan_create")
+    return int(handle.value)
+
+
+def destroy_plan(handle: int) -> None:
+    if handle and _lib is not None:
+        _lib.pesq_plan_destroy(ctypes.c_void_p(handle))
+
+
+def query_shape(handle: int, n_src: int):
+    shape = Shape()
+    check(library().pesq_query_shape(ctypes.c_void_p(handle), int(n_src), ctypes.byref(shape)), "pesq_query_shape")
+    return shape.n16, shape.frames, shape.windows

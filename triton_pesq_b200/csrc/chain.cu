@@ -1,0 +1,632 @@
+// Perceptual chain of the PESQ model, forward and adjoint.
+//
+// One thread block cluster per utterance; CTA q of the cluster owns a
+// contiguous slice of frames and each of its warps a contiguous sub-slice
+// (lanes cover the Bark bands k and k + 32).  The three genuine whole-signal
+// dependencies of the model -- the band means over all non-silent frames
+// (torch_pesq/loss.py:205-216), the two-tap smoothing of the frame power
+// ratio across frames (loss.py:224-226) and the overlapping 20-frame windows
+// (loss.py:257-266) -- are resolved with cluster barriers: band partial sums
+// are exchanged through distributed shared memory, per-frame values through
+// the saved-state arrays in global memory.  Every reduction has a fixed
+// order, so results are bitwise reproducible.
+//
+// The Bark spectra arrive unscaled; the level alignment (loss.py:132-139)
+// enters as s^2 = 1e7 / P with P = sum (H x)^2 / (N + 5120) / 1.04684.
+#include <math.h>
+
+#include "kernels.cuh"
+
+namespace pesq {
+
+constexpr int kChainThreads = 256;
+constexpr int kChainWarps = kChainThreads / 32;
+// Above this distance from the threshold the loudness base^e - 1 is evaluated
+// with powf; below it with expm1(e log1p(.)), which keeps full relative
+// precision as the base approaches one.
+constexpr float kLoudSplit = 64.0f;
+
+ChainLayout ChainLayout::make(int T, int nb) {
+  ChainLayout l;
+  l.T = T;
+  l.nb = nb;
+  l.L = T >= 20 ? (T - 20) / 10 + 1 : 0;
+  auto up = [](int64_t v) { return (v + 3) & ~int64_t(3); };
+  int64_t o = 0;
+  auto take = [&](int64_t n) {
+    const int64_t at = o;
+    o += up(n);
+    return at;
+  };
+  l.keep = take(T);
+  l.taer = take(T);
+  l.tad = take(T);
+  l.fpr0 = take(T);
+  l.fpr1 = take(T);
+  l.h = take(T);
+  l.sraw = take(T);
+  l.araw = take(T);
+  l.sp = take(T);
+  l.ap = take(T);
+  l.gfpr = 0;
+  l.psqm_s = take(l.L);
+  l.psqm_a = take(l.L);
+  l.bpr = take(nb);
+  l.ratio = take(nb);
+  l.mref = take(nb);
+  l.mdeg = take(nb);
+  l.scal = take(kNumScalars);
+  l.stride = o;
+  return l;
+}
+
+namespace {
+
+__device__ __forceinline__ float loudness(float x, float th, float inv2th, float e, float ls) {
+  if (!(x > th)) return 0.0f;
+  const float bm1 = (x - th) * inv2th;
+  const float v = bm1 <= kLoudSplit ? expm1f(e * log1pf(bm1)) : powf(1.0f + bm1, e) - 1.0f;
+  return ls * v;
+}
+
+// d loudness / dx
+__device__ __forceinline__ float dloudness(float x, float th, float inv2th, float e, float dls) {
+  if (!(x > th)) return 0.0f;
+  const float bm1 = (x - th) * inv2th;
+  return dls * powf(1.0f + bm1, e - 1.0f);
+}
+
+__device__ __forceinline__ float sgnf(float v) { return v > 0.0f ? 1.0f : (v < 0.0f ? -1.0f : 0.0f); }
+
+struct Band {
+  int k;
+  bool ok;    // k < nb
+  bool norm;  // contributes to the weighted norms (k >= 1)
+  float th, inv2th, e, ls, dls, w, th100;
+  __device__ void load(const DevTables& t, int kk) {
+    k = kk;
+    ok = kk < t.nb;
+    norm = ok && kk >= 1;
+    const int i = ok ? kk : 0;
+    th = t.thresh[i];
+    inv2th = t.inv2th[i];
+    e = t.expo[i];
+    ls = t.loud_scale[i];
+    dls = t.dloud_scale[i];
+    w = t.width[i];
+    th100 = th * 100.0f;
+  }
+};
+
+// loudness, disturbance and the asymmetry factor of one band of one frame
+struct Cell {
+  float er, ed, lr, ld, u, zz, dist, asc_raw, asc;
+  __device__ void eval(const Band& b, float R, float D, float bpr, float fpr) {
+    er = bpr * R;
+    ed = fpr * D;
+    lr = loudness(er, b.th, b.inv2th, b.e, b.ls);
+    ld = loudness(ed, b.th, b.inv2th, b.e, b.ls);
+    u = ld - lr;
+    zz = fabsf(u) - 0.25f * fminf(ld, lr);
+    dist = sgnf(u) * fmaxf(zz, 0.0f);
+    asc_raw = powf((ed + 50.0f) / (er + 50.0f), 1.2f);
+    asc = asc_raw < 3.0f ? 0.0f : fminf(asc_raw, 12.0f);
+  }
+};
+
+__device__ __forceinline__ void load_tables(DevTables* dst, const DevTables* src) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  for (int i = threadIdx.x; i < (int)(sizeof(DevTables) / 16); i += blockDim.x) d4[i] = s4[i];
+}
+
+__device__ __forceinline__ void slice(int T, int& lo, int& hi) {
+  const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
+  const int warp = threadIdx.x >> 5;
+  const int c_lo = (int)((int64_t)q * T / C), c_hi = (int)((int64_t)(q + 1) * T / C);
+  const int n = c_hi - c_lo;
+  lo = c_lo + warp * n / kChainWarps;
+  hi = c_lo + (warp + 1) * n / kChainWarps;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __grid_constant__ ChainFwdArgs p) {
+  __shared__ DevTables tab;
+  __shared__ double wpr[kChainWarps][kMaxBands], wpd[kChainWarps][kMaxBands];
+  __shared__ double part_r[kMaxBands], part_d[kMaxBands];
+  __shared__ float bpr_s[kMaxBands];
+  __shared__ float s2s[2];
+
+  const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
+  const int u = blockIdx.x / C;
+  const int B = p.batch, T = p.lay.T, L = p.lay.L;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  load_tables(&tab, p.tab);
+  if (threadIdx.x == 0) {
+    // level alignment power of both rows, loss.py:132-136
+    const double denom = ((double)p.n + 5120.0) * 1.04684;
+    for (int side = 0; side < 2; ++side) {
+      const int r = side == 0 ? u : B + u;
+      double tot = 0.0;
+      for (int s = 0; s < p.nseg; ++s) tot += p.partial[(int64_t)r * p.nseg + s];
+      s2s[side] = (float)(1e7 / (tot / denom));
+      if (q == 0) p.sumsq[r] = tot;
+    }
+  }
+  __syncthreads();
+  const float s2r = s2s[0], s2d = s2s[1];
+  const int nb = tab.nb;
+  float* sv = p.saved + (int64_t)u * p.lay.stride;
+  const float* Fr = p.bark + (int64_t)u * T * nb;
+  const float* Fd = p.bark + (int64_t)(B + u) * T * nb;
+
+  Band b0, b1;
+  b0.load(tab, lane);
+  b1.load(tab, lane + 32);
+  int lo, hi;
+  slice(T, lo, hi);
+
+  // pass A: silent frames (loss.py:206) and band sums of audible power over
+  // the non-silent frames (loudness.py:297-320)
+  {
+    double ar0 = 0.0, ar1 = 0.0, ad0 = 0.0, ad1 = 0.0;
+    for (int t = lo; t < hi; ++t) {
+      const float* fr = Fr + (int64_t)t * nb;
+      const float* fd = Fd + (int64_t)t * nb;
+      const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+      const float a0 = R0 > b0.th100 ? R0 : 0.0f, a1 = R1 > b1.th100 ? R1 : 0.0f;
+      const float tot = warp_sum(a0 + a1);
+      const bool keep = !(tot < 1e7f);
+      if (lane == 0) sv[p.lay.keep + t] = keep ? 1.0f : 0.0f;
+      if (keep) {
+        ar0 += a0;
+        ar1 += a1;
+        ad0 += D0 > b0.th100 ? D0 : 0.0f;
+        ad1 += D1 > b1.th100 ? D1 : 0.0f;
+      }
+    }
+    wpr[warp][lane] = ar0;
+    wpd[warp][lane] = ad0;
+    if (lane + 32 < kMaxBands) {
+      wpr[warp][lane + 32] = ar1;
+      wpd[warp][lane + 32] = ad1;
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+    double r = 0.0, d = 0.0;
+    for (int w = 0; w < kChainWarps; ++w) {
+      r += wpr[w][k];
+      d += wpd[w][k];
+    }
+    part_r[k] = r;
+    part_d[k] = d;
+  }
+  cluster_sync();
+  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+    double r = 0.0, d = 0.0;
+    for (int c = 0; c < C; ++c) {
+      r += dsmem_ld_f64(dsmem_addr(&part_r[k], c));
+      d += dsmem_ld_f64(dsmem_addr(&part_d[k], c));
+    }
+    // band power ratio, loss.py:212-216
+    const float mr = (float)(r / T), md = (float)(d / T);
+    const float ratio = (md + 1000.0f) / (mr + 1000.0f);
+    const float bpr = fminf(fmaxf(ratio, 0.01f), 100.0f);
+    bpr_s[k] = bpr;
+    if (q == 0) {
+      sv[p.lay.bpr + k] = bpr;
+      sv[p.lay.ratio + k] = ratio;
+      sv[p.lay.mref + k] = mr;
+      sv[p.lay.mdeg + k] = md;
+    }
+  }
+  if (q == 0 && threadIdx.x == 0) {
+    sv[p.lay.scal + kS2Ref] = s2r;
+    sv[p.lay.scal + kS2Deg] = s2d;
+  }
+  __syncthreads();
+
+  // pass B: frame power ratio, loudness, disturbance and the weighted norms
+  // (loss.py:217-255)
+  {
+    const float bpr0 = b0.ok ? bpr_s[b0.k] : 0.0f, bpr1 = b1.ok ? bpr_s[b1.k] : 0.0f;
+    const float W = tab.total_width, sqW = tab.sqrt_total_width;
+    auto audible = [&](int t, float& taer, float& tad) {
+      const float* fr = Fr + (int64_t)t * nb;
+      const float* fd = Fd + (int64_t)t * nb;
+      const float er0 = b0.ok ? bpr0 * (s2r * fr[b0.k]) : 0.0f, er1 = b1.ok ? bpr1 * (s2r * fr[b1.k]) : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+      taer = warp_sum((er0 > b0.th ? er0 : 0.0f) + (er1 > b1.th ? er1 : 0.0f));
+      tad = warp_sum((D0 > b0.th ? D0 : 0.0f) + (D1 > b1.th ? D1 : 0.0f));
+    };
+    float fpr0_prev = 0.0f;
+    if (lo < hi && lo > 0) {
+      float ta, td;
+      audible(lo - 1, ta, td);
+      fpr0_prev = (ta + 5e3f) / (td + 5e3f);
+    }
+    for (int t = lo; t < hi; ++t) {
+      const float* fr = Fr + (int64_t)t * nb;
+      const float* fd = Fd + (int64_t)t * nb;
+      const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+      float taer, tad;
+      audible(t, taer, tad);
+      const float fpr0 = (taer + 5e3f) / (tad + 5e3f);
+      const float fpr1 = t == 0 ? fpr0 : fpr0 * 0.8f + fpr0_prev * 0.2f;
+      const float fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
+      const float h = powf((taer + 1e5f) / 1e7f, 0.04f);
+      Cell c0, c1;
+      c0.eval(b0, R0, D0, bpr0, fpr);
+      c1.eval(b1, R1, D1, bpr1, fpr);
+      float qs = 0.0f, qa = 0.0f;
+      if (b0.norm) {
+        const float v = b0.w * c0.dist;
+        qs = v * v;
+        qa = fabsf(b0.w * (c0.dist * c0.asc));
+      }
+      if (b1.norm) {
+        const float v = b1.w * c1.dist;
+        qs = fmaf(v, v, qs);
+        qa += fabsf(b1.w * (c1.dist * c1.asc));
+      }
+      qs = warp_sum(qs);
+      qa = warp_sum(qa);
+      const float sraw = sqW * sqrtf(qs);
+      const float araw = qa;
+      const float sp = fminf(fmaxf(sraw, 1e-20f) / h, 45.0f);
+      const float ap = fminf(fmaxf(araw, 1e-20f) / h, 45.0f);
+      if (lane == 0) {
+        sv[p.lay.taer + t] = taer;
+        sv[p.lay.tad + t] = tad;
+        sv[p.lay.fpr0 + t] = fpr0;
+        sv[p.lay.fpr1 + t] = fpr1;
+        sv[p.lay.h + t] = h;
+        sv[p.lay.sraw + t] = sraw;
+        sv[p.lay.araw + t] = araw;
+        sv[p.lay.sp + t] = sp;
+        sv[p.lay.ap + t] = ap;
+      }
+      fpr0_prev = fpr0;
+    }
+    (void)W;
+  }
+  __threadfence();
+  cluster_sync();
+
+  // pass C (rank 0): sixth-power means over 20-frame windows, then the RMS
+  // over windows (loss.py:257-266), both normalised by their maximum so that
+  // the 1e-20 floor of the disturbance does not underflow
+  if (q == 0) {
+    for (int side = 0; side < 2; ++side) {
+      const int64_t src = side == 0 ? p.lay.sp : p.lay.ap;
+      const int64_t dst = side == 0 ? p.lay.psqm_s : p.lay.psqm_a;
+      for (int l = warp; l < L; l += kChainWarps) {
+        const float s = lane < 20 ? __ldcg(sv + src + 10 * l + lane) : 0.0f;
+        const float mx = warp_max(s);
+        const float sc = mx > 0.0f ? mx : 1.0f;
+        const float v = s / sc, v2 = v * v;
+        const float m6 = warp_sum(lane < 20 ? v2 * v2 * v2 : 0.0f) / 20.0f;
+        if (lane == 0) sv[dst + l] = mx * powf(m6, 1.0f / 6.0f);
+      }
+    }
+    __syncthreads();
+    if (warp < 2) {
+      const int64_t src = warp == 0 ? p.lay.psqm_s : p.lay.psqm_a;
+      float mx = 0.0f;
+      for (int l = lane; l < L; l += 32) mx = fmaxf(mx, sv[src + l]);
+      mx = warp_max(mx);
+      const float sc = mx > 0.0f ? mx : 1.0f;
+      float acc = 0.0f;
+      for (int l = lane; l < L; l += 32) {
+        const float v = sv[src + l] / sc;
+        acc = fmaf(v, v, acc);
+      }
+      acc = warp_sum(acc);
+      const float d = mx * sqrtf(acc / (float)L);
+      if (lane == 0) {
+        sv[p.lay.scal + (warp == 0 ? kDSymm : kDAsymm)] = d;
+        s2s[warp] = d;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float ds = s2s[0], da = s2s[1];
+      if (p.d_symm) p.d_symm[u] = ds;
+      if (p.d_asymm) p.d_asymm[u] = da;
+      // MOS compression and loss (loss.py:289-297, loss.py:320-322)
+      const float m = 4.5f - 0.1f * ds - 0.0309f * da;
+      if (p.mos) p.mos[u] = 0.999f + 4.0f / (1.0f + expf(-1.3669f * m + 3.8224f));
+      if (p.loss) p.loss[u] = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
+    }
+  }
+  // keep every CTA's shared memory alive until the cluster is done with it
+  cluster_sync();
+}
+
+// ---------------------------------------------------------------------------
+// adjoint
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __grid_constant__ ChainBwdArgs p) {
+  __shared__ DevTables tab;
+  __shared__ double wpart[kChainWarps][kMaxBands];
+  __shared__ double part[kMaxBands];
+  __shared__ float gm_r[kMaxBands], gm_d[kMaxBands];
+  __shared__ double kap[kChainWarps][2];
+  __shared__ double kpart[2];
+
+  const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
+  const int u = blockIdx.x / C;
+  const int B = p.batch, T = p.lay.T, L = p.lay.L;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  load_tables(&tab, p.tab);
+  __syncthreads();
+  const int nb = tab.nb;
+  const float* sv = p.saved + (int64_t)u * p.lay.stride;
+  float* gf = p.scratch + (int64_t)u * 2 * T;  // [g_fpr | g_h] per frame
+  const float s2r = sv[p.lay.scal + kS2Ref], s2d = sv[p.lay.scal + kS2Deg];
+  const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
+  const float* Fr = p.bark + (int64_t)u * T * nb;
+  const float* Fd = p.bark + (int64_t)(B + u) * T * nb;
+  float* gR = p.g_bark + (int64_t)u * T * nb;
+  float* gD = p.g_bark + (int64_t)(B + u) * T * nb;
+
+  // upstream gradients of both distances (epilogue adjoint)
+  float gds = p.g_dsymm ? p.g_dsymm[u] : 0.0f;
+  float gda = p.g_dasymm ? p.g_dasymm[u] : 0.0f;
+  if (p.g_loss) {
+    gds += (float)(p.g_loss[u] * p.factor * 0.1);
+    gda += (float)(p.g_loss[u] * p.factor * 0.0309);
+  }
+  if (p.g_mos) {
+    const float m = 4.5f - 0.1f * ds - 0.0309f * da;
+    const float ex = expf(-1.3669f * m + 3.8224f);
+    const float den = 1.0f + ex;
+    const float dm = 4.0f * 1.3669f * ex / (den * den);
+    gds += p.g_mos[u] * dm * -0.1f;
+    gda += p.g_mos[u] * dm * -0.0309f;
+  }
+
+  Band b0, b1;
+  b0.load(tab, lane);
+  b1.load(tab, lane + 32);
+  const float bpr0 = b0.ok ? sv[p.lay.bpr + b0.k] : 0.0f, bpr1 = b1.ok ? sv[p.lay.bpr + b1.k] : 0.0f;
+  const float W = tab.total_width;
+  int lo, hi;
+  slice(T, lo, hi);
+
+  // dL/d(frame distance) through the windows, the RMS, the 45 clamp, /h and
+  // the 1e-20 floor
+  auto frame_grads = [&](int t, float& g_sraw, float& g_araw, float& g_h) {
+    const float h = sv[p.lay.h + t];
+    g_sraw = g_araw = g_h = 0.0f;
+    for (int side = 0; side < 2; ++side) {
+      const float d = side == 0 ? ds : da;
+      const float gd = side == 0 ? gds : gda;
+      const int64_t pq = side == 0 ? p.lay.psqm_s : p.lay.psqm_a;
+      const float s = sv[(side == 0 ? p.lay.sp : p.lay.ap) + t];
+      const float raw = sv[(side == 0 ? p.lay.sraw : p.lay.araw) + t];
+      float gs = 0.0f;
+      if (d > 0.0f) {
+        const int l_lo = t >= 19 ? (t - 19 + 9) / 10 : 0;
+        const int l_hi = min(L - 1, t / 10);
+        for (int l = l_lo; l <= l_hi; ++l) {
+          const float pl = sv[pq + l];
+          if (pl > 0.0f) {
+            const float r = s / pl, r2 = r * r;
+            gs += pl * (r2 * r2 * r);
+          }
+        }
+        gs *= gd / (20.0f * (float)L * d);
+      }
+      const float c = fmaxf(raw, 1e-20f);
+      const bool inside = c / h <= 45.0f;
+      const float gc = inside ? gs / h : 0.0f;
+      g_h -= inside ? gs * c / (h * h) : 0.0f;
+      const float graw = raw >= 1e-20f ? gc : 0.0f;
+      if (side == 0)
+        g_sraw = graw;
+      else
+        g_araw = graw;
+    }
+  };
+
+  // pass 1: loudness / disturbance / norm adjoint per band; per-frame dL/dfpr
+  for (int t = lo; t < hi; ++t) {
+    const float* fr = Fr + (int64_t)t * nb;
+    const float* fd = Fd + (int64_t)t * nb;
+    const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
+    const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+    const float fpr = fminf(fmaxf(sv[p.lay.fpr1 + t], 3e-4f), 5.0f);
+    const float sraw = sv[p.lay.sraw + t];
+    float g_sraw, g_araw, g_h;
+    frame_grads(t, g_sraw, g_araw, g_h);
+    const float coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
+
+    float gfpr = 0.0f;
+    for (int half = 0; half < 2; ++half) {
+      const Band& b = half == 0 ? b0 : b1;
+      if (!b.ok) continue;
+      const float R = half == 0 ? R0 : R1, D = half == 0 ? D0 : D1;
+      Cell c;
+      c.eval(b, R, D, half == 0 ? bpr0 : bpr1, fpr);
+      float g_dist = 0.0f, g_asc = 0.0f;
+      if (b.norm) {
+        g_dist = coef * (b.w * b.w) * c.dist;
+        const float y = c.dist * c.asc;
+        const float g_y = g_araw * b.w * sgnf(y);
+        g_dist += g_y * c.asc;
+        g_asc = g_y * c.dist;
+      }
+      const float su = sgnf(c.u);
+      const float g_z = c.zz >= 0.0f ? g_dist * su : 0.0f;
+      const float g_u = g_z * su;
+      const float g_dz = -g_z;
+      const float wd = c.ld < c.lr ? 1.0f : (c.ld == c.lr ? 0.5f : 0.0f);
+      const float wr = c.lr < c.ld ? 1.0f : (c.ld == c.lr ? 0.5f : 0.0f);
+      const float g_ld = g_u + 0.25f * g_dz * wd;
+      const float g_lr = -g_u + 0.25f * g_dz * wr;
+      float g_ed = g_ld * dloudness(c.ed, b.th, b.inv2th, b.e, b.dls);
+      float g_er = g_lr * dloudness(c.er, b.th, b.inv2th, b.e, b.dls);
+      if (c.asc_raw >= 3.0f && c.asc_raw <= 12.0f) {
+        g_ed += g_asc * 1.2f * c.asc_raw / (c.ed + 50.0f);
+        g_er -= g_asc * 1.2f * c.asc_raw / (c.er + 50.0f);
+      }
+      gfpr = fmaf(g_ed, D, gfpr);
+      gD[(int64_t)t * nb + b.k] = g_ed;
+      gR[(int64_t)t * nb + b.k] = g_er;
+    }
+    gfpr = warp_sum(gfpr);
+    if (lane == 0) {
+      gf[t] = gfpr;
+      gf[T + t] = g_h;
+    }
+  }
+  __threadfence();
+  cluster_sync();
+
+  // pass 2: smoothing / clamp / frame ratio adjoint, then the total audible
+  // energies; band sums of dL/dbpr
+  {
+    double acc0 = 0.0, acc1 = 0.0;
+    for (int t = lo; t < hi; ++t) {
+      const float* fr = Fr + (int64_t)t * nb;
+      const float* fd = Fd + (int64_t)t * nb;
+      auto clamp_pass = [&](int tt) {
+        const float f1 = sv[p.lay.fpr1 + tt];
+        return (f1 >= 3e-4f && f1 <= 5.0f) ? __ldcg(gf + tt) : 0.0f;
+      };
+      const float g1 = clamp_pass(t);
+      const float g1n = t + 1 < T ? clamp_pass(t + 1) : 0.0f;
+      const float g_fpr0 = (t == 0 ? g1 : 0.8f * g1) + 0.2f * g1n;
+      const float taer = sv[p.lay.taer + t], tad = sv[p.lay.tad + t];
+      const float fpr0 = sv[p.lay.fpr0 + t], h = sv[p.lay.h + t];
+      const float fpr = fminf(fmaxf(sv[p.lay.fpr1 + t], 3e-4f), 5.0f);
+      const float g_h = __ldcg(gf + T + t);
+      const float g_taer = g_fpr0 / (tad + 5e3f) + g_h * 0.04f * h / (taer + 1e5f);
+      const float g_tad = -g_fpr0 * fpr0 / (tad + 5e3f);
+      for (int half = 0; half < 2; ++half) {
+        const Band& b = half == 0 ? b0 : b1;
+        if (!b.ok) continue;
+        const int64_t o = (int64_t)t * nb + b.k;
+        const float R = s2r * fr[b.k], D = s2d * fd[b.k];
+        const float bpr = half == 0 ? bpr0 : bpr1;
+        const float er = bpr * R;
+        const float g_er = gR[o] + (er > b.th ? g_taer : 0.0f);
+        gR[o] = g_er * bpr;
+        const double contrib = (double)g_er * (double)R;
+        if (half == 0)
+          acc0 += contrib;
+        else
+          acc1 += contrib;
+        gD[o] = gD[o] * fpr + (D > b.th ? g_tad : 0.0f);
+      }
+    }
+    wpart[warp][lane] = acc0;
+    if (lane + 32 < kMaxBands) wpart[warp][lane + 32] = acc1;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+    double s = 0.0;
+    for (int w = 0; w < kChainWarps; ++w) s += wpart[w][k];
+    part[k] = s;
+  }
+  cluster_sync();
+  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+    double g = 0.0;
+    for (int c = 0; c < C; ++c) g += dsmem_ld_f64(dsmem_addr(&part[k], c));
+    // band ratio clamp and quotient (loss.py:212-216), then the mean over T
+    const float ratio = sv[p.lay.ratio + k], mr = sv[p.lay.mref + k];
+    const float g_ratio = (ratio >= 0.01f && ratio <= 100.0f) ? (float)g : 0.0f;
+    gm_r[k] = -g_ratio * ratio / (mr + 1000.0f) / (float)T;
+    gm_d[k] = g_ratio / (mr + 1000.0f) / (float)T;
+  }
+  __syncthreads();
+
+  // pass 3: band means over the non-silent frames; scale to the unscaled
+  // spectrum and accumulate <g, F> for the alignment term
+  {
+    double kr = 0.0, kd = 0.0;
+    const float gmr0 = b0.ok ? gm_r[b0.k] : 0.0f, gmr1 = b1.ok ? gm_r[b1.k] : 0.0f;
+    const float gmd0 = b0.ok ? gm_d[b0.k] : 0.0f, gmd1 = b1.ok ? gm_d[b1.k] : 0.0f;
+    for (int t = lo; t < hi; ++t) {
+      const float* fr = Fr + (int64_t)t * nb;
+      const float* fd = Fd + (int64_t)t * nb;
+      const bool keep = sv[p.lay.keep + t] != 0.0f;
+      for (int half = 0; half < 2; ++half) {
+        const Band& b = half == 0 ? b0 : b1;
+        if (!b.ok) continue;
+        const int64_t o = (int64_t)t * nb + b.k;
+        const float Fv = fr[b.k], Gv = fd[b.k];
+        const float R = s2r * Fv, D = s2d * Gv;
+        float gr = gR[o], gd = gD[o];
+        if (keep && R > b.th100) gr += half == 0 ? gmr0 : gmr1;
+        if (keep && D > b.th100) gd += half == 0 ? gmd0 : gmd1;
+        gr *= s2r;
+        gd *= s2d;
+        gR[o] = gr;
+        gD[o] = gd;
+        kr += (double)gr * (double)Fv;
+        kd += (double)gd * (double)Gv;
+      }
+    }
+    kr = warp_sum(kr);
+    kd = warp_sum(kd);
+    if (lane == 0) {
+      kap[warp][0] = kr;
+      kap[warp][1] = kd;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 2) {
+    double s = 0.0;
+    for (int w = 0; w < kChainWarps; ++w) s += kap[w][threadIdx.x];
+    kpart[threadIdx.x] = s;
+  }
+  cluster_sync();
+  if (q == 0 && threadIdx.x < 2) {
+    double s = 0.0;
+    for (int c = 0; c < C; ++c) s += dsmem_ld_f64(dsmem_addr(&kpart[threadIdx.x], c));
+    const int r = threadIdx.x == 0 ? u : B + u;
+    p.kappa[r] = (float)(2.0 * s / p.sumsq[r]);
+  }
+  cluster_sync();
+}
+
+template <class Kernel, class Args>
+cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, cudaStream_t s) {
+  if (batch <= 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * cluster));
+  cfg.blockDim = dim3(kChainThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, a);
+}
+
+}  // namespace
+
+cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s) {
+  return launch_cluster(chain_fwd_kernel, a, a.batch, cluster, s);
+}
+
+cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s) {
+  return launch_cluster(chain_bwd_kernel, a, a.batch, cluster, s);
+}
+
+}  // namespace pesq

@@ -1,0 +1,169 @@
+// Shared constants and small device helpers of the PESQ engine (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pesq {
+
+// ---------------------------------------------------------------------------
+// geometry of the streaming kernels
+// ---------------------------------------------------------------------------
+
+// Threads of the streaming (front / back / iir) kernels; each thread owns one
+// chunk of the covered span.
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+// Samples per thread chunk.  33 is coprime with the 32 shared memory banks, so
+// the stride-33 per-thread walks over a linearly staged span never conflict.
+constexpr int kChunk = 33;
+// Kogge-Stone doubling levels of the in-CTA state scan: the state handed to a
+// chunk accounts for the previous kHorizonChunks chunks exactly and drops
+// A^(kChunk * kHorizonChunks), whose norm the host checks (< 1e-11).
+constexpr int kLevels = 5;
+constexpr int kHorizonChunks = 1 << kLevels;
+constexpr int kHorizon = kChunk * kHorizonChunks;  // 1056 samples
+constexpr int kSpan = kThreads * kChunk;           // 16896 samples per CTA
+
+// STFT of the PESQ model: 512-point frames, hop 256, 256 usable bins.
+constexpr int kNfft = 512;
+constexpr int kHop = 256;
+constexpr int kBins = 256;
+constexpr int kMaxBands = 64;
+
+// Largest state size of a filter handled by the chunked scan.
+constexpr int kMaxStates = 16;
+
+// ---------------------------------------------------------------------------
+// small helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Linear fade of the first and last 15 samples of a row, applied as
+// (value * head) * tail in that order; both factors are 1 outside their ramp.
+// Mirrors the two sequential in-place products of torch_pesq/loss.py:163-165.
+__device__ __forceinline__ float edge_ramp(float v, int64_t n, int64_t len) {
+  const float head = n < 15 ? (float)(n + 1) * 0.0625f : 1.0f;
+  const float tail = n >= len - 15 ? (float)(len - n) * 0.0625f : 1.0f;
+  return (v * head) * tail;
+}
+
+// ---------------------------------------------------------------------------
+// thread block cluster primitives (distributed shared memory)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Full cluster barrier with release/acquire semantics on shared::cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of `ptr` (a shared memory variable of this CTA) in the shared
+// memory window of cluster rank `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* ptr, uint32_t rank) {
+  uint32_t local = (uint32_t)__cvta_generic_to_shared(ptr);
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ float dsmem_ld_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ double dsmem_ld_f64(uint32_t addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// 1D bulk copy (TMA) global -> shared, completion on an mbarrier
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          (uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
+      : "memory");
+}
+
+// Bounded wait on phase `parity` of an mbarrier.  Returns false when the wait
+// gave up; the caller records the failure instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = (uint32_t)__cvta_generic_to_shared(bar);
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Device-side error flags, OR-ed into a word the host reads back on demand.
+enum : uint32_t {
+  kErrBulkTimeout = 1u << 0,
+  kErrBadGeometry = 1u << 1,
+};
+
+}  // namespace pesq

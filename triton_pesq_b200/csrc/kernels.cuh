@@ -1,0 +1,164 @@
+// Launch-side declarations shared by the kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "scan.cuh"
+
+namespace pesq {
+
+using PowTab = ScanTab<10>;
+using PreTab = ScanTab<2>;
+
+// Device constant tables of a plan (uploaded once, read-only afterwards).
+struct alignas(16) DevTables {
+  float window[kNfft];      // analysis window, zero padded/centred to n_fft
+  float2 tw256[256];        // exp(-2 pi i k / 256)
+  float2 tw512[256];        // exp(-2 pi i k / 512), k < 256
+  int bin_band[kBins];         // band owning bin f, -1 if none (bin 0 never has one)
+  int band_start[kMaxBands];
+  int band_end[kMaxBands];
+  float band_corr[kMaxBands];  // power density correction
+  float thresh[kMaxBands];     // hearing threshold
+  float inv2th[kMaxBands];     // 0.5 / threshold
+  float expo[kMaxBands];       // loudness exponent
+  float loud_scale[kMaxBands]; // Sl * (2 th)^e
+  float dloud_scale[kMaxBands];// Sl * (2 th)^e * e * 0.5 / th
+  float width[kMaxBands];      // band width in Bark
+  float width_sq[kMaxBands];   // width^2
+  int nb;
+  float total_width;           // sum of widths of bands 1..nb-1
+  float sqrt_total_width;
+};
+
+// Rows of one call: ref rows are 0..B-1, deg rows B..2B-1.
+struct RowSource {
+  const float* ref;
+  const float* deg;
+  int64_t ld_ref;
+  int64_t ld_deg;
+  int batch;
+  __device__ __forceinline__ const float* row(int r) const {
+    return r < batch ? ref + (int64_t)r * ld_ref : deg + (int64_t)(r - batch) * ld_deg;
+  }
+};
+
+struct RowSink {
+  float* ref;
+  float* deg;
+  int64_t ld_ref;
+  int64_t ld_deg;
+  int batch;
+  __device__ __forceinline__ float* row(int r) const {
+    return r < batch ? ref + (int64_t)r * ld_ref : deg + (int64_t)(r - batch) * ld_deg;
+  }
+};
+
+struct FrontArgs {
+  RowSource src;     // 16 kHz rows
+  int64_t n;         // samples per row
+  int frames;        // T
+  int seg_frames;    // frames per segment
+  int nseg;          // segments per row
+  int z_begin;       // rows [z_begin, z_end) also produce z = H^T H x
+  int z_end;
+  const DevTables* tab;
+  float* bark;       // [rows][T][nb]   unscaled Bark spectrum
+  double* partial;   // [rows][nseg]    partial sums of (H x)^2
+  float* z;          // [rows][n]
+  uint32_t* err;
+};
+
+struct BackArgs {
+  RowSource src;     // 16 kHz rows (the forward input)
+  int row_begin;     // rows [row_begin, row_end) get a gradient
+  int64_t n;
+  int frames;
+  int seg_frames;
+  int nseg;
+  const DevTables* tab;
+  const float* g_bark;  // [rows][T][nb]  dL/d(unscaled Bark)
+  const float* kappa;   // [rows]
+  const float* z;       // [rows][n]
+  RowSink out;          // gradient rows (16 kHz)
+  uint32_t* err;
+};
+
+// Chain state saved by the forward for the backward, per utterance.
+struct ChainLayout {
+  int T;   // frames
+  int L;   // psqm windows
+  int nb;  // bands
+  int64_t stride;  // floats per utterance
+  // offsets (floats) of the per-utterance arrays
+  int64_t keep, taer, tad, fpr0, fpr1, h, sraw, araw, sp, ap, gfpr, psqm_s, psqm_a;
+  int64_t bpr, ratio, mref, mdeg, scal;
+  static ChainLayout make(int T, int nb);
+};
+
+enum ChainScalar { kS2Ref = 0, kS2Deg, kDSymm, kDAsymm, kNumScalars = 8 };
+
+struct ChainFwdArgs {
+  int batch;
+  int nseg;                 // partial sums per row
+  int64_t n;                // samples per row (for the power denominator)
+  const DevTables* tab;
+  const float* bark;        // [2B][T][nb]
+  const double* partial;    // [2B][nseg]
+  double* sumsq;            // [2B]  out
+  float* saved;             // [B][layout.stride]
+  ChainLayout lay;
+  double factor;
+  float* d_symm;            // [B] (nullable)
+  float* d_asymm;
+  float* mos;
+  float* loss;
+};
+
+struct ChainBwdArgs {
+  int batch;
+  const DevTables* tab;
+  const float* bark;
+  const double* sumsq;
+  const float* saved;       // forward state (read only)
+  float* scratch;           // [B][T] per-frame scratch (g_fpr)
+  ChainLayout lay;
+  double factor;
+  const float* g_loss;      // [B] nullable
+  const float* g_mos;       // [B] nullable
+  const float* g_dsymm;     // [B] nullable
+  const float* g_dasymm;    // [B] nullable
+  int want_ref, want_deg;
+  float* g_bark;            // [2B][T][nb]  out
+  float* kappa;             // [2B]         out
+};
+
+struct ResampleArgs {
+  RowSource src;        // source rows (fwd) / gradient of 16 kHz rows (adjoint)
+  RowSink dst;
+  int rows;             // 2B or the gradient rows
+  int row_begin;
+  int64_t n_in;
+  int64_t n_out;
+  int orig_step, new_step, width;
+  const float* taps;    // compact nonzero taps [new_step][max_count]
+  const int* first;     // [new_step]
+  const int* count;     // [new_step]
+  int max_count;
+  // adjoint gather lists per residue mod orig_step
+  const int* adj_offset;   // [orig_step + 1]
+  const int4* adj_entries; // (dl, phase, tap bits, 0)
+};
+
+cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab& pre, int rows, cudaStream_t s);
+cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s);
+cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
+cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);
+cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
+cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
+
+size_t front_smem_bytes();
+size_t back_smem_bytes();
+
+}  // namespace pesq

@@ -1,0 +1,527 @@
+// C ABI of the PESQ engine: plans, workspace layout and launch sequencing.
+//
+// Forward  : [resample] -> front (per row segment) -> chain forward (per utterance cluster)
+// Backward : chain adjoint (per utterance cluster) -> back (per row segment) -> [resample adjoint]
+//
+// Four kernels per direction at 16 kHz (the reference issues about forty).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../../include/pesq_cuda.h"
+#include "kernels.cuh"
+
+using namespace pesq;
+
+namespace pesq {
+cudaError_t configure_front();
+cudaError_t configure_back();
+}
+
+struct pesq_plan {
+  int device;
+  int sample_rate;
+  int nb;
+  double factor;
+  PowTab pow;
+  PreTab pre;
+  DevTables* dtab;  // device copy
+  // resampler
+  bool resample;
+  int orig_step, new_step, width, width_total, max_count;
+  float* taps;       // device [new_step][max_count]
+  int* first;        // device [new_step]
+  int* count;        // device [new_step]
+  int* adj_offset;   // device [orig_step + 1]
+  int4* adj_entries; // device
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PESQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define PESQ_CUDA_TRY(expr, what)             \
+  do {                                        \
+    cudaError_t _e = (expr);                  \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+template <int P>
+int fill_scan(ScanTab<P>& t, const pesq_scan_desc& d, const char* name) {
+  if (d.states != P) return fail(PESQ_ERR_UNSUPPORTED, "%s: %d states, the kernels need %d", name, d.states, P);
+  if (d.chunk != kChunk || d.levels != kLevels)
+    return fail(PESQ_ERR_UNSUPPORTED, "%s: chunk %d / levels %d, the kernels need %d / %d", name, d.chunk,
+                d.levels, kChunk, kLevels);
+  if (!d.impulse || !d.carry || !d.drive || !d.power || !d.trans || !d.input || !d.output)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "%s: missing table", name);
+  for (int k = 0; k < kChunk; ++k) {
+    t.h[k] = (float)d.impulse[k];
+    for (int j = 0; j < P; ++j) {
+      t.G[k][j] = (float)d.carry[k * P + j];
+      t.W[k][j] = (float)d.drive[k * P + j];
+    }
+  }
+  for (int l = 0; l < kLevels; ++l)
+    for (int i = 0; i < P; ++i)
+      for (int j = 0; j < P; ++j) t.M[l][i][j] = (float)d.power[(l * P + i) * P + j];
+  for (int i = 0; i < P; ++i) {
+    for (int j = 0; j < P; ++j) t.A[i][j] = (float)d.trans[i * P + j];
+    t.B[i] = (float)d.input[i];
+    t.C[i] = (float)d.output[i];
+  }
+  t.D = (float)d.feed;
+  return PESQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// per-call geometry and workspace layout
+// ---------------------------------------------------------------------------
+
+constexpr int kMaxFrontFrames = (kSpan - 2 * kHorizon) / kHop;         // 57
+constexpr int kMaxBackFrames = (kSpan - 2 * kHorizon - 3 * kHop) / kHop;  // 54
+
+struct Geometry {
+  int64_t batch, rows, n_src, n16;
+  int T, L, nb;
+  int f_seg, f_nseg;  // front segmentation
+  int b_seg, b_nseg;  // back segmentation
+  int cluster;
+  bool resample, grad;
+  int grad_begin, grad_end;
+  ChainLayout lay;
+  // byte offsets
+  size_t x16, partial, sumsq, bark, z, saved, gbark, kappa, cscratch, gx16, err, total;
+};
+
+void balance(int64_t n16, int max_frames, int& seg, int& nseg) {
+  const int64_t hops = ceil_div(n16, kHop);
+  nseg = (int)std::max<int64_t>(1, ceil_div(hops, max_frames));
+  seg = (int)ceil_div(hops, nseg);
+}
+
+int64_t resampled_length(const pesq_plan* p, int64_t n) {
+  if (!p->resample) return n;
+  const float q = (float)((double)p->new_step * (double)n / (double)p->orig_step);
+  return (int64_t)ceilf(q);
+}
+
+int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, Geometry& g) {
+  if (batch < 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "negative batch %lld", (long long)batch);
+  if (n_src <= 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "signals need at least one sample");
+  g.batch = batch;
+  g.rows = 2 * batch;
+  g.n_src = n_src;
+  g.resample = p->resample;
+  g.n16 = resampled_length(p, n_src);
+  const int64_t padded = g.n16 + g.n16 % 256;
+  g.T = padded < kNfft ? 0 : (int)(1 + (padded - kNfft) / kHop);
+  if (g.T < 20)
+    return fail(PESQ_ERR_INVALID_ARGUMENT,
+                "The PESQ chain needs at least 20 frames for the overlapping sums, got %d (%lld samples at 16 kHz).",
+                g.T, (long long)g.n16);
+  if (g.n16 > (int64_t)1 << 31 || g.rows > 65535)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "signal or batch too large (%lld samples, %lld rows)",
+                (long long)g.n16, (long long)g.rows);
+  g.L = (g.T - 20) / 10 + 1;
+  g.nb = p->nb;
+  balance(g.n16, kMaxFrontFrames, g.f_seg, g.f_nseg);
+  balance(g.n16, kMaxBackFrames, g.b_seg, g.b_nseg);
+  g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 48)));
+  g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
+  g.grad_begin = (flags & PESQ_GRAD_REF) ? 0 : (int)batch;
+  g.grad_end = (flags & PESQ_GRAD_DEG) ? (int)g.rows : (int)batch;
+  g.lay = ChainLayout::make(g.T, g.nb);
+
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += (bytes + 255) & ~(size_t)255;
+    return at;
+  };
+  const size_t rows = (size_t)g.rows;
+  g.x16 = take(g.resample ? rows * g.n16 * 4 : 0);
+  g.partial = take(rows * g.f_nseg * 8);
+  g.sumsq = take(rows * 8);
+  g.bark = take(rows * (size_t)g.T * g.nb * 4);
+  g.z = take(g.grad ? rows * g.n16 * 4 : 0);
+  g.saved = take((size_t)batch * g.lay.stride * 4);
+  g.gbark = take(g.grad ? rows * (size_t)g.T * g.nb * 4 : 0);
+  g.kappa = take(g.grad ? rows * 4 : 0);
+  g.cscratch = take(g.grad ? (size_t)batch * 2 * g.T * 4 : 0);
+  g.gx16 = take(g.grad && g.resample ? rows * g.n16 * 4 : 0);
+  g.err = take(16);
+  g.total = o;
+  return PESQ_OK;
+}
+
+template <class T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+int check_call(const pesq_plan* p, const Geometry& g, void* ws, size_t ws_bytes) {
+  if (!ws && g.total) return fail(PESQ_ERR_WORKSPACE, "workspace is NULL");
+  if (ws_bytes < g.total)
+    return fail(PESQ_ERR_WORKSPACE, "workspace of %zu bytes, the call needs %zu", ws_bytes, g.total);
+  if (((uintptr_t)ws & 255) != 0) return fail(PESQ_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != p->device)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "plan lives on device %d but device %d is current", p->device, dev);
+  return PESQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pesq_abi_version(void) { return PESQ_CUDA_ABI_VERSION; }
+
+const char* pesq_last_error(void) { return g_error.c_str(); }
+
+int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
+  g_error.clear();
+  if (!d || !out) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  *out = nullptr;
+  if (d->abi_version != PESQ_CUDA_ABI_VERSION)
+    return fail(PESQ_ERR_UNSUPPORTED, "ABI version %d, library has %d", d->abi_version, PESQ_CUDA_ABI_VERSION);
+  if (d->n_fft != kNfft || d->hop_length != kHop)
+    return fail(PESQ_ERR_UNSUPPORTED, "n_fft %d / hop %d: the kernels implement n_fft 512, hop 256", d->n_fft,
+                d->hop_length);
+  if (d->nbarks < 1 || d->nbarks > kMaxBands)
+    return fail(PESQ_ERR_UNSUPPORTED, "%d Bark bands, the kernels support 1..%d", d->nbarks, kMaxBands);
+  if (d->sample_rate <= 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "sample rate must be positive");
+  if (!d->window || !d->band_start || !d->band_end || !d->band_corr || !d->threshold || !d->exponent || !d->width)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing table");
+
+  pesq_plan* p = new pesq_plan();
+  memset(p, 0, sizeof(*p));
+  auto bail = [&](int code) {
+    pesq_plan_destroy(p);
+    return code;
+  };
+  if (cudaGetDevice(&p->device) != cudaSuccess) return bail(fail(PESQ_ERR_CUDA, "no CUDA device"));
+  p->sample_rate = d->sample_rate;
+  p->nb = d->nbarks;
+  p->factor = d->factor;
+  int rc = fill_scan<10>(p->pow, d->power_filter, "power filter");
+  if (rc) return bail(rc);
+  rc = fill_scan<2>(p->pre, d->pre_filter, "pre-emphasis filter");
+  if (rc) return bail(rc);
+
+  // constant tables
+  DevTables h;
+  memset(&h, 0, sizeof(h));
+  for (int k = 0; k < kNfft; ++k) h.window[k] = (float)d->window[k];
+  for (int k = 0; k < 256; ++k) {
+    h.tw256[k] = make_float2((float)cos(-2.0 * M_PI * k / 256.0), (float)sin(-2.0 * M_PI * k / 256.0));
+    h.tw512[k] = make_float2((float)cos(-2.0 * M_PI * k / 512.0), (float)sin(-2.0 * M_PI * k / 512.0));
+    h.bin_band[k] = -1;
+  }
+  int prev_end = 0;
+  for (int b = 0; b < d->nbarks; ++b) {
+    const int s = d->band_start[b], e = d->band_end[b];
+    if (s < 0 || e < s || e > kBins || s < prev_end)
+      return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "band %d covers [%d, %d): bands must be sorted, disjoint and below bin %d",
+                       b, s, e, kBins));
+    prev_end = e;
+    h.band_start[b] = s;
+    h.band_end[b] = e;
+    for (int f = std::max(s, 1); f < e; ++f) h.bin_band[f] = b;
+    const double th = d->threshold[b], ex = d->exponent[b];
+    if (!(th > 0.0)) return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "hearing thresholds must be positive"));
+    h.band_corr[b] = (float)d->band_corr[b];
+    h.thresh[b] = (float)th;
+    h.inv2th[b] = (float)(0.5 / (double)(float)th);
+    h.expo[b] = (float)ex;
+    const double ls = d->loudness_sl * pow(2.0 * th, ex);
+    h.loud_scale[b] = (float)ls;
+    h.dloud_scale[b] = (float)(ls * ex * 0.5 / th);
+    h.width[b] = (float)d->width[b];
+    h.width_sq[b] = (float)(d->width[b] * d->width[b]);
+  }
+  h.nb = d->nbarks;
+  h.total_width = (float)d->total_width;
+  h.sqrt_total_width = (float)sqrt(d->total_width);
+
+  if (cudaMalloc(&p->dtab, sizeof(DevTables)) != cudaSuccess)
+    return bail(fail(PESQ_ERR_CUDA, "cudaMalloc of the constant tables failed"));
+  if (cudaMemcpy(p->dtab, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(PESQ_ERR_CUDA, "upload of the constant tables failed"));
+
+  // resampler tables
+  p->resample = d->sample_rate != 16000;
+  if (p->resample) {
+    const int os = d->rs_orig_step, ns = d->rs_new_step, wt = d->rs_width_total;
+    if (os <= 0 || ns <= 0 || wt <= 0 || d->rs_width < 0 || !d->rs_taps)
+      return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "invalid resampler description"));
+    p->orig_step = os;
+    p->new_step = ns;
+    p->width = d->rs_width;
+    p->width_total = wt;
+    std::vector<int> first(ns), count(ns);
+    int maxc = 1;
+    for (int j = 0; j < ns; ++j) {
+      int lo = -1, hi = -1;
+      for (int k = 0; k < wt; ++k)
+        if ((float)d->rs_taps[(size_t)j * wt + k] != 0.0f) {
+          if (lo < 0) lo = k;
+          hi = k;
+        }
+      first[j] = lo < 0 ? 0 : lo;
+      count[j] = lo < 0 ? 0 : hi + 1 - lo;
+      maxc = std::max(maxc, count[j]);
+    }
+    std::vector<float> taps((size_t)ns * maxc, 0.0f);
+    for (int j = 0; j < ns; ++j)
+      for (int i = 0; i < count[j]; ++i) taps[(size_t)j * maxc + i] = (float)d->rs_taps[(size_t)j * wt + first[j] + i];
+    p->max_count = maxc;
+    // adjoint: per residue rho = k mod orig_step the (k / orig_step, phase, tap) triples
+    std::vector<int> offs(os + 1, 0);
+    std::vector<int4> ents;
+    for (int rho = 0; rho < os; ++rho) {
+      offs[rho] = (int)ents.size();
+      for (int k = rho; k < wt; k += os)
+        for (int j = 0; j < ns; ++j) {
+          const float v = (float)d->rs_taps[(size_t)j * wt + k];
+          if (v != 0.0f) {
+            int bits;
+            memcpy(&bits, &v, 4);
+            ents.push_back(make_int4((k - rho) / os, j, bits, 0));
+          }
+        }
+    }
+    offs[os] = (int)ents.size();
+    if (ents.empty()) ents.push_back(make_int4(0, 0, 0, 0));
+    bool ok = cudaMalloc(&p->taps, taps.size() * 4) == cudaSuccess &&
+              cudaMalloc(&p->first, ns * 4) == cudaSuccess && cudaMalloc(&p->count, ns * 4) == cudaSuccess &&
+              cudaMalloc(&p->adj_offset, (os + 1) * 4) == cudaSuccess &&
+              cudaMalloc(&p->adj_entries, ents.size() * sizeof(int4)) == cudaSuccess;
+    ok = ok && cudaMemcpy(p->taps, taps.data(), taps.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->first, first.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->count, count.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->adj_offset, offs.data(), (os + 1) * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->adj_entries, ents.data(), ents.size() * sizeof(int4), cudaMemcpyHostToDevice) ==
+             cudaSuccess;
+    if (!ok) return bail(fail(PESQ_ERR_CUDA, "upload of the resampler tables failed"));
+  }
+
+  cudaError_t e = configure_front();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the front kernel"));
+  e = configure_back();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the back kernel"));
+  *out = p;
+  return PESQ_OK;
+}
+
+int pesq_plan_destroy(pesq_plan* p) {
+  if (!p) return PESQ_OK;
+  cudaFree(p->dtab);
+  cudaFree(p->taps);
+  cudaFree(p->first);
+  cudaFree(p->count);
+  cudaFree(p->adj_offset);
+  cudaFree(p->adj_entries);
+  delete p;
+  return PESQ_OK;
+}
+
+int pesq_plan_device(const pesq_plan* p, int* device) {
+  if (!p || !device) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  *device = p->device;
+  return PESQ_OK;
+}
+
+int pesq_query_shape(const pesq_plan* p, int64_t n_src, pesq_shape* s) {
+  if (!p || !s) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  Geometry g;
+  const int rc = geometry(p, 1, n_src, 0, g);
+  if (rc) return rc;
+  s->n16 = g.n16;
+  s->frames = g.T;
+  s->windows = g.L;
+  return PESQ_OK;
+}
+
+int pesq_workspace_size(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, size_t* bytes) {
+  if (!p || !bytes) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  Geometry g;
+  const int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  *bytes = g.total;
+  return PESQ_OK;
+}
+
+int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                 int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
+                 float* d_symm, float* d_asymm, float* mos, float* loss) {
+  if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
+  Geometry g;
+  int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  if (batch == 0) return PESQ_OK;
+  if (!ref || !deg) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL input");
+  if (ld_ref < n_src || ld_deg < n_src) return fail(PESQ_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+  rc = check_call(p, g, ws, ws_bytes);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch};
+  if (g.resample) {
+    float* x16 = at<float>(ws, g.x16);
+    ResampleArgs ra{};
+    ra.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
+    ra.dst = RowSink{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+    ra.rows = (int)g.rows;
+    ra.row_begin = 0;
+    ra.n_in = n_src;
+    ra.n_out = g.n16;
+    ra.orig_step = p->orig_step;
+    ra.new_step = p->new_step;
+    ra.width = p->width;
+    ra.taps = p->taps;
+    ra.first = p->first;
+    ra.count = p->count;
+    ra.max_count = p->max_count;
+    ra.adj_offset = p->adj_offset;
+    ra.adj_entries = p->adj_entries;
+    PESQ_CUDA_TRY(launch_resample_fwd(ra, s), "resample kernel");
+    src16 = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+  }
+
+  FrontArgs fa{};
+  fa.src = src16;
+  fa.n = g.n16;
+  fa.frames = g.T;
+  fa.seg_frames = g.f_seg;
+  fa.nseg = g.f_nseg;
+  fa.z_begin = g.grad ? g.grad_begin : 0;
+  fa.z_end = g.grad ? g.grad_end : 0;
+  fa.tab = p->dtab;
+  fa.bark = at<float>(ws, g.bark);
+  fa.partial = at<double>(ws, g.partial);
+  fa.z = at<float>(ws, g.z);
+  fa.err = at<uint32_t>(ws, g.err);
+  PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre, (int)g.rows, s), "front kernel");
+
+  ChainFwdArgs ca{};
+  ca.batch = (int)batch;
+  ca.nseg = g.f_nseg;
+  ca.n = g.n16;
+  ca.tab = p->dtab;
+  ca.bark = fa.bark;
+  ca.partial = fa.partial;
+  ca.sumsq = at<double>(ws, g.sumsq);
+  ca.saved = at<float>(ws, g.saved);
+  ca.lay = g.lay;
+  ca.factor = p->factor;
+  ca.d_symm = d_symm;
+  ca.d_asymm = d_asymm;
+  ca.mos = mos;
+  ca.loss = loss;
+  PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, s), "chain forward kernel");
+  return PESQ_OK;
+}
+
+int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
+                  const float* g_loss, const float* g_mos, const float* g_dsymm, const float* g_dasymm,
+                  float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
+  if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
+  Geometry g;
+  int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  if (!g.grad) return fail(PESQ_ERR_INVALID_ARGUMENT, "backward without PESQ_GRAD_REF or PESQ_GRAD_DEG");
+  if (batch == 0) return PESQ_OK;
+  if ((flags & PESQ_GRAD_REF) && (!g_ref || ld_gref < n_src))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/dref output");
+  if ((flags & PESQ_GRAD_DEG) && (!g_deg || ld_gdeg < n_src))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/ddeg output");
+  rc = check_call(p, g, ws, ws_bytes);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  ChainBwdArgs cb{};
+  cb.batch = (int)batch;
+  cb.tab = p->dtab;
+  cb.bark = at<float>(ws, g.bark);
+  cb.sumsq = at<double>(ws, g.sumsq);
+  cb.saved = at<float>(ws, g.saved);
+  cb.scratch = at<float>(ws, g.cscratch);
+  cb.lay = g.lay;
+  cb.factor = p->factor;
+  cb.g_loss = g_loss;
+  cb.g_mos = g_mos;
+  cb.g_dsymm = g_dsymm;
+  cb.g_dasymm = g_dasymm;
+  cb.want_ref = (flags & PESQ_GRAD_REF) != 0;
+  cb.want_deg = (flags & PESQ_GRAD_DEG) != 0;
+  cb.g_bark = at<float>(ws, g.gbark);
+  cb.kappa = at<float>(ws, g.kappa);
+  PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, s), "chain backward kernel");
+
+  RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch};
+  float* gx16 = at<float>(ws, g.gx16);
+  if (g.resample) {
+    const float* x16 = at<float>(ws, g.x16);
+    src16 = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+  }
+  BackArgs ba{};
+  ba.src = src16;
+  ba.row_begin = g.grad_begin;
+  ba.n = g.n16;
+  ba.frames = g.T;
+  ba.seg_frames = g.b_seg;
+  ba.nseg = g.b_nseg;
+  ba.tab = p->dtab;
+  ba.g_bark = cb.g_bark;
+  ba.kappa = cb.kappa;
+  ba.z = at<float>(ws, g.z);
+  ba.out = g.resample ? RowSink{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch}
+                      : RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
+  ba.err = at<uint32_t>(ws, g.err);
+  PESQ_CUDA_TRY(launch_back(ba, p->pre, g.grad_end - g.grad_begin, s), "back kernel");
+
+  if (g.resample) {
+    ResampleArgs ra{};
+    ra.src = RowSource{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch};
+    ra.dst = RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
+    ra.rows = g.grad_end - g.grad_begin;
+    ra.row_begin = g.grad_begin;
+    ra.n_in = n_src;
+    ra.n_out = g.n16;
+    ra.orig_step = p->orig_step;
+    ra.new_step = p->new_step;
+    ra.width = p->width;
+    ra.taps = p->taps;
+    ra.first = p->first;
+    ra.count = p->count;
+    ra.max_count = p->max_count;
+    ra.adj_offset = p->adj_offset;
+    ra.adj_entries = p->adj_entries;
+    PESQ_CUDA_TRY(launch_resample_adj(ra, s), "resample adjoint kernel");
+  }
+  return PESQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+// Chunked parallel scan of a causal LTI filter over one CTA span.
+//
+// The filter is a state space recursion s[n+1] = A s[n] + B x[n],
+// y[n] = C s[n] + D x[n] (a series of balanced second order sections, built on
+// the host in float64, see triton_pesq_b200/tables.py).  A CTA covers
+// kSpan = kThreads * kChunk consecutive samples; thread c owns chunk c.
+//
+//   1. every thread forms the zero-state end state of its chunk,
+//      a_c = sum_k A^(L-1-k) B x[k]  (table W)
+//   2. a Kogge-Stone scan over the chunks with the doubling steps
+//      M_i = A^(L 2^i) turns a_c into E_c = sum_{j < 32} A^(L j) a_{c-j}: the
+//      end state of chunk c with everything older than kHorizon samples
+//      dropped.  The dropped term is bounded by ||A^kHorizon|| (< 1e-11,
+//      checked on the host), far below float32 rounding, so E_{c-1} is the
+//      state chunk c starts in for every c >= kHorizonChunks.
+//   3. each chunk evaluates its outputs from that state: either the impulse
+//      response convolution plus the state read-out,
+//      y[t] = sum_{k<=t} h[t-k] x[k] + C A^t S   (kRerun == false), or by
+//      re-running the recursion from S (kRerun == true, cheaper for P <= 4).
+//
+// The first kHorizonChunks chunks of the span are the warm-up: their inputs
+// must be the true signal (zeros before the start of a row, which reproduces
+// the zero initial state exactly) but their outputs are not exact and are
+// never used.  The same routine evaluates the adjoint (time reversed) filter
+// when the caller's load/store map logical positions backwards in time.
+#pragma once
+
+#include "common.cuh"
+
+namespace pesq {
+
+template <int P>
+struct ScanTab {
+  float h[kChunk];         // impulse response h[0..L-1]
+  float G[kChunk][P];      // C A^t
+  float W[kChunk][P];      // A^(L-1-k) B
+  float M[kLevels][P][P];  // A^(L * 2^i)
+  float A[P][P];           // one step, for the re-run form
+  float B[P];
+  float C[P];
+  float D;
+};
+
+// Shared memory floats the scan needs as scratch.
+template <int P>
+__host__ __device__ constexpr int scan_scratch_floats() {
+  return P * kThreads;
+}
+
+// `load(p)` returns the input at logical position p (0 <= p < kSpan) and
+// `store(p, y)` consumes the output there.  `es` is scan scratch of
+// scan_scratch_floats<P>() floats.  Must be called by all kThreads threads.
+template <int P, bool kRerun, class Load, class Store>
+__device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Load&& load, Store&& store) {
+  const int c = threadIdx.x;
+  const int p0 = c * kChunk;
+
+  float x[kChunk];
+#pragma unroll
+  for (int k = 0; k < kChunk; ++k) x[k] = load(p0 + k);
+
+  // 1. zero-state end state of the chunk
+  float e[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) acc = fmaf(tab.W[k][j], x[k], acc);
+    e[j] = acc;
+  }
+
+  // 2. Kogge-Stone over the chunks of the span
+#pragma unroll
+  for (int j = 0; j < P; ++j) es[j * kThreads + c] = e[j];
+  __syncthreads();
+#pragma unroll
+  for (int lv = 0; lv < kLevels; ++lv) {
+    const int d = 1 << lv;
+    float prev[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) prev[j] = c >= d ? es[j * kThreads + c - d] : 0.0f;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float acc = e[i];
+#pragma unroll
+      for (int j = 0; j < P; ++j) acc = fmaf(tab.M[lv][i][j], prev[j], acc);
+      e[i] = acc;
+    }
+#pragma unroll
+    for (int j = 0; j < P; ++j) es[j * kThreads + c] = e[j];
+    __syncthreads();
+  }
+
+  float s[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) s[j] = c >= 1 ? es[j * kThreads + c - 1] : 0.0f;
+  // the scratch is free again once every thread holds its start state
+  __syncthreads();
+
+  // 3. outputs of the chunk
+  if constexpr (kRerun) {
+#pragma unroll
+    for (int t = 0; t < kChunk; ++t) {
+      float y = tab.D * x[t];
+#pragma unroll
+      for (int j = 0; j < P; ++j) y = fmaf(tab.C[j], s[j], y);
+      float nxt[P];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        float acc = tab.B[i] * x[t];
+#pragma unroll
+        for (int j = 0; j < P; ++j) acc = fmaf(tab.A[i][j], s[j], acc);
+        nxt[i] = acc;
+      }
+#pragma unroll
+      for (int i = 0; i < P; ++i) s[i] = nxt[i];
+      store(p0 + t, y);
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < kChunk; ++t) {
+      float y = 0.0f;
+#pragma unroll
+      for (int j = 0; j < P; ++j) y = fmaf(tab.G[t][j], s[j], y);
+#pragma unroll
+      for (int k = 0; k <= t; ++k) y = fmaf(tab.h[t - k], x[k], y);
+      store(p0 + t, y);
+    }
+  }
+}
+
+}  // namespace pesq

@@ -1,0 +1,109 @@
+// torch custom ops over the C ABI of libpesq_cuda.so.
+//
+// The ops only allocate tensors with torch's caching allocator (so they are
+// safe under CUDA graph capture), pick the current stream and forward to
+// pesq_forward / pesq_backward.  Plans are created from Python through the
+// same C ABI (ctypes) and passed in as an opaque integer handle.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "../../include/pesq_cuda.h"
+
+namespace {
+
+void check_status(int status, const char* what) {
+  if (status == PESQ_OK) return;
+  const char* msg = pesq_last_error();
+  if (status == PESQ_ERR_INVALID_ARGUMENT) {
+    TORCH_CHECK_VALUE(false, what, ": ", msg);
+  }
+  TORCH_CHECK(false, what, " failed (status ", status, "): ", msg);
+}
+
+void check_signal(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "The CUDA PESQ backend needs `", name, "` to live on a GPU.");
+  TORCH_CHECK(t.scalar_type() == at::kFloat, "The CUDA PESQ backend only supports float32, `", name, "` is ",
+              t.scalar_type(), ".");
+  TORCH_CHECK(t.dim() == 2, "`", name, "` must be [batch, sample], got ", t.sizes());
+  TORCH_CHECK(t.stride(1) == 1, "`", name, "` rows must be contiguous");
+}
+
+const pesq_plan* as_plan(int64_t handle) {
+  TORCH_CHECK(handle != 0, "invalid PESQ plan handle");
+  return reinterpret_cast<const pesq_plan*>(static_cast<uintptr_t>(handle));
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> pesq_forward_op(int64_t plan_handle,
+                                                                                       const at::Tensor& ref,
+                                                                                       const at::Tensor& deg,
+                                                                                       int64_t flags) {
+  check_signal(ref, "ref");
+  check_signal(deg, "deg");
+  TORCH_CHECK_VALUE(ref.sizes() == deg.sizes(), "Reference and degraded signal must have the same shape, got ",
+                    ref.sizes(), " and ", deg.sizes(), ".");
+  TORCH_CHECK(ref.device() == deg.device(), "ref and deg must be on the same device");
+  const pesq_plan* plan = as_plan(plan_handle);
+  c10::cuda::CUDAGuard guard(ref.device());
+  const int64_t batch = ref.size(0), n = ref.size(1);
+  size_t bytes = 0;
+  check_status(pesq_workspace_size(plan, batch, n, (uint32_t)flags, &bytes), "pesq_workspace_size");
+  auto opts = ref.options();
+  at::Tensor ws = at::empty({(int64_t)((bytes + 3) / 4)}, opts);
+  at::Tensor d_symm = at::empty({batch}, opts), d_asymm = at::empty({batch}, opts);
+  at::Tensor mos = at::empty({batch}, opts), loss = at::empty({batch}, opts);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index());
+  check_status(pesq_forward(plan, stream, ref.data_ptr<float>(), ref.stride(0), deg.data_ptr<float>(),
+                            deg.stride(0), batch, n, (uint32_t)flags, ws.data_ptr(), bytes,
+                            d_symm.data_ptr<float>(), d_asymm.data_ptr<float>(), mos.data_ptr<float>(),
+                            loss.data_ptr<float>()),
+               "pesq_forward");
+  return {d_symm, d_asymm, mos, loss, ws};
+}
+
+const float* opt_ptr(const c10::optional<at::Tensor>& t, int64_t batch, const char* name) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->numel() == batch && t->is_contiguous(),
+              "upstream gradient `", name, "` must be a contiguous float32 CUDA tensor of ", batch, " elements");
+  return t->data_ptr<float>();
+}
+
+std::tuple<at::Tensor, at::Tensor> pesq_backward_op(int64_t plan_handle, const at::Tensor& ref,
+                                                    const at::Tensor& deg, int64_t flags, const at::Tensor& ws,
+                                                    const c10::optional<at::Tensor>& g_loss,
+                                                    const c10::optional<at::Tensor>& g_mos,
+                                                    const c10::optional<at::Tensor>& g_dsymm,
+                                                    const c10::optional<at::Tensor>& g_dasymm) {
+  check_signal(ref, "ref");
+  check_signal(deg, "deg");
+  const pesq_plan* plan = as_plan(plan_handle);
+  c10::cuda::CUDAGuard guard(ref.device());
+  const int64_t batch = ref.size(0), n = ref.size(1);
+  // a gradient that was not asked for comes back as an empty tensor
+  at::Tensor g_ref = (flags & PESQ_GRAD_REF) ? at::empty({batch, n}, ref.options()) : at::empty({0}, ref.options());
+  at::Tensor g_deg = (flags & PESQ_GRAD_DEG) ? at::empty({batch, n}, deg.options()) : at::empty({0}, deg.options());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index());
+  check_status(pesq_backward(plan, stream, ref.data_ptr<float>(), ref.stride(0), deg.data_ptr<float>(),
+                             deg.stride(0), batch, n, (uint32_t)flags, ws.data_ptr(), (size_t)ws.numel() * 4,
+                             opt_ptr(g_loss, batch, "g_loss"), opt_ptr(g_mos, batch, "g_mos"),
+                             opt_ptr(g_dsymm, batch, "g_dsymm"), opt_ptr(g_dasymm, batch, "g_dasymm"),
+                             (flags & PESQ_GRAD_REF) ? g_ref.data_ptr<float>() : nullptr, n,
+                             (flags & PESQ_GRAD_DEG) ? g_deg.data_ptr<float>() : nullptr, n),
+               "pesq_backward");
+  return {g_ref, g_deg};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(pesq_cuda, m) {
+  m.def("forward(int plan, Tensor ref, Tensor deg, int flags) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  m.def(
+      "backward(int plan, Tensor ref, Tensor deg, int flags, Tensor workspace, Tensor? g_loss, Tensor? g_mos, "
+      "Tensor? g_dsymm, Tensor? g_dasymm) -> (Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(pesq_cuda, CUDA, m) {
+  m.impl("forward", &pesq_forward_op);
+  m.impl("backward", &pesq_backward_op);
+}

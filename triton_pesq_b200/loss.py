@@ -1,0 +1,220 @@
+"""``PesqLossCuda``: the PESQ loss on hand-written sm_100a kernels.
+
+Drop-in for the reference's ``PesqLossTriton`` (torch_pesq/triton_ops/loss.py:18-215):
+same constructor arguments, ``raw`` / ``mos`` / ``forward`` / ``graphed`` and
+an autograd backward w.r.t. either input.  Every evaluation goes through the
+C ABI of ``libpesq_cuda.so`` (via the ``torch.ops.pesq_cuda`` custom ops);
+there is no Triton, no CPU path and no fallback.
+
+Pipeline per call (four kernels each way at 16 kHz, plus the resampler at
+other rates): front (level-alignment band pass and its adjoint term,
+pre-emphasis, STFT -> Bark), chain forward (silent frames, equalisation,
+loudness, disturbance, pooling, MOS/loss), and in the backward the chain
+adjoint and the back end (spectral adjoint, reverse pre-emphasis, alignment
+term).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from .tables import PlanConfig
+
+__all__ = ["PesqLossCuda"]
+
+
+class _PesqFunction(torch.autograd.Function):
+    """(ref, deg) -> (d_symm, d_asymm, mos, loss), one forward launch sequence.
+
+    The backward takes the upstream gradient of all four outputs at once (the
+    epilogue adjoint runs inside the chain adjoint kernel) and returns the
+    gradients of the inputs that asked for one.
+    """
+
+    @staticmethod
+    def forward(ctx, ref, deg, plan):
+        flags = (_lib.GRAD_REF if ctx.needs_input_grad[0] else 0) | (
+            _lib.GRAD_DEG if ctx.needs_input_grad[1] else 0
+        )
+        d_symm, d_asymm, mos, loss, ws = torch.ops.pesq_cuda.forward(plan, ref, deg, flags)
+        ctx.plan = plan
+        ctx.flags = flags
+        if flags:
+            ctx.save_for_backward(ref, deg)
+            ctx.workspace = ws
+        ctx.mark_non_differentiable()
+        return d_symm, d_asymm, mos, loss
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_dsymm, g_dasymm, g_mos, g_loss):
+        ref, deg = ctx.saved_tensors
+
+        def prep(g):
+            return None if g is None else g.contiguous().float()
+
+        g_ref, g_deg = torch.ops.pesq_cuda.backward(
+            ctx.plan, ref, deg, ctx.flags, ctx.workspace,
+            prep(g_loss), prep(g_mos), prep(g_dsymm), prep(g_dasymm),
+        )
+        return (
+            g_ref if ctx.flags & _lib.GRAD_REF else None,
+            g_deg if ctx.flags & _lib.GRAD_DEG else None,
+            None,
+        )
+
+
+def _check_signal(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"`{name}` must be a torch.Tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"The CUDA PESQ backend needs `{name}` to live on a GPU.")
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"The CUDA PESQ backend only supports float32, `{name}` is {t.dtype}.")
+    return t
+
+
+class PesqLossCuda(torch.nn.Module):
+    """Perceptual Evaluation of Speech Quality on B200 CUDA kernels.
+
+    Same interface as ``PesqLossTriton(factor, sample_rate, nbarks, win_length,
+    n_fft, hop_length)`` (triton_ops/loss.py:60-92); the perceptual model and
+    every constant are those of ``PesqLoss`` (torch_pesq/loss.py:61-108).
+
+    Inputs are float32 CUDA tensors ``[batch, sample]`` (``[sample]`` is promoted
+    to a batch of one); rows may have any stride.  Gradients flow to whichever
+    input requires one.
+
+    Attributes
+    ----------
+    factor : float
+        Scaling of the loss
+    source_sample_rate : int
+        Input sampling rate; other rates than 16 kHz are resampled first
+    power_filter, pre_filter : torch.nn.Parameter
+        The float32 filter coefficients of the level alignment band pass and
+        the pre-emphasis, as in ``PesqLoss`` (no gradient)
+    config : PlanConfig
+        The host float64 tables the plans are built from
+    """
+
+    def __init__(
+        self,
+        factor: float,
+        sample_rate: int = 48000,
+        nbarks: int = 49,
+        win_length: int = 512,
+        n_fft: int = 512,
+        hop_length: int = 256,
+    ):
+        super().__init__()
+        self.factor = float(factor)
+        self.source_sample_rate = int(sample_rate)
+        self.config = PlanConfig.build(factor, sample_rate, nbarks, win_length, n_fft, hop_length)
+        self.power_filter = torch.nn.Parameter(
+            torch.tensor(np.stack([self.config.power_b, self.config.power_a]), dtype=torch.float32),
+            requires_grad=False,
+        )
+        self.pre_filter = torch.nn.Parameter(
+            torch.tensor(np.stack([self.config.pre_b, self.config.pre_a]), dtype=torch.float32),
+            requires_grad=False,
+        )
+        self._plans: Dict[int, int] = {}
+        _lib.load_ops()
+
+    # ------------------------------------------------------------------
+    # plans
+    # ------------------------------------------------------------------
+
+    def _plan(self, device: torch.device) -> int:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        plan = self._plans.get(index)
+        if plan is None:
+            with torch.cuda.device(index):
+                plan = _lib.create_plan(self.config)
+            self._plans[index] = plan
+        return plan
+
+    def __del__(self):
+        plans = getattr(self, "_plans", None)
+        if plans:
+            for handle in plans.values():
+                try:
+                    _lib.destroy_plan(handle)
+                except Exception:  # pragma: no cover - interpreter shutdown
+                    pass
+            plans.clear()
+
+    def __getstate__(self):
+        state = self.__dict__.copy()
+        state["_plans"] = {}
+        return state
+
+    # ------------------------------------------------------------------
+    # evaluation
+    # ------------------------------------------------------------------
+
+    def _evaluate(self, ref: torch.Tensor, deg: torch.Tensor):
+        deg, ref = torch.atleast_2d(deg), torch.atleast_2d(ref)
+        if ref.shape != deg.shape:
+            raise ValueError(
+                "Reference and degraded signal must have the same shape, "
+                f"got {tuple(ref.shape)} and {tuple(deg.shape)}."
+            )
+        _check_signal(ref, "ref")
+        _check_signal(deg, "deg")
+        if ref.dim() != 2:
+            raise ValueError(f"expected [batch, sample] signals, got {tuple(ref.shape)}")
+        if ref.device != deg.device:
+            raise RuntimeError("ref and deg must live on the same device")
+        if ref.stride(-1) != 1:
+            ref = ref.contiguous()
+        if deg.stride(-1) != 1:
+            deg = deg.contiguous()
+        plan = self._plan(ref.device)
+        return _PesqFunction.apply(ref, deg, plan)
+
+    def raw(self, ref: torch.Tensor, deg: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Symmetric and asymmetric distance, both ``[batch]`` (loss.py:172-268)."""
+
+        d_symm, d_asymm, _, _ = self._evaluate(ref, deg)
+        return d_symm, d_asymm
+
+    def mos(self, ref: torch.Tensor, deg: torch.Tensor) -> torch.Tensor:
+        """Mean opinion score in (1.08, 4.999) (loss.py:271-297)."""
+
+        return self._evaluate(ref, deg)[2]
+
+    def forward(self, ref: torch.Tensor, deg: torch.Tensor) -> torch.Tensor:
+        """Loss ``factor * (0.1 d_symm + 0.0309 d_asymm)`` (loss.py:300-322)."""
+
+        return self._evaluate(ref, deg)[3]
+
+    def graphed(self, ref: torch.Tensor, deg: torch.Tensor):
+        """Capture forward (and backward) in a CUDA graph for one input shape.
+
+        Mirrors ``PesqLossTriton.graphed`` (triton_ops/loss.py:149-201): the
+        returned callable replaces ``self.__call__`` for inputs of this shape
+        and these ``requires_grad`` flags and is bit exact w.r.t. eager
+        evaluation.  The plan is built and every kernel configured before the
+        capture, which then only records launches.
+        """
+
+        sample = tuple(t.detach().clone().requires_grad_(t.requires_grad) for t in (ref, deg))
+        self._plan(sample[0].device)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            out = self(*sample)
+            if out.requires_grad:
+                torch.autograd.grad(out.sum(), [t for t in sample if t.requires_grad])
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        return torch.cuda.make_graphed_callables(self, sample)
+
+    def extra_repr(self) -> str:
+        return f"factor={self.factor}, sample_rate={self.source_sample_rate}"
