@@ -7,35 +7,31 @@
 //   dL/dx = ramp . H_pre^T [ sum_t w . adj_t(g_t) ]  -  kappa * H_pow^T H_pow x
 //
 // where adj_t is the adjoint of "power spectrum -> Bark segment sums" of frame
-// t, evaluated as an inverse real FFT of (dL/dP_f) X_f, and
-// kappa = 2 <g, F> / sum (H_pow x)^2 is the derivative through the level
-// alignment scale (torch_pesq/loss.py:132-139).  z = H_pow^T H_pow x was saved
-// by the front kernel.
+// t, evaluated as an inverse real FFT of (dL/dP_f) X_f with the spectrum X_t
+// the front kernel saved, and kappa = 2 <g, F> / sum (H_pow x)^2 is the
+// derivative through the level alignment scale (torch_pesq/loss.py:132-139).
+// z = H_pow^T H_pow x was saved by the front kernel as well.
 //
-// The CTA recomputes y = H_pre ramp(x) over its span (forward warm-up before
-// the segment, frames around it), overlap-adds the per-frame gradients in a
-// fixed order (even frames, then odd frames: no atomics, bitwise
-// reproducible), and runs the pre-emphasis adjoint backwards in time with
-// kHorizon samples of look-ahead.
-#include "fft.cuh"
+// The CTA overlap-adds the per-frame gradients around its segment in a fixed
+// order (even frames, then odd frames: no atomics, bitwise reproducible) and
+// runs the pre-emphasis adjoint backwards in time with kHorizon samples of
+// look-ahead.
 #include "kernels.cuh"
 
 namespace pesq {
 
 namespace {
 
-constexpr int kBackSmemFloats = 2 * kSpan + scan_scratch_floats<2>() + kWarps * kFftScratch * 2 +
-                                kWarps * kNfft + kWarps * kMaxBands + sizeof(DevTables) / 4 + 64;
+constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * kFftScratch * 8 +
+                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables);
 
 __global__ void __launch_bounds__(kThreads, 1)
     back_kernel(const __grid_constant__ BackArgs p, const __grid_constant__ PreTab pre) {
   extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                 // kSpan: input, then y in place
-  float* gy = xs + kSpan;           // kSpan: dL/dy, then dL/d(ramped x) in place
+  float* gy = smem;  // kSpan: dL/dy, then dL/d(ramped x) in place
   float* es = gy + kSpan;
-  float2* fft = reinterpret_cast<float2*>(es + scan_scratch_floats<2>());
-  float* gu = reinterpret_cast<float*>(fft + kWarps * kFftScratch);  // per warp kNfft
-  float* gb = gu + kWarps * kNfft;                                    // per warp kMaxBands
+  Cx<float>* fft = reinterpret_cast<Cx<float>*>(es + scan_scratch_floats<2>());
+  float* gb = reinterpret_cast<float*>(fft + kWarps * kFftScratch);  // per warp kMaxBands
   DevTables* tab = reinterpret_cast<DevTables*>(gb + kWarps * kMaxBands);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -44,30 +40,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t n_row = p.n;
   const int64_t a = (int64_t)seg * p.seg_frames * kHop;
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
-  // one hop before the segment (frame t0-1 overlaps it) plus the warm-up
-  const int64_t base = a - kHop - kHorizon;
-  const float* xr = p.src.row(row);
+  // the span starts at frame t0 - 1, which overlaps the segment
+  const int64_t base = a - kHop;
 
   {
-    const float4* src4 = reinterpret_cast<const float4*>(p.tab);
-    float4* dst4 = reinterpret_cast<float4*>(tab);
-    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) dst4[i] = src4[i];
+    const float4* s4 = reinterpret_cast<const float4*>(p.tab);
+    float4* d4 = reinterpret_cast<float4*>(tab);
+    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) d4[i] = s4[i];
   }
-  for (int i = tid; i < kSpan; i += kThreads) {
-    const int64_t n = base + i;
-    xs[i] = (n >= 0 && n < n_row) ? __ldg(xr + n) : 0.0f;
-    gy[i] = 0.0f;
-  }
-  __syncthreads();
-
-  // y = H_pre ramp(x), zero past the row end
-  chunk_scan<2, true>(
-      pre, es,
-      [&](int q) {
-        const int64_t n = base + q;
-        return (n >= 0 && n < n_row) ? edge_ramp(xs[q], n, n_row) : 0.0f;
-      },
-      [&](int q, float y) { xs[q] = (base + q < n_row) ? y : 0.0f; });
+  for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   __syncthreads();
 
   // frames that touch [a, send + kHorizon)
@@ -76,27 +57,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_lo = max(0, t0 - 1);
   const int t_hi = min(p.frames - 1, (int)((send + kHorizon - 1) / kHop));
   const float kappa = p.kappa[row];
-  float2* sh = fft + warp * kFftScratch;
-  float* gw = gu + warp * kNfft;
+  Cx<float>* sh = fft + warp * kFftScratch;
+  float* gw = reinterpret_cast<float*>(sh);
   float* gbw = gb + warp * kMaxBands;
 
   for (int parity = 0; parity < 2; ++parity) {
     const int first = t_lo + ((t_lo & 1) != parity ? 1 : 0);
     for (int t = first + 2 * warp; t <= t_hi; t += 2 * kWarps) {
       const int off = (int)(t * (int64_t)kHop - base);
-      const float* gsrc = p.g_bark + ((int64_t)row * p.frames + t) * nb;
+      const int64_t frame = (int64_t)row * p.frames + t;
+      const float* gsrc = p.g_bark + frame * nb;
       for (int b = lane; b < nb; b += 32) gbw[b] = gsrc[b] * tab->band_corr[b];
       __syncwarp();
-      float2 X[8];
-      warp_rfft512(xs + off, tab->window, sh, tab->tw256, tab->tw512, lane, X);
       // V_f = dL/dP_f * X_f, with dL/dP_f = corr_b dL/dB_b for the band b of bin f
+      const Cx<float>* spec = p.spec + frame * kBins;
+      Cx<float> V[8];
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         const int f = lane + 32 * m;
         const int b = tab->bin_band[f];
-        X[m] = c_scale(X[m], b >= 0 ? gbw[b] : 0.0f);
+        V[m] = c_scale(spec[f], b >= 0 ? gbw[b] : 0.0f);
       }
-      warp_irfft512_adjoint(X, sh, tab->tw256, tab->tw512, lane, gw);
+      warp_irfft512_adjoint(V, sh, tab->tw256, tab->tw512, lane, gw);
       for (int k = lane; k < kNfft; k += 32) gy[off + k] += tab->window[k] * gw[k];
       __syncwarp();
     }
@@ -105,8 +87,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // pre-emphasis adjoint on [a, send): backwards in time from send + kHorizon;
   // the gradient of the zero padding after the row end is dropped
-  const int top = kHop + 2 * kHorizon + (int)(send - a) - 1;
-  chunk_scan<2, true>(
+  const int top = kHop + kHorizon + (int)(send - a) - 1;
+  chunk_scan<2, true, float>(
       pre, es,
       [&](int q) {
         const int idx = top - q;
@@ -122,14 +104,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* outr = p.out.row(row);
   for (int i = tid; i < (int)(send - a); i += kThreads) {
     const int64_t n = a + i;
-    const float g = edge_ramp(gy[kHop + kHorizon + i], n, n_row);
+    const float g = edge_ramp(gy[kHop + i], n, n_row);
     outr[n] = fmaf(-kappa, zr[n], g);
   }
 }
 
 }  // namespace
 
-size_t back_smem_bytes() { return (size_t)kBackSmemFloats * sizeof(float); }
+size_t back_smem_bytes() { return (size_t)kBackSmemBytes; }
 
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;

@@ -4,9 +4,11 @@
 // in shared memory and without touching HBM in between:
 //
 //   f  = H_pow x            level-alignment band pass (order 10)    -> sum f^2
-//   z  = H_pow^T f          (only for rows that need a gradient)    -> HBM
-//   y  = H_pre ramp(x)      edge fade + pre-emphasis biquad
-//   B  = corr * segsum |rfft512(w * y_t)|^2   for the frames starting in [a, a+S)
+//   z  = H_pow^T f          (rows that need a gradient)             -> HBM
+//   y  = H_pre ramp(x)      edge fade + pre-emphasis biquad, float64
+//   X_t = rfft512(w * y_t)  for the frames starting in [a, a+S), float64
+//   B  = corr * segsum |X_t|^2                                      -> HBM
+//   X_t                     (rows that need a gradient)             -> HBM
 //
 // all on the *unscaled* signal: everything up to the power spectrum is linear,
 // so the level alignment scale s = sqrt(1e7 / P) enters the Bark spectrum as
@@ -15,29 +17,36 @@
 // normalisation of loss.py:179-183 is a no-op for the same reason: the
 // pipeline output is invariant to the scale of each input.
 //
+// y and the spectrum are evaluated in double precision: the weak high bands
+// of speech sit 50-60 dB below the frame peak, where float32 rounding of the
+// signal would leave ~1e-4 relative error in their power, and the loss
+// gradient is most sensitive exactly there.  y is kept in shared memory as a
+// float hi/lo pair.
+//
 // The CTA stages kSpan samples starting kHorizon before `a`: the first
 // kHorizon are the warm-up of the forward scans, and the reverse scan that
 // produces z looks kHorizon samples past the end of the segment.
-#include "fft.cuh"
 #include "kernels.cuh"
 
 namespace pesq {
 
 namespace {
 
-constexpr int kFrontSmemFloats = 2 * kSpan + scan_scratch_floats<10>() + kWarps * kFftScratch * 2 +
-                                 sizeof(DevTables) / 4 + 2 * kWarps + 64;
+constexpr int kFrontScratchFloats =
+    (kWarps * kFftScratch * 4 > scan_scratch_floats<10>()) ? kWarps * kFftScratch * 4 : scan_scratch_floats<10>();
+constexpr int kFrontSmemBytes = 2 * kSpan * 4 + kFrontScratchFloats * 4 + (int)sizeof(DevTables) +
+                                (int)sizeof(DevTwiddle64) + kWarps * 8;
 
 __global__ void __launch_bounds__(kThreads, 1)
     front_kernel(const __grid_constant__ FrontArgs p, const __grid_constant__ PowTab pow,
-                 const __grid_constant__ PreTab pre) {
+                 const __grid_constant__ PreTab64 pre) {
   extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                       // kSpan: input, then y in place
-  float* fb = xs + kSpan;                 // kSpan: f, then z in place
-  float* es = fb + kSpan;                 // scan scratch
-  float2* fft = reinterpret_cast<float2*>(es + scan_scratch_floats<10>());  // per-warp FFT scratch
-  DevTables* tab = reinterpret_cast<DevTables*>(fft + kWarps * kFftScratch);
-  double* red = reinterpret_cast<double*>(tab + 1);  // kWarps
+  float* xs = smem;                 // kSpan: input, then y (hi part) in place
+  float* fb = xs + kSpan;           // kSpan: f, then z in place, then y (lo part)
+  float* scratch = fb + kSpan;      // scan scratch, later the per-warp FFT scratch
+  DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
+  DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
+  double* red = reinterpret_cast<double*>(tw + 1);  // kWarps
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x / p.nseg;
@@ -47,12 +56,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   const int64_t base = a - kHorizon;
   const float* xr = p.src.row(row);
+  const bool grad_row = row >= p.z_begin && row < p.z_end;
 
   // constant tables
   {
-    const float4* src4 = reinterpret_cast<const float4*>(p.tab);
-    float4* dst4 = reinterpret_cast<float4*>(tab);
-    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) dst4[i] = src4[i];
+    const float4* s4 = reinterpret_cast<const float4*>(p.tab);
+    float4* d4 = reinterpret_cast<float4*>(tab);
+    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) d4[i] = s4[i];
+    const float4* t4 = reinterpret_cast<const float4*>(p.tw64);
+    float4* e4 = reinterpret_cast<float4*>(tw);
+    for (int i = tid; i < (int)(sizeof(DevTwiddle64) / 16); i += kThreads) e4[i] = t4[i];
   }
   // stage the span; zeros outside the row reproduce the zero initial state
   for (int i = tid; i < kSpan; i += kThreads) {
@@ -67,12 +80,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Both passes share one instance of the scan code (pass 0 forward from xs
   // into fb, pass 1 backward over fb in place), which keeps the two unrolled
   // scans from competing for registers.
-  const int passes = (row >= p.z_begin && row < p.z_end) ? 2 : 1;
+  const int passes = grad_row ? 2 : 1;
   const int top = 2 * kHorizon + (int)(send - a) - 1;
   double ssq = 0.0;
   for (int pass = 0; pass < passes; ++pass) {
-    chunk_scan<10, false>(
-        pow, es,
+    chunk_scan<10, false, float>(
+        pow, scratch,
         [&](int q) {
           if (pass == 0) return xs[q];
           const int idx = top - q;
@@ -95,42 +108,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; w < kWarps; ++w) tot += red[w];
     p.partial[(int64_t)row * p.nseg + seg] = tot;
   }
-  if (passes == 2) {
+  if (grad_row) {
     float* zr = p.z + (int64_t)row * n_row;
     for (int i = tid; i < (int)(send - a); i += kThreads) zr[a + i] = fb[kHorizon + i];
   }
+  // the low part of a resampled input (x = hi + lo) joins the pre-emphasis
+  const bool has_lo = p.src_lo.ref != nullptr;
+  if (has_lo) {
+    __syncthreads();
+    const float* lr = p.src_lo.row(row);
+    for (int i = tid; i < kSpan; i += kThreads) {
+      const int64_t n = base + i;
+      fb[i] = (n >= 0 && n < n_row) ? __ldg(lr + n) : 0.0f;
+    }
+    __syncthreads();
+  }
 
-  // 3. edge fade + pre-emphasis, in place; the padding after the row end is 0
-  chunk_scan<2, true>(
-      pre, es,
+  // 3. edge fade + pre-emphasis in double precision; y = hi + lo with hi in
+  //    xs (in place) and lo in fb; the padding after the row end is 0
+  chunk_scan<2, true, double>(
+      pre, reinterpret_cast<double*>(scratch),
       [&](int q) {
         const int64_t n = base + q;
-        return (n >= 0 && n < n_row) ? edge_ramp(xs[q], n, n_row) : 0.0f;
+        if (n < 0 || n >= n_row) return 0.0;
+        const double head = n < 15 ? (double)(n + 1) * 0.0625 : 1.0;
+        const double tail = n >= n_row - 15 ? (double)(n_row - n) * 0.0625 : 1.0;
+        const double v = has_lo ? (double)xs[q] + (double)fb[q] : (double)xs[q];
+        return (v * head) * tail;
       },
-      [&](int q, float y) { xs[q] = (base + q < n_row) ? y : 0.0f; });
+      [&](int q, double y) {
+        if (base + q >= n_row) y = 0.0;
+        const float hi = (float)y;
+        xs[q] = hi;
+        fb[q] = (float)(y - (double)hi);
+      });
   __syncthreads();
 
   // 4. frames starting in this segment: window, rfft, power, Bark segment sums
   const int nb = tab->nb;
   const int t0 = seg * p.seg_frames;
   const int t1 = min(t0 + p.seg_frames, p.frames);
-  float2* sh = fft + warp * kFftScratch;
-  float* pw = reinterpret_cast<float*>(fft + warp * kFftScratch);
+  Cx<double>* sh = reinterpret_cast<Cx<double>*>(scratch) + warp * kFftScratch;
+  double* pw = reinterpret_cast<double*>(sh);
   for (int t = t0 + warp; t < t1; t += kWarps) {
-    const float* frame = xs + kHorizon + (t - t0) * kHop;
-    float2 X[8];
-    warp_rfft512(frame, tab->window, sh, tab->tw256, tab->tw512, lane, X);
+    const int off = kHorizon + (t - t0) * kHop;
+    Cx<double> v[8], X[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int n = 2 * (lane + 32 * m);
+      const float2 hi = *reinterpret_cast<const float2*>(xs + off + n);
+      const float2 lo = *reinterpret_cast<const float2*>(fb + off + n);
+      const float2 w = *reinterpret_cast<const float2*>(tab->window + n);
+      v[m] = mk(((double)hi.x + (double)lo.x) * (double)w.x, ((double)hi.y + (double)lo.y) * (double)w.y);
+    }
+    warp_rfft512<double>(v, sh, tw->tw256, tw->tw512, lane, X);
+    if (grad_row) {
+      Cx<float>* out = p.spec + ((int64_t)row * p.frames + t) * kBins;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) out[lane + 32 * m] = mk((float)X[m].x, (float)X[m].y);
+    }
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       const int f = lane + 32 * m;
-      pw[f] = f == 0 ? 0.0f : fmaf(X[m].x, X[m].x, X[m].y * X[m].y);
+      pw[f] = f == 0 ? 0.0 : fma(X[m].x, X[m].x, X[m].y * X[m].y);
     }
     __syncwarp();
     float* out = p.bark + ((int64_t)row * p.frames + t) * nb;
     for (int b = lane; b < nb; b += 32) {
-      float acc = 0.0f;
+      double acc = 0.0;
       for (int f = tab->band_start[b]; f < tab->band_end[b]; ++f) acc += pw[f];
-      out[b] = acc * tab->band_corr[b];
+      out[b] = (float)(acc * (double)tab->band_corr[b]);
     }
     __syncwarp();
   }
@@ -138,13 +185,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t front_smem_bytes() { return (size_t)kFrontSmemFloats * sizeof(float); }
+size_t front_smem_bytes() { return (size_t)kFrontSmemBytes; }
 
 cudaError_t configure_front() {
   return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
 }
 
-cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab& pre, int rows, cudaStream_t s) {
+cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
   front_kernel<<<(unsigned)blocks, kThreads, front_smem_bytes(), s>>>(a, pow, pre);

@@ -4,18 +4,20 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "fft.cuh"
 #include "scan.cuh"
 
 namespace pesq {
 
 using PowTab = ScanTab<10>;
 using PreTab = ScanTab<2>;
+using PreTab64 = ScanTab<2, double>;
 
 // Device constant tables of a plan (uploaded once, read-only afterwards).
 struct alignas(16) DevTables {
   float window[kNfft];      // analysis window, zero padded/centred to n_fft
-  float2 tw256[256];        // exp(-2 pi i k / 256)
-  float2 tw512[256];        // exp(-2 pi i k / 512), k < 256
+  Cx<float> tw256[256];     // exp(-2 pi i k / 256)
+  Cx<float> tw512[256];     // exp(-2 pi i k / 512), k < 256
   int bin_band[kBins];         // band owning bin f, -1 if none (bin 0 never has one)
   int band_start[kMaxBands];
   int band_end[kMaxBands];
@@ -30,6 +32,12 @@ struct alignas(16) DevTables {
   int nb;
   float total_width;           // sum of widths of bands 1..nb-1
   float sqrt_total_width;
+};
+
+// Double precision twiddles of the forward spectrum.
+struct alignas(16) DevTwiddle64 {
+  Cx<double> tw256[256];
+  Cx<double> tw512[256];
 };
 
 // Rows of one call: ref rows are 0..B-1, deg rows B..2B-1.
@@ -57,21 +65,23 @@ struct RowSink {
 
 struct FrontArgs {
   RowSource src;     // 16 kHz rows
+  RowSource src_lo;  // low parts of the resampled rows (x = hi + lo), ref == nullptr if none
   int64_t n;         // samples per row
   int frames;        // T
   int seg_frames;    // frames per segment
   int nseg;          // segments per row
-  int z_begin;       // rows [z_begin, z_end) also produce z = H^T H x
-  int z_end;
+  int z_begin;       // rows [z_begin, z_end) also produce z = H^T H x and
+  int z_end;         // the spectrum X for the backward
   const DevTables* tab;
+  const DevTwiddle64* tw64;
   float* bark;       // [rows][T][nb]   unscaled Bark spectrum
   double* partial;   // [rows][nseg]    partial sums of (H x)^2
   float* z;          // [rows][n]
+  Cx<float>* spec;   // [rows][T][256]  rfft bins 0..255 of every frame
   uint32_t* err;
 };
 
 struct BackArgs {
-  RowSource src;     // 16 kHz rows (the forward input)
   int row_begin;     // rows [row_begin, row_end) get a gradient
   int64_t n;
   int frames;
@@ -81,6 +91,7 @@ struct BackArgs {
   const float* g_bark;  // [rows][T][nb]  dL/d(unscaled Bark)
   const float* kappa;   // [rows]
   const float* z;       // [rows][n]
+  const Cx<float>* spec;  // [rows][T][256] saved by the front kernel
   RowSink out;          // gradient rows (16 kHz)
   uint32_t* err;
 };
@@ -137,6 +148,7 @@ struct ChainBwdArgs {
 struct ResampleArgs {
   RowSource src;        // source rows (fwd) / gradient of 16 kHz rows (adjoint)
   RowSink dst;
+  RowSink dst_lo;       // forward only: float32 rounding residual of each output
   int rows;             // 2B or the gradient rows
   int row_begin;
   int64_t n_in;
@@ -151,7 +163,7 @@ struct ResampleArgs {
   const int4* adj_entries; // (dl, phase, tap bits, 0)
 };
 
-cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab& pre, int rows, cudaStream_t s);
+cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s);
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s);
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);

@@ -30,8 +30,10 @@ struct pesq_plan {
   int nb;
   double factor;
   PowTab pow;
-  PreTab pre;
-  DevTables* dtab;  // device copy
+  PreTab pre;        // float32 tables: pre-emphasis adjoint of the back kernel
+  PreTab64 pre64;    // float64 tables: pre-emphasis of the front kernel
+  DevTables* dtab;   // device copy
+  DevTwiddle64* tw64;
   // resampler
   bool resample;
   int orig_step, new_step, width, width_total, max_count;
@@ -66,8 +68,8 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
 
-template <int P>
-int fill_scan(ScanTab<P>& t, const pesq_scan_desc& d, const char* name) {
+template <int P, class R>
+int fill_scan(ScanTab<P, R>& t, const pesq_scan_desc& d, const char* name) {
   if (d.states != P) return fail(PESQ_ERR_UNSUPPORTED, "%s: %d states, the kernels need %d", name, d.states, P);
   if (d.chunk != kChunk || d.levels != kLevels)
     return fail(PESQ_ERR_UNSUPPORTED, "%s: chunk %d / levels %d, the kernels need %d / %d", name, d.chunk,
@@ -75,21 +77,21 @@ int fill_scan(ScanTab<P>& t, const pesq_scan_desc& d, const char* name) {
   if (!d.impulse || !d.carry || !d.drive || !d.power || !d.trans || !d.input || !d.output)
     return fail(PESQ_ERR_INVALID_ARGUMENT, "%s: missing table", name);
   for (int k = 0; k < kChunk; ++k) {
-    t.h[k] = (float)d.impulse[k];
+    t.h[k] = (R)d.impulse[k];
     for (int j = 0; j < P; ++j) {
-      t.G[k][j] = (float)d.carry[k * P + j];
-      t.W[k][j] = (float)d.drive[k * P + j];
+      t.G[k][j] = (R)d.carry[k * P + j];
+      t.W[k][j] = (R)d.drive[k * P + j];
     }
   }
   for (int l = 0; l < kLevels; ++l)
     for (int i = 0; i < P; ++i)
-      for (int j = 0; j < P; ++j) t.M[l][i][j] = (float)d.power[(l * P + i) * P + j];
+      for (int j = 0; j < P; ++j) t.M[l][i][j] = (R)d.power[(l * P + i) * P + j];
   for (int i = 0; i < P; ++i) {
-    for (int j = 0; j < P; ++j) t.A[i][j] = (float)d.trans[i * P + j];
-    t.B[i] = (float)d.input[i];
-    t.C[i] = (float)d.output[i];
+    for (int j = 0; j < P; ++j) t.A[i][j] = (R)d.trans[i * P + j];
+    t.B[i] = (R)d.input[i];
+    t.C[i] = (R)d.output[i];
   }
-  t.D = (float)d.feed;
+  t.D = (R)d.feed;
   return PESQ_OK;
 }
 
@@ -97,20 +99,21 @@ int fill_scan(ScanTab<P>& t, const pesq_scan_desc& d, const char* name) {
 // per-call geometry and workspace layout
 // ---------------------------------------------------------------------------
 
-constexpr int kMaxFrontFrames = (kSpan - 2 * kHorizon) / kHop;         // 57
-constexpr int kMaxBackFrames = (kSpan - 2 * kHorizon - 3 * kHop) / kHop;  // 54
+// Frames per segment: the front kernel stages kHorizon before and after the
+// segment, the back kernel one hop before and kHorizon + 3 hops after it.
+constexpr int kMaxSegFrames = (kSpan - 2 * kHorizon) / kHop;  // 57
+static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel span");
 
 struct Geometry {
   int64_t batch, rows, n_src, n16;
   int T, L, nb;
-  int f_seg, f_nseg;  // front segmentation
-  int b_seg, b_nseg;  // back segmentation
+  int seg, nseg;  // segmentation of a row
   int cluster;
   bool resample, grad;
   int grad_begin, grad_end;
   ChainLayout lay;
   // byte offsets
-  size_t x16, partial, sumsq, bark, z, saved, gbark, kappa, cscratch, gx16, err, total;
+  size_t x16, x16lo, partial, sumsq, bark, z, spec, saved, gbark, kappa, cscratch, gx16, err, total;
 };
 
 void balance(int64_t n16, int max_frames, int& seg, int& nseg) {
@@ -144,8 +147,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
                 (long long)g.n16, (long long)g.rows);
   g.L = (g.T - 20) / 10 + 1;
   g.nb = p->nb;
-  balance(g.n16, kMaxFrontFrames, g.f_seg, g.f_nseg);
-  balance(g.n16, kMaxBackFrames, g.b_seg, g.b_nseg);
+  balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 48)));
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
   g.grad_begin = (flags & PESQ_GRAD_REF) ? 0 : (int)batch;
@@ -160,10 +162,12 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   };
   const size_t rows = (size_t)g.rows;
   g.x16 = take(g.resample ? rows * g.n16 * 4 : 0);
-  g.partial = take(rows * g.f_nseg * 8);
+  g.x16lo = take(g.resample ? rows * g.n16 * 4 : 0);
+  g.partial = take(rows * g.nseg * 8);
   g.sumsq = take(rows * 8);
   g.bark = take(rows * (size_t)g.T * g.nb * 4);
   g.z = take(g.grad ? rows * g.n16 * 4 : 0);
+  g.spec = take(g.grad ? rows * (size_t)g.T * kBins * 8 : 0);
   g.saved = take((size_t)batch * g.lay.stride * 4);
   g.gbark = take(g.grad ? rows * (size_t)g.T * g.nb * 4 : 0);
   g.kappa = take(g.grad ? rows * 4 : 0);
@@ -224,18 +228,30 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   p->sample_rate = d->sample_rate;
   p->nb = d->nbarks;
   p->factor = d->factor;
-  int rc = fill_scan<10>(p->pow, d->power_filter, "power filter");
+  int rc = fill_scan(p->pow, d->power_filter, "power filter");
   if (rc) return bail(rc);
-  rc = fill_scan<2>(p->pre, d->pre_filter, "pre-emphasis filter");
+  rc = fill_scan(p->pre, d->pre_filter, "pre-emphasis filter");
+  if (rc) return bail(rc);
+  rc = fill_scan(p->pre64, d->pre_filter, "pre-emphasis filter");
   if (rc) return bail(rc);
 
   // constant tables
   DevTables h;
   memset(&h, 0, sizeof(h));
   for (int k = 0; k < kNfft; ++k) h.window[k] = (float)d->window[k];
+  DevTwiddle64 h64;
   for (int k = 0; k < 256; ++k) {
-    h.tw256[k] = make_float2((float)cos(-2.0 * M_PI * k / 256.0), (float)sin(-2.0 * M_PI * k / 256.0));
-    h.tw512[k] = make_float2((float)cos(-2.0 * M_PI * k / 512.0), (float)sin(-2.0 * M_PI * k / 512.0));
+    // exact argument reduction: k / 256 and k / 512 are exact in double
+    const double c256 = cos(-2.0 * M_PI * (k / 256.0)), s256 = sin(-2.0 * M_PI * (k / 256.0));
+    const double c512 = cos(-2.0 * M_PI * (k / 512.0)), s512 = sin(-2.0 * M_PI * (k / 512.0));
+    h64.tw256[k].x = c256;
+    h64.tw256[k].y = s256;
+    h64.tw512[k].x = c512;
+    h64.tw512[k].y = s512;
+    h.tw256[k].x = (float)c256;
+    h.tw256[k].y = (float)s256;
+    h.tw512[k].x = (float)c512;
+    h.tw512[k].y = (float)s512;
     h.bin_band[k] = -1;
   }
   int prev_end = 0;
@@ -268,6 +284,9 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
     return bail(fail(PESQ_ERR_CUDA, "cudaMalloc of the constant tables failed"));
   if (cudaMemcpy(p->dtab, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess)
     return bail(fail(PESQ_ERR_CUDA, "upload of the constant tables failed"));
+  if (cudaMalloc(&p->tw64, sizeof(DevTwiddle64)) != cudaSuccess ||
+      cudaMemcpy(p->tw64, &h64, sizeof(h64), cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(PESQ_ERR_CUDA, "upload of the twiddle tables failed"));
 
   // resampler tables
   p->resample = d->sample_rate != 16000;
@@ -337,6 +356,7 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
 int pesq_plan_destroy(pesq_plan* p) {
   if (!p) return PESQ_OK;
   cudaFree(p->dtab);
+  cudaFree(p->tw64);
   cudaFree(p->taps);
   cudaFree(p->first);
   cudaFree(p->count);
@@ -387,11 +407,14 @@ int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch};
+  RowSource lo16{nullptr, nullptr, 0, 0, (int)batch};
   if (g.resample) {
     float* x16 = at<float>(ws, g.x16);
+    float* x16lo = at<float>(ws, g.x16lo);
     ResampleArgs ra{};
     ra.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
     ra.dst = RowSink{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+    ra.dst_lo = RowSink{x16lo, x16lo + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.rows = (int)g.rows;
     ra.row_begin = 0;
     ra.n_in = n_src;
@@ -407,26 +430,30 @@ int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_
     ra.adj_entries = p->adj_entries;
     PESQ_CUDA_TRY(launch_resample_fwd(ra, s), "resample kernel");
     src16 = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+    lo16 = RowSource{x16lo, x16lo + batch * g.n16, g.n16, g.n16, (int)batch};
   }
 
   FrontArgs fa{};
   fa.src = src16;
+  fa.src_lo = lo16;
   fa.n = g.n16;
   fa.frames = g.T;
-  fa.seg_frames = g.f_seg;
-  fa.nseg = g.f_nseg;
+  fa.seg_frames = g.seg;
+  fa.nseg = g.nseg;
   fa.z_begin = g.grad ? g.grad_begin : 0;
   fa.z_end = g.grad ? g.grad_end : 0;
   fa.tab = p->dtab;
+  fa.tw64 = p->tw64;
   fa.bark = at<float>(ws, g.bark);
   fa.partial = at<double>(ws, g.partial);
   fa.z = at<float>(ws, g.z);
+  fa.spec = at<Cx<float>>(ws, g.spec);
   fa.err = at<uint32_t>(ws, g.err);
-  PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre, (int)g.rows, s), "front kernel");
+  PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
 
   ChainFwdArgs ca{};
   ca.batch = (int)batch;
-  ca.nseg = g.f_nseg;
+  ca.nseg = g.nseg;
   ca.n = g.n16;
   ca.tab = p->dtab;
   ca.bark = fa.bark;
@@ -480,23 +507,18 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
   cb.kappa = at<float>(ws, g.kappa);
   PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, s), "chain backward kernel");
 
-  RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch};
   float* gx16 = at<float>(ws, g.gx16);
-  if (g.resample) {
-    const float* x16 = at<float>(ws, g.x16);
-    src16 = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
-  }
   BackArgs ba{};
-  ba.src = src16;
   ba.row_begin = g.grad_begin;
   ba.n = g.n16;
   ba.frames = g.T;
-  ba.seg_frames = g.b_seg;
-  ba.nseg = g.b_nseg;
+  ba.seg_frames = g.seg;
+  ba.nseg = g.nseg;
   ba.tab = p->dtab;
   ba.g_bark = cb.g_bark;
   ba.kappa = cb.kappa;
   ba.z = at<float>(ws, g.z);
+  ba.spec = at<Cx<float>>(ws, g.spec);
   ba.out = g.resample ? RowSink{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch}
                       : RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
   ba.err = at<uint32_t>(ws, g.err);

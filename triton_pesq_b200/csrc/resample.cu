@@ -1,6 +1,6 @@
 // Polyphase sinc resampler to 16 kHz and its adjoint.
 //
-// Output m = l * new_step + j of a row is
+// Output m = l * new_step + j of a row is (accumulated in double)
 //   y[m] = sum_k taps[j][k] x[l * orig_step + k - width]     (x = 0 outside)
 // which is torchaudio's strided conv1d over the (width, width + orig_step)
 // padded input (torch_pesq/loss.py:76, Resample(sample_rate, 16000)).  Only
@@ -29,17 +29,23 @@ __global__ void __launch_bounds__(kResampleThreads) resample_fwd_kernel(const __
   const float* taps = p.taps + (int64_t)j * p.max_count;
   const float* x = p.src.row(r);
   const int64_t s0 = l * p.orig_step + p.first[j] - p.width;
-  float acc = 0.0f;
+  // accumulated in double and returned as a float hi/lo pair: the resampled
+  // signal feeds the double precision pre-emphasis and spectrum of the front
+  // kernel, and near-silent bands make the loss gradient sensitive to its
+  // rounding
+  double acc = 0.0;
   if (s0 >= 0 && s0 + cnt <= p.n_in) {
-    for (int i = 0; i < cnt; ++i) acc = fmaf(taps[i], __ldg(x + s0 + i), acc);
+    for (int i = 0; i < cnt; ++i) acc = fma((double)taps[i], (double)__ldg(x + s0 + i), acc);
   } else {
     for (int i = 0; i < cnt; ++i) {
       const int64_t s = s0 + i;
       const float v = (s >= 0 && s < p.n_in) ? __ldg(x + s) : 0.0f;
-      acc = fmaf(taps[i], v, acc);
+      acc = fma((double)taps[i], (double)v, acc);
     }
   }
-  p.dst.row(r)[m] = acc;
+  const float hi = (float)acc;
+  p.dst.row(r)[m] = hi;
+  p.dst_lo.row(r)[m] = (float)(acc - (double)hi);
 }
 
 __global__ void __launch_bounds__(kResampleThreads) resample_adj_kernel(const __grid_constant__ ResampleArgs p) {

@@ -29,43 +29,44 @@
 
 namespace pesq {
 
-template <int P>
+// Tables of the scan in the arithmetic type R (float or double).
+template <int P, class R = float>
 struct ScanTab {
-  float h[kChunk];         // impulse response h[0..L-1]
-  float G[kChunk][P];      // C A^t
-  float W[kChunk][P];      // A^(L-1-k) B
-  float M[kLevels][P][P];  // A^(L * 2^i)
-  float A[P][P];           // one step, for the re-run form
-  float B[P];
-  float C[P];
-  float D;
+  R h[kChunk];         // impulse response h[0..L-1]
+  R G[kChunk][P];      // C A^t
+  R W[kChunk][P];      // A^(L-1-k) B
+  R M[kLevels][P][P];  // A^(L * 2^i)
+  R A[P][P];           // one step, for the re-run form
+  R B[P];
+  R C[P];
+  R D;
 };
 
 // Shared memory floats the scan needs as scratch.
-template <int P>
+template <int P, class R = float>
 __host__ __device__ constexpr int scan_scratch_floats() {
-  return P * kThreads;
+  return P * kThreads * (int)(sizeof(R) / sizeof(float));
 }
 
 // `load(p)` returns the input at logical position p (0 <= p < kSpan) and
 // `store(p, y)` consumes the output there.  `es` is scan scratch of
-// scan_scratch_floats<P>() floats.  Must be called by all kThreads threads.
-template <int P, bool kRerun, class Load, class Store>
-__device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Load&& load, Store&& store) {
+// scan_scratch_floats<P, R>() floats.  Must be called by all kThreads threads.
+template <int P, bool kRerun, class R, class Load, class Store>
+__device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load&& load, Store&& store) {
   const int c = threadIdx.x;
   const int p0 = c * kChunk;
 
-  float x[kChunk];
+  R x[kChunk];
 #pragma unroll
   for (int k = 0; k < kChunk; ++k) x[k] = load(p0 + k);
 
   // 1. zero-state end state of the chunk
-  float e[P];
+  R e[P];
 #pragma unroll
   for (int j = 0; j < P; ++j) {
-    float acc = 0.0f;
+    R acc = R(0);
 #pragma unroll
-    for (int k = 0; k < kChunk; ++k) acc = fmaf(tab.W[k][j], x[k], acc);
+    for (int k = 0; k < kChunk; ++k) acc = fma(tab.W[k][j], x[k], acc);
     e[j] = acc;
   }
 
@@ -76,15 +77,15 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Loa
 #pragma unroll
   for (int lv = 0; lv < kLevels; ++lv) {
     const int d = 1 << lv;
-    float prev[P];
+    R prev[P];
 #pragma unroll
-    for (int j = 0; j < P; ++j) prev[j] = c >= d ? es[j * kThreads + c - d] : 0.0f;
+    for (int j = 0; j < P; ++j) prev[j] = c >= d ? es[j * kThreads + c - d] : R(0);
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < P; ++i) {
-      float acc = e[i];
+      R acc = e[i];
 #pragma unroll
-      for (int j = 0; j < P; ++j) acc = fmaf(tab.M[lv][i][j], prev[j], acc);
+      for (int j = 0; j < P; ++j) acc = fma(tab.M[lv][i][j], prev[j], acc);
       e[i] = acc;
     }
 #pragma unroll
@@ -92,9 +93,9 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Loa
     __syncthreads();
   }
 
-  float s[P];
+  R s[P];
 #pragma unroll
-  for (int j = 0; j < P; ++j) s[j] = c >= 1 ? es[j * kThreads + c - 1] : 0.0f;
+  for (int j = 0; j < P; ++j) s[j] = c >= 1 ? es[j * kThreads + c - 1] : R(0);
   // the scratch is free again once every thread holds its start state
   __syncthreads();
 
@@ -102,15 +103,15 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Loa
   if constexpr (kRerun) {
 #pragma unroll
     for (int t = 0; t < kChunk; ++t) {
-      float y = tab.D * x[t];
+      R y = tab.D * x[t];
 #pragma unroll
-      for (int j = 0; j < P; ++j) y = fmaf(tab.C[j], s[j], y);
-      float nxt[P];
+      for (int j = 0; j < P; ++j) y = fma(tab.C[j], s[j], y);
+      R nxt[P];
 #pragma unroll
       for (int i = 0; i < P; ++i) {
-        float acc = tab.B[i] * x[t];
+        R acc = tab.B[i] * x[t];
 #pragma unroll
-        for (int j = 0; j < P; ++j) acc = fmaf(tab.A[i][j], s[j], acc);
+        for (int j = 0; j < P; ++j) acc = fma(tab.A[i][j], s[j], acc);
         nxt[i] = acc;
       }
 #pragma unroll
@@ -120,11 +121,11 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P>& tab, float* es, Loa
   } else {
 #pragma unroll
     for (int t = 0; t < kChunk; ++t) {
-      float y = 0.0f;
+      R y = R(0);
 #pragma unroll
-      for (int j = 0; j < P; ++j) y = fmaf(tab.G[t][j], s[j], y);
+      for (int j = 0; j < P; ++j) y = fma(tab.G[t][j], s[j], y);
 #pragma unroll
-      for (int k = 0; k <= t; ++k) y = fmaf(tab.h[t - k], x[k], y);
+      for (int k = 0; k <= t; ++k) y = fma(tab.h[t - k], x[k], y);
       store(p0 + t, y);
     }
   }
