@@ -1,0 +1,519 @@
+#!/usr/bin/env python
+"""Benchmark: PESQ loss forward + backward on B200, utterance-seconds per second.
+
+Workload (the configuration the headline metric is quoted on): batch 8 x 8 s
+at 16 kHz per GPU, speech-like seeded synthetic signals with f0 ~ U[90, 250]
+Hz and SNR ~ U[0, 20] dB, forward + backward w.r.t. the degraded signal,
+CUDA-graph replayed.  With N GPUs every rank runs its own batch (weak
+scaling, batch sharding) and the mean loss is all-reduced over NCCL each
+step, the only collective of the path.
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
+on the launching stream; the L2 is flushed (a 256 MiB write) between steps
+outside the events, because the step's inputs (8 MiB) fit in L2.  The K-step
+loop is bracketed by a barrier and synchronize; the reported time is the sum
+of the K step times, maximum over ranks.
+
+Also reported: e2e (same metric through the public API, ``PesqLossCuda.graphed``,
+with the inputs copied from pinned host memory and the loss read back every
+step), eager latency, per-stage kernel times, the roofline of the dominant
+kernel and the reference's CPU path (the oracle port, reference dtype mode)
+timed on this host.
+
+``--impl reference`` times the reference CPU implementation of the path (the
+oracle port in the reference's dtype mode) on this host's cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "PESQ fwd+bwd utterance-seconds/s per GPU and 1–8 GPU box; 8×8s@16k latency"
+UNIT = "utterance-seconds/s"
+RATE = 16000
+#: per-GPU batch and utterance length of the workloads bench.py can run
+WORKLOADS = {"cfg2": (8, 8.0), "cfg5": (512, 3.0)}
+BATCH, SECONDS = WORKLOADS["cfg2"]
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
+                    help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
+    ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
+    args = ap.parse_args()
+    global BATCH, SECONDS
+    BATCH, SECONDS = WORKLOADS[args.workload]
+    return args
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            data = json.load(fh)
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per front-kernel launch of the committed ncu summary."""
+
+    path = os.path.join(ROOT, "profiles", "front_kernel_cfg2.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":")[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+def cpu_reference_step(ref, deg, params):
+    """One forward + backward (w.r.t. deg) of the reference CPU path: the
+    oracle port in the reference's dtype mode (float32 signal stages, float64
+    perceptual chain, as PesqLoss evaluates on the CPU)."""
+
+    import torch
+
+    from oracle import pesq_oracle as O
+
+    d = deg.detach().clone().requires_grad_(True)
+    loss = O.forward(ref, d, params, mode="reference")
+    (g,) = torch.autograd.grad(loss.sum(), [d])
+    return loss, g
+
+
+def cpu_baseline(budget_s: float):
+    import torch
+
+    from oracle import pesq_oracle as O
+    from triton_pesq_b200.signals import workload
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref, deg, sr = workload("cfg2", seed=0)
+    params = O.OracleParams(factor=1.0, sample_rate=sr)
+    cpu_reference_step(ref[:1], deg[:1], params)  # warm-up
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        cpu_reference_step(ref, deg, params)
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= budget_s and steps >= 2:
+            break
+    utt_s = steps * BATCH * SECONDS
+    return {
+        "value": utt_s / elapsed,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{steps} x forward+backward(deg) of the full 8 x 8 s @16 kHz batch, {elapsed:.1f} s, "
+                  f"oracle port in the reference dtype mode (float32 signal path, float64 chain)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import pesq_oracle as O
+    from triton_pesq_b200.signals import workload
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref, deg, sr = workload("cfg2", seed=0)
+    params = O.OracleParams(factor=1.0, sample_rate=sr)
+    # each step is a bounded sample of the workload: 2 of the 8 utterances
+    sample = 2
+    for _ in range(args.warmup):
+        cpu_reference_step(ref[:sample], deg[:sample], params)
+    times = []
+    for k in range(args.steps):
+        lo = (2 * k) % BATCH
+        t0 = time.perf_counter()
+        cpu_reference_step(ref[lo:lo + sample], deg[lo:lo + sample], params)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps * sample * SECONDS / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "8x8s@16k fwd+bwd(deg)", "sample_per_step": f"{sample} x 8 s utterances",
+                   "global_batch": BATCH, "seconds": SECONDS, "sample_rate": RATE},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} of the 8 utterances per step, oracle port in the reference "
+                                   "dtype mode (float32 signal path, float64 chain)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CUDA arm
+# ---------------------------------------------------------------------------
+
+
+def stage_times(model, ref, deg, dev, launches=40):
+    """Average device time of every kernel stage, each timed alone with CUDA
+    events on the launching stream, inputs rotating over more than L2."""
+
+    import ctypes
+
+    import torch
+
+    from triton_pesq_b200 import _lib
+
+    lib = _lib.library()
+    plan = model._plan(dev)
+    flags = _lib.GRAD_DEG
+    b, n = ref.shape
+    nbytes = ctypes.c_size_t()
+    _lib.check(lib.pesq_workspace_size(ctypes.c_void_p(plan), b, n, flags, ctypes.byref(nbytes)), "workspace")
+    ws = torch.empty(nbytes.value // 4 + 64, dtype=torch.float32, device=dev)
+    sets = max(2, (320 << 20) // (2 * ref.numel() * 4))
+    refs = [ref.roll(k * 997, dims=1).contiguous() for k in range(sets)]
+    degs = [deg.roll(k * 997, dims=1).contiguous() for k in range(sets)]
+    outs = [torch.empty(b, device=dev) for _ in range(4)]
+    g_loss = torch.ones(b, device=dev)
+    g_deg = torch.empty_like(deg)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = ctypes.c_void_p(plan)
+    W = ctypes.c_void_p(ws.data_ptr())
+    wb = nbytes.value
+
+    def front(i):
+        return lib.pesq_forward_front(P, sp, ctypes.c_void_p(refs[i].data_ptr()), n,
+                                      ctypes.c_void_p(degs[i].data_ptr()), n, b, n, flags, W, wb)
+
+    def chain_fwd(i):
+        return lib.pesq_forward_chain(P, sp, b, n, flags, W, wb, *[ctypes.c_void_p(o.data_ptr()) for o in outs])
+
+    def chain_bwd(i):
+        return lib.pesq_backward_chain(P, sp, b, n, flags, W, wb, ctypes.c_void_p(g_loss.data_ptr()), None, None,
+                                       None)
+
+    def back(i):
+        return lib.pesq_backward_back(P, sp, b, n, flags, W, wb, None, n, ctypes.c_void_p(g_deg.data_ptr()), n)
+
+    # populate the workspace once in order
+    for fn in (front, chain_fwd, chain_bwd, back):
+        _lib.check(fn(0), "stage")
+    torch.cuda.synchronize()
+    result = {}
+    for name, fn in (("front", front), ("chain_forward", chain_fwd), ("chain_backward", chain_bwd), ("back", back)):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)  # keep the stream busy while the host enqueues
+        start.record(stream)
+        for i in range(launches):
+            fn(i % sets)
+        stop.record(stream)
+        torch.cuda.synchronize()
+        result[name] = 1e3 * start.elapsed_time(stop) / launches  # microseconds
+    return result
+
+
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.signals import workload
+
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    model = PesqLossCuda(1.0, sample_rate=RATE)
+    ref_cpu, deg_cpu, _ = workload(args.workload, seed=rank)
+    ref = ref_cpu.to(dev)
+    deg = deg_cpu.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    # ---- graph-replayed forward + backward (the headline value)
+    deg_p = deg.detach().clone().requires_grad_(True)
+
+    def step():
+        loss = model(ref, deg_p)
+        (g,) = torch.autograd.grad(loss.sum(), [deg_p])
+        return loss, g
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loss_g, grad_g = step()
+    torch.cuda.synchronize()
+
+    mean_loss = torch.zeros(1, device=dev)
+
+    def replay():
+        graph.replay()
+        if world > 1:
+            mean_loss.copy_(loss_g.sum().reshape(1) / (BATCH * world))
+            dist.all_reduce(mean_loss)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        replay()
+        flush.zero_()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            events[k][0].record(stream)
+            replay()
+            events[k][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    step_ms = [a.elapsed_time(b) for a, b in events]
+    total_ms = torch.tensor([sum(step_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_s = float(total_ms.item()) / 1e3
+    utt_per_step = BATCH * SECONDS * world
+    value = utt_per_step * args.steps / total_s
+
+    # ---- eager latency (host dispatch included)
+    eager = []
+    for k in range(max(5, args.steps // 5)):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        step()
+        torch.cuda.synchronize()
+        eager.append(time.perf_counter() - t0)
+
+    # ---- end to end through the public API with host buffers
+    ref_h = ref_cpu.pin_memory()
+    deg_h = deg_cpu.pin_memory()
+    loss_h = torch.empty(BATCH, pin_memory=True)
+    ref_d = torch.empty_like(ref)
+    deg_d = torch.empty_like(deg).requires_grad_(True)
+    graphed = model.graphed(ref_d, deg_d)
+    for _ in range(3):
+        with torch.no_grad():
+            ref_d.copy_(ref_h, non_blocking=True)
+            deg_d.copy_(deg_h, non_blocking=True)
+        out = graphed(ref_d, deg_d)
+        torch.autograd.grad(out.sum(), [deg_d])
+        loss_h.copy_(out.detach(), non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_ms = []
+    for k in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        with torch.no_grad():
+            ref_d.copy_(ref_h, non_blocking=True)
+            deg_d.copy_(deg_h, non_blocking=True)
+        out = graphed(ref_d, deg_d)
+        torch.autograd.grad(out.sum(), [deg_d])
+        loss_h.copy_(out.detach(), non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        e2e_ms.append(a.elapsed_time(b))
+    e2e_total = torch.tensor([sum(e2e_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+    e2e_value = utt_per_step * args.steps / (float(e2e_total.item()) / 1e3)
+
+    # ---- stage kernels alone, roofline of the dominant one
+    stages = stage_times(model, ref, deg, dev)
+    dominant = max(stages, key=stages.get)
+    peak, peak_kind = measured_peaks()
+    # algorithmic bytes per launch: the front kernel must read both input
+    # signals (2 x 4 B per utterance sample); the back kernel must write the
+    # gradient (4 B); the chain kernels have no compulsory traffic of their own
+    alg = {"front": 2 * 4 * BATCH * SECONDS * RATE, "back": 4 * BATCH * SECONDS * RATE,
+           "chain_forward": 0.0, "chain_backward": 0.0}
+    front_us = stages["front"]
+    achieved = alg["front"] / (front_us * 1e-6) / 1e9
+    traffic = profiled_traffic()
+
+    if world > 1:
+        graph.reset()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * total_s / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"{BATCH}x{SECONDS:g}s@16k fwd+bwd(deg), CUDA-graph replay ({args.workload})",
+            "global_batch": BATCH * world,
+            "seconds": SECONDS,
+            "sample_rate": RATE,
+            "parallelism": f"dp{world}",
+            "l2": "flushed between steps (256 MiB write, outside the step events)",
+        },
+        "clocks": clocks.summary(),
+        "e2e": {
+            "value": e2e_value,
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(ref.numel() * 4 * 2),
+            "d2h_bytes_per_step": int(BATCH * 4),
+            "api": "PesqLossCuda.graphed, inputs from pinned host memory, loss read back",
+            "ms_per_step": statistics.mean(e2e_ms),
+        },
+        "gpu_launches": 4 * args.steps,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "front",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_source": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": alg["front"],
+            "launch_us": front_us,
+        },
+        "stages_us": stages,
+        "dominant_stage": dominant,
+        "eager_ms_per_step": 1e3 * statistics.median(eager),
+        "step_ms_min": min(step_ms),
+        "step_ms_median": statistics.median(step_ms),
+        "wall_s_timed_loop": wall,
+    }
+    if not args.skip_cpu:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -143,6 +143,34 @@ int pesq_backward(const pesq_plan* plan, void* stream, const float* ref, int64_t
                   size_t workspace_bytes, const float* g_loss, const float* g_mos, const float* g_dsymm,
                   const float* g_dasymm, float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg);
 
+/* The two stages of pesq_forward, callable on their own with the same
+ * arguments (used to time the stages separately; pesq_forward is exactly
+ * pesq_forward_front followed by pesq_forward_chain):
+ *   front: [resampling to 16 kHz] + level alignment, pre-emphasis, STFT -> Bark
+ *          (replaces triton_ops/loss.py:133-143: peak_normalize .. spectral)
+ *   chain: perceptual model, distances, MOS and loss
+ *          (replaces triton_ops/loss.py:145-147 and elementwise.py:683-747) */
+int pesq_forward_front(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                       int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
+                       size_t workspace_bytes);
+int pesq_forward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
+                       void* workspace, size_t workspace_bytes, float* d_symm, float* d_asymm, float* mos,
+                       float* loss);
+
+/* The two stages of pesq_backward (pesq_backward is exactly
+ * pesq_backward_chain followed by pesq_backward_back):
+ *   chain: adjoint of the perceptual model and of the epilogue
+ *          (replaces chain.py:892-1021 and elementwise.py:800-827)
+ *   back:  spectral adjoint, pre-emphasis adjoint, level-alignment term
+ *          [+ resampler adjoint] (replaces spectral.py:526-581, iir.py:1249-1258,
+ *          elementwise.py:234-265, 372-389, 608-652, resample.py:431-439) */
+int pesq_backward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
+                        void* workspace, size_t workspace_bytes, const float* g_loss, const float* g_mos,
+                        const float* g_dsymm, const float* g_dasymm);
+int pesq_backward_back(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
+                       void* workspace, size_t workspace_bytes, float* g_ref, int64_t ld_gref, float* g_deg,
+                       int64_t ld_gdeg);
+
 #ifdef __cplusplus
 }
 #endif

@@ -392,9 +392,8 @@ int pesq_workspace_size(const pesq_plan* p, int64_t batch, int64_t n_src, uint32
   return PESQ_OK;
 }
 
-int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
-                 int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
-                 float* d_symm, float* d_asymm, float* mos, float* loss) {
+int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                       int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes) {
   if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
   Geometry g;
   int rc = geometry(p, batch, n_src, flags, g);
@@ -450,14 +449,25 @@ int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_
   fa.spec = at<Cx<float>>(ws, g.spec);
   fa.err = at<uint32_t>(ws, g.err);
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
+  return PESQ_OK;
+}
 
+int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t n_src, uint32_t flags, void* ws,
+                       size_t ws_bytes, float* d_symm, float* d_asymm, float* mos, float* loss) {
+  if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
+  Geometry g;
+  int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  if (batch == 0) return PESQ_OK;
+  rc = check_call(p, g, ws, ws_bytes);
+  if (rc) return rc;
   ChainFwdArgs ca{};
   ca.batch = (int)batch;
   ca.nseg = g.nseg;
   ca.n = g.n16;
   ca.tab = p->dtab;
-  ca.bark = fa.bark;
-  ca.partial = fa.partial;
+  ca.bark = at<float>(ws, g.bark);
+  ca.partial = at<double>(ws, g.partial);
   ca.sumsq = at<double>(ws, g.sumsq);
   ca.saved = at<float>(ws, g.saved);
   ca.lay = g.lay;
@@ -466,28 +476,29 @@ int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_
   ca.d_asymm = d_asymm;
   ca.mos = mos;
   ca.loss = loss;
-  PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, s), "chain forward kernel");
+  PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, static_cast<cudaStream_t>(stream)), "chain forward kernel");
   return PESQ_OK;
 }
 
-int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
-                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
-                  const float* g_loss, const float* g_mos, const float* g_dsymm, const float* g_dasymm,
-                  float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
+int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                 int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
+                 float* d_symm, float* d_asymm, float* mos, float* loss) {
+  const int rc = pesq_forward_front(p, stream, ref, ld_ref, deg, ld_deg, batch, n_src, flags, ws, ws_bytes);
+  if (rc) return rc;
+  return pesq_forward_chain(p, stream, batch, n_src, flags, ws, ws_bytes, d_symm, d_asymm, mos, loss);
+}
+
+int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t n_src, uint32_t flags, void* ws,
+                        size_t ws_bytes, const float* g_loss, const float* g_mos, const float* g_dsymm,
+                        const float* g_dasymm) {
   if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
   Geometry g;
   int rc = geometry(p, batch, n_src, flags, g);
   if (rc) return rc;
   if (!g.grad) return fail(PESQ_ERR_INVALID_ARGUMENT, "backward without PESQ_GRAD_REF or PESQ_GRAD_DEG");
   if (batch == 0) return PESQ_OK;
-  if ((flags & PESQ_GRAD_REF) && (!g_ref || ld_gref < n_src))
-    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/dref output");
-  if ((flags & PESQ_GRAD_DEG) && (!g_deg || ld_gdeg < n_src))
-    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/ddeg output");
   rc = check_call(p, g, ws, ws_bytes);
   if (rc) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-
   ChainBwdArgs cb{};
   cb.batch = (int)batch;
   cb.tab = p->dtab;
@@ -505,7 +516,25 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
   cb.want_deg = (flags & PESQ_GRAD_DEG) != 0;
   cb.g_bark = at<float>(ws, g.gbark);
   cb.kappa = at<float>(ws, g.kappa);
-  PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, s), "chain backward kernel");
+  PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, static_cast<cudaStream_t>(stream)), "chain backward kernel");
+  return PESQ_OK;
+}
+
+int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t n_src, uint32_t flags, void* ws,
+                       size_t ws_bytes, float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
+  if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
+  Geometry g;
+  int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  if (!g.grad) return fail(PESQ_ERR_INVALID_ARGUMENT, "backward without PESQ_GRAD_REF or PESQ_GRAD_DEG");
+  if (batch == 0) return PESQ_OK;
+  if ((flags & PESQ_GRAD_REF) && (!g_ref || ld_gref < n_src))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/dref output");
+  if ((flags & PESQ_GRAD_DEG) && (!g_deg || ld_gdeg < n_src))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "missing dL/ddeg output");
+  rc = check_call(p, g, ws, ws_bytes);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   float* gx16 = at<float>(ws, g.gx16);
   BackArgs ba{};
@@ -515,8 +544,8 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
   ba.seg_frames = g.seg;
   ba.nseg = g.nseg;
   ba.tab = p->dtab;
-  ba.g_bark = cb.g_bark;
-  ba.kappa = cb.kappa;
+  ba.g_bark = at<float>(ws, g.gbark);
+  ba.kappa = at<float>(ws, g.kappa);
   ba.z = at<float>(ws, g.z);
   ba.spec = at<Cx<float>>(ws, g.spec);
   ba.out = g.resample ? RowSink{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch}
@@ -544,6 +573,20 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
     PESQ_CUDA_TRY(launch_resample_adj(ra, s), "resample adjoint kernel");
   }
   return PESQ_OK;
+}
+
+int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
+                  const float* g_loss, const float* g_mos, const float* g_dsymm, const float* g_dasymm,
+                  float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
+  (void)ref;
+  (void)ld_ref;
+  (void)deg;
+  (void)ld_deg;
+  const int rc =
+      pesq_backward_chain(p, stream, batch, n_src, flags, ws, ws_bytes, g_loss, g_mos, g_dsymm, g_dasymm);
+  if (rc) return rc;
+  return pesq_backward_back(p, stream, batch, n_src, flags, ws, ws_bytes, g_ref, ld_gref, g_deg, ld_gdeg);
 }
 
 }  // extern "C"
