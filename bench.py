@@ -182,7 +182,8 @@ def cpu_baseline(budget_s: float):
         elapsed = time.perf_counter() - t0
         if elapsed >= budget_s and steps >= 2:
             break
-    utt_s = steps * BATCH * SECONDS
+    b, secs = WORKLOADS["cfg2"]
+    utt_s = steps * b * secs
     return {
         "value": utt_s / elapsed,
         "unit": UNIT,
