@@ -171,6 +171,20 @@ int pesq_backward_back(const pesq_plan* plan, void* stream, int64_t batch, int64
                        void* workspace, size_t workspace_bytes, float* g_ref, int64_t ld_gref, float* g_deg,
                        int64_t ld_gdeg);
 
+/* Forward pass (distances, MOS, loss; no gradient) that allocates nothing and
+ * takes no workspace: for callers that cannot allocate device memory when they
+ * evaluate, such as real-time audio callbacks, plugins whose host owns all
+ * device memory, or code running during a global-mode stream capture.  Its
+ * scratch is a 16 MiB static device array of the library, held on every
+ * device this entry point has been used on; the first call on a device looks
+ * up that array and should come before any stream capture; calls sharing a
+ * device must not overlap on the GPU (they share the array).  Batches needing
+ * more than 16 MiB of scratch get PESQ_ERR_WORKSPACE.  This entry point has
+ * no counterpart in the reference. */
+int pesq_forward_noalloc(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                         int64_t ld_deg, int64_t batch, int64_t n_src, float* d_symm, float* d_asymm, float* mos,
+                         float* loss);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,7 @@ GRAD_DEG = 2
 
 PESQ_OK = 0
 PESQ_ERR_INVALID_ARGUMENT = 1
+PESQ_ERR_WORKSPACE = 3
 
 _lock = threading.Lock()
 _lib = None
@@ -123,6 +124,11 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p,
          ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64],
+    ),
+    "pesq_forward_noalloc": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
     ),
 }
 

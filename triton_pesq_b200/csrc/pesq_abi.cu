@@ -197,6 +197,12 @@ int check_call(const pesq_plan* p, const Geometry& g, void* ws, size_t ws_bytes)
 
 }  // namespace
 
+namespace pesq {
+// Records `msg` as the calling thread's last error (used by the entry points
+// that live in other translation units) and returns `code`.
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace pesq
+
 extern "C" {
 
 int pesq_abi_version(void) { return PESQ_CUDA_ABI_VERSION; }
