@@ -1,15 +1,17 @@
 // Perceptual chain of the PESQ model, forward and adjoint.
 //
 // One thread block cluster per utterance; CTA q of the cluster owns a
-// contiguous slice of frames and each of its warps a contiguous sub-slice
-// (lanes cover the Bark bands k and k + 32).  The three genuine whole-signal
-// dependencies of the model -- the band means over all non-silent frames
-// (torch_pesq/loss.py:205-216), the two-tap smoothing of the frame power
-// ratio across frames (loss.py:224-226) and the overlapping 20-frame windows
-// (loss.py:257-266) -- are resolved with cluster barriers: band partial sums
-// are exchanged through distributed shared memory, per-frame values through
-// the saved-state arrays in global memory.  Every reduction has a fixed
-// order, so results are bitwise reproducible.
+// contiguous slice of frames and each of its 16 warps a contiguous sub-slice
+// (lanes cover the Bark bands k and k + 32).  The slice's Bark spectra (and,
+// in the adjoint, their gradient accumulators) are staged in shared memory.
+// The genuine whole-signal dependencies of the model -- the band means over
+// all non-silent frames (torch_pesq/loss.py:205-216), the two-tap smoothing of
+// the frame power ratio across frames (loss.py:224-226), the overlapping
+// 20-frame windows and the RMS over them (loss.py:257-266) -- are resolved
+// with cluster barriers: band partial sums are exchanged through distributed
+// shared memory, per-frame values through the saved-state arrays in global
+// memory.  Every reduction has a fixed order, so results are bitwise
+// reproducible.
 //
 // The Bark spectra arrive unscaled; the level alignment (loss.py:132-139)
 // enters as s^2 = 1e7 / P with P = sum (H x)^2 / (N + 5120) / 1.04684.
@@ -19,12 +21,14 @@
 
 namespace pesq {
 
-constexpr int kChainThreads = 256;
+constexpr int kChainThreads = 512;
 constexpr int kChainWarps = kChainThreads / 32;
 // Above this distance from the threshold the loudness base^e - 1 is evaluated
 // with powf; below it with expm1(e log1p(.)), which keeps full relative
 // precision as the base approaches one.
 constexpr float kLoudSplit = 64.0f;
+// Dynamic shared memory the staged kernels may use.
+constexpr size_t kChainSmemLimit = 180 * 1024;
 
 ChainLayout ChainLayout::make(int T, int nb) {
   ChainLayout l;
@@ -59,6 +63,11 @@ ChainLayout ChainLayout::make(int T, int nb) {
   l.stride = o;
   return l;
 }
+
+int chain_slice_frames(int T, int cluster) { return (int)ceil_div(T, cluster); }
+size_t chain_fwd_smem_bytes(int slice, int nb) { return (size_t)2 * (slice + 1) * nb * sizeof(float); }
+size_t chain_bwd_smem_bytes(int slice, int nb) { return (size_t)4 * slice * nb * sizeof(float); }
+size_t chain_smem_limit() { return kChainSmemLimit; }
 
 namespace {
 
@@ -120,13 +129,38 @@ __device__ __forceinline__ void load_tables(DevTables* dst, const DevTables* src
   for (int i = threadIdx.x; i < (int)(sizeof(DevTables) / 16); i += blockDim.x) d4[i] = s4[i];
 }
 
-__device__ __forceinline__ void slice(int T, int& lo, int& hi) {
-  const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
-  const int warp = threadIdx.x >> 5;
-  const int c_lo = (int)((int64_t)q * T / C), c_hi = (int)((int64_t)(q + 1) * T / C);
-  const int n = c_hi - c_lo;
-  lo = c_lo + warp * n / kChainWarps;
-  hi = c_lo + (warp + 1) * n / kChainWarps;
+// Frames of this CTA (a contiguous slice of the utterance) and of this warp
+// (a contiguous sub-slice of that).
+struct Slice {
+  int c_lo, c_hi, w_lo, w_hi;
+  __device__ Slice(int T) {
+    const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
+    const int per = (int)ceil_div(T, C);
+    c_lo = min(T, q * per);
+    c_hi = min(T, c_lo + per);
+    const int n = c_hi - c_lo;
+    const int warp = threadIdx.x >> 5;
+    w_lo = c_lo + warp * n / kChainWarps;
+    w_hi = c_lo + (warp + 1) * n / kChainWarps;
+  }
+};
+
+// Sum over the cluster of a per-CTA shared double, identical order in every CTA.
+__device__ __forceinline__ double cluster_sum(const double* local, int C) {
+  double v[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) v[c] = c < C ? dsmem_ld_f64(dsmem_addr(local, c)) : 0.0;
+  double s = 0.0;
+#pragma unroll
+  for (int c = 0; c < 16; ++c) s += v[c];
+  return s;
+}
+
+// sum of squares of a row from its per-segment partials, one warp
+__device__ __forceinline__ double warp_row_sumsq(const double* partial, int nseg, int lane) {
+  double s = 0.0;
+  for (int i = lane; i < nseg; i += 32) s += partial[i];
+  return warp_sum(s);
 }
 
 // ---------------------------------------------------------------------------
@@ -134,9 +168,11 @@ __device__ __forceinline__ void slice(int T, int& lo, int& hi) {
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __grid_constant__ ChainFwdArgs p) {
+  extern __shared__ __align__(16) float dsm[];
   __shared__ DevTables tab;
   __shared__ double wpr[kChainWarps][kMaxBands], wpd[kChainWarps][kMaxBands];
   __shared__ double part_r[kMaxBands], part_d[kMaxBands];
+  __shared__ double band_tot[2][kMaxBands];
   __shared__ float bpr_s[kMaxBands];
   __shared__ float s2s[2];
 
@@ -144,41 +180,57 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   const int u = blockIdx.x / C;
   const int B = p.batch, T = p.lay.T, L = p.lay.L;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const Slice sl(T);
 
   load_tables(&tab, p.tab);
-  if (threadIdx.x == 0) {
+  if (warp < 2) {
     // level alignment power of both rows, loss.py:132-136
-    const double denom = ((double)p.n + 5120.0) * 1.04684;
-    for (int side = 0; side < 2; ++side) {
-      const int r = side == 0 ? u : B + u;
-      double tot = 0.0;
-      for (int s = 0; s < p.nseg; ++s) tot += p.partial[(int64_t)r * p.nseg + s];
-      s2s[side] = (float)(1e7 / (tot / denom));
+    const int r = warp == 0 ? u : B + u;
+    const double tot = warp_row_sumsq(p.partial + (int64_t)r * p.nseg, p.nseg, lane);
+    if (lane == 0) {
+      const double denom = ((double)p.n + 5120.0) * 1.04684;
+      s2s[warp] = (float)(1e7 / (tot / denom));
       if (q == 0) p.sumsq[r] = tot;
     }
   }
+  const float* Fr = p.bark + (int64_t)u * T * p.lay.nb;
+  const float* Fd = p.bark + (int64_t)(B + u) * T * p.lay.nb;
+  const int nb = p.lay.nb;
+  // staged frames c_lo - 1 .. c_hi - 1 (the one before the slice feeds the
+  // frame power ratio smoothing of its first frame)
+  const int t_first = sl.c_lo - 1;
+  const float* fr = Fr;
+  const float* fd = Fd;
+  int64_t origin = 0;
+  if (p.staged) {
+    const int cnt = (sl.c_hi - t_first) * nb;
+    float* sr = dsm;
+    float* sd = dsm + (int64_t)(sl.c_hi - sl.c_lo + 1) * nb;
+    for (int i = threadIdx.x; i < cnt; i += kChainThreads) {
+      const int64_t g = (int64_t)t_first * nb + i;
+      sr[i] = g >= 0 ? Fr[g] : 0.0f;
+      sd[i] = g >= 0 ? Fd[g] : 0.0f;
+    }
+    fr = sr;
+    fd = sd;
+    origin = (int64_t)t_first * nb;
+  }
   __syncthreads();
   const float s2r = s2s[0], s2d = s2s[1];
-  const int nb = tab.nb;
   float* sv = p.saved + (int64_t)u * p.lay.stride;
-  const float* Fr = p.bark + (int64_t)u * T * nb;
-  const float* Fd = p.bark + (int64_t)(B + u) * T * nb;
+  auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
 
   Band b0, b1;
   b0.load(tab, lane);
   b1.load(tab, lane + 32);
-  int lo, hi;
-  slice(T, lo, hi);
 
   // pass A: silent frames (loss.py:206) and band sums of audible power over
   // the non-silent frames (loudness.py:297-320)
   {
     double ar0 = 0.0, ar1 = 0.0, ad0 = 0.0, ad1 = 0.0;
-    for (int t = lo; t < hi; ++t) {
-      const float* fr = Fr + (int64_t)t * nb;
-      const float* fd = Fd + (int64_t)t * nb;
-      const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
-      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
+      const float R0 = b0.ok ? s2r * fr[at(t, b0.k)] : 0.0f, R1 = b1.ok ? s2r * fr[at(t, b1.k)] : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
       const float a0 = R0 > b0.th100 ? R0 : 0.0f, a1 = R1 > b1.th100 ? R1 : 0.0f;
       const float tot = warp_sum(a0 + a1);
       const bool keep = !(tot < 1e7f);
@@ -192,13 +244,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     }
     wpr[warp][lane] = ar0;
     wpd[warp][lane] = ad0;
-    if (lane + 32 < kMaxBands) {
-      wpr[warp][lane + 32] = ar1;
-      wpd[warp][lane + 32] = ad1;
-    }
+    wpr[warp][lane + 32] = ar1;
+    wpd[warp][lane + 32] = ad1;
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+  if (threadIdx.x < nb) {
+    const int k = threadIdx.x;
     double r = 0.0, d = 0.0;
     for (int w = 0; w < kChainWarps; ++w) {
       r += wpr[w][k];
@@ -208,14 +259,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     part_d[k] = d;
   }
   cluster_sync();
-  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
-    double r = 0.0, d = 0.0;
-    for (int c = 0; c < C; ++c) {
-      r += dsmem_ld_f64(dsmem_addr(&part_r[k], c));
-      d += dsmem_ld_f64(dsmem_addr(&part_d[k], c));
-    }
+  if (threadIdx.x < 2 * nb) {
+    const int k = threadIdx.x % nb, side = threadIdx.x / nb;
+    band_tot[side][k] = cluster_sum(side == 0 ? &part_r[k] : &part_d[k], C);
+  }
+  __syncthreads();
+  if (threadIdx.x < nb) {
+    const int k = threadIdx.x;
     // band power ratio, loss.py:212-216
-    const float mr = (float)(r / T), md = (float)(d / T);
+    const float mr = (float)(band_tot[0][k] / T), md = (float)(band_tot[1][k] / T);
     const float ratio = (md + 1000.0f) / (mr + 1000.0f);
     const float bpr = fminf(fmaxf(ratio, 0.01f), 100.0f);
     bpr_s[k] = bpr;
@@ -236,26 +288,23 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   // (loss.py:217-255)
   {
     const float bpr0 = b0.ok ? bpr_s[b0.k] : 0.0f, bpr1 = b1.ok ? bpr_s[b1.k] : 0.0f;
-    const float W = tab.total_width, sqW = tab.sqrt_total_width;
+    const float sqW = tab.sqrt_total_width;
     auto audible = [&](int t, float& taer, float& tad) {
-      const float* fr = Fr + (int64_t)t * nb;
-      const float* fd = Fd + (int64_t)t * nb;
-      const float er0 = b0.ok ? bpr0 * (s2r * fr[b0.k]) : 0.0f, er1 = b1.ok ? bpr1 * (s2r * fr[b1.k]) : 0.0f;
-      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+      const float er0 = b0.ok ? bpr0 * (s2r * fr[at(t, b0.k)]) : 0.0f;
+      const float er1 = b1.ok ? bpr1 * (s2r * fr[at(t, b1.k)]) : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
       taer = warp_sum((er0 > b0.th ? er0 : 0.0f) + (er1 > b1.th ? er1 : 0.0f));
       tad = warp_sum((D0 > b0.th ? D0 : 0.0f) + (D1 > b1.th ? D1 : 0.0f));
     };
     float fpr0_prev = 0.0f;
-    if (lo < hi && lo > 0) {
+    if (sl.w_lo < sl.w_hi && sl.w_lo > 0) {
       float ta, td;
-      audible(lo - 1, ta, td);
+      audible(sl.w_lo - 1, ta, td);
       fpr0_prev = (ta + 5e3f) / (td + 5e3f);
     }
-    for (int t = lo; t < hi; ++t) {
-      const float* fr = Fr + (int64_t)t * nb;
-      const float* fd = Fd + (int64_t)t * nb;
-      const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
-      const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
+      const float R0 = b0.ok ? s2r * fr[at(t, b0.k)] : 0.0f, R1 = b1.ok ? s2r * fr[at(t, b1.k)] : 0.0f;
+      const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
       float taer, tad;
       audible(t, taer, tad);
       const float fpr0 = (taer + 5e3f) / (tad + 5e3f);
@@ -295,59 +344,61 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       }
       fpr0_prev = fpr0;
     }
-    (void)W;
   }
   __threadfence();
   cluster_sync();
 
-  // pass C (rank 0): sixth-power means over 20-frame windows, then the RMS
-  // over windows (loss.py:257-266), both normalised by their maximum so that
-  // the 1e-20 floor of the disturbance does not underflow
-  if (q == 0) {
-    for (int side = 0; side < 2; ++side) {
+  // pass C: sixth-power means over 20-frame windows (loss.py:257-266),
+  // normalised by the window maximum so that the 1e-20 floor of the
+  // disturbance does not underflow; every CTA evaluates the windows that start
+  // in its slice
+  {
+    const int l_lo = (sl.c_lo + 9) / 10, l_hi = min(L, (sl.c_hi + 9) / 10);
+    const int nw = max(0, l_hi - l_lo);
+    for (int job = warp; job < 2 * nw; job += kChainWarps) {
+      const int side = job / nw, l = l_lo + job % nw;
       const int64_t src = side == 0 ? p.lay.sp : p.lay.ap;
       const int64_t dst = side == 0 ? p.lay.psqm_s : p.lay.psqm_a;
-      for (int l = warp; l < L; l += kChainWarps) {
-        const float s = lane < 20 ? __ldcg(sv + src + 10 * l + lane) : 0.0f;
-        const float mx = warp_max(s);
-        const float sc = mx > 0.0f ? mx : 1.0f;
-        const float v = s / sc, v2 = v * v;
-        const float m6 = warp_sum(lane < 20 ? v2 * v2 * v2 : 0.0f) / 20.0f;
-        if (lane == 0) sv[dst + l] = mx * powf(m6, 1.0f / 6.0f);
-      }
-    }
-    __syncthreads();
-    if (warp < 2) {
-      const int64_t src = warp == 0 ? p.lay.psqm_s : p.lay.psqm_a;
-      float mx = 0.0f;
-      for (int l = lane; l < L; l += 32) mx = fmaxf(mx, sv[src + l]);
-      mx = warp_max(mx);
+      const float s = lane < 20 ? __ldcg(sv + src + 10 * l + lane) : 0.0f;
+      const float mx = warp_max(s);
       const float sc = mx > 0.0f ? mx : 1.0f;
-      float acc = 0.0f;
-      for (int l = lane; l < L; l += 32) {
-        const float v = sv[src + l] / sc;
-        acc = fmaf(v, v, acc);
-      }
-      acc = warp_sum(acc);
-      const float d = mx * sqrtf(acc / (float)L);
-      if (lane == 0) {
-        sv[p.lay.scal + (warp == 0 ? kDSymm : kDAsymm)] = d;
-        s2s[warp] = d;
-      }
+      const float v = s / sc, v2 = v * v;
+      const float m6 = warp_sum(lane < 20 ? v2 * v2 * v2 : 0.0f) / 20.0f;
+      if (lane == 0) sv[dst + l] = mx * powf(m6, 1.0f / 6.0f);
     }
+  }
+  __threadfence();
+  cluster_sync();
+
+  // RMS over the windows (rank 0), then MOS and loss (loss.py:289-297, 320-322)
+  if (q == 0 && warp < 2) {
+    const int64_t src = warp == 0 ? p.lay.psqm_s : p.lay.psqm_a;
+    float mx = 0.0f;
+    for (int l = lane; l < L; l += 32) mx = fmaxf(mx, __ldcg(sv + src + l));
+    mx = warp_max(mx);
+    const float sc = mx > 0.0f ? mx : 1.0f;
+    float acc = 0.0f;
+    for (int l = lane; l < L; l += 32) {
+      const float v = __ldcg(sv + src + l) / sc;
+      acc = fmaf(v, v, acc);
+    }
+    acc = warp_sum(acc);
+    const float d = mx * sqrtf(acc / (float)L);
+    if (lane == 0) {
+      sv[p.lay.scal + (warp == 0 ? kDSymm : kDAsymm)] = d;
+      if (warp == 0 && p.d_symm) p.d_symm[u] = d;
+      if (warp == 1 && p.d_asymm) p.d_asymm[u] = d;
+    }
+  }
+  if (q == 0) {
     __syncthreads();
     if (threadIdx.x == 0) {
-      const float ds = s2s[0], da = s2s[1];
-      if (p.d_symm) p.d_symm[u] = ds;
-      if (p.d_asymm) p.d_asymm[u] = da;
-      // MOS compression and loss (loss.py:289-297, loss.py:320-322)
+      const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
       const float m = 4.5f - 0.1f * ds - 0.0309f * da;
       if (p.mos) p.mos[u] = 0.999f + 4.0f / (1.0f + expf(-1.3669f * m + 3.8224f));
       if (p.loss) p.loss[u] = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
     }
   }
-  // keep every CTA's shared memory alive until the cluster is done with it
-  cluster_sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -355,6 +406,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __grid_constant__ ChainBwdArgs p) {
+  extern __shared__ __align__(16) float dsm[];
   __shared__ DevTables tab;
   __shared__ double wpart[kChainWarps][kMaxBands];
   __shared__ double part[kMaxBands];
@@ -364,20 +416,42 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
 
   const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
   const int u = blockIdx.x / C;
-  const int B = p.batch, T = p.lay.T, L = p.lay.L;
+  const int B = p.batch, T = p.lay.T, L = p.lay.L, nb = p.lay.nb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const Slice sl(T);
 
   load_tables(&tab, p.tab);
-  __syncthreads();
-  const int nb = tab.nb;
   const float* sv = p.saved + (int64_t)u * p.lay.stride;
   float* gf = p.scratch + (int64_t)u * 2 * T;  // [g_fpr | g_h] per frame
-  const float s2r = sv[p.lay.scal + kS2Ref], s2d = sv[p.lay.scal + kS2Deg];
-  const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
   const float* Fr = p.bark + (int64_t)u * T * nb;
   const float* Fd = p.bark + (int64_t)(B + u) * T * nb;
-  float* gR = p.g_bark + (int64_t)u * T * nb;
-  float* gD = p.g_bark + (int64_t)(B + u) * T * nb;
+  float* GR = p.g_bark + (int64_t)u * T * nb;
+  float* GD = p.g_bark + (int64_t)(B + u) * T * nb;
+  // the slice's spectra and gradient accumulators: shared memory if staged,
+  // else the gradient outputs themselves serve as accumulators
+  const float* fr = Fr;
+  const float* fd = Fd;
+  float* gr = GR;
+  float* gd = GD;
+  int64_t origin = 0;
+  if (p.staged) {
+    const int n = (sl.c_hi - sl.c_lo) * nb;
+    float* sr = dsm;
+    float* sd = sr + n;
+    for (int i = threadIdx.x; i < n; i += kChainThreads) {
+      sr[i] = Fr[(int64_t)sl.c_lo * nb + i];
+      sd[i] = Fd[(int64_t)sl.c_lo * nb + i];
+    }
+    fr = sr;
+    fd = sd;
+    gr = sd + n;
+    gd = gr + n;
+    origin = (int64_t)sl.c_lo * nb;
+  }
+  __syncthreads();
+  auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
+  const float s2r = sv[p.lay.scal + kS2Ref], s2d = sv[p.lay.scal + kS2Deg];
+  const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
 
   // upstream gradients of both distances (epilogue adjoint)
   float gds = p.g_dsymm ? p.g_dsymm[u] : 0.0f;
@@ -400,17 +474,16 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   b1.load(tab, lane + 32);
   const float bpr0 = b0.ok ? sv[p.lay.bpr + b0.k] : 0.0f, bpr1 = b1.ok ? sv[p.lay.bpr + b1.k] : 0.0f;
   const float W = tab.total_width;
-  int lo, hi;
-  slice(T, lo, hi);
 
   // dL/d(frame distance) through the windows, the RMS, the 45 clamp, /h and
   // the 1e-20 floor
   auto frame_grads = [&](int t, float& g_sraw, float& g_araw, float& g_h) {
     const float h = sv[p.lay.h + t];
     g_sraw = g_araw = g_h = 0.0f;
+#pragma unroll
     for (int side = 0; side < 2; ++side) {
       const float d = side == 0 ? ds : da;
-      const float gd = side == 0 ? gds : gda;
+      const float gdist = side == 0 ? gds : gda;
       const int64_t pq = side == 0 ? p.lay.psqm_s : p.lay.psqm_a;
       const float s = sv[(side == 0 ? p.lay.sp : p.lay.ap) + t];
       const float raw = sv[(side == 0 ? p.lay.sraw : p.lay.araw) + t];
@@ -425,7 +498,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
             gs += pl * (r2 * r2 * r);
           }
         }
-        gs *= gd / (20.0f * (float)L * d);
+        gs *= gdist / (20.0f * (float)L * d);
       }
       const float c = fmaxf(raw, 1e-20f);
       const bool inside = c / h <= 45.0f;
@@ -440,11 +513,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   };
 
   // pass 1: loudness / disturbance / norm adjoint per band; per-frame dL/dfpr
-  for (int t = lo; t < hi; ++t) {
-    const float* fr = Fr + (int64_t)t * nb;
-    const float* fd = Fd + (int64_t)t * nb;
-    const float R0 = b0.ok ? s2r * fr[b0.k] : 0.0f, R1 = b1.ok ? s2r * fr[b1.k] : 0.0f;
-    const float D0 = b0.ok ? s2d * fd[b0.k] : 0.0f, D1 = b1.ok ? s2d * fd[b1.k] : 0.0f;
+  for (int t = sl.w_lo; t < sl.w_hi; ++t) {
     const float fpr = fminf(fmaxf(sv[p.lay.fpr1 + t], 3e-4f), 5.0f);
     const float sraw = sv[p.lay.sraw + t];
     float g_sraw, g_araw, g_h;
@@ -452,10 +521,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     const float coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
 
     float gfpr = 0.0f;
+#pragma unroll
     for (int half = 0; half < 2; ++half) {
       const Band& b = half == 0 ? b0 : b1;
       if (!b.ok) continue;
-      const float R = half == 0 ? R0 : R1, D = half == 0 ? D0 : D1;
+      const int64_t o = at(t, b.k);
+      const float R = s2r * fr[o], D = s2d * fd[o];
       Cell c;
       c.eval(b, R, D, half == 0 ? bpr0 : bpr1, fpr);
       float g_dist = 0.0f, g_asc = 0.0f;
@@ -481,8 +552,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
         g_er -= g_asc * 1.2f * c.asc_raw / (c.er + 50.0f);
       }
       gfpr = fmaf(g_ed, D, gfpr);
-      gD[(int64_t)t * nb + b.k] = g_ed;
-      gR[(int64_t)t * nb + b.k] = g_er;
+      gd[o] = g_ed;
+      gr[o] = g_er;
     }
     gfpr = warp_sum(gfpr);
     if (lane == 0) {
@@ -497,13 +568,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   // energies; band sums of dL/dbpr
   {
     double acc0 = 0.0, acc1 = 0.0;
-    for (int t = lo; t < hi; ++t) {
-      const float* fr = Fr + (int64_t)t * nb;
-      const float* fd = Fd + (int64_t)t * nb;
-      auto clamp_pass = [&](int tt) {
-        const float f1 = sv[p.lay.fpr1 + tt];
-        return (f1 >= 3e-4f && f1 <= 5.0f) ? __ldcg(gf + tt) : 0.0f;
-      };
+    auto clamp_pass = [&](int tt) {
+      const float f1 = sv[p.lay.fpr1 + tt];
+      return (f1 >= 3e-4f && f1 <= 5.0f) ? __ldcg(gf + tt) : 0.0f;
+    };
+    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
       const float g1 = clamp_pass(t);
       const float g1n = t + 1 < T ? clamp_pass(t + 1) : 0.0f;
       const float g_fpr0 = (t == 0 ? g1 : 0.8f * g1) + 0.2f * g1n;
@@ -513,36 +582,37 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       const float g_h = __ldcg(gf + T + t);
       const float g_taer = g_fpr0 / (tad + 5e3f) + g_h * 0.04f * h / (taer + 1e5f);
       const float g_tad = -g_fpr0 * fpr0 / (tad + 5e3f);
+#pragma unroll
       for (int half = 0; half < 2; ++half) {
         const Band& b = half == 0 ? b0 : b1;
         if (!b.ok) continue;
-        const int64_t o = (int64_t)t * nb + b.k;
-        const float R = s2r * fr[b.k], D = s2d * fd[b.k];
+        const int64_t o = at(t, b.k);
+        const float R = s2r * fr[o], D = s2d * fd[o];
         const float bpr = half == 0 ? bpr0 : bpr1;
         const float er = bpr * R;
-        const float g_er = gR[o] + (er > b.th ? g_taer : 0.0f);
-        gR[o] = g_er * bpr;
+        const float g_er = gr[o] + (er > b.th ? g_taer : 0.0f);
+        gr[o] = g_er * bpr;
         const double contrib = (double)g_er * (double)R;
         if (half == 0)
           acc0 += contrib;
         else
           acc1 += contrib;
-        gD[o] = gD[o] * fpr + (D > b.th ? g_tad : 0.0f);
+        gd[o] = gd[o] * fpr + (D > b.th ? g_tad : 0.0f);
       }
     }
     wpart[warp][lane] = acc0;
-    if (lane + 32 < kMaxBands) wpart[warp][lane + 32] = acc1;
+    wpart[warp][lane + 32] = acc1;
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
+  if (threadIdx.x < nb) {
     double s = 0.0;
-    for (int w = 0; w < kChainWarps; ++w) s += wpart[w][k];
-    part[k] = s;
+    for (int w = 0; w < kChainWarps; ++w) s += wpart[w][threadIdx.x];
+    part[threadIdx.x] = s;
   }
   cluster_sync();
-  for (int k = threadIdx.x; k < nb; k += kChainThreads) {
-    double g = 0.0;
-    for (int c = 0; c < C; ++c) g += dsmem_ld_f64(dsmem_addr(&part[k], c));
+  if (threadIdx.x < nb) {
+    const int k = threadIdx.x;
+    const double g = cluster_sum(&part[k], C);
     // band ratio clamp and quotient (loss.py:212-216), then the mean over T
     const float ratio = sv[p.lay.ratio + k], mr = sv[p.lay.mref + k];
     const float g_ratio = (ratio >= 0.01f && ratio <= 100.0f) ? (float)g : 0.0f;
@@ -557,25 +627,25 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     double kr = 0.0, kd = 0.0;
     const float gmr0 = b0.ok ? gm_r[b0.k] : 0.0f, gmr1 = b1.ok ? gm_r[b1.k] : 0.0f;
     const float gmd0 = b0.ok ? gm_d[b0.k] : 0.0f, gmd1 = b1.ok ? gm_d[b1.k] : 0.0f;
-    for (int t = lo; t < hi; ++t) {
-      const float* fr = Fr + (int64_t)t * nb;
-      const float* fd = Fd + (int64_t)t * nb;
+    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
       const bool keep = sv[p.lay.keep + t] != 0.0f;
+#pragma unroll
       for (int half = 0; half < 2; ++half) {
         const Band& b = half == 0 ? b0 : b1;
         if (!b.ok) continue;
-        const int64_t o = (int64_t)t * nb + b.k;
-        const float Fv = fr[b.k], Gv = fd[b.k];
+        const int64_t o = at(t, b.k);
+        const int64_t og = (int64_t)t * nb + b.k;
+        const float Fv = fr[o], Gv = fd[o];
         const float R = s2r * Fv, D = s2d * Gv;
-        float gr = gR[o], gd = gD[o];
-        if (keep && R > b.th100) gr += half == 0 ? gmr0 : gmr1;
-        if (keep && D > b.th100) gd += half == 0 ? gmd0 : gmd1;
-        gr *= s2r;
-        gd *= s2d;
-        gR[o] = gr;
-        gD[o] = gd;
-        kr += (double)gr * (double)Fv;
-        kd += (double)gd * (double)Gv;
+        float vr = gr[o], vd = gd[o];
+        if (keep && R > b.th100) vr += half == 0 ? gmr0 : gmr1;
+        if (keep && D > b.th100) vd += half == 0 ? gmd0 : gmd1;
+        vr *= s2r;
+        vd *= s2d;
+        GR[og] = vr;
+        GD[og] = vd;
+        kr += (double)vr * (double)Fv;
+        kd += (double)vd * (double)Gv;
       }
     }
     kr = warp_sum(kr);
@@ -593,21 +663,21 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   }
   cluster_sync();
   if (q == 0 && threadIdx.x < 2) {
-    double s = 0.0;
-    for (int c = 0; c < C; ++c) s += dsmem_ld_f64(dsmem_addr(&kpart[threadIdx.x], c));
+    const double s = cluster_sum(&kpart[threadIdx.x], C);
     const int r = threadIdx.x == 0 ? u : B + u;
     p.kappa[r] = (float)(2.0 * s / p.sumsq[r]);
   }
+  // keep every CTA's shared memory alive until rank 0 has read it
   cluster_sync();
 }
 
 template <class Kernel, class Args>
-cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, cudaStream_t s) {
+cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, size_t smem, cudaStream_t s) {
   if (batch <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(batch * cluster));
   cfg.blockDim = dim3(kChainThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -621,12 +691,23 @@ cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, cuda
 
 }  // namespace
 
+cudaError_t configure_chain() {
+  cudaError_t e = cudaFuncSetAttribute(chain_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kChainSmemLimit);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmemLimit);
+}
+
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s) {
-  return launch_cluster(chain_fwd_kernel, a, a.batch, cluster, s);
+  const int slice = chain_slice_frames(a.lay.T, cluster);
+  const size_t smem = a.staged ? chain_fwd_smem_bytes(slice, a.lay.nb) : 0;
+  return launch_cluster(chain_fwd_kernel, a, a.batch, cluster, smem, s);
 }
 
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s) {
-  return launch_cluster(chain_bwd_kernel, a, a.batch, cluster, s);
+  const int slice = chain_slice_frames(a.lay.T, cluster);
+  const size_t smem = a.staged ? chain_bwd_smem_bytes(slice, a.lay.nb) : 0;
+  return launch_cluster(chain_bwd_kernel, a, a.batch, cluster, smem, s);
 }
 
 }  // namespace pesq

@@ -125,6 +125,7 @@ struct ChainFwdArgs {
   float* d_asymm;
   float* mos;
   float* loss;
+  int staged;               // Bark slice staged in shared memory
 };
 
 struct ChainBwdArgs {
@@ -143,6 +144,7 @@ struct ChainBwdArgs {
   int want_ref, want_deg;
   float* g_bark;            // [2B][T][nb]  out
   float* kappa;             // [2B]         out
+  int staged;               // Bark slice and its gradients live in shared memory
 };
 
 struct ResampleArgs {
@@ -167,6 +169,13 @@ cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& 
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s);
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);
+cudaError_t configure_chain();
+// frames of the largest cluster slice, and the dynamic shared memory of the
+// staged forward / backward chain kernels for it
+int chain_slice_frames(int T, int cluster);
+size_t chain_fwd_smem_bytes(int slice, int nb);
+size_t chain_bwd_smem_bytes(int slice, int nb);
+size_t chain_smem_limit();
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
 

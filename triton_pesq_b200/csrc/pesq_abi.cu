@@ -22,7 +22,7 @@ using namespace pesq;
 namespace pesq {
 cudaError_t configure_front();
 cudaError_t configure_back();
-}
+}  // namespace pesq
 
 struct pesq_plan {
   int device;
@@ -109,6 +109,7 @@ struct Geometry {
   int T, L, nb;
   int seg, nseg;  // segmentation of a row
   int cluster;
+  bool fwd_staged, bwd_staged;
   bool resample, grad;
   int grad_begin, grad_end;
   ChainLayout lay;
@@ -148,7 +149,13 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.L = (g.T - 20) / 10 + 1;
   g.nb = p->nb;
   balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
-  g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 48)));
+  // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
+  g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
+  {
+    const int slice = chain_slice_frames(g.T, g.cluster);
+    g.fwd_staged = chain_fwd_smem_bytes(slice, p->nb) <= chain_smem_limit();
+    g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb) <= chain_smem_limit();
+  }
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
   g.grad_begin = (flags & PESQ_GRAD_REF) ? 0 : (int)batch;
   g.grad_end = (flags & PESQ_GRAD_DEG) ? (int)g.rows : (int)batch;
@@ -355,6 +362,8 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the front kernel"));
   e = configure_back();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the back kernel"));
+  e = configure_chain();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the chain kernels"));
   *out = p;
   return PESQ_OK;
 }
@@ -482,6 +491,7 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ca.d_asymm = d_asymm;
   ca.mos = mos;
   ca.loss = loss;
+  ca.staged = g.fwd_staged;
   PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, static_cast<cudaStream_t>(stream)), "chain forward kernel");
   return PESQ_OK;
 }
@@ -522,6 +532,7 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   cb.want_deg = (flags & PESQ_GRAD_DEG) != 0;
   cb.g_bark = at<float>(ws, g.gbark);
   cb.kappa = at<float>(ws, g.kappa);
+  cb.staged = g.bwd_staged;
   PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, static_cast<cudaStream_t>(stream)), "chain backward kernel");
   return PESQ_OK;
 }
