@@ -22,7 +22,7 @@ namespace pesq {
 
 namespace {
 
-constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * kFftScratch * 8 +
+constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * FftLayout<float>::kSlots * 8 +
                                kWarps * kMaxBands * 4 + (int)sizeof(DevTables);
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* gy = smem;  // kSpan: dL/dy, then dL/d(ramped x) in place
   float* es = gy + kSpan;
   Cx<float>* fft = reinterpret_cast<Cx<float>*>(es + scan_scratch_floats<2>());
-  float* gb = reinterpret_cast<float*>(fft + kWarps * kFftScratch);  // per warp kMaxBands
+  float* gb = reinterpret_cast<float*>(fft + kWarps * FftLayout<float>::kSlots);  // per warp kMaxBands
   DevTables* tab = reinterpret_cast<DevTables*>(gb + kWarps * kMaxBands);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -57,8 +57,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_lo = max(0, t0 - 1);
   const int t_hi = min(p.frames - 1, (int)((send + kHorizon - 1) / kHop));
   const float kappa = p.kappa[row];
-  Cx<float>* sh = fft + warp * kFftScratch;
-  float* gw = reinterpret_cast<float*>(sh);
+  Cx<float>* sh = fft + warp * FftLayout<float>::kSlots;
   float* gbw = gb + warp * kMaxBands;
 
   for (int parity = 0; parity < 2; ++parity) {
@@ -78,8 +77,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = tab->bin_band[f];
         V[m] = c_scale(spec[f], b >= 0 ? gbw[b] : 0.0f);
       }
-      warp_irfft512_adjoint(V, sh, tab->tw256, tab->tw512, lane, gw);
-      for (int k = lane; k < kNfft; k += 32) gy[off + k] += tab->window[k] * gw[k];
+      Cx<float> g[8];
+      warp_irfft512_adjoint(V, sh, tab->fft, lane, g);
+      // overlap-add of the windowed frame gradient: samples 2n, 2n + 1 with
+      // n = lane + 32 m (frames of one parity never overlap)
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int k = 2 * (lane + 32 * m);
+        const float2 w = *reinterpret_cast<const float2*>(tab->window + k);
+        float2* dst = reinterpret_cast<float2*>(gy + off + k);
+        float2 acc = *dst;
+        acc.x = fmaf(w.x, g[m].x, acc.x);
+        acc.y = fmaf(w.y, g[m].y, acc.y);
+        *dst = acc;
+      }
       __syncwarp();
     }
     __syncthreads();

@@ -32,8 +32,9 @@ namespace pesq {
 
 namespace {
 
+constexpr int kFftFloats = kWarps * FftLayout<double>::kSlots * 4;
 constexpr int kFrontScratchFloats =
-    (kWarps * kFftScratch * 4 > scan_scratch_floats<10>()) ? kWarps * kFftScratch * 4 : scan_scratch_floats<10>();
+    kFftFloats > scan_scratch_floats<10>() ? kFftFloats : scan_scratch_floats<10>();
 constexpr int kFrontSmemBytes = 2 * kSpan * 4 + kFrontScratchFloats * 4 + (int)sizeof(DevTables) +
                                 (int)sizeof(DevTwiddle64) + kWarps * 8;
 
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nb = tab->nb;
   const int t0 = seg * p.seg_frames;
   const int t1 = min(t0 + p.seg_frames, p.frames);
-  Cx<double>* sh = reinterpret_cast<Cx<double>*>(scratch) + warp * kFftScratch;
+  Cx<double>* sh = reinterpret_cast<Cx<double>*>(scratch) + warp * FftLayout<double>::kSlots;
   double* pw = reinterpret_cast<double*>(sh);
   for (int t = t0 + warp; t < t1; t += kWarps) {
     const int off = kHorizon + (t - t0) * kHop;
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float2 w = *reinterpret_cast<const float2*>(tab->window + n);
       v[m] = mk(((double)hi.x + (double)lo.x) * (double)w.x, ((double)hi.y + (double)lo.y) * (double)w.y);
     }
-    warp_rfft512<double>(v, sh, tw->tw256, tw->tw512, lane, X);
+    warp_rfft512<double>(v, sh, *tw, lane, X);
     if (grad_row) {
       Cx<float>* out = p.spec + ((int64_t)row * p.frames + t) * kBins;
 #pragma unroll

@@ -16,8 +16,7 @@ using PreTab64 = ScanTab<2, double>;
 // Device constant tables of a plan (uploaded once, read-only afterwards).
 struct alignas(16) DevTables {
   float window[kNfft];      // analysis window, zero padded/centred to n_fft
-  Cx<float> tw256[256];     // exp(-2 pi i k / 256)
-  Cx<float> tw512[256];     // exp(-2 pi i k / 512), k < 256
+  FftTwiddles<float> fft;   // twiddles of the backward (single precision) transform
   int bin_band[kBins];         // band owning bin f, -1 if none (bin 0 never has one)
   int band_start[kMaxBands];
   int band_end[kMaxBands];
@@ -35,10 +34,7 @@ struct alignas(16) DevTables {
 };
 
 // Double precision twiddles of the forward spectrum.
-struct alignas(16) DevTwiddle64 {
-  Cx<double> tw256[256];
-  Cx<double> tw512[256];
-};
+using DevTwiddle64 = FftTwiddles<double>;
 
 // Rows of one call: ref rows are 0..B-1, deg rows B..2B-1.
 struct RowSource {

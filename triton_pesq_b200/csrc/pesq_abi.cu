@@ -253,18 +253,20 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   memset(&h, 0, sizeof(h));
   for (int k = 0; k < kNfft; ++k) h.window[k] = (float)d->window[k];
   DevTwiddle64 h64;
+  // exp(-2 pi i k / n); the argument reduction k mod n, k / n is exact in double
+  auto root = [](int k, int n, Cx<double>& w64, Cx<float>& w32) {
+    const double t = -2.0 * M_PI * ((double)(k % n) / (double)n);
+    w64.x = cos(t);
+    w64.y = sin(t);
+    w32.x = (float)w64.x;
+    w32.y = (float)w64.y;
+  };
+  for (int q = 1; q < 8; ++q)
+    for (int l = 0; l < 32; ++l) root(l * q, 256, h64.lane[q - 1][l], h.fft.lane[q - 1][l]);
+  for (int r = 0; r < 4; ++r)
+    for (int j = 0; j < 8; ++j) root(r * j, 32, h64.quarter[r][j], h.fft.quarter[r][j]);
   for (int k = 0; k < 256; ++k) {
-    // exact argument reduction: k / 256 and k / 512 are exact in double
-    const double c256 = cos(-2.0 * M_PI * (k / 256.0)), s256 = sin(-2.0 * M_PI * (k / 256.0));
-    const double c512 = cos(-2.0 * M_PI * (k / 512.0)), s512 = sin(-2.0 * M_PI * (k / 512.0));
-    h64.tw256[k].x = c256;
-    h64.tw256[k].y = s256;
-    h64.tw512[k].x = c512;
-    h64.tw512[k].y = s512;
-    h.tw256[k].x = (float)c256;
-    h.tw256[k].y = (float)s256;
-    h.tw512[k].x = (float)c512;
-    h.tw512[k].y = (float)s512;
+    root(k, 512, h64.bin[k], h.fft.bin[k]);
     h.bin_band[k] = -1;
   }
   int prev_end = 0;
