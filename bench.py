@@ -293,15 +293,22 @@ def stage_times(model, ref, deg, dev, launches=40):
         return lib.pesq_backward_chain(P, sp, b, n, flags, W, wb, ctypes.c_void_p(g_loss.data_ptr()), None, None,
                                        None)
 
+    def align(i):
+        return lib.pesq_backward_align(P, sp, ctypes.c_void_p(refs[i].data_ptr()), n,
+                                       ctypes.c_void_p(degs[i].data_ptr()), n, b, n, flags, W, wb)
+
     def back(i):
         return lib.pesq_backward_back(P, sp, b, n, flags, W, wb, None, n, ctypes.c_void_p(g_deg.data_ptr()), n)
 
     # populate the workspace once in order
-    for fn in (front, chain_fwd, chain_bwd, back):
+    for fn in (front, chain_fwd, chain_bwd, align, back):
         _lib.check(fn(0), "stage")
     torch.cuda.synchronize()
     result = {}
-    for name, fn in (("front", front), ("chain_forward", chain_fwd), ("chain_backward", chain_bwd), ("back", back)):
+    # align runs concurrently with chain_backward inside a step; alone it is
+    # timed back to back with itself
+    for name, fn in (("front", front), ("chain_forward", chain_fwd), ("chain_backward", chain_bwd),
+                     ("align", align), ("back", back)):
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda._sleep(20_000_000)  # keep the stream busy while the host enqueues
         start.record(stream)
@@ -354,13 +361,11 @@ def run_cuda(args):
         loss_g, grad_g = step()
     torch.cuda.synchronize()
 
-    mean_loss = torch.zeros(1, device=dev)
-
+    # utterances are independent: every rank replays its own shard and no data
+    # crosses ranks inside a step (the ranks meet only at the barriers around
+    # the timed region and in the max-over-ranks of the timings)
     def replay():
         graph.replay()
-        if world > 1:
-            mean_loss.copy_(loss_g.sum().reshape(1) / (BATCH * world))
-            dist.all_reduce(mean_loss)
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -442,7 +447,7 @@ def run_cuda(args):
     # signals (2 x 4 B per utterance sample); the back kernel must write the
     # gradient (4 B); the chain kernels have no compulsory traffic of their own
     alg = {"front": 2 * 4 * BATCH * SECONDS * RATE, "back": 4 * BATCH * SECONDS * RATE,
-           "chain_forward": 0.0, "chain_backward": 0.0}
+           "align": 4 * BATCH * SECONDS * RATE, "chain_forward": 0.0, "chain_backward": 0.0}
     front_us = stages["front"]
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
@@ -483,7 +488,8 @@ def run_cuda(args):
             "api": "PesqLossCuda.graphed, inputs from pinned host memory, loss read back",
             "ms_per_step": statistics.mean(e2e_ms),
         },
-        "gpu_launches": 4 * args.steps,
+        # front + chain forward, chain adjoint + align + back per step
+        "gpu_launches": 5 * args.steps,
         "roofline": {
             "bound": "hbm",
             "kernel": "front",

@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libpesq_cuda.so")
 OPS_PATH = os.path.join(HERE, "_pesq_torch_ops.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 GRAD_REF = 1
 GRAD_DEG = 2
 
@@ -119,6 +119,11 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p,
          ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "pesq_backward_align": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t],
     ),
     "pesq_backward_back": (
         ctypes.c_int,

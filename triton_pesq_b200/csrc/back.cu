@@ -22,8 +22,9 @@ namespace pesq {
 
 namespace {
 
+constexpr int kSegMax = kSpan - kHorizon - 3 * kHop;  // samples of the longest segment
 constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * FftLayout<float>::kSlots * 8 +
-                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables);
+                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4;
 
 __global__ void __launch_bounds__(kThreads, 1)
     back_kernel(const __grid_constant__ BackArgs p, const __grid_constant__ PreTab pre) {
@@ -33,6 +34,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Cx<float>* fft = reinterpret_cast<Cx<float>*>(es + scan_scratch_floats<2>());
   float* gb = reinterpret_cast<float*>(fft + kWarps * FftLayout<float>::kSlots);  // per warp kMaxBands
   DevTables* tab = reinterpret_cast<DevTables*>(gb + kWarps * kMaxBands);
+  float* zs = reinterpret_cast<float*>(tab + 1);  // z on [a, send), staged asynchronously
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = p.row_begin + blockIdx.x / p.nseg;
@@ -48,6 +50,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float4* d4 = reinterpret_cast<float4*>(tab);
     for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) d4[i] = s4[i];
   }
+  // z = H^T H x of the segment is only needed at the very end: its copy into
+  // shared memory runs in the background of the frame loop
+  const float* zr = p.z + (int64_t)row * n_row;
+  for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
+  cp_async_commit();
   for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   __syncthreads();
 
@@ -111,12 +118,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       });
   __syncthreads();
 
-  const float* zr = p.z + (int64_t)row * n_row;
+  cp_async_wait_all();
+  __syncthreads();
   float* outr = p.out.row(row);
   for (int i = tid; i < (int)(send - a); i += kThreads) {
     const int64_t n = a + i;
     const float g = edge_ramp(gy[kHop + i], n, n_row);
-    outr[n] = fmaf(-kappa, zr[n], g);
+    outr[n] = fmaf(-kappa, zs[i], g);
   }
 }
 

@@ -414,6 +414,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   __shared__ double kap[kChainWarps][2];
   __shared__ double kpart[2];
 
+  // the next kernel on the stream (the align kernel, which reads nothing this
+  // kernel writes) may start on the SMs the clusters leave free
+  asm volatile("griddepcontrol.launch_dependents;");
+
   const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
   const int u = blockIdx.x / C;
   const int B = p.batch, T = p.lay.T, L = p.lay.L, nb = p.lay.nb;

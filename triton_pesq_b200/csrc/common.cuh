@@ -115,6 +115,38 @@ __device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
 }
 
 // ---------------------------------------------------------------------------
+// global -> shared staging
+// ---------------------------------------------------------------------------
+
+static_assert(kSpan % kThreads == 0, "a span is a whole number of rows of the CTA");
+
+// dst[i] = src[base + i] for i in [0, kSpan), 0 where base + i lies outside
+// [0, n).  Every thread issues all of its loads before its first shared
+// store, so the whole span is in flight at once instead of one DRAM round
+// trip per loop iteration.  Must be called by all kThreads threads.
+__device__ __forceinline__ void stage_span(float* dst, const float* src, int64_t base, int64_t n) {
+  constexpr int kPer = kSpan / kThreads;
+  float v[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int64_t g = base + threadIdx.x + k * kThreads;
+    v[k] = (g >= 0 && g < n) ? __ldg(src + g) : 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) dst[threadIdx.x + k * kThreads] = v[k];
+}
+
+// 4-byte asynchronous copy global -> shared; complete after cp_async_wait_all
+// (then __syncthreads before other threads read the data)
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // 1D bulk copy (TMA) global -> shared, completion on an mbarrier
 // ---------------------------------------------------------------------------
 

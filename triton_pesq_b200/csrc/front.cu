@@ -4,7 +4,6 @@
 // in shared memory and without touching HBM in between:
 //
 //   f  = H_pow x            level-alignment band pass (order 10)    -> sum f^2
-//   z  = H_pow^T f          (rows that need a gradient)             -> HBM
 //   y  = H_pre ramp(x)      edge fade + pre-emphasis biquad, float64
 //   X_t = rfft512(w * y_t)  for the frames starting in [a, a+S), float64
 //   B  = corr * segsum |X_t|^2                                      -> HBM
@@ -24,8 +23,7 @@
 // float hi/lo pair.
 //
 // The CTA stages kSpan samples starting kHorizon before `a`: the first
-// kHorizon are the warm-up of the forward scans, and the reverse scan that
-// produces z looks kHorizon samples past the end of the segment.
+// kHorizon are the warm-up of the forward scans.
 #include "kernels.cuh"
 
 namespace pesq {
@@ -43,7 +41,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                  const __grid_constant__ PreTab64 pre) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;                 // kSpan: input, then y (hi part) in place
-  float* fb = xs + kSpan;           // kSpan: f, then z in place, then y (lo part)
+  float* fb = xs + kSpan;           // kSpan: low part of a resampled x, then y (lo part)
   float* scratch = fb + kSpan;      // scan scratch, later the per-warp FFT scratch
   DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
   DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
@@ -57,7 +55,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   const int64_t base = a - kHorizon;
   const float* xr = p.src.row(row);
-  const bool grad_row = row >= p.z_begin && row < p.z_end;
+  const bool grad_row = row >= p.spec_begin && row < p.spec_end;
 
   // constant tables
   {
@@ -68,61 +66,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     float4* e4 = reinterpret_cast<float4*>(tw);
     for (int i = tid; i < (int)(sizeof(DevTwiddle64) / 16); i += kThreads) e4[i] = t4[i];
   }
-  // stage the span; zeros outside the row reproduce the zero initial state
-  for (int i = tid; i < kSpan; i += kThreads) {
-    const int64_t n = base + i;
-    xs[i] = (n >= 0 && n < n_row) ? __ldg(xr + n) : 0.0f;
-  }
+  // stage the span; zeros outside the row reproduce the zero initial state.
+  // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
+  const bool has_lo = p.src_lo.ref != nullptr;
+  stage_span(xs, xr, base, n_row);
+  if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
   __syncthreads();
 
-  // 1. level alignment filter f = H x, sum of squares over [a, send)
-  // 2. z = H^T f on [a, send): the adjoint filter runs backwards in time from
-  //    send + kHorizon; f beyond the row end is not part of the signal.
-  // Both passes share one instance of the scan code (pass 0 forward from xs
-  // into fb, pass 1 backward over fb in place), which keeps the two unrolled
-  // scans from competing for registers.
-  const int passes = grad_row ? 2 : 1;
-  const int top = 2 * kHorizon + (int)(send - a) - 1;
+  // 1. level alignment filter f = H x: only its sum of squares over [a, send)
+  //    is needed (the adjoint H^T f of the backward is evaluated by the align
+  //    kernel of the backward pass)
   double ssq = 0.0;
-  for (int pass = 0; pass < passes; ++pass) {
-    chunk_scan<10, false, float>(
-        pow, scratch,
-        [&](int q) {
-          if (pass == 0) return xs[q];
-          const int idx = top - q;
-          return (idx >= 0 && base + idx < n_row) ? fb[idx] : 0.0f;
-        },
-        [&](int q, float y) {
-          const int idx = pass == 0 ? q : top - q;
-          if (idx >= 0) fb[idx] = y;
-          const int64_t n = base + q;
-          if (pass == 0 && n >= a && n < send) ssq = fma((double)y, (double)y, ssq);
-        });
-    if (pass == 0) {
-      ssq = warp_sum(ssq);
-      if (lane == 0) red[warp] = ssq;
-    }
-    __syncthreads();
-  }
+  chunk_scan<10, false, float>(
+      pow, scratch, [&](int q) { return xs[q]; },
+      [&](int q, float y) {
+        const int64_t n = base + q;
+        if (n >= a && n < send) ssq = fma((double)y, (double)y, ssq);
+      });
+  ssq = warp_sum(ssq);
+  if (lane == 0) red[warp] = ssq;
+  __syncthreads();
   if (tid == 0) {
     double tot = 0.0;
     for (int w = 0; w < kWarps; ++w) tot += red[w];
     p.partial[(int64_t)row * p.nseg + seg] = tot;
-  }
-  if (grad_row) {
-    float* zr = p.z + (int64_t)row * n_row;
-    for (int i = tid; i < (int)(send - a); i += kThreads) zr[a + i] = fb[kHorizon + i];
-  }
-  // the low part of a resampled input (x = hi + lo) joins the pre-emphasis
-  const bool has_lo = p.src_lo.ref != nullptr;
-  if (has_lo) {
-    __syncthreads();
-    const float* lr = p.src_lo.row(row);
-    for (int i = tid; i < kSpan; i += kThreads) {
-      const int64_t n = base + i;
-      fb[i] = (n >= 0 && n < n_row) ? __ldg(lr + n) : 0.0f;
-    }
-    __syncthreads();
   }
 
   // 3. edge fade + pre-emphasis in double precision; y = hi + lo with hi in

@@ -66,15 +66,23 @@ struct FrontArgs {
   int frames;        // T
   int seg_frames;    // frames per segment
   int nseg;          // segments per row
-  int z_begin;       // rows [z_begin, z_end) also produce z = H^T H x and
-  int z_end;         // the spectrum X for the backward
+  int spec_begin;    // rows [spec_begin, spec_end) also save the spectrum X
+  int spec_end;      // for the backward
   const DevTables* tab;
   const DevTwiddle64* tw64;
   float* bark;       // [rows][T][nb]   unscaled Bark spectrum
   double* partial;   // [rows][nseg]    partial sums of (H x)^2
-  float* z;          // [rows][n]
   Cx<float>* spec;   // [rows][T][256]  rfft bins 0..255 of every frame
   uint32_t* err;
+};
+
+struct AlignArgs {
+  RowSource src;     // 16 kHz rows (hi part if resampled)
+  int row_begin;     // rows [row_begin, row_begin + rows) get z
+  int64_t n;
+  int seg_frames;
+  int nseg;
+  float* z;          // [rows][n]  H^T H x
 };
 
 struct BackArgs {
@@ -163,6 +171,10 @@ struct ResampleArgs {
 
 cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s);
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s);
+// launched with programmatic stream serialisation: it may start while the
+// preceding kernel on the stream runs, and completes after it
+cudaError_t launch_align(const AlignArgs& a, const PowTab& pow, int rows, cudaStream_t s);
+cudaError_t configure_align();
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t configure_chain();
@@ -177,5 +189,6 @@ cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
 
 size_t front_smem_bytes();
 size_t back_smem_bytes();
+size_t align_smem_bytes();
 
 }  // namespace pesq

@@ -1,9 +1,12 @@
 // C ABI of the PESQ engine: plans, workspace layout and launch sequencing.
 //
 // Forward  : [resample] -> front (per row segment) -> chain forward (per utterance cluster)
-// Backward : chain adjoint (per utterance cluster) -> back (per row segment) -> [resample adjoint]
+// Backward : chain adjoint (per utterance cluster)
+//              || align (per gradient row segment, overlapping the chain adjoint)
+//            -> back (per gradient row segment) -> [resample adjoint]
 //
-// Four kernels per direction at 16 kHz (the reference issues about forty).
+// Two kernels forward and three backward at 16 kHz (the reference issues
+// about forty).
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdarg.h>
@@ -99,7 +102,7 @@ int fill_scan(ScanTab<P, R>& t, const pesq_scan_desc& d, const char* name) {
 // per-call geometry and workspace layout
 // ---------------------------------------------------------------------------
 
-// Frames per segment: the front kernel stages kHorizon before and after the
+// Frames per segment: the align kernel stages kHorizon before and after the
 // segment, the back kernel one hop before and kHorizon + 3 hops after it.
 constexpr int kMaxSegFrames = (kSpan - 2 * kHorizon) / kHop;  // 57
 static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel span");
@@ -366,6 +369,8 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the back kernel"));
   e = configure_chain();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the chain kernels"));
+  e = configure_align();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the align kernel"));
   *out = p;
   return PESQ_OK;
 }
@@ -456,13 +461,12 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64
   fa.frames = g.T;
   fa.seg_frames = g.seg;
   fa.nseg = g.nseg;
-  fa.z_begin = g.grad ? g.grad_begin : 0;
-  fa.z_end = g.grad ? g.grad_end : 0;
+  fa.spec_begin = g.grad ? g.grad_begin : 0;
+  fa.spec_end = g.grad ? g.grad_end : 0;
   fa.tab = p->dtab;
   fa.tw64 = p->tw64;
   fa.bark = at<float>(ws, g.bark);
   fa.partial = at<double>(ws, g.partial);
-  fa.z = at<float>(ws, g.z);
   fa.spec = at<Cx<float>>(ws, g.spec);
   fa.err = at<uint32_t>(ws, g.err);
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
@@ -539,6 +543,38 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   return PESQ_OK;
 }
 
+int pesq_backward_align(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes) {
+  if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
+  Geometry g;
+  int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  if (!g.grad) return fail(PESQ_ERR_INVALID_ARGUMENT, "backward without PESQ_GRAD_REF or PESQ_GRAD_DEG");
+  if (batch == 0) return PESQ_OK;
+  rc = check_call(p, g, ws, ws_bytes);
+  if (rc) return rc;
+  AlignArgs aa{};
+  if (g.resample) {
+    // the 16 kHz rows the forward resampled into the workspace
+    float* x16 = at<float>(ws, g.x16);
+    aa.src = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
+  } else {
+    if ((flags & PESQ_GRAD_REF) && (!ref || ld_ref < n_src))
+      return fail(PESQ_ERR_INVALID_ARGUMENT, "the backward needs the reference rows");
+    if ((flags & PESQ_GRAD_DEG) && (!deg || ld_deg < n_src))
+      return fail(PESQ_ERR_INVALID_ARGUMENT, "the backward needs the degraded rows");
+    aa.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
+  }
+  aa.row_begin = g.grad_begin;
+  aa.n = g.n16;
+  aa.seg_frames = g.seg;
+  aa.nseg = g.nseg;
+  aa.z = at<float>(ws, g.z);
+  PESQ_CUDA_TRY(launch_align(aa, p->pow, g.grad_end - g.grad_begin, static_cast<cudaStream_t>(stream)),
+                "align kernel");
+  return PESQ_OK;
+}
+
 int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t n_src, uint32_t flags, void* ws,
                        size_t ws_bytes, float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
   if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
@@ -598,12 +634,9 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
                   int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
                   const float* g_loss, const float* g_mos, const float* g_dsymm, const float* g_dasymm,
                   float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
-  (void)ref;
-  (void)ld_ref;
-  (void)deg;
-  (void)ld_deg;
-  const int rc =
-      pesq_backward_chain(p, stream, batch, n_src, flags, ws, ws_bytes, g_loss, g_mos, g_dsymm, g_dasymm);
+  int rc = pesq_backward_chain(p, stream, batch, n_src, flags, ws, ws_bytes, g_loss, g_mos, g_dsymm, g_dasymm);
+  if (rc) return rc;
+  rc = pesq_backward_align(p, stream, ref, ld_ref, deg, ld_deg, batch, n_src, flags, ws, ws_bytes);
   if (rc) return rc;
   return pesq_backward_back(p, stream, batch, n_src, flags, ws, ws_bytes, g_ref, ld_gref, g_deg, ld_gdeg);
 }
