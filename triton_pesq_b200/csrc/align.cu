@@ -26,6 +26,8 @@
 
 namespace pesq {
 
+PESQ_PHASE_TABLE(g_phase_align)
+
 namespace {
 
 constexpr int kAlignSmemBytes = kSpan * 4 + scan_scratch_floats<10>() * 4;
@@ -44,10 +46,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   const int64_t base = a - kHorizon;
   const float* xr = p.src.row(row);
+  PESQ_STAMP(g_phase_align, 0);
 
   // zeros outside the row reproduce the zero initial state
   stage_span(xs, xr, base, n_row);
   __syncthreads();
+  PESQ_STAMP(g_phase_align, 1);
 
   // pass 0: f = H x over the span, in place; pass 1: z = H^T f on [a, send),
   // logical position q at physical index top - q.  One instance of the scan
@@ -68,9 +72,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         });
     __syncthreads();
   }
+  PESQ_STAMP(g_phase_align, 2);
 
   float* zr = p.z + (int64_t)row * n_row;
   for (int i = tid; i < (int)(send - a); i += kThreads) zr[a + i] = xs[kHorizon + i];
+  PESQ_STAMP(g_phase_align, 3);
 
   // complete only after the kernel this one was released early from
   asm volatile("griddepcontrol.wait;" ::: "memory");

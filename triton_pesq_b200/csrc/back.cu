@@ -20,6 +20,8 @@
 
 namespace pesq {
 
+PESQ_PHASE_TABLE(g_phase_back)
+
 namespace {
 
 constexpr int kSegMax = kSpan - kHorizon - 3 * kHop;  // samples of the longest segment
@@ -44,6 +46,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   // the span starts at frame t0 - 1, which overlaps the segment
   const int64_t base = a - kHop;
+  PESQ_STAMP(g_phase_back, 0);
 
   {
     const float4* s4 = reinterpret_cast<const float4*>(p.tab);
@@ -57,6 +60,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cp_async_commit();
   for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   __syncthreads();
+  PESQ_STAMP(g_phase_back, 1);
 
   // frames that touch [a, send + kHorizon)
   const int nb = tab->nb;
@@ -102,6 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
   }
+  PESQ_STAMP(g_phase_back, 2);
 
   // pre-emphasis adjoint on [a, send): backwards in time from send + kHorizon;
   // the gradient of the zero padding after the row end is dropped
@@ -120,12 +125,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   cp_async_wait_all();
   __syncthreads();
+  PESQ_STAMP(g_phase_back, 3);
   float* outr = p.out.row(row);
   for (int i = tid; i < (int)(send - a); i += kThreads) {
     const int64_t n = a + i;
     const float g = edge_ramp(gy[kHop + i], n, n_row);
     outr[n] = fmaf(-kappa, zs[i], g);
   }
+  PESQ_STAMP(g_phase_back, 4);
 }
 
 }  // namespace

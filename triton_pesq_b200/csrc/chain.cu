@@ -66,8 +66,16 @@ ChainLayout ChainLayout::make(int T, int nb) {
 
 int chain_slice_frames(int T, int cluster) { return (int)ceil_div(T, cluster); }
 size_t chain_fwd_smem_bytes(int slice, int nb) { return (size_t)2 * (slice + 1) * nb * sizeof(float); }
-size_t chain_bwd_smem_bytes(int slice, int nb) { return (size_t)4 * slice * nb * sizeof(float); }
+// Bark spectra and their gradient accumulators (4 slices), the ten per-frame
+// saved arrays and two per-frame gradients of frames c_lo..c_hi, and the two
+// window arrays over the slice
+size_t chain_bwd_smem_bytes(int slice, int nb) {
+  return ((size_t)4 * slice * nb + (size_t)12 * (slice + 1) + (size_t)2 * (slice / 10 + 4)) * sizeof(float);
+}
 size_t chain_smem_limit() { return kChainSmemLimit; }
+
+PESQ_PHASE_TABLE(g_phase_chain_fwd)
+PESQ_PHASE_TABLE(g_phase_chain_bwd)
 
 namespace {
 
@@ -181,6 +189,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   const int B = p.batch, T = p.lay.T, L = p.lay.L;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const Slice sl(T);
+  PESQ_STAMP(g_phase_chain_fwd, 0);
 
   load_tables(&tab, p.tab);
   if (warp < 2) {
@@ -203,19 +212,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   const float* fd = Fd;
   int64_t origin = 0;
   if (p.staged) {
-    const int cnt = (sl.c_hi - t_first) * nb;
+    const int pitch = (sl.c_hi - sl.c_lo + 1) * nb;
     float* sr = dsm;
-    float* sd = dsm + (int64_t)(sl.c_hi - sl.c_lo + 1) * nb;
-    for (int i = threadIdx.x; i < cnt; i += kChainThreads) {
-      const int64_t g = (int64_t)t_first * nb + i;
-      sr[i] = g >= 0 ? Fr[g] : 0.0f;
-      sd[i] = g >= 0 ? Fd[g] : 0.0f;
-    }
+    float* sd = dsm + pitch;
+    // frame -1 (before the signal) reads as zeros
+    const int skip = t_first < 0 ? nb : 0;
+    for (int i = threadIdx.x; i < skip; i += kChainThreads) sr[i] = sd[i] = 0.0f;
+    stage_rows<kChainThreads>(sr + skip, pitch, Fr + (int64_t)t_first * nb + skip, Fd - Fr, 2,
+                              (sl.c_hi - t_first) * nb - skip);
     fr = sr;
     fd = sd;
     origin = (int64_t)t_first * nb;
   }
   __syncthreads();
+  PESQ_STAMP(g_phase_chain_fwd, 1);
   const float s2r = s2s[0], s2d = s2s[1];
   float* sv = p.saved + (int64_t)u * p.lay.stride;
   auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
@@ -283,6 +293,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     sv[p.lay.scal + kS2Deg] = s2d;
   }
   __syncthreads();
+  PESQ_STAMP(g_phase_chain_fwd, 2);
 
   // pass B: frame power ratio, loudness, disturbance and the weighted norms
   // (loss.py:217-255)
@@ -347,6 +358,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   }
   __threadfence();
   cluster_sync();
+  PESQ_STAMP(g_phase_chain_fwd, 3);
 
   // pass C: sixth-power means over 20-frame windows (loss.py:257-266),
   // normalised by the window maximum so that the 1e-20 floor of the
@@ -369,6 +381,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   }
   __threadfence();
   cluster_sync();
+  PESQ_STAMP(g_phase_chain_fwd, 4);
 
   // RMS over the windows (rank 0), then MOS and loss (loss.py:289-297, 320-322)
   if (q == 0 && warp < 2) {
@@ -399,6 +412,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       if (p.loss) p.loss[u] = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
     }
   }
+  PESQ_STAMP(g_phase_chain_fwd, 5);
 }
 
 // ---------------------------------------------------------------------------
@@ -423,6 +437,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const int B = p.batch, T = p.lay.T, L = p.lay.L, nb = p.lay.nb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const Slice sl(T);
+  PESQ_STAMP(g_phase_chain_bwd, 0);
 
   load_tables(&tab, p.tab);
   const float* sv = p.saved + (int64_t)u * p.lay.stride;
@@ -438,22 +453,44 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   float* gr = GR;
   float* gd = GD;
   int64_t origin = 0;
+  // per-frame saved state (frames c_lo..c_hi) and the 20-frame windows over
+  // the slice: staged next to the spectra, or read from global memory
+  enum { kKeep, kTaer, kTad, kFpr0, kFpr1, kH, kSraw, kAraw, kSp, kAp, kFrameArrays };
+  const int64_t upT = p.lay.taer - p.lay.keep;  // pitch of the saved per-frame arrays
+  const int fpitch = sl.c_hi - sl.c_lo + 1;
+  const int l_min = sl.c_lo >= 19 ? (sl.c_lo - 10) / 10 : 0;
+  const int l_max = min(L - 1, (sl.c_hi - 1) / 10);
+  const int wpitch = (T + C - 1) / C / 10 + 4;
+  float* fs = nullptr;   // [kFrameArrays][fpitch]
+  float* gfs = nullptr;  // [2][fpitch]: dL/dfpr, dL/dh of the slice's frames
+  float* ws = nullptr;   // [2][wpitch]: psqm_s, psqm_a of windows l_min..l_max
   if (p.staged) {
     const int n = (sl.c_hi - sl.c_lo) * nb;
     float* sr = dsm;
     float* sd = sr + n;
-    for (int i = threadIdx.x; i < n; i += kChainThreads) {
-      sr[i] = Fr[(int64_t)sl.c_lo * nb + i];
-      sd[i] = Fd[(int64_t)sl.c_lo * nb + i];
-    }
+    stage_rows<kChainThreads>(sr, n, Fr + (int64_t)sl.c_lo * nb, Fd - Fr, 2, n);
     fr = sr;
     fd = sd;
     gr = sd + n;
     gd = gr + n;
     origin = (int64_t)sl.c_lo * nb;
+    fs = gd + n;
+    gfs = fs + kFrameArrays * fpitch;
+    ws = gfs + 2 * fpitch;
+    stage_rows<kChainThreads>(fs, fpitch, sv + p.lay.keep + sl.c_lo, upT, kFrameArrays,
+                              min(sl.c_hi + 1, T) - sl.c_lo);
+    stage_rows<kChainThreads>(ws, wpitch, sv + p.lay.psqm_s + l_min, p.lay.psqm_a - p.lay.psqm_s, 2,
+                              max(0, l_max - l_min + 1));
   }
   __syncthreads();
+  PESQ_STAMP(g_phase_chain_bwd, 1);
   auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
+  auto FS = [&](int k, int t) -> float {
+    return p.staged ? fs[k * fpitch + (t - sl.c_lo)] : __ldg(sv + p.lay.keep + k * upT + t);
+  };
+  auto PQ = [&](int side, int l) -> float {
+    return p.staged ? ws[side * wpitch + (l - l_min)] : __ldg(sv + (side ? p.lay.psqm_a : p.lay.psqm_s) + l);
+  };
   const float s2r = sv[p.lay.scal + kS2Ref], s2d = sv[p.lay.scal + kS2Deg];
   const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
 
@@ -482,21 +519,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   // dL/d(frame distance) through the windows, the RMS, the 45 clamp, /h and
   // the 1e-20 floor
   auto frame_grads = [&](int t, float& g_sraw, float& g_araw, float& g_h) {
-    const float h = sv[p.lay.h + t];
+    const float h = FS(kH, t);
     g_sraw = g_araw = g_h = 0.0f;
 #pragma unroll
     for (int side = 0; side < 2; ++side) {
       const float d = side == 0 ? ds : da;
       const float gdist = side == 0 ? gds : gda;
-      const int64_t pq = side == 0 ? p.lay.psqm_s : p.lay.psqm_a;
-      const float s = sv[(side == 0 ? p.lay.sp : p.lay.ap) + t];
-      const float raw = sv[(side == 0 ? p.lay.sraw : p.lay.araw) + t];
+      const float s = FS(side == 0 ? kSp : kAp, t);
+      const float raw = FS(side == 0 ? kSraw : kAraw, t);
       float gs = 0.0f;
       if (d > 0.0f) {
         const int l_lo = t >= 19 ? (t - 19 + 9) / 10 : 0;
         const int l_hi = min(L - 1, t / 10);
         for (int l = l_lo; l <= l_hi; ++l) {
-          const float pl = sv[pq + l];
+          const float pl = PQ(side, l);
           if (pl > 0.0f) {
             const float r = s / pl, r2 = r * r;
             gs += pl * (r2 * r2 * r);
@@ -518,8 +554,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
 
   // pass 1: loudness / disturbance / norm adjoint per band; per-frame dL/dfpr
   for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-    const float fpr = fminf(fmaxf(sv[p.lay.fpr1 + t], 3e-4f), 5.0f);
-    const float sraw = sv[p.lay.sraw + t];
+    const float fpr = fminf(fmaxf(FS(kFpr1, t), 3e-4f), 5.0f);
+    const float sraw = FS(kSraw, t);
     float g_sraw, g_araw, g_h;
     frame_grads(t, g_sraw, g_araw, g_h);
     const float coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
@@ -563,27 +599,35 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     if (lane == 0) {
       gf[t] = gfpr;
       gf[T + t] = g_h;
+      if (p.staged) {
+        gfs[t - sl.c_lo] = gfpr;
+        gfs[fpitch + t - sl.c_lo] = g_h;
+      }
     }
   }
   __threadfence();
   cluster_sync();
+  PESQ_STAMP(g_phase_chain_bwd, 2);
 
   // pass 2: smoothing / clamp / frame ratio adjoint, then the total audible
   // energies; band sums of dL/dbpr
   {
     double acc0 = 0.0, acc1 = 0.0;
+    // dL/dfpr of frame tt; the first frame after the slice belongs to the
+    // next CTA of the cluster (visible after the cluster barrier)
     auto clamp_pass = [&](int tt) {
-      const float f1 = sv[p.lay.fpr1 + tt];
-      return (f1 >= 3e-4f && f1 <= 5.0f) ? __ldcg(gf + tt) : 0.0f;
+      const float f1 = FS(kFpr1, tt);
+      const float g = (p.staged && tt < sl.c_hi) ? gfs[tt - sl.c_lo] : __ldcg(gf + tt);
+      return (f1 >= 3e-4f && f1 <= 5.0f) ? g : 0.0f;
     };
     for (int t = sl.w_lo; t < sl.w_hi; ++t) {
       const float g1 = clamp_pass(t);
       const float g1n = t + 1 < T ? clamp_pass(t + 1) : 0.0f;
       const float g_fpr0 = (t == 0 ? g1 : 0.8f * g1) + 0.2f * g1n;
-      const float taer = sv[p.lay.taer + t], tad = sv[p.lay.tad + t];
-      const float fpr0 = sv[p.lay.fpr0 + t], h = sv[p.lay.h + t];
-      const float fpr = fminf(fmaxf(sv[p.lay.fpr1 + t], 3e-4f), 5.0f);
-      const float g_h = __ldcg(gf + T + t);
+      const float taer = FS(kTaer, t), tad = FS(kTad, t);
+      const float fpr0 = FS(kFpr0, t), h = FS(kH, t);
+      const float fpr = fminf(fmaxf(FS(kFpr1, t), 3e-4f), 5.0f);
+      const float g_h = p.staged ? gfs[fpitch + t - sl.c_lo] : __ldcg(gf + T + t);
       const float g_taer = g_fpr0 / (tad + 5e3f) + g_h * 0.04f * h / (taer + 1e5f);
       const float g_tad = -g_fpr0 * fpr0 / (tad + 5e3f);
 #pragma unroll
@@ -624,6 +668,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     gm_d[k] = g_ratio / (mr + 1000.0f) / (float)T;
   }
   __syncthreads();
+  PESQ_STAMP(g_phase_chain_bwd, 3);
 
   // pass 3: band means over the non-silent frames; scale to the unscaled
   // spectrum and accumulate <g, F> for the alignment term
@@ -632,7 +677,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     const float gmr0 = b0.ok ? gm_r[b0.k] : 0.0f, gmr1 = b1.ok ? gm_r[b1.k] : 0.0f;
     const float gmd0 = b0.ok ? gm_d[b0.k] : 0.0f, gmd1 = b1.ok ? gm_d[b1.k] : 0.0f;
     for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-      const bool keep = sv[p.lay.keep + t] != 0.0f;
+      const bool keep = FS(kKeep, t) != 0.0f;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const Band& b = half == 0 ? b0 : b1;
@@ -660,6 +705,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     }
   }
   __syncthreads();
+  PESQ_STAMP(g_phase_chain_bwd, 4);
   if (threadIdx.x < 2) {
     double s = 0.0;
     for (int w = 0; w < kChainWarps; ++w) s += kap[w][threadIdx.x];
@@ -673,6 +719,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   }
   // keep every CTA's shared memory alive until rank 0 has read it
   cluster_sync();
+  PESQ_STAMP(g_phase_chain_bwd, 5);
 }
 
 template <class Kernel, class Args>

@@ -4,6 +4,31 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// Phase timing of the kernels.  A build with -DPESQ_PHASE_PROBE records
+// clock64() at each PESQ_STAMP(table, i) of the first and the last CTA of a
+// launch (slots i and 8 + i of a 16-entry table defined by
+// PESQ_PHASE_TABLE(table), readable from the host through the extern "C"
+// function table_read); each stamp is preceded by a CTA barrier.  In a normal
+// build both macros expand to nothing.
+#ifdef PESQ_PHASE_PROBE
+#define PESQ_PHASE_TABLE(name)                                                  \
+  __device__ unsigned long long name[16];                                       \
+  extern "C" int name##_read(unsigned long long* host) {                        \
+    return (int)cudaMemcpyFromSymbol(host, name, sizeof(unsigned long long) * 16); \
+  }
+#define PESQ_STAMP(name, i)                                                          \
+  do {                                                                               \
+    __syncthreads();                                                                 \
+    if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))        \
+      name[(blockIdx.x ? 8 : 0) + (i)] = clock64();                                  \
+  } while (0)
+#else
+#define PESQ_PHASE_TABLE(name)
+#define PESQ_STAMP(name, i) \
+  do {                      \
+  } while (0)
+#endif
+
 namespace pesq {
 
 // ---------------------------------------------------------------------------
@@ -134,6 +159,31 @@ __device__ __forceinline__ void stage_span(float* dst, const float* src, int64_t
   }
 #pragma unroll
   for (int k = 0; k < kPer; ++k) dst[threadIdx.x + k * kThreads] = v[k];
+}
+
+// dst[k * pitch + t] = src[k * src_pitch + t] for k < rows, t < cnt, by a CTA
+// of kBlock threads with 8 loads per thread in flight at a time (one memory
+// round trip for up to 8 * kBlock elements).  src must be read-only for the
+// whole kernel.
+template <int kBlock>
+__device__ __forceinline__ void stage_rows(float* dst, int pitch, const float* src, int64_t src_pitch, int rows,
+                                           int cnt) {
+  const int n = rows * cnt;
+  for (int base = threadIdx.x; base < n; base += 8 * kBlock) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * kBlock;
+      const int k = i / max(cnt, 1), t = i - k * cnt;
+      v[j] = i < n ? __ldg(src + k * src_pitch + t) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * kBlock;
+      const int k = i / max(cnt, 1), t = i - k * cnt;
+      if (i < n) dst[k * pitch + t] = v[j];
+    }
+  }
 }
 
 // 4-byte asynchronous copy global -> shared; complete after cp_async_wait_all

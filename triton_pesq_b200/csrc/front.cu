@@ -28,6 +28,8 @@
 
 namespace pesq {
 
+PESQ_PHASE_TABLE(g_phase_front)
+
 namespace {
 
 constexpr int kFftFloats = kWarps * FftLayout<double>::kSlots * 4;
@@ -56,6 +58,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t base = a - kHorizon;
   const float* xr = p.src.row(row);
   const bool grad_row = row >= p.spec_begin && row < p.spec_end;
+  PESQ_STAMP(g_phase_front, 0);
 
   // constant tables
   {
@@ -72,6 +75,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   stage_span(xs, xr, base, n_row);
   if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
   __syncthreads();
+  PESQ_STAMP(g_phase_front, 1);
 
   // 1. level alignment filter f = H x: only its sum of squares over [a, send)
   //    is needed (the adjoint H^T f of the backward is evaluated by the align
@@ -91,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; w < kWarps; ++w) tot += red[w];
     p.partial[(int64_t)row * p.nseg + seg] = tot;
   }
+  PESQ_STAMP(g_phase_front, 2);
 
   // 3. edge fade + pre-emphasis in double precision; y = hi + lo with hi in
   //    xs (in place) and lo in fb; the padding after the row end is 0
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fb[q] = (float)(y - (double)hi);
       });
   __syncthreads();
+  PESQ_STAMP(g_phase_front, 3);
 
   // 4. frames starting in this segment: window, rfft, power, Bark segment sums
   const int nb = tab->nb;
@@ -149,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   }
+  PESQ_STAMP(g_phase_front, 4);
 }
 
 }  // namespace
