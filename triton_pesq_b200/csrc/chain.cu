@@ -23,10 +23,6 @@ namespace pesq {
 
 constexpr int kChainThreads = 512;
 constexpr int kChainWarps = kChainThreads / 32;
-// Above this distance from the threshold the loudness base^e - 1 is evaluated
-// with powf; below it with expm1(e log1p(.)), which keeps full relative
-// precision as the base approaches one.
-constexpr float kLoudSplit = 64.0f;
 // Dynamic shared memory the staged kernels may use.
 constexpr size_t kChainSmemLimit = 180 * 1024;
 
@@ -79,20 +75,6 @@ PESQ_PHASE_TABLE(g_phase_chain_bwd)
 
 namespace {
 
-__device__ __forceinline__ float loudness(float x, float th, float inv2th, float e, float ls) {
-  if (!(x > th)) return 0.0f;
-  const float bm1 = (x - th) * inv2th;
-  const float v = bm1 <= kLoudSplit ? expm1f(e * log1pf(bm1)) : powf(1.0f + bm1, e) - 1.0f;
-  return ls * v;
-}
-
-// d loudness / dx
-__device__ __forceinline__ float dloudness(float x, float th, float inv2th, float e, float dls) {
-  if (!(x > th)) return 0.0f;
-  const float bm1 = (x - th) * inv2th;
-  return dls * powf(1.0f + bm1, e - 1.0f);
-}
-
 __device__ __forceinline__ float sgnf(float v) { return v > 0.0f ? 1.0f : (v < 0.0f ? -1.0f : 0.0f); }
 
 struct Band {
@@ -115,20 +97,46 @@ struct Band {
   }
 };
 
+// Zwicker loudness of one band (loudness.py:52-61),
+//   L = Sl (2 th)^e ((0.5 + 0.5 x / th)^e - 1) = ls ((1 + bm1)^e - 1),
+//   bm1 = (x - th) / (2 th),
+// evaluated as ls * expm1(e log1p(bm1)), which keeps full relative precision
+// as x approaches the threshold and needs one log1p / expm1 pair at any
+// distance from it.  `pw` returns (1 + bm1)^e and `base` 1 + bm1 for the
+// derivative dL/dx = dls (1 + bm1)^(e - 1) = dls pw / base.
+__device__ __forceinline__ float loudness(float x, const Band& b, float& pw, float& base) {
+  if (!(x > b.th)) {
+    pw = 0.0f;
+    base = 1.0f;
+    return 0.0f;
+  }
+  const float bm1 = (x - b.th) * b.inv2th;
+  const float em1 = expm1f(b.e * log1pf(bm1));
+  pw = 1.0f + em1;
+  base = 1.0f + bm1;
+  return b.ls * em1;
+}
+
 // loudness, disturbance and the asymmetry factor of one band of one frame
+// (loss.py:228-255)
 struct Cell {
   float er, ed, lr, ld, u, zz, dist, asc_raw, asc;
+  float pr, br, pd, bd;  // (1 + bm1)^e and 1 + bm1 of er and ed
   __device__ void eval(const Band& b, float R, float D, float bpr, float fpr) {
     er = bpr * R;
     ed = fpr * D;
-    lr = loudness(er, b.th, b.inv2th, b.e, b.ls);
-    ld = loudness(ed, b.th, b.inv2th, b.e, b.ls);
+    lr = loudness(er, b, pr, br);
+    ld = loudness(ed, b, pd, bd);
     u = ld - lr;
     zz = fabsf(u) - 0.25f * fminf(ld, lr);
     dist = sgnf(u) * fmaxf(zz, 0.0f);
-    asc_raw = powf((ed + 50.0f) / (er + 50.0f), 1.2f);
+    // ((ed + 50) / (er + 50))^1.2
+    asc_raw = expf(1.2f * logf((ed + 50.0f) / (er + 50.0f)));
     asc = asc_raw < 3.0f ? 0.0f : fminf(asc_raw, 12.0f);
   }
+  // dL/dx of the two loudnesses
+  __device__ float dld(const Band& b) const { return ed > b.th ? b.dls * (pd / bd) : 0.0f; }
+  __device__ float dlr(const Band& b) const { return er > b.th ? b.dls * (pr / br) : 0.0f; }
 };
 
 __device__ __forceinline__ void load_tables(DevTables* dst, const DevTables* src) {
@@ -321,7 +329,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       const float fpr0 = (taer + 5e3f) / (tad + 5e3f);
       const float fpr1 = t == 0 ? fpr0 : fpr0 * 0.8f + fpr0_prev * 0.2f;
       const float fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
-      const float h = powf((taer + 1e5f) / 1e7f, 0.04f);
+      const float h = expf(0.04f * logf((taer + 1e5f) / 1e7f));
       Cell c0, c1;
       c0.eval(b0, R0, D0, bpr0, fpr);
       c1.eval(b1, R1, D1, bpr1, fpr);
@@ -585,8 +593,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       const float wr = c.lr < c.ld ? 1.0f : (c.ld == c.lr ? 0.5f : 0.0f);
       const float g_ld = g_u + 0.25f * g_dz * wd;
       const float g_lr = -g_u + 0.25f * g_dz * wr;
-      float g_ed = g_ld * dloudness(c.ed, b.th, b.inv2th, b.e, b.dls);
-      float g_er = g_lr * dloudness(c.er, b.th, b.inv2th, b.e, b.dls);
+      float g_ed = g_ld * c.dld(b);
+      float g_er = g_lr * c.dlr(b);
       if (c.asc_raw >= 3.0f && c.asc_raw <= 12.0f) {
         g_ed += g_asc * 1.2f * c.asc_raw / (c.ed + 50.0f);
         g_er -= g_asc * 1.2f * c.asc_raw / (c.er + 50.0f);
