@@ -48,17 +48,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t base = a - kHop;
   PESQ_STAMP(g_phase_back, 0);
 
-  {
-    const float4* s4 = reinterpret_cast<const float4*>(p.tab);
-    float4* d4 = reinterpret_cast<float4*>(tab);
-    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) d4[i] = s4[i];
-  }
-  // z = H^T H x of the segment is only needed at the very end: its copy into
-  // shared memory runs in the background of the frame loop
+  // constant tables (first copy group); z = H^T H x of the segment is only
+  // needed at the very end, its copy (second group) runs in the background of
+  // the frame loop
+  copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
+  cp_async_commit();
   const float* zr = p.z + (int64_t)row * n_row;
   for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
   cp_async_commit();
   for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
+  cp_async_wait_group<1>();
   __syncthreads();
   PESQ_STAMP(g_phase_back, 1);
 

@@ -135,15 +135,10 @@ struct Cell {
     asc = asc_raw < 3.0f ? 0.0f : fminf(asc_raw, 12.0f);
   }
   // dL/dx of the two loudnesses
-  __device__ float dld(const Band& b) const { return ed > b.th ? b.dls * (pd / bd) : 0.0f; }
-  __device__ float dlr(const Band& b) const { return er > b.th ? b.dls * (pr / br) : 0.0f; }
+  // (gradient only: the 2-ulp fast division is far inside the gradient tolerance)
+  __device__ float dld(const Band& b) const { return ed > b.th ? b.dls * __fdividef(pd, bd) : 0.0f; }
+  __device__ float dlr(const Band& b) const { return er > b.th ? b.dls * __fdividef(pr, br) : 0.0f; }
 };
-
-__device__ __forceinline__ void load_tables(DevTables* dst, const DevTables* src) {
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-  float4* d4 = reinterpret_cast<float4*>(dst);
-  for (int i = threadIdx.x; i < (int)(sizeof(DevTables) / 16); i += blockDim.x) d4[i] = s4[i];
-}
 
 // Frames of this CTA (a contiguous slice of the utterance) and of this warp
 // (a contiguous sub-slice of that).
@@ -199,17 +194,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   const Slice sl(T);
   PESQ_STAMP(g_phase_chain_fwd, 0);
 
-  load_tables(&tab, p.tab);
-  if (warp < 2) {
-    // level alignment power of both rows, loss.py:132-136
-    const int r = warp == 0 ? u : B + u;
-    const double tot = warp_row_sumsq(p.partial + (int64_t)r * p.nseg, p.nseg, lane);
-    if (lane == 0) {
-      const double denom = ((double)p.n + 5120.0) * 1.04684;
-      s2s[warp] = (float)(1e7 / (tot / denom));
-      if (q == 0) p.sumsq[r] = tot;
-    }
-  }
+  // tables and the slice's spectra are copied asynchronously while warps 0-1
+  // reduce the level alignment power
+  copy_async<kChainThreads>(&tab, p.tab, (int)sizeof(DevTables));
   const float* Fr = p.bark + (int64_t)u * T * p.lay.nb;
   const float* Fd = p.bark + (int64_t)(B + u) * T * p.lay.nb;
   const int nb = p.lay.nb;
@@ -226,12 +213,24 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     // frame -1 (before the signal) reads as zeros
     const int skip = t_first < 0 ? nb : 0;
     for (int i = threadIdx.x; i < skip; i += kChainThreads) sr[i] = sd[i] = 0.0f;
-    stage_rows<kChainThreads>(sr + skip, pitch, Fr + (int64_t)t_first * nb + skip, Fd - Fr, 2,
-                              (sl.c_hi - t_first) * nb - skip);
+    stage_rows_async<kChainThreads>(sr + skip, pitch, Fr + (int64_t)t_first * nb + skip, Fd - Fr, 2,
+                                    (sl.c_hi - t_first) * nb - skip);
     fr = sr;
     fd = sd;
     origin = (int64_t)t_first * nb;
   }
+  cp_async_commit();
+  if (warp < 2) {
+    // level alignment power of both rows, loss.py:132-136
+    const int r = warp == 0 ? u : B + u;
+    const double tot = warp_row_sumsq(p.partial + (int64_t)r * p.nseg, p.nseg, lane);
+    if (lane == 0) {
+      const double denom = ((double)p.n + 5120.0) * 1.04684;
+      s2s[warp] = (float)(1e7 / (tot / denom));
+      if (q == 0) p.sumsq[r] = tot;
+    }
+  }
+  cp_async_wait_all();
   __syncthreads();
   PESQ_STAMP(g_phase_chain_fwd, 1);
   const float s2r = s2s[0], s2d = s2s[1];
@@ -447,7 +446,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const Slice sl(T);
   PESQ_STAMP(g_phase_chain_bwd, 0);
 
-  load_tables(&tab, p.tab);
+  copy_async<kChainThreads>(&tab, p.tab, (int)sizeof(DevTables));
   const float* sv = p.saved + (int64_t)u * p.lay.stride;
   float* gf = p.scratch + (int64_t)u * 2 * T;  // [g_fpr | g_h] per frame
   const float* Fr = p.bark + (int64_t)u * T * nb;
@@ -476,7 +475,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     const int n = (sl.c_hi - sl.c_lo) * nb;
     float* sr = dsm;
     float* sd = sr + n;
-    stage_rows<kChainThreads>(sr, n, Fr + (int64_t)sl.c_lo * nb, Fd - Fr, 2, n);
+    stage_rows_async<kChainThreads>(sr, n, Fr + (int64_t)sl.c_lo * nb, Fd - Fr, 2, n);
     fr = sr;
     fd = sd;
     gr = sd + n;
@@ -485,13 +484,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     fs = gd + n;
     gfs = fs + kFrameArrays * fpitch;
     ws = gfs + 2 * fpitch;
-    stage_rows<kChainThreads>(fs, fpitch, sv + p.lay.keep + sl.c_lo, upT, kFrameArrays,
-                              min(sl.c_hi + 1, T) - sl.c_lo);
-    stage_rows<kChainThreads>(ws, wpitch, sv + p.lay.psqm_s + l_min, p.lay.psqm_a - p.lay.psqm_s, 2,
-                              max(0, l_max - l_min + 1));
+    stage_rows_async<kChainThreads>(fs, fpitch, sv + p.lay.keep + sl.c_lo, upT, kFrameArrays,
+                                    min(sl.c_hi + 1, T) - sl.c_lo);
+    stage_rows_async<kChainThreads>(ws, wpitch, sv + p.lay.psqm_s + l_min, p.lay.psqm_a - p.lay.psqm_s, 2,
+                                    max(0, l_max - l_min + 1));
   }
-  __syncthreads();
-  PESQ_STAMP(g_phase_chain_bwd, 1);
+  cp_async_commit();
   auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
   auto FS = [&](int k, int t) -> float {
     return p.staged ? fs[k * fpitch + (t - sl.c_lo)] : __ldg(sv + p.lay.keep + k * upT + t);
@@ -518,6 +516,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     gda += p.g_mos[u] * dm * -0.0309f;
   }
 
+  cp_async_wait_all();
+  __syncthreads();
+  PESQ_STAMP(g_phase_chain_bwd, 1);
+
   Band b0, b1;
   b0.load(tab, lane);
   b1.load(tab, lane + 32);
@@ -542,7 +544,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
         for (int l = l_lo; l <= l_hi; ++l) {
           const float pl = PQ(side, l);
           if (pl > 0.0f) {
-            const float r = s / pl, r2 = r * r;
+            const float r = __fdividef(s, pl), r2 = r * r;
             gs += pl * (r2 * r2 * r);
           }
         }
@@ -596,8 +598,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       float g_ed = g_ld * c.dld(b);
       float g_er = g_lr * c.dlr(b);
       if (c.asc_raw >= 3.0f && c.asc_raw <= 12.0f) {
-        g_ed += g_asc * 1.2f * c.asc_raw / (c.ed + 50.0f);
-        g_er -= g_asc * 1.2f * c.asc_raw / (c.er + 50.0f);
+        g_ed += __fdividef(g_asc * 1.2f * c.asc_raw, c.ed + 50.0f);
+        g_er -= __fdividef(g_asc * 1.2f * c.asc_raw, c.er + 50.0f);
       }
       gfpr = fmaf(g_ed, D, gfpr);
       gd[o] = g_ed;

@@ -193,8 +193,41 @@ __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
                "l"(src)
                : "memory");
 }
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// wait until at most N of this thread's committed groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Asynchronous form of stage_rows: every thread only issues cp.async copies,
+// so any number of stagings can be in flight together; the data is in place
+// after cp_async_wait_all() and a CTA barrier.
+template <int kBlock>
+__device__ __forceinline__ void stage_rows_async(float* dst, int pitch, const float* src, int64_t src_pitch,
+                                                 int rows, int cnt) {
+  const int n = rows * cnt;
+  for (int i = threadIdx.x; i < n; i += kBlock) {
+    const int k = i / cnt, t = i - k * cnt;
+    cp_async4(dst + k * pitch + t, src + k * src_pitch + t);
+  }
+}
+
+// Asynchronous copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) by a CTA of kBlock threads; complete as for stage_rows_async.
+template <int kBlock>
+__device__ __forceinline__ void copy_async(void* dst, const void* src, int bytes) {
+  char* d = static_cast<char*>(dst);
+  const char* s = static_cast<const char*>(src);
+  for (int i = threadIdx.x; i < bytes / 16; i += kBlock) cp_async16(d + 16 * i, s + 16 * i);
+}
 
 // ---------------------------------------------------------------------------
 // 1D bulk copy (TMA) global -> shared, completion on an mbarrier

@@ -60,20 +60,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool grad_row = row >= p.spec_begin && row < p.spec_end;
   PESQ_STAMP(g_phase_front, 0);
 
-  // constant tables
-  {
-    const float4* s4 = reinterpret_cast<const float4*>(p.tab);
-    float4* d4 = reinterpret_cast<float4*>(tab);
-    for (int i = tid; i < (int)(sizeof(DevTables) / 16); i += kThreads) d4[i] = s4[i];
-    const float4* t4 = reinterpret_cast<const float4*>(p.tw64);
-    float4* e4 = reinterpret_cast<float4*>(tw);
-    for (int i = tid; i < (int)(sizeof(DevTwiddle64) / 16); i += kThreads) e4[i] = t4[i];
-  }
+  // constant tables, copied in the background of the span staging
+  copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
+  copy_async<kThreads>(tw, p.tw64, (int)sizeof(DevTwiddle64));
+  cp_async_commit();
   // stage the span; zeros outside the row reproduce the zero initial state.
   // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
   const bool has_lo = p.src_lo.ref != nullptr;
   stage_span(xs, xr, base, n_row);
   if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
+  cp_async_wait_all();
   __syncthreads();
   PESQ_STAMP(g_phase_front, 1);
 
