@@ -46,6 +46,10 @@ typedef enum pesq_status {
 /* flags of a forward / backward pair */
 #define PESQ_GRAD_REF 1u /* the backward will be asked for dL/dref */
 #define PESQ_GRAD_DEG 2u /* the backward will be asked for dL/ddeg */
+/* backward only: each non-NULL upstream gradient (g_loss, g_mos, g_dsymm,
+ * g_dasymm) points to ONE value shared by every utterance of the batch, as
+ * the gradient of a sum or mean over the batch is; saves materialising it */
+#define PESQ_UPSTREAM_SCALAR 4u
 
 typedef struct pesq_plan pesq_plan;
 

@@ -146,6 +146,37 @@ def test_gradient_only_for_requested_inputs(cuda_device):
     assert torch.equal(g_ref_only, g_ref)
 
 
+def test_upstream_gradients(cuda_device):
+    """Broadcast upstream gradients (sum / mean over the batch, passed as one
+    shared value) match the same values given as full arrays, and gradients
+    through several outputs add up."""
+
+    ref = speech_like(3, 16000, 16000, seed=45).to(cuda_device)
+    deg = add_noise(ref.cpu(), 6.0, seed=46).to(cuda_device).requires_grad_(True)
+    model = PesqLossCuda(0.5, sample_rate=16000)
+    loss = model(ref, deg)
+    (g_sum,) = torch.autograd.grad(loss.sum(), [deg])
+    loss = model(ref, deg)
+    (g_arr,) = torch.autograd.grad(loss, [deg], grad_outputs=torch.ones(3, device=cuda_device))
+    assert torch.equal(g_sum, g_arr)
+    loss = model(ref, deg)
+    (g_mean,) = torch.autograd.grad(loss.mean(), [deg])
+    torch.testing.assert_close(g_mean, g_arr / 3, rtol=1e-5, atol=1e-6 * float(g_arr.abs().max()))
+    w = torch.tensor([0.5, -2.0, 1.5], device=cuda_device)
+    loss = model(ref, deg)
+    (g_w,) = torch.autograd.grad((w * loss).sum(), [deg])
+    for i in range(3):
+        torch.testing.assert_close(g_w[i], w[i] * g_arr[i], rtol=1e-5, atol=1e-6 * float(g_arr.abs().max()))
+    # dL/dmos and dL/dloss together: mos = f(0.1 ds + 0.0309 da) = f(loss / factor)
+    ds, da = model.raw(ref, deg.detach())
+    m = 4.5 - 0.1 * ds - 0.0309 * da
+    dmos_dloss = -4 * 1.3669 * torch.exp(-1.3669 * m + 3.8224) / (1 + torch.exp(-1.3669 * m + 3.8224)) ** 2 / 0.5
+    _, _, mos, loss = model._evaluate(ref, deg)  # one call, two differentiated outputs
+    (g_both,) = torch.autograd.grad((mos + loss).sum(), [deg])
+    want = g_arr * (1.0 + dmos_dloss)[:, None]
+    torch.testing.assert_close(g_both, want, rtol=1e-4, atol=1e-4 * float(want.abs().max()))
+
+
 def test_cuda_graph_is_bit_exact(cuda_device):
     ref = speech_like(2, 16000, 16000, seed=43).to(cuda_device).requires_grad_(True)
     deg = add_noise(ref.detach().cpu(), 5.0, seed=44).to(cuda_device).requires_grad_(True)

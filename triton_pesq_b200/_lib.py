@@ -22,6 +22,7 @@ OPS_PATH = os.path.join(HERE, "_pesq_torch_ops.so")
 ABI_VERSION = 2
 GRAD_REF = 1
 GRAD_DEG = 2
+UPSTREAM_SCALAR = 4
 
 PESQ_OK = 0
 PESQ_ERR_INVALID_ARGUMENT = 1

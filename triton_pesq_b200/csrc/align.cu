@@ -14,9 +14,9 @@
 //     after the chain adjoint, which releases it as soon as its own CTAs are
 //     resident, so its CTAs fill the SMs the chain leaves idle;
 //   * it reads nothing the chain adjoint writes, and it waits for the chain
-//     adjoint's grid to complete (griddepcontrol.wait) only after its own
-//     work, so the next kernel on the stream (the back kernel, launched
-//     normally) starts after both.
+//     adjoint's grid to complete (pdl_wait) only after its own work, so the
+//     next kernel on the stream (the back kernel, launched normally) starts
+//     after both.
 //
 // The CTA stages kSpan samples from kHorizon before the segment: the forward
 // scan H_pow runs in place over them (the first kHorizon outputs are warm-up),
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_STAMP(g_phase_align, 3);
 
   // complete only after the kernel this one was released early from
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
 }
 
 }  // namespace
@@ -94,17 +94,8 @@ cudaError_t configure_align() {
 cudaError_t launch_align(const AlignArgs& a, const PowTab& pow, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)blocks);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = align_smem_bytes();
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, align_adjoint_kernel, a, pow);
+  LaunchShape l((unsigned)blocks, kThreads, align_smem_bytes(), s, true);
+  return cudaLaunchKernelEx(&l.cfg, align_adjoint_kernel, a, pow);
 }
 
 }  // namespace pesq

@@ -53,10 +53,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the frame loop
   copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
   cp_async_commit();
+  for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   const float* zr = p.z + (int64_t)row * n_row;
   for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
   cp_async_commit();
-  for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   cp_async_wait_group<1>();
   __syncthreads();
   PESQ_STAMP(g_phase_back, 1);
@@ -141,8 +141,8 @@ size_t back_smem_bytes() { return (size_t)kBackSmemBytes; }
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
-  back_kernel<<<(unsigned)blocks, kThreads, back_smem_bytes(), s>>>(a, pre);
-  return cudaGetLastError();
+  LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(), s, false);
+  return cudaLaunchKernelEx(&l.cfg, back_kernel, a, pre);
 }
 
 cudaError_t configure_back() {

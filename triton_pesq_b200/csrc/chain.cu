@@ -435,10 +435,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   __shared__ double kap[kChainWarps][2];
   __shared__ double kpart[2];
 
-  // the next kernel on the stream (the align kernel, which reads nothing this
-  // kernel writes) may start on the SMs the clusters leave free
-  asm volatile("griddepcontrol.launch_dependents;");
-
   const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
   const int u = blockIdx.x / C;
   const int B = p.batch, T = p.lay.T, L = p.lay.L, nb = p.lay.nb;
@@ -446,6 +442,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const Slice sl(T);
   PESQ_STAMP(g_phase_chain_bwd, 0);
 
+  // the next kernel on the stream (the align kernel, which reads nothing this
+  // kernel writes) may start on the SMs the clusters leave free
+  pdl_trigger();
   copy_async<kChainThreads>(&tab, p.tab, (int)sizeof(DevTables));
   const float* sv = p.saved + (int64_t)u * p.lay.stride;
   float* gf = p.scratch + (int64_t)u * 2 * T;  // [g_fpr | g_h] per frame
@@ -501,19 +500,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
 
   // upstream gradients of both distances (epilogue adjoint)
-  float gds = p.g_dsymm ? p.g_dsymm[u] : 0.0f;
-  float gda = p.g_dasymm ? p.g_dasymm[u] : 0.0f;
+  const int gu = u * p.g_stride;
+  float gds = p.g_dsymm ? p.g_dsymm[gu] : 0.0f;
+  float gda = p.g_dasymm ? p.g_dasymm[gu] : 0.0f;
   if (p.g_loss) {
-    gds += (float)(p.g_loss[u] * p.factor * 0.1);
-    gda += (float)(p.g_loss[u] * p.factor * 0.0309);
+    gds += (float)(p.g_loss[gu] * p.factor * 0.1);
+    gda += (float)(p.g_loss[gu] * p.factor * 0.0309);
   }
   if (p.g_mos) {
     const float m = 4.5f - 0.1f * ds - 0.0309f * da;
     const float ex = expf(-1.3669f * m + 3.8224f);
     const float den = 1.0f + ex;
     const float dm = 4.0f * 1.3669f * ex / (den * den);
-    gds += p.g_mos[u] * dm * -0.1f;
-    gda += p.g_mos[u] * dm * -0.0309f;
+    gds += p.g_mos[gu] * dm * -0.1f;
+    gda += p.g_mos[gu] * dm * -0.0309f;
   }
 
   cp_async_wait_all();
@@ -735,19 +735,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
 template <class Kernel, class Args>
 cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, size_t smem, cudaStream_t s) {
   if (batch <= 0) return cudaSuccess;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(batch * cluster));
-  cfg.blockDim = dim3(kChainThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, a);
+  LaunchShape l((unsigned)(batch * cluster), kChainThreads, smem, s, false, cluster);
+  return cudaLaunchKernelEx(&l.cfg, k, a);
 }
 
 }  // namespace

@@ -140,6 +140,22 @@ __device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
 }
 
 // ---------------------------------------------------------------------------
+// programmatic dependent launch
+// ---------------------------------------------------------------------------
+
+// A kernel launched with programmatic stream serialisation may start before
+// the kernel preceding it on the stream has ended.  pdl_trigger() allows the
+// kernel following this one to start (once every CTA of this grid has called
+// it or exited); pdl_wait() blocks until the preceding kernel has completed and
+// its memory is visible, and is a no-op in a kernel launched normally.  The
+// one kernel of this library launched this way (the align kernel, released by
+// the chain adjoint) calls pdl_wait() before it exits, so its completion
+// implies the completion of the chain adjoint.  (Releasing the other kernels
+// early as well was measured to slow the captured step down.)
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // global -> shared staging
 // ---------------------------------------------------------------------------
 

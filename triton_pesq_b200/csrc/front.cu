@@ -165,8 +165,8 @@ cudaError_t configure_front() {
 cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
-  front_kernel<<<(unsigned)blocks, kThreads, front_smem_bytes(), s>>>(a, pow, pre);
-  return cudaGetLastError();
+  LaunchShape l((unsigned)blocks, kThreads, front_smem_bytes(), s, false);
+  return cudaLaunchKernelEx(&l.cfg, front_kernel, a, pow, pre);
 }
 
 }  // namespace pesq

@@ -145,6 +145,7 @@ struct ChainBwdArgs {
   const float* g_mos;       // [B] nullable
   const float* g_dsymm;     // [B] nullable
   const float* g_dasymm;    // [B] nullable
+  int g_stride;             // element stride of the four upstream gradients (0: one shared value)
   int want_ref, want_deg;
   float* g_bark;            // [2B][T][nb]  out
   float* kappa;             // [2B]         out
@@ -167,6 +168,36 @@ struct ResampleArgs {
   // adjoint gather lists per residue mod orig_step
   const int* adj_offset;   // [orig_step + 1]
   const int4* adj_entries; // (dl, phase, tap bits, 0)
+};
+
+// Launch configuration of one kernel; `pdl` adds programmatic stream
+// serialisation (the kernel may start while its predecessor on the stream
+// runs, see pdl_wait), `cluster` > 0 a thread block cluster dimension.
+struct LaunchShape {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[2];
+  LaunchShape(unsigned blocks, unsigned threads, size_t smem, cudaStream_t s, bool pdl, int cluster = 0) {
+    cfg = cudaLaunchConfig_t{};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    int n = 0;
+    if (pdl) {
+      attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[n].val.programmaticStreamSerializationAllowed = 1;
+      ++n;
+    }
+    if (cluster > 0) {
+      attr[n].id = cudaLaunchAttributeClusterDimension;
+      attr[n].val.clusterDim.x = (unsigned)cluster;
+      attr[n].val.clusterDim.y = 1;
+      attr[n].val.clusterDim.z = 1;
+      ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+  }
 };
 
 cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s);

@@ -133,6 +133,8 @@ int64_t resampled_length(const pesq_plan* p, int64_t n) {
 }
 
 int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, Geometry& g) {
+  if (flags & ~(PESQ_GRAD_REF | PESQ_GRAD_DEG | PESQ_UPSTREAM_SCALAR))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
   if (batch < 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "negative batch %lld", (long long)batch);
   if (n_src <= 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "signals need at least one sample");
   g.batch = batch;
@@ -534,6 +536,7 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   cb.g_mos = g_mos;
   cb.g_dsymm = g_dsymm;
   cb.g_dasymm = g_dasymm;
+  cb.g_stride = (flags & PESQ_UPSTREAM_SCALAR) ? 0 : 1;
   cb.want_ref = (flags & PESQ_GRAD_REF) != 0;
   cb.want_deg = (flags & PESQ_GRAD_DEG) != 0;
   cb.g_bark = at<float>(ws, g.gbark);

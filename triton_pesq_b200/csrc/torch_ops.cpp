@@ -62,12 +62,34 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> pesq_forw
   return {d_symm, d_asymm, mos, loss, ws};
 }
 
-const float* opt_ptr(const c10::optional<at::Tensor>& t, int64_t batch, const char* name) {
-  if (!t.has_value() || !t->defined()) return nullptr;
-  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->numel() == batch && t->is_contiguous(),
-              "upstream gradient `", name, "` must be a contiguous float32 CUDA tensor of ", batch, " elements");
-  return t->data_ptr<float>();
-}
+// The four upstream gradients of one backward call.  When every one that is
+// present is a broadcast of one value over the batch (stride 0, as autograd
+// hands over the gradient of a sum or mean) they are passed as that single
+// value with PESQ_UPSTREAM_SCALAR; otherwise as contiguous [batch] arrays.
+struct Upstream {
+  at::Tensor t[4];
+  const float* ptr[4] = {nullptr, nullptr, nullptr, nullptr};
+  uint32_t flag = 0;
+  Upstream(const c10::optional<at::Tensor>* g[4], int64_t batch) {
+    static const char* names[4] = {"g_loss", "g_mos", "g_dsymm", "g_dasymm"};
+    bool any = false, shared = true;
+    for (int i = 0; i < 4; ++i) {
+      if (!g[i]->has_value() || !(*g[i])->defined()) continue;
+      const at::Tensor& v = **g[i];
+      TORCH_CHECK(v.is_cuda() && v.scalar_type() == at::kFloat && v.dim() == 1 && v.numel() == batch,
+                  "upstream gradient `", names[i], "` must be a float32 CUDA tensor of ", batch, " elements");
+      any = true;
+      shared = shared && batch > 1 && v.stride(0) == 0;
+    }
+    if (!any) return;
+    if (shared) flag = PESQ_UPSTREAM_SCALAR;
+    for (int i = 0; i < 4; ++i) {
+      if (!g[i]->has_value() || !(*g[i])->defined()) continue;
+      t[i] = shared ? **g[i] : (*g[i])->contiguous();
+      ptr[i] = t[i].data_ptr<float>();
+    }
+  }
+};
 
 std::tuple<at::Tensor, at::Tensor> pesq_backward_op(int64_t plan_handle, const at::Tensor& ref,
                                                     const at::Tensor& deg, int64_t flags, const at::Tensor& ws,
@@ -84,10 +106,11 @@ std::tuple<at::Tensor, at::Tensor> pesq_backward_op(int64_t plan_handle, const a
   at::Tensor g_ref = (flags & PESQ_GRAD_REF) ? at::empty({batch, n}, ref.options()) : at::empty({0}, ref.options());
   at::Tensor g_deg = (flags & PESQ_GRAD_DEG) ? at::empty({batch, n}, deg.options()) : at::empty({0}, deg.options());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index());
+  const c10::optional<at::Tensor>* g[4] = {&g_loss, &g_mos, &g_dsymm, &g_dasymm};
+  const Upstream up(g, batch);
   check_status(pesq_backward(plan, stream, ref.data_ptr<float>(), ref.stride(0), deg.data_ptr<float>(),
-                             deg.stride(0), batch, n, (uint32_t)flags, ws.data_ptr(), (size_t)ws.numel() * 4,
-                             opt_ptr(g_loss, batch, "g_loss"), opt_ptr(g_mos, batch, "g_mos"),
-                             opt_ptr(g_dsymm, batch, "g_dsymm"), opt_ptr(g_dasymm, batch, "g_dasymm"),
+                             deg.stride(0), batch, n, (uint32_t)flags | up.flag, ws.data_ptr(),
+                             (size_t)ws.numel() * 4, up.ptr[0], up.ptr[1], up.ptr[2], up.ptr[3],
                              (flags & PESQ_GRAD_REF) ? g_ref.data_ptr<float>() : nullptr, n,
                              (flags & PESQ_GRAD_DEG) ? g_deg.data_ptr<float>() : nullptr, n),
                "pesq_backward");

@@ -6,12 +6,12 @@ an autograd backward w.r.t. either input.  Every evaluation goes through the
 C ABI of ``libpesq_cuda.so`` (via the ``torch.ops.pesq_cuda`` custom ops);
 there is no Triton, no CPU path and no fallback.
 
-Pipeline per call (four kernels each way at 16 kHz, plus the resampler at
-other rates): front (level-alignment band pass and its adjoint term,
-pre-emphasis, STFT -> Bark), chain forward (silent frames, equalisation,
-loudness, disturbance, pooling, MOS/loss), and in the backward the chain
-adjoint and the back end (spectral adjoint, reverse pre-emphasis, alignment
-term).
+Pipeline per call at 16 kHz (plus the resampler and its adjoint at other
+rates): front (level-alignment power, pre-emphasis, STFT -> Bark) and chain
+forward (silent frames, equalisation, loudness, disturbance, pooling,
+MOS/loss); in the backward the chain adjoint, the align kernel
+(H^T H x of the level-alignment band pass, overlapping the chain adjoint) and
+the back end (spectral adjoint, reverse pre-emphasis, alignment term).
 """
 
 from __future__ import annotations
@@ -41,6 +41,8 @@ class _PesqFunction(torch.autograd.Function):
             _lib.GRAD_DEG if ctx.needs_input_grad[1] else 0
         )
         d_symm, d_asymm, mos, loss, ws = torch.ops.pesq_cuda.forward(plan, ref, deg, flags)
+        # outputs nobody differentiates get no (zero-filled) gradient
+        ctx.set_materialize_grads(False)
         ctx.plan = plan
         ctx.flags = flags
         if flags:
@@ -54,8 +56,10 @@ class _PesqFunction(torch.autograd.Function):
     def backward(ctx, g_dsymm, g_dasymm, g_mos, g_loss):
         ref, deg = ctx.saved_tensors
 
+        # broadcast gradients (of a sum or mean over the batch) are passed on
+        # as one shared value, without materialising them
         def prep(g):
-            return None if g is None else g.contiguous().float()
+            return None if g is None else g.float()
 
         g_ref, g_deg = torch.ops.pesq_cuda.backward(
             ctx.plan, ref, deg, ctx.flags, ctx.workspace,
