@@ -294,8 +294,7 @@ def stage_times(model, ref, deg, dev, launches=40):
                                        None)
 
     def align(i):
-        return lib.pesq_backward_align(P, sp, ctypes.c_void_p(refs[i].data_ptr()), n,
-                                       ctypes.c_void_p(degs[i].data_ptr()), n, b, n, flags, W, wb)
+        return lib.pesq_backward_align(P, sp, b, n, flags, W, wb)
 
     def back(i):
         return lib.pesq_backward_back(P, sp, b, n, flags, W, wb, None, n, ctypes.c_void_p(g_deg.data_ptr()), n)

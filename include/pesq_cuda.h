@@ -141,10 +141,9 @@ int pesq_forward(const pesq_plan* plan, void* stream, const float* ref, int64_t 
  * workspace.  Upstream gradients g_loss / g_mos / g_dsymm / g_dasymm ([batch],
  * any may be NULL = zero) are summed.  Writes dL/dref into g_ref (row stride
  * ld_gref) if flags has PESQ_GRAD_REF and dL/ddeg into g_deg if it has
- * PESQ_GRAD_DEG.  The input rows whose gradient is requested are read again
- * (at 16 kHz; other rates use the resampled copy in the workspace), so they
- * must be unchanged since the forward.  Replaces the autograd backward of
- * PesqLossTriton. */
+ * PESQ_GRAD_DEG.  ref / deg are those of the forward; everything the
+ * backward needs from them was saved in the workspace, so they are not read
+ * again.  Replaces the autograd backward of PesqLossTriton. */
 int pesq_backward(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
                   int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
                   size_t workspace_bytes, const float* g_loss, const float* g_mos, const float* g_dsymm,
@@ -169,10 +168,11 @@ int pesq_forward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64
  * order on one stream):
  *   chain: adjoint of the perceptual model and of the epilogue
  *          (replaces chain.py:892-1021 and elementwise.py:800-827)
- *   align: z = H^T H x of the level-alignment band pass H for the gradient
- *          rows, the input of the alignment-scale term (replaces the adjoint
- *          IIR of iir.py:1249-1258 on the level-alignment filter); it depends
- *          on the inputs only and is launched with programmatic stream
+ *   align: z = H^T f of the level-alignment band pass H, from the f = H x
+ *          the forward saved for the gradient rows: the input of the
+ *          alignment-scale term (replaces the adjoint IIR of
+ *          iir.py:1249-1258 on the level-alignment filter); it reads nothing
+ *          the chain stage writes and is launched with programmatic stream
  *          serialisation, so it overlaps the chain stage before it
  *   back:  spectral adjoint, pre-emphasis adjoint, level-alignment term
  *          [+ resampler adjoint] (replaces spectral.py:526-581, iir.py:1249-1258,
@@ -180,9 +180,8 @@ int pesq_forward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64
 int pesq_backward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
                         void* workspace, size_t workspace_bytes, const float* g_loss, const float* g_mos,
                         const float* g_dsymm, const float* g_dasymm);
-int pesq_backward_align(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
-                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
-                        size_t workspace_bytes);
+int pesq_backward_align(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
+                        void* workspace, size_t workspace_bytes);
 int pesq_backward_back(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,
                        void* workspace, size_t workspace_bytes, float* g_ref, int64_t ld_gref, float* g_deg,
                        int64_t ld_gdeg);

@@ -123,8 +123,8 @@ SIGNATURES = {
     ),
     "pesq_backward_align": (
         ctypes.c_int,
-        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
-         ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t],
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p,
+         ctypes.c_size_t],
     ),
     "pesq_backward_back": (
         ctypes.c_int,

@@ -62,11 +62,15 @@ ChainLayout ChainLayout::make(int T, int nb) {
 
 int chain_slice_frames(int T, int cluster) { return (int)ceil_div(T, cluster); }
 size_t chain_fwd_smem_bytes(int slice, int nb) { return (size_t)2 * (slice + 1) * nb * sizeof(float); }
-// Bark spectra and their gradient accumulators (4 slices), the ten per-frame
+// Bark spectra and their gradient accumulators (4 slices), the forward's
+// adjoint coefficients of the slice (kCellFields slices), the ten per-frame
 // saved arrays and two per-frame gradients of frames c_lo..c_hi, and the two
 // window arrays over the slice
 size_t chain_bwd_smem_bytes(int slice, int nb) {
-  return ((size_t)4 * slice * nb + (size_t)12 * (slice + 1) + (size_t)2 * (slice / 10 + 4)) * sizeof(float);
+  const size_t cblk = ((size_t)slice * nb + 3) & ~(size_t)3;
+  return ((size_t)kCellFields * cblk + (size_t)4 * slice * nb + (size_t)12 * (slice + 1) +
+          (size_t)2 * (slice / 10 + 4)) *
+         sizeof(float);
 }
 size_t chain_smem_limit() { return kChainSmemLimit; }
 
@@ -134,10 +138,25 @@ struct Cell {
     asc_raw = expf(1.2f * logf((ed + 50.0f) / (er + 50.0f)));
     asc = asc_raw < 3.0f ? 0.0f : fminf(asc_raw, 12.0f);
   }
-  // dL/dx of the two loudnesses
-  // (gradient only: the 2-ulp fast division is far inside the gradient tolerance)
-  __device__ float dld(const Band& b) const { return ed > b.th ? b.dls * __fdividef(pd, bd) : 0.0f; }
-  __device__ float dlr(const Band& b) const { return er > b.th ? b.dls * __fdividef(pr, br) : 0.0f; }
+  // The adjoint of eval for the two norms' gradients g_dist and g_asc, as the
+  // coefficients of kCellEdDist .. kCellErAsc (loss.py:236-255 differentiated;
+  // gradient only, so the 2-ulp fast division is far inside the tolerance):
+  //   dist = sgn(u) max(|u| - min(ld, lr) / 4, 0), u = ld - lr,
+  //   asc  = clamp(((ed + 50) / (er + 50))^1.2 -> 0 below 3, 12 above).
+  __device__ void adjoint(const Band& b, float co[4]) const {
+    const float su = sgnf(u);
+    const float live = zz >= 0.0f ? 1.0f : 0.0f;  // the dead zone is not active
+    const float e = live * su * su;
+    const float wd = ld < lr ? 1.0f : (ld == lr ? 0.5f : 0.0f);  // d min(ld, lr) / d ld
+    const float wr = lr < ld ? 1.0f : (ld == lr ? 0.5f : 0.0f);
+    const float dld = ed > b.th ? b.dls * __fdividef(pd, bd) : 0.0f;  // dL/dx of the loudnesses
+    const float dlr = er > b.th ? b.dls * __fdividef(pr, br) : 0.0f;
+    const bool slope = asc_raw >= 3.0f && asc_raw <= 12.0f;
+    co[0] = dld * (e - 0.25f * live * su * wd);
+    co[1] = slope ? __fdividef(1.2f * asc_raw, ed + 50.0f) : 0.0f;
+    co[2] = dlr * (-e - 0.25f * live * su * wr);
+    co[3] = slope ? -__fdividef(1.2f * asc_raw, er + 50.0f) : 0.0f;
+  }
 };
 
 // Frames of this CTA (a contiguous slice of the utterance) and of this warp
@@ -332,6 +351,23 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       Cell c0, c1;
       c0.eval(b0, R0, D0, bpr0, fpr);
       c1.eval(b1, R1, D1, bpr1, fpr);
+      if (p.cells) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const Band& b = half == 0 ? b0 : b1;
+          const Cell& c = half == 0 ? c0 : c1;
+          if (!b.ok) continue;
+          float co[4];
+          c.adjoint(b, co);
+          float* dst = p.cells + ((int64_t)u * C + q) * cell_block(T, C, nb) + (t - sl.c_lo) * nb + b.k;
+          dst[kCellDist * p.cell_stride] = c.dist;
+          dst[kCellAsc * p.cell_stride] = c.asc;
+          dst[kCellEdDist * p.cell_stride] = co[0];
+          dst[kCellEdAsc * p.cell_stride] = co[1];
+          dst[kCellErDist * p.cell_stride] = co[2];
+          dst[kCellErAsc * p.cell_stride] = co[3];
+        }
+      }
       float qs = 0.0f, qa = 0.0f;
       if (b0.norm) {
         const float v = b0.w * c0.dist;
@@ -467,12 +503,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const int l_min = sl.c_lo >= 19 ? (sl.c_lo - 10) / 10 : 0;
   const int l_max = min(L - 1, (sl.c_hi - 1) / 10);
   const int wpitch = (T + C - 1) / C / 10 + 4;
+  // the coefficients of this CTA's slice: one 16-byte aligned block per field
+  const int64_t cblk = cell_block(T, C, nb);
+  const float* cells = p.cells + ((int64_t)u * C + q) * cblk;
+  const int cpitch = (int)cblk;  // floats between the staged fields
+  float* cs = nullptr;   // [kCellFields][cpitch]
   float* fs = nullptr;   // [kFrameArrays][fpitch]
   float* gfs = nullptr;  // [2][fpitch]: dL/dfpr, dL/dh of the slice's frames
   float* ws = nullptr;   // [2][wpitch]: psqm_s, psqm_a of windows l_min..l_max
   if (p.staged) {
     const int n = (sl.c_hi - sl.c_lo) * nb;
-    float* sr = dsm;
+    cs = dsm;  // first: 16-byte aligned
+    for (int f = 0; f < kCellFields; ++f)
+      copy_async<kChainThreads>(cs + f * cpitch, cells + f * p.cell_stride, ((n + 3) & ~3) * 4);
+    float* sr = cs + kCellFields * cpitch;
     float* sd = sr + n;
     stage_rows_async<kChainThreads>(sr, n, Fr + (int64_t)sl.c_lo * nb, Fd - Fr, 2, n);
     fr = sr;
@@ -492,6 +536,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   auto at = [&](int t, int k) { return (int64_t)t * nb + k - origin; };
   auto FS = [&](int k, int t) -> float {
     return p.staged ? fs[k * fpitch + (t - sl.c_lo)] : __ldg(sv + p.lay.keep + k * upT + t);
+  };
+  auto CELL = [&](int f, int t, int k) -> float {
+    const int i = (t - sl.c_lo) * nb + k;
+    return p.staged ? cs[f * cpitch + i] : __ldg(cells + f * p.cell_stride + i);
   };
   auto PQ = [&](int side, int l) -> float {
     return p.staged ? ws[side * wpitch + (l - l_min)] : __ldg(sv + (side ? p.lay.psqm_a : p.lay.psqm_s) + l);
@@ -562,9 +610,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
     }
   };
 
-  // pass 1: loudness / disturbance / norm adjoint per band; per-frame dL/dfpr
+  // pass 1: norm / disturbance / loudness adjoint per band from the forward's
+  // coefficients; per-frame dL/dfpr
   for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-    const float fpr = fminf(fmaxf(FS(kFpr1, t), 3e-4f), 5.0f);
     const float sraw = FS(kSraw, t);
     float g_sraw, g_araw, g_h;
     frame_grads(t, g_sraw, g_araw, g_h);
@@ -576,31 +624,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       const Band& b = half == 0 ? b0 : b1;
       if (!b.ok) continue;
       const int64_t o = at(t, b.k);
-      const float R = s2r * fr[o], D = s2d * fd[o];
-      Cell c;
-      c.eval(b, R, D, half == 0 ? bpr0 : bpr1, fpr);
+      const float D = s2d * fd[o];
       float g_dist = 0.0f, g_asc = 0.0f;
       if (b.norm) {
-        g_dist = coef * (b.w * b.w) * c.dist;
-        const float y = c.dist * c.asc;
-        const float g_y = g_araw * b.w * sgnf(y);
-        g_dist += g_y * c.asc;
-        g_asc = g_y * c.dist;
+        const float dist = CELL(kCellDist, t, b.k), asc = CELL(kCellAsc, t, b.k);
+        g_dist = coef * (b.w * b.w) * dist;
+        const float g_y = g_araw * b.w * sgnf(dist * asc);
+        g_dist += g_y * asc;
+        g_asc = g_y * dist;
       }
-      const float su = sgnf(c.u);
-      const float g_z = c.zz >= 0.0f ? g_dist * su : 0.0f;
-      const float g_u = g_z * su;
-      const float g_dz = -g_z;
-      const float wd = c.ld < c.lr ? 1.0f : (c.ld == c.lr ? 0.5f : 0.0f);
-      const float wr = c.lr < c.ld ? 1.0f : (c.ld == c.lr ? 0.5f : 0.0f);
-      const float g_ld = g_u + 0.25f * g_dz * wd;
-      const float g_lr = -g_u + 0.25f * g_dz * wr;
-      float g_ed = g_ld * c.dld(b);
-      float g_er = g_lr * c.dlr(b);
-      if (c.asc_raw >= 3.0f && c.asc_raw <= 12.0f) {
-        g_ed += __fdividef(g_asc * 1.2f * c.asc_raw, c.ed + 50.0f);
-        g_er -= __fdividef(g_asc * 1.2f * c.asc_raw, c.er + 50.0f);
-      }
+      const float g_ed = g_dist * CELL(kCellEdDist, t, b.k) + g_asc * CELL(kCellEdAsc, t, b.k);
+      const float g_er = g_dist * CELL(kCellErDist, t, b.k) + g_asc * CELL(kCellErAsc, t, b.k);
       gfpr = fmaf(g_ed, D, gfpr);
       gd[o] = g_ed;
       gr[o] = g_er;

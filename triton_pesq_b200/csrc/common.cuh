@@ -229,11 +229,8 @@ __device__ __forceinline__ void cp_async_wait_group() {
 template <int kBlock>
 __device__ __forceinline__ void stage_rows_async(float* dst, int pitch, const float* src, int64_t src_pitch,
                                                  int rows, int cnt) {
-  const int n = rows * cnt;
-  for (int i = threadIdx.x; i < n; i += kBlock) {
-    const int k = i / cnt, t = i - k * cnt;
-    cp_async4(dst + k * pitch + t, src + k * src_pitch + t);
-  }
+  for (int k = 0; k < rows; ++k)
+    for (int t = threadIdx.x; t < cnt; t += kBlock) cp_async4(dst + k * pitch + t, src + k * src_pitch + t);
 }
 
 // Asynchronous copy of `bytes` (a multiple of 16, both addresses 16-byte

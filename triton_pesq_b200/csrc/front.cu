@@ -4,6 +4,7 @@
 // in shared memory and without touching HBM in between:
 //
 //   f  = H_pow x            level-alignment band pass (order 10)    -> sum f^2
+//                           (rows that need a gradient: f itself)  -> HBM
 //   y  = H_pre ramp(x)      edge fade + pre-emphasis biquad, float64
 //   X_t = rfft512(w * y_t)  for the frames starting in [a, a+S), float64
 //   B  = corr * segsum |X_t|^2                                      -> HBM
@@ -43,7 +44,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                  const __grid_constant__ PreTab64 pre) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;                 // kSpan: input, then y (hi part) in place
-  float* fb = xs + kSpan;           // kSpan: low part of a resampled x, then y (lo part)
+  float* fb = xs + kSpan;           // kSpan: [f = H x,] low part of a resampled x, then y (lo part)
   float* scratch = fb + kSpan;      // scan scratch, later the per-warp FFT scratch
   DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
   DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
@@ -66,22 +67,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   cp_async_commit();
   // stage the span; zeros outside the row reproduce the zero initial state.
   // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
+  // On gradient rows fb first holds f = H x (below), the low part only after.
   const bool has_lo = p.src_lo.ref != nullptr;
   stage_span(xs, xr, base, n_row);
-  if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
+  if (has_lo && !grad_row) stage_span(fb, p.src_lo.row(row), base, n_row);
   cp_async_wait_all();
   __syncthreads();
   PESQ_STAMP(g_phase_front, 1);
 
-  // 1. level alignment filter f = H x: only its sum of squares over [a, send)
-  //    is needed (the adjoint H^T f of the backward is evaluated by the align
-  //    kernel of the backward pass)
+  // 1. level alignment filter f = H x: its sum of squares over [a, send), and
+  //    on gradient rows f itself on [a, send), from which the align kernel of
+  //    the backward evaluates the adjoint term H^T f
   double ssq = 0.0;
   chunk_scan<10, false, float>(
       pow, scratch, [&](int q) { return xs[q]; },
       [&](int q, float y) {
         const int64_t n = base + q;
         if (n >= a && n < send) ssq = fma((double)y, (double)y, ssq);
+        if (grad_row) fb[q] = y;
       });
   ssq = warp_sum(ssq);
   if (lane == 0) red[warp] = ssq;
@@ -90,6 +93,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     double tot = 0.0;
     for (int w = 0; w < kWarps; ++w) tot += red[w];
     p.partial[(int64_t)row * p.nseg + seg] = tot;
+  }
+  if (grad_row) {
+    float* fr = p.fpow + (int64_t)row * n_row;
+    for (int i = tid; i < (int)(send - a); i += kThreads) fr[a + i] = fb[kHorizon + i];
+    if (has_lo) {
+      __syncthreads();
+      stage_span(fb, p.src_lo.row(row), base, n_row);
+      __syncthreads();
+    }
   }
   PESQ_STAMP(g_phase_front, 2);
 

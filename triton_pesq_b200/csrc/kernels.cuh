@@ -73,16 +73,17 @@ struct FrontArgs {
   float* bark;       // [rows][T][nb]   unscaled Bark spectrum
   double* partial;   // [rows][nseg]    partial sums of (H x)^2
   Cx<float>* spec;   // [rows][T][256]  rfft bins 0..255 of every frame
+  float* fpow;       // [rows][n]       f = H x, written for the rows that save the spectrum
   uint32_t* err;
 };
 
 struct AlignArgs {
-  RowSource src;     // 16 kHz rows (hi part if resampled)
+  const float* fpow; // [rows][n]  f = H x saved by the front kernel (gradient rows)
   int row_begin;     // rows [row_begin, row_begin + rows) get z
   int64_t n;
   int seg_frames;
   int nseg;
-  float* z;          // [rows][n]  H^T H x
+  float* z;          // [rows][n]  H^T f
 };
 
 struct BackArgs {
@@ -130,7 +131,25 @@ struct ChainFwdArgs {
   float* mos;
   float* loss;
   int staged;               // Bark slice staged in shared memory
+  // per (frame, band) adjoint coefficients for the backward (nullable: no
+  // gradient requested), see CellField and cell_block
+  float* cells;
+  int64_t cell_stride;
 };
+
+// Layout of the adjoint coefficients: field f of frame t, band k of utterance
+// u lives at f * cell_stride + (u * C + q) * cell_block(T, C, nb)
+// + (t - c_lo) * nb + k, where q is the cluster rank whose frame slice
+// [c_lo, c_hi) holds t: every CTA's block starts on a 16-byte boundary.
+__host__ __device__ inline int64_t cell_block(int T, int C, int nb) {
+  return ((int64_t)((T + C - 1) / C) * nb + 3) & ~(int64_t)3;
+}
+
+// Fields of the per (frame, band) record the forward chain saves for its
+// adjoint: the disturbance, the clamped asymmetry factor and the derivatives
+// of the two scaled spectra's gradients w.r.t. the gradients of those two,
+//   g_ed = g_dist * ed_dist + g_asc * ed_asc,  g_er = g_dist * er_dist + g_asc * er_asc.
+enum CellField { kCellDist = 0, kCellAsc, kCellEdDist, kCellEdAsc, kCellErDist, kCellErAsc, kCellFields };
 
 struct ChainBwdArgs {
   int batch;
@@ -150,6 +169,8 @@ struct ChainBwdArgs {
   float* g_bark;            // [2B][T][nb]  out
   float* kappa;             // [2B]         out
   int staged;               // Bark slice and its gradients live in shared memory
+  const float* cells;       // the forward's adjoint coefficients (see CellField)
+  int64_t cell_stride;
 };
 
 struct ResampleArgs {

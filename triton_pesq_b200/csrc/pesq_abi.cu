@@ -117,7 +117,8 @@ struct Geometry {
   int grad_begin, grad_end;
   ChainLayout lay;
   // byte offsets
-  size_t x16, x16lo, partial, sumsq, bark, z, spec, saved, gbark, kappa, cscratch, gx16, err, total;
+  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, err, total;
+  int64_t cell_stride;  // floats between the fields of the chain's adjoint coefficients
 };
 
 void balance(int64_t n16, int max_frames, int& seg, int& nseg) {
@@ -178,9 +179,12 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.partial = take(rows * g.nseg * 8);
   g.sumsq = take(rows * 8);
   g.bark = take(rows * (size_t)g.T * g.nb * 4);
+  g.fpow = take(g.grad ? rows * g.n16 * 4 : 0);
   g.z = take(g.grad ? rows * g.n16 * 4 : 0);
   g.spec = take(g.grad ? rows * (size_t)g.T * kBins * 8 : 0);
   g.saved = take((size_t)batch * g.lay.stride * 4);
+  g.cell_stride = (int64_t)batch * g.cluster * cell_block(g.T, g.cluster, g.nb);
+  g.cells = take(g.grad ? (size_t)kCellFields * g.cell_stride * 4 : 0);
   g.gbark = take(g.grad ? rows * (size_t)g.T * g.nb * 4 : 0);
   g.kappa = take(g.grad ? rows * 4 : 0);
   g.cscratch = take(g.grad ? (size_t)batch * 2 * g.T * 4 : 0);
@@ -470,6 +474,7 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64
   fa.bark = at<float>(ws, g.bark);
   fa.partial = at<double>(ws, g.partial);
   fa.spec = at<Cx<float>>(ws, g.spec);
+  fa.fpow = at<float>(ws, g.fpow);
   fa.err = at<uint32_t>(ws, g.err);
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
   return PESQ_OK;
@@ -500,6 +505,8 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ca.mos = mos;
   ca.loss = loss;
   ca.staged = g.fwd_staged;
+  ca.cells = g.grad ? at<float>(ws, g.cells) : nullptr;
+  ca.cell_stride = g.cell_stride;
   PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, static_cast<cudaStream_t>(stream)), "chain forward kernel");
   return PESQ_OK;
 }
@@ -542,12 +549,14 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   cb.g_bark = at<float>(ws, g.gbark);
   cb.kappa = at<float>(ws, g.kappa);
   cb.staged = g.bwd_staged;
+  cb.cells = at<float>(ws, g.cells);
+  cb.cell_stride = g.cell_stride;
   PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, static_cast<cudaStream_t>(stream)), "chain backward kernel");
   return PESQ_OK;
 }
 
-int pesq_backward_align(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
-                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes) {
+int pesq_backward_align(const pesq_plan* p, void* stream, int64_t batch, int64_t n_src, uint32_t flags, void* ws,
+                        size_t ws_bytes) {
   if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
   Geometry g;
   int rc = geometry(p, batch, n_src, flags, g);
@@ -557,17 +566,7 @@ int pesq_backward_align(const pesq_plan* p, void* stream, const float* ref, int6
   rc = check_call(p, g, ws, ws_bytes);
   if (rc) return rc;
   AlignArgs aa{};
-  if (g.resample) {
-    // the 16 kHz rows the forward resampled into the workspace
-    float* x16 = at<float>(ws, g.x16);
-    aa.src = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
-  } else {
-    if ((flags & PESQ_GRAD_REF) && (!ref || ld_ref < n_src))
-      return fail(PESQ_ERR_INVALID_ARGUMENT, "the backward needs the reference rows");
-    if ((flags & PESQ_GRAD_DEG) && (!deg || ld_deg < n_src))
-      return fail(PESQ_ERR_INVALID_ARGUMENT, "the backward needs the degraded rows");
-    aa.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
-  }
+  aa.fpow = at<float>(ws, g.fpow);
   aa.row_begin = g.grad_begin;
   aa.n = g.n16;
   aa.seg_frames = g.seg;
@@ -637,9 +636,13 @@ int pesq_backward(const pesq_plan* p, void* stream, const float* ref, int64_t ld
                   int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
                   const float* g_loss, const float* g_mos, const float* g_dsymm, const float* g_dasymm,
                   float* g_ref, int64_t ld_gref, float* g_deg, int64_t ld_gdeg) {
+  (void)ref;
+  (void)ld_ref;
+  (void)deg;
+  (void)ld_deg;
   int rc = pesq_backward_chain(p, stream, batch, n_src, flags, ws, ws_bytes, g_loss, g_mos, g_dsymm, g_dasymm);
   if (rc) return rc;
-  rc = pesq_backward_align(p, stream, ref, ld_ref, deg, ld_deg, batch, n_src, flags, ws, ws_bytes);
+  rc = pesq_backward_align(p, stream, batch, n_src, flags, ws, ws_bytes);
   if (rc) return rc;
   return pesq_backward_back(p, stream, batch, n_src, flags, ws, ws_bytes, g_ref, ld_gref, g_deg, ld_gdeg);
 }
