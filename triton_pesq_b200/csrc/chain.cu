@@ -61,7 +61,14 @@ ChainLayout ChainLayout::make(int T, int nb) {
 }
 
 int chain_slice_frames(int T, int cluster) { return (int)ceil_div(T, cluster); }
-size_t chain_fwd_smem_bytes(int slice, int nb) { return (size_t)2 * (slice + 1) * nb * sizeof(float); }
+// Bark spectra of the slice and the frame before it; with `cells`, also the
+// slice's adjoint coefficients, written to shared memory and stored with one
+// bulk copy per field
+size_t chain_fwd_smem_bytes(int slice, int nb, bool cells) {
+  const size_t spectra = ((size_t)2 * (slice + 1) * nb + 3) & ~(size_t)3;
+  const size_t cblk = ((size_t)slice * nb + 3) & ~(size_t)3;
+  return (spectra + (cells ? (size_t)kCellFields * cblk : 0)) * sizeof(float);
+}
 // Bark spectra and their gradient accumulators (4 slices), the forward's
 // adjoint coefficients of the slice (kCellFields slices), the ten per-frame
 // saved arrays and two per-frame gradients of frames c_lo..c_hi, and the two
@@ -134,8 +141,10 @@ struct Cell {
     u = ld - lr;
     zz = fabsf(u) - 0.25f * fminf(ld, lr);
     dist = sgnf(u) * fmaxf(zz, 0.0f);
-    // ((ed + 50) / (er + 50))^1.2
-    asc_raw = expf(1.2f * logf((ed + 50.0f) / (er + 50.0f)));
+    // ((ed + 50) / (er + 50))^1.2 with the hardware exp2 / log2 (about
+    // 1e-6 relative: asc only enters through its clamp to [3, 12] and the
+    // asymmetric norm)
+    asc_raw = exp2f_fast(1.2f * log2f_fast(__fdividef(ed + 50.0f, er + 50.0f)));
     asc = asc_raw < 3.0f ? 0.0f : fminf(asc_raw, 12.0f);
   }
   // The adjoint of eval for the two norms' gradients g_dist and g_asc, as the
@@ -239,6 +248,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     origin = (int64_t)t_first * nb;
   }
   cp_async_commit();
+  // adjoint coefficients of the slice: staged in shared memory after the
+  // spectra when they fit (p.stage_cells), else stored directly
+  const int64_t cblk = cell_block(T, C, nb);
+  float* cst = nullptr;
+  if (p.cells && p.staged && p.stage_cells) cst = dsm + ((2 * (sl.c_hi - sl.c_lo + 1) * nb + 3) & ~3);
   if (warp < 2) {
     // level alignment power of both rows, loss.py:132-136
     const int r = warp == 0 ? u : B + u;
@@ -347,7 +361,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       const float fpr0 = (taer + 5e3f) / (tad + 5e3f);
       const float fpr1 = t == 0 ? fpr0 : fpr0 * 0.8f + fpr0_prev * 0.2f;
       const float fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
-      const float h = expf(0.04f * logf((taer + 1e5f) / 1e7f));
+      const float h = exp2f_fast(0.04f * log2f_fast((taer + 1e5f) * 1e-7f));
       Cell c0, c1;
       c0.eval(b0, R0, D0, bpr0, fpr);
       c1.eval(b1, R1, D1, bpr1, fpr);
@@ -359,13 +373,16 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
           if (!b.ok) continue;
           float co[4];
           c.adjoint(b, co);
-          float* dst = p.cells + ((int64_t)u * C + q) * cell_block(T, C, nb) + (t - sl.c_lo) * nb + b.k;
-          dst[kCellDist * p.cell_stride] = c.dist;
-          dst[kCellAsc * p.cell_stride] = c.asc;
-          dst[kCellEdDist * p.cell_stride] = co[0];
-          dst[kCellEdAsc * p.cell_stride] = co[1];
-          dst[kCellErDist * p.cell_stride] = co[2];
-          dst[kCellErAsc * p.cell_stride] = co[3];
+          const int i = (t - sl.c_lo) * nb + b.k;
+          // shared memory block (bulk-stored after the pass) or straight to global
+          float* dst = cst ? cst + i : p.cells + ((int64_t)u * C + q) * cblk + i;
+          const int64_t fs = cst ? cblk : p.cell_stride;
+          dst[kCellDist * fs] = c.dist;
+          dst[kCellAsc * fs] = c.asc;
+          dst[kCellEdDist * fs] = co[0];
+          dst[kCellEdAsc * fs] = co[1];
+          dst[kCellErDist * fs] = co[2];
+          dst[kCellErAsc * fs] = co[3];
         }
       }
       float qs = 0.0f, qa = 0.0f;
@@ -399,7 +416,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       fpr0_prev = fpr0;
     }
   }
-  __threadfence();
+  if (cst) {
+    // the slice's coefficients: one bulk copy per field
+    fence_proxy_async_shared();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float* dst = p.cells + ((int64_t)u * C + q) * cblk;
+      for (int f = 0; f < kCellFields; ++f)
+        bulk_s2g(dst + f * p.cell_stride, cst + f * cblk, (uint32_t)(cblk * sizeof(float)));
+      bulk_commit();
+    }
+  }
   cluster_sync();
   PESQ_STAMP(g_phase_chain_fwd, 3);
 
@@ -422,7 +449,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       if (lane == 0) sv[dst + l] = mx * powf(m6, 1.0f / 6.0f);
     }
   }
-  __threadfence();
   cluster_sync();
   PESQ_STAMP(g_phase_chain_fwd, 4);
 
@@ -455,6 +481,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       if (p.loss) p.loss[u] = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
     }
   }
+  if (cst && threadIdx.x == 0) bulk_wait_all();
   PESQ_STAMP(g_phase_chain_fwd, 5);
 }
 
@@ -649,7 +676,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       }
     }
   }
-  __threadfence();
   cluster_sync();
   PESQ_STAMP(g_phase_chain_bwd, 2);
 
@@ -784,7 +810,7 @@ cudaError_t configure_chain() {
 
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s) {
   const int slice = chain_slice_frames(a.lay.T, cluster);
-  const size_t smem = a.staged ? chain_fwd_smem_bytes(slice, a.lay.nb) : 0;
+  const size_t smem = a.staged ? chain_fwd_smem_bytes(slice, a.lay.nb, a.cells && a.stage_cells) : 0;
   return launch_cluster(chain_fwd_kernel, a, a.batch, cluster, smem, s);
 }
 

@@ -109,6 +109,11 @@ __device__ __forceinline__ uint32_t cluster_nctarank() {
 }
 
 // Full cluster barrier with release/acquire semantics on shared::cluster.
+// Cluster-wide barrier.  The release / acquire pair orders every memory
+// access of the arriving threads (shared, distributed shared and global)
+// before the accesses of all cluster threads after the wait, so values that
+// one CTA writes to global memory before the barrier are read by the other
+// CTAs of its cluster after it (through L2, ld.global.cg) without a fence.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -137,6 +142,19 @@ __device__ __forceinline__ double dsmem_ld_f64(uint32_t addr) {
 
 __device__ __forceinline__ void dsmem_st_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Hardware base-2 exponential and logarithm (ex2.approx / lg2.approx, about
+// 2^-22 relative error), for quantities whose use tolerates it.
+__device__ __forceinline__ float exp2f_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float log2f_fast(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ---------------------------------------------------------------------------
@@ -243,50 +261,25 @@ __device__ __forceinline__ void copy_async(void* dst, const void* src, int bytes
 }
 
 // ---------------------------------------------------------------------------
-// 1D bulk copy (TMA) global -> shared, completion on an mbarrier
+// bulk copy (TMA, no multicast) shared -> global
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(bar)),
-               "r"(count)
+// Makes this thread's earlier generic-proxy writes to shared memory visible
+// to the async proxy (bulk copies); followed by a CTA barrier before the copy.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// shared to global memory, tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"((uint32_t)__cvta_generic_to_shared(src)), "r"(bytes)
                : "memory");
 }
-
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned).
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          (uint32_t)__cvta_generic_to_shared(dst)),
-      "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
-      : "memory");
-}
-
-// Bounded wait on phase `parity` of an mbarrier.  Returns false when the wait
-// gave up; the caller records the failure instead of spinning forever.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = (uint32_t)__cvta_generic_to_shared(bar);
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the issuing thread's bulk copies have completed (their writes are done)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Device-side error flags, OR-ed into a word the host reads back on demand.
 enum : uint32_t {

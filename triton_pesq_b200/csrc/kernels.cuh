@@ -135,6 +135,7 @@ struct ChainFwdArgs {
   // gradient requested), see CellField and cell_block
   float* cells;
   int64_t cell_stride;
+  int stage_cells;          // write them to shared memory first (when staged and they fit)
 };
 
 // Layout of the adjoint coefficients: field f of frame t, band k of utterance
@@ -233,7 +234,7 @@ cudaError_t configure_chain();
 // frames of the largest cluster slice, and the dynamic shared memory of the
 // staged forward / backward chain kernels for it
 int chain_slice_frames(int T, int cluster);
-size_t chain_fwd_smem_bytes(int slice, int nb);
+size_t chain_fwd_smem_bytes(int slice, int nb, bool cells);
 size_t chain_bwd_smem_bytes(int slice, int nb);
 size_t chain_smem_limit();
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);

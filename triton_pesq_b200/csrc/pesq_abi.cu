@@ -112,7 +112,7 @@ struct Geometry {
   int T, L, nb;
   int seg, nseg;  // segmentation of a row
   int cluster;
-  bool fwd_staged, bwd_staged;
+  bool fwd_staged, fwd_stage_cells, bwd_staged;
   bool resample, grad;
   int grad_begin, grad_end;
   ChainLayout lay;
@@ -159,7 +159,8 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
   {
     const int slice = chain_slice_frames(g.T, g.cluster);
-    g.fwd_staged = chain_fwd_smem_bytes(slice, p->nb) <= chain_smem_limit();
+    g.fwd_staged = chain_fwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
+    g.fwd_stage_cells = chain_fwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
     g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb) <= chain_smem_limit();
   }
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
@@ -507,6 +508,7 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ca.staged = g.fwd_staged;
   ca.cells = g.grad ? at<float>(ws, g.cells) : nullptr;
   ca.cell_stride = g.cell_stride;
+  ca.stage_cells = g.fwd_stage_cells;
   PESQ_CUDA_TRY(launch_chain_fwd(ca, g.cluster, static_cast<cudaStream_t>(stream)), "chain forward kernel");
   return PESQ_OK;
 }
