@@ -28,6 +28,8 @@
 namespace pesq {
 
 PESQ_PHASE_TABLE(g_phase_align)
+PESQ_SPAN_TABLE(g_span_align)
+PESQ_CTA_TABLE(g_cta_align)
 
 namespace {
 
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t a = (int64_t)seg * p.seg_frames * kHop;
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   const int64_t base = a - kHorizon;
+  PESQ_SPAN_BEGIN(g_span_align, 0);
+  PESQ_CTA_BEGIN(g_cta_align);
   PESQ_STAMP(g_phase_align, 0);
 
   // f on [a, send + kHorizon) at physical indices kHorizon.., zeros elsewhere
@@ -83,6 +87,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* zr = p.z + (int64_t)row * n_row;
   for (int i = tid; i < (int)(send - a); i += kThreads) zr[a + i] = xs[kHorizon + i];
   PESQ_STAMP(g_phase_align, 3);
+  PESQ_CTA_END(g_cta_align);
+  PESQ_SPAN_END(g_span_align, 0);
 
   // complete only after the kernel this one was released early from
   pdl_wait();

@@ -21,6 +21,8 @@
 namespace pesq {
 
 PESQ_PHASE_TABLE(g_phase_back)
+PESQ_SPAN_TABLE(g_span_back)
+PESQ_CTA_TABLE(g_cta_back)
 
 namespace {
 
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   // the span starts at frame t0 - 1, which overlaps the segment
   const int64_t base = a - kHop;
+  PESQ_SPAN_BEGIN(g_span_back, 0);
+  PESQ_CTA_BEGIN(g_cta_back);
   PESQ_STAMP(g_phase_back, 0);
 
   // constant tables (first copy group); z = H^T H x of the segment is only
@@ -132,6 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     outr[n] = fmaf(-kappa, zs[i], g);
   }
   PESQ_STAMP(g_phase_back, 4);
+  PESQ_CTA_END(g_cta_back);
+  PESQ_SPAN_END(g_span_back, 0);
 }
 
 }  // namespace

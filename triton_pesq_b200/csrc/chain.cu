@@ -82,6 +82,7 @@ size_t chain_bwd_smem_bytes(int slice, int nb) {
 size_t chain_smem_limit() { return kChainSmemLimit; }
 
 PESQ_PHASE_TABLE(g_phase_chain_fwd)
+PESQ_SPAN_TABLE(g_span_chain)
 PESQ_PHASE_TABLE(g_phase_chain_bwd)
 
 namespace {
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   const int B = p.batch, T = p.lay.T, L = p.lay.L;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const Slice sl(T);
+  PESQ_SPAN_BEGIN(g_span_chain, 0);
   PESQ_STAMP(g_phase_chain_fwd, 0);
 
   // tables and the slice's spectra are copied asynchronously while warps 0-1
@@ -483,6 +485,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   }
   if (cst && threadIdx.x == 0) bulk_wait_all();
   PESQ_STAMP(g_phase_chain_fwd, 5);
+  PESQ_SPAN_END(g_span_chain, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -503,6 +506,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   const int B = p.batch, T = p.lay.T, L = p.lay.L, nb = p.lay.nb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const Slice sl(T);
+  PESQ_SPAN_BEGIN(g_span_chain, 1);
   PESQ_STAMP(g_phase_chain_bwd, 0);
 
   // the next kernel on the stream (the align kernel, which reads nothing this
@@ -790,6 +794,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   // keep every CTA's shared memory alive until rank 0 has read it
   cluster_sync();
   PESQ_STAMP(g_phase_chain_bwd, 5);
+  PESQ_SPAN_END(g_span_chain, 1);
 }
 
 template <class Kernel, class Args>

@@ -22,10 +22,67 @@
     if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))        \
       name[(blockIdx.x ? 8 : 0) + (i)] = clock64();                                  \
   } while (0)
+// PESQ_SPAN(table, i) brackets a whole kernel on the global nanosecond timer:
+// slot i keeps the earliest CTA start, slot 8 + i the latest CTA end (the
+// host zeroes the table, then reads it, through table_read / table_clear).
+#define PESQ_SPAN_TABLE(name)                                                        \
+  __device__ unsigned long long name[16];                                            \
+  extern "C" int name##_read(unsigned long long* host) {                             \
+    return (int)cudaMemcpyFromSymbol(host, name, sizeof(unsigned long long) * 16);   \
+  }                                                                                  \
+  extern "C" int name##_clear() {                                                    \
+    unsigned long long init[16];                                                     \
+    for (int i = 0; i < 16; ++i) init[i] = i < 8 ? ~0ull : 0ull;                     \
+    return (int)cudaMemcpyToSymbol(name, init, sizeof(init));                        \
+  }
+__device__ __forceinline__ unsigned long long pesq_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define PESQ_SPAN_BEGIN(name, i) \
+  do {                           \
+    if (threadIdx.x == 0) atomicMin(&name[(i)], pesq_globaltimer()); \
+  } while (0)
+#define PESQ_SPAN_END(name, i)                                                \
+  do {                                                                        \
+    __syncthreads();                                                          \
+    if (threadIdx.x == 0) atomicMax(&name[8 + (i)], pesq_globaltimer());      \
+  } while (0)
+// Per-CTA start / end on the global timer (CTA b: slots 2b, 2b + 1), for up
+// to 4096 CTAs of one kernel.
+#define PESQ_CTA_TABLE(name)                                                         \
+  __device__ unsigned long long name[8192];                                          \
+  extern "C" int name##_read(unsigned long long* host) {                             \
+    return (int)cudaMemcpyFromSymbol(host, name, sizeof(unsigned long long) * 8192); \
+  }
+#define PESQ_CTA_BEGIN(name) \
+  do {                       \
+    if (threadIdx.x == 0 && blockIdx.x < 4096) name[2 * blockIdx.x] = pesq_globaltimer(); \
+  } while (0)
+#define PESQ_CTA_END(name)                                                                    \
+  do {                                                                                        \
+    __syncthreads();                                                                          \
+    if (threadIdx.x == 0 && blockIdx.x < 4096) name[2 * blockIdx.x + 1] = pesq_globaltimer(); \
+  } while (0)
 #else
+#define PESQ_CTA_TABLE(name)
+#define PESQ_CTA_BEGIN(name) \
+  do {                       \
+  } while (0)
+#define PESQ_CTA_END(name) \
+  do {                     \
+  } while (0)
 #define PESQ_PHASE_TABLE(name)
 #define PESQ_STAMP(name, i) \
   do {                      \
+  } while (0)
+#define PESQ_SPAN_TABLE(name)
+#define PESQ_SPAN_BEGIN(name, i) \
+  do {                           \
+  } while (0)
+#define PESQ_SPAN_END(name, i) \
+  do {                         \
   } while (0)
 #endif
 

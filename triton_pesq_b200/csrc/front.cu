@@ -30,6 +30,8 @@
 namespace pesq {
 
 PESQ_PHASE_TABLE(g_phase_front)
+PESQ_SPAN_TABLE(g_span_front)
+PESQ_CTA_TABLE(g_cta_front)
 
 namespace {
 
@@ -59,6 +61,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t base = a - kHorizon;
   const float* xr = p.src.row(row);
   const bool grad_row = row >= p.spec_begin && row < p.spec_end;
+  PESQ_SPAN_BEGIN(g_span_front, 0);
+  PESQ_CTA_BEGIN(g_cta_front);
   PESQ_STAMP(g_phase_front, 0);
 
   // constant tables, copied in the background of the span staging
@@ -97,28 +101,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (grad_row) {
     float* fr = p.fpow + (int64_t)row * n_row;
     for (int i = tid; i < (int)(send - a); i += kThreads) fr[a + i] = fb[kHorizon + i];
-    if (has_lo) {
-      __syncthreads();
-      stage_span(fb, p.src_lo.row(row), base, n_row);
-      __syncthreads();
+    __syncthreads();
+    if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
+  }
+  // x = xs + fb from here on (fb = 0 for a 16 kHz input)
+  if (!has_lo)
+    for (int i = tid; i < kSpan; i += kThreads) fb[i] = 0.0f;
+  __syncthreads();
+  // 2. edge fade (15 samples at each end of the row), in place: the product
+  //    of x with the ramp value k/16 is exact in double and splits exactly
+  //    into a float hi/lo pair
+  if (tid < 30) {
+    const int64_t n = tid < 15 ? tid : n_row - 30 + tid;
+    const int idx = (int)(n - base);
+    // (a sample in both ranges, possible only for rows shorter than 30, is
+    // handled once, by the head branch)
+    if (n >= 0 && n < n_row && (tid < 15 || n >= 15) && idx >= 0 && idx < kSpan) {
+      const double head = n < 15 ? (double)(n + 1) * 0.0625 : 1.0;
+      const double tail = n >= n_row - 15 ? (double)(n_row - n) * 0.0625 : 1.0;
+      const double v = (((double)xs[idx] + (double)fb[idx]) * head) * tail;
+      const float hi = (float)v;
+      xs[idx] = hi;
+      fb[idx] = (float)(v - (double)hi);
     }
   }
+  __syncthreads();
   PESQ_STAMP(g_phase_front, 2);
 
-  // 3. edge fade + pre-emphasis in double precision; y = hi + lo with hi in
-  //    xs (in place) and lo in fb; the padding after the row end is 0
+  // 3. pre-emphasis in double precision; y = hi + lo with hi in xs (in
+  //    place) and lo in fb; the padding after the row end is 0
+  const int q_end = (int)min((int64_t)kSpan, n_row - base);
   chunk_scan<2, true, double>(
-      pre, reinterpret_cast<double*>(scratch),
-      [&](int q) {
-        const int64_t n = base + q;
-        if (n < 0 || n >= n_row) return 0.0;
-        const double head = n < 15 ? (double)(n + 1) * 0.0625 : 1.0;
-        const double tail = n >= n_row - 15 ? (double)(n_row - n) * 0.0625 : 1.0;
-        const double v = has_lo ? (double)xs[q] + (double)fb[q] : (double)xs[q];
-        return (v * head) * tail;
-      },
+      pre, reinterpret_cast<double*>(scratch), [&](int q) { return (double)xs[q] + (double)fb[q]; },
       [&](int q, double y) {
-        if (base + q >= n_row) y = 0.0;
+        if (q >= q_end) y = 0.0;
         const float hi = (float)y;
         xs[q] = hi;
         fb[q] = (float)(y - (double)hi);
@@ -164,6 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
   PESQ_STAMP(g_phase_front, 4);
+  PESQ_CTA_END(g_cta_front);
+  PESQ_SPAN_END(g_span_front, 0);
 }
 
 }  // namespace
