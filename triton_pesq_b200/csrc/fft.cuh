@@ -17,7 +17,8 @@
 // conflict (per quarter warp for the 16-byte complex double, per half warp for
 // the 8-byte complex float), and the pairing of bin f with bin 256 - f that
 // the real-signal post-processing needs is a warp shuffle from lane 32 - l.
-// Twiddles are read from tables laid out in the order the lanes use them.
+// Twiddles are read from tables laid out in the order the lanes use them (in
+// double precision: one entry per stage and lane, the rest by products).
 //
 // The real spectrum follows from X[f] = E[f] + w512^f O[f] with
 // E = (Z[f] + conj Z[256-f]) / 2 and O = -i (Z[f] - conj Z[256-f]) / 2.
@@ -123,6 +124,33 @@ __device__ __forceinline__ void dft8(Cx<R> v[8]) {
   v[7] = c_sub(e3, o3);
 }
 
+// Powers w^1 .. w^7 of a twiddle, pw[k - 1] = w^k, by complex products (a few
+// ulp in double precision): the double precision transform derives its
+// per-lane twiddles this way from one table entry instead of reading seven.
+template <class R>
+__device__ __forceinline__ void twiddle_powers(Cx<R> w, Cx<R> pw[7]) {
+  pw[0] = w;
+  pw[1] = c_mul(w, w);
+  pw[2] = c_mul(pw[1], w);
+  pw[3] = c_mul(pw[1], pw[1]);
+  pw[4] = c_mul(pw[3], w);
+  pw[5] = c_mul(pw[2], pw[2]);
+  pw[6] = c_mul(pw[5], w);
+}
+
+// Per-lane twiddles of stage 1 (w256^{l q}) and stage 2 (w32^{r q}), q = 1..7:
+// table reads in single precision, products of one table entry in double.
+template <class R>
+__device__ __forceinline__ Cx<R> stage1_twiddle(const FftTwiddles<R>& tw, const Cx<R>* pw, int q, int lane) {
+  if constexpr (sizeof(R) == 8) return pw[q - 1];
+  else return tw.lane[q - 1][lane];
+}
+template <class R>
+__device__ __forceinline__ Cx<R> stage2_twiddle(const FftTwiddles<R>& tw, const Cx<R>* pw, int q, int r) {
+  if constexpr (sizeof(R) == 8) return pw[q - 1];
+  else return tw.quarter[r][q];
+}
+
 // Forward 256-point complex DFT of one warp, Z[f] = sum_n z[n] w256^{n f}.
 // On entry v[m] = z[lane + 32 m], on exit v[m] = Z[lane + 32 m].  `sh` is the
 // warp's FftLayout<R>::kSlots elements of shared memory; the call starts and
@@ -131,9 +159,11 @@ template <class R>
 __device__ __forceinline__ void warp_dft256(Cx<R> v[8], Cx<R>* sh, const FftTwiddles<R>& tw, int lane) {
   using L = FftLayout<R>;
   const int q = lane & 7, r = lane >> 3;
+  Cx<R> pw[7];
+  if constexpr (sizeof(R) == 8) twiddle_powers(tw.lane[0][lane], pw);
   dft8<-1>(v);
 #pragma unroll
-  for (int k = 1; k < 8; ++k) v[k] = c_mul(v[k], tw.lane[k - 1][lane]);
+  for (int k = 1; k < 8; ++k) v[k] = c_mul(v[k], stage1_twiddle(tw, pw, k, lane));
 #pragma unroll
   for (int k = 0; k < 8; ++k) sh[k * L::kP1 + lane] = v[k];
   __syncwarp();
@@ -141,9 +171,10 @@ __device__ __forceinline__ void warp_dft256(Cx<R> v[8], Cx<R>* sh, const FftTwid
 #pragma unroll
   for (int i = 0; i < 8; ++i) a[i] = sh[q * L::kP1 + r + 4 * i];
   __syncwarp();
+  if constexpr (sizeof(R) == 8) twiddle_powers(tw.quarter[r][1], pw);
   dft8<-1>(a);
 #pragma unroll
-  for (int j = 1; j < 8; ++j) a[j] = c_mul(a[j], tw.quarter[r][j]);
+  for (int j = 1; j < 8; ++j) a[j] = c_mul(a[j], stage2_twiddle(tw, pw, j, r));
 #pragma unroll
   for (int j = 0; j < 8; ++j) sh[q * L::kQ2 + r * L::kR2 + j] = a[j];
   __syncwarp();
@@ -216,18 +247,38 @@ __device__ __forceinline__ void warp_mirror_bins(const Cx<R> v[8], Cx<R> p[8], i
 // Real spectrum of a 512-sample frame given lane l's packed inputs
 // v[m] = (u[2n], u[2n+1]), n = l + 32 m.  On exit X[m] holds bin
 // f = lane + 32 m (bins 0..255); `sh` is clobbered.
+// exp(-2 pi i m / 16), m = 0..7 (cos and sin of multiples of pi / 8)
+template <class R>
+__device__ __forceinline__ Cx<R> w16(int m) {
+  const R c1 = R(0.92387953251128675613), s1 = R(0.38268343236508977173), h = R(0.70710678118654752440);
+  switch (m) {
+    case 0: return mk(R(1), R(0));
+    case 1: return mk(c1, -s1);
+    case 2: return mk(h, -h);
+    case 3: return mk(s1, -c1);
+    case 4: return mk(R(0), R(-1));
+    case 5: return mk(-s1, -c1);
+    case 6: return mk(-h, -h);
+    default: return mk(-c1, -s1);
+  }
+}
+
 template <class R>
 __device__ __forceinline__ void warp_rfft512(Cx<R> v[8], Cx<R>* sh, const FftTwiddles<R>& tw, int lane,
                                              Cx<R> X[8]) {
   warp_dft256(v, sh, tw, lane);
   Cx<R> p[8];
   warp_mirror_bins(v, p, lane);
+  const Cx<R> wl = tw.bin[lane];  // w512^lane; w512^(lane + 32 m) = w512^lane w16^m
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
     const Cx<R> zc = c_conj(p[m]);
     const Cx<R> e = c_scale(c_add(v[m], zc), R(0.5));
     const Cx<R> o = c_scale(c_rot90<-1>(c_sub(v[m], zc)), R(0.5));
-    X[m] = c_add(e, c_mul(tw.bin[lane + 32 * m], o));
+    Cx<R> w;
+    if constexpr (sizeof(R) == 8) w = m == 0 ? wl : (m == 4 ? c_rot90<-1>(wl) : c_mul(wl, w16<R>(m)));
+    else w = tw.bin[lane + 32 * m];
+    X[m] = c_add(e, c_mul(w, o));
   }
 }
 
