@@ -27,8 +27,13 @@ PESQ_CTA_TABLE(g_cta_back)
 namespace {
 
 constexpr int kSegMax = kSpan - kHorizon - 3 * kHop;  // samples of the longest segment
+// frames a CTA processes: one before its segment, the segment (<= 57 frames)
+// and those reaching kHorizon past its end
+constexpr int kBackFrames = 64;
+static_assert((kSpan - 2 * kHorizon) / kHop + 6 <= kBackFrames, "frames of the longest segment");
 constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * FftLayout<float>::kSlots * 8 +
-                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4;
+                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4 +
+                               kBackFrames * kMaxBands * 4;
 
 __global__ void __launch_bounds__(kThreads, 1)
     back_kernel(const __grid_constant__ BackArgs p, const __grid_constant__ PreTab pre) {
@@ -39,6 +44,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* gb = reinterpret_cast<float*>(fft + kWarps * FftLayout<float>::kSlots);  // per warp kMaxBands
   DevTables* tab = reinterpret_cast<DevTables*>(gb + kWarps * kMaxBands);
   float* zs = reinterpret_cast<float*>(tab + 1);  // z on [a, send), staged asynchronously
+  float* gs = zs + kSegMax;                       // dL/dB of frames t_lo..t_hi
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = p.row_begin + blockIdx.x / p.nseg;
@@ -52,10 +58,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_CTA_BEGIN(g_cta_back);
   PESQ_STAMP(g_phase_back, 0);
 
-  // constant tables (first copy group); z = H^T H x of the segment is only
-  // needed at the very end, its copy (second group) runs in the background of
-  // the frame loop
+  // frames that touch [a, send + kHorizon)
+  const int nb = p.nb;
+  const int t0 = seg * p.seg_frames;
+  const int t_lo = max(0, t0 - 1);
+  const int t_hi = min(p.frames - 1, (int)((send + kHorizon - 1) / kHop));
+
+  // first copy group: constant tables and dL/dB of the CTA's frames; second
+  // group: z = H^T H x of the segment, only needed at the very end, copied in
+  // the background of the frame loop
   copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
+  {
+    const float* src = p.g_bark + ((int64_t)row * p.frames + t_lo) * nb;
+    const int cnt = (t_hi - t_lo + 1) * nb;
+    for (int i = tid; i < cnt; i += kThreads) cp_async4(gs + i, src + i);
+  }
   cp_async_commit();
   for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
   const float* zr = p.z + (int64_t)row * n_row;
@@ -65,32 +82,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   PESQ_STAMP(g_phase_back, 1);
 
-  // frames that touch [a, send + kHorizon)
-  const int nb = tab->nb;
-  const int t0 = seg * p.seg_frames;
-  const int t_lo = max(0, t0 - 1);
-  const int t_hi = min(p.frames - 1, (int)((send + kHorizon - 1) / kHop));
   const float kappa = p.kappa[row];
   Cx<float>* sh = fft + warp * FftLayout<float>::kSlots;
   float* gbw = gb + warp * kMaxBands;
+  int band_of[8];  // band of bin lane + 32 m (-1: none)
+#pragma unroll
+  for (int m = 0; m < 8; ++m) band_of[m] = tab->bin_band[lane + 32 * m];
 
   for (int parity = 0; parity < 2; ++parity) {
     const int first = t_lo + ((t_lo & 1) != parity ? 1 : 0);
+    // the saved spectrum of the warp's next frame is loaded one frame ahead
+    Cx<float> X[8];
+    auto load_spec = [&](int t, Cx<float> dst[8]) {
+      const Cx<float>* spec = p.spec + ((int64_t)row * p.frames + t) * kBins;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) dst[m] = spec[lane + 32 * m];
+    };
+    if (first + 2 * warp <= t_hi) load_spec(first + 2 * warp, X);
     for (int t = first + 2 * warp; t <= t_hi; t += 2 * kWarps) {
+      Cx<float> Xn[8];
+      if (t + 2 * kWarps <= t_hi) load_spec(t + 2 * kWarps, Xn);
       const int off = (int)(t * (int64_t)kHop - base);
-      const int64_t frame = (int64_t)row * p.frames + t;
-      const float* gsrc = p.g_bark + frame * nb;
+      const float* gsrc = gs + (t - t_lo) * nb;
       for (int b = lane; b < nb; b += 32) gbw[b] = gsrc[b] * tab->band_corr[b];
       __syncwarp();
       // V_f = dL/dP_f * X_f, with dL/dP_f = corr_b dL/dB_b for the band b of bin f
-      const Cx<float>* spec = p.spec + frame * kBins;
       Cx<float> V[8];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int f = lane + 32 * m;
-        const int b = tab->bin_band[f];
-        V[m] = c_scale(spec[f], b >= 0 ? gbw[b] : 0.0f);
-      }
+      for (int m = 0; m < 8; ++m) V[m] = c_scale(X[m], band_of[m] >= 0 ? gbw[band_of[m]] : 0.0f);
       Cx<float> g[8];
       warp_irfft512_adjoint(V, sh, tab->fft, lane, g);
       // overlap-add of the windowed frame gradient: samples 2n, 2n + 1 with
@@ -106,6 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         *dst = acc;
       }
       __syncwarp();
+#pragma unroll
+      for (int m = 0; m < 8; ++m) X[m] = Xn[m];
     }
     __syncthreads();
   }

@@ -88,6 +88,7 @@ struct AlignArgs {
 
 struct BackArgs {
   int row_begin;     // rows [row_begin, row_end) get a gradient
+  int nb;            // Bark bands
   int64_t n;
   int frames;
   int seg_frames;

@@ -598,6 +598,7 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   float* gx16 = at<float>(ws, g.gx16);
   BackArgs ba{};
   ba.row_begin = g.grad_begin;
+  ba.nb = g.nb;
   ba.n = g.n16;
   ba.frames = g.T;
   ba.seg_frames = g.seg;
