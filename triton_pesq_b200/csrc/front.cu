@@ -20,8 +20,8 @@
 // y and the spectrum are evaluated in double precision: the weak high bands
 // of speech sit 50-60 dB below the frame peak, where float32 rounding of the
 // signal would leave ~1e-4 relative error in their power, and the loss
-// gradient is most sensitive exactly there.  y is kept in shared memory as a
-// float hi/lo pair.
+// gradient is most sensitive exactly there.  y is kept in shared memory in
+// double precision.
 //
 // The CTA stages kSpan samples starting kHorizon before `a`: the first
 // kHorizon are the warm-up of the forward scans.
@@ -45,8 +45,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     front_kernel(const __grid_constant__ FrontArgs p, const __grid_constant__ PowTab pow,
                  const __grid_constant__ PreTab64 pre) {
   extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                 // kSpan: input, then y (hi part) in place
-  float* fb = xs + kSpan;           // kSpan: [f = H x,] low part of a resampled x, then y (lo part)
+  float* xs = smem;                 // kSpan: input (hi part)
+  float* fb = xs + kSpan;           // kSpan: [f = H x,] low part of a resampled x
+                                    // (xs, fb) then hold y as kSpan doubles
   float* scratch = fb + kSpan;      // scan scratch, later the per-warp FFT scratch
   DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
   DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
@@ -128,17 +129,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   PESQ_STAMP(g_phase_front, 2);
 
-  // 3. pre-emphasis in double precision; y = hi + lo with hi in xs (in
-  //    place) and lo in fb; the padding after the row end is 0
+  // 3. pre-emphasis in double precision, y written as doubles over the
+  //    (xs, fb) pair (every thread reads all of its inputs before the scan's
+  //    first barrier, so the overlapping in-place writes are safe); the
+  //    padding after the row end is 0
+  double* yd = reinterpret_cast<double*>(xs);
   const int q_end = (int)min((int64_t)kSpan, n_row - base);
   chunk_scan<2, true, double>(
       pre, reinterpret_cast<double*>(scratch), [&](int q) { return (double)xs[q] + (double)fb[q]; },
-      [&](int q, double y) {
-        if (q >= q_end) y = 0.0;
-        const float hi = (float)y;
-        xs[q] = hi;
-        fb[q] = (float)(y - (double)hi);
-      });
+      [&](int q, double y) { yd[q] = q < q_end ? y : 0.0; });
   __syncthreads();
   PESQ_STAMP(g_phase_front, 3);
 
@@ -154,10 +153,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       const int n = 2 * (lane + 32 * m);
-      const float2 hi = *reinterpret_cast<const float2*>(xs + off + n);
-      const float2 lo = *reinterpret_cast<const float2*>(fb + off + n);
+      const double2 y = *reinterpret_cast<const double2*>(yd + off + n);
       const float2 w = *reinterpret_cast<const float2*>(tab->window + n);
-      v[m] = mk(((double)hi.x + (double)lo.x) * (double)w.x, ((double)hi.y + (double)lo.y) * (double)w.y);
+      v[m] = mk(y.x * (double)w.x, y.y * (double)w.y);
     }
     warp_rfft512<double>(v, sh, *tw, lane, X);
     if (grad_row) {
