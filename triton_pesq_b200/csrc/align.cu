@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // z = H^T f on [a, send): logical position q at physical index top - q
   const int top = 2 * kHorizon + (int)(send - a) - 1;
-  chunk_scan<10, false, float>(
+  chunk_scan<10, false, float, true>(
       pow, scratch,
       [&](int q) {
         const int idx = top - q;

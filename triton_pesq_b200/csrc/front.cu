@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   //    on gradient rows f itself on [a, send), from which the align kernel of
   //    the backward evaluates the adjoint term H^T f
   double ssq = 0.0;
-  chunk_scan<10, false, float>(
+  chunk_scan<10, false, float, true>(
       pow, scratch, [&](int q) { return xs[q]; },
       [&](int q, float y) {
         const int64_t n = base + q;

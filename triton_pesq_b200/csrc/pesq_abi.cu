@@ -253,6 +253,14 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   p->factor = d->factor;
   int rc = fill_scan(p->pow, d->power_filter, "power filter");
   if (rc) return bail(rc);
+  // the kernels skip the structural zeros of the band pass's doubling
+  // matrices (a series of second order sections: block lower triangular)
+  for (int l = 0; l < kLevels; ++l)
+    for (int i = 0; i < 10; ++i)
+      for (int j = 0; j < 10; ++j)
+        if ((j >> 1) > (i >> 1) && p->pow.M[l][i][j] != 0.0f)
+          return bail(fail(PESQ_ERR_UNSUPPORTED,
+                           "level-alignment filter: the state matrix must be block lower triangular in 2 x 2 blocks"));
   rc = fill_scan(p->pre, d->pre_filter, "pre-emphasis filter");
   if (rc) return bail(rc);
   rc = fill_scan(p->pre64, d->pre_filter, "pre-emphasis filter");

@@ -51,7 +51,10 @@ __host__ __device__ constexpr int scan_scratch_floats() {
 // `load(p)` returns the input at logical position p (0 <= p < kSpan) and
 // `store(p, y)` consumes the output there.  `es` is scan scratch of
 // scan_scratch_floats<P, R>() floats.  Must be called by all kThreads threads.
-template <int P, bool kRerun, class R, class Load, class Store>
+// kBlockLower: A (hence every doubling matrix M) is block lower triangular in
+// 2 x 2 blocks, as for a series of second order sections; the structurally
+// zero entries above the block diagonal are skipped (the host checks them).
+template <int P, bool kRerun, class R, bool kBlockLower = false, class Load, class Store>
 __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load&& load, Store&& store) {
   const int c = threadIdx.x;
   const int p0 = c * kChunk;
@@ -85,7 +88,10 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load
     for (int i = 0; i < P; ++i) {
       R acc = e[i];
 #pragma unroll
-      for (int j = 0; j < P; ++j) acc = fma(tab.M[lv][i][j], prev[j], acc);
+      for (int j = 0; j < P; ++j) {
+        if (kBlockLower && (j >> 1) > (i >> 1)) continue;
+        acc = fma(tab.M[lv][i][j], prev[j], acc);
+      }
       e[i] = acc;
     }
 #pragma unroll
