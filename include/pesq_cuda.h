@@ -200,6 +200,42 @@ int pesq_forward_noalloc(const pesq_plan* plan, void* stream, const float* ref, 
                          int64_t ld_deg, int64_t batch, int64_t n_src, float* d_symm, float* d_asymm, float* mos,
                          float* loss);
 
+/* ---------------------------------------------------------------------------
+ * Standalone polyphase resampler: the reference's TritonResample
+ * (torch_pesq/triton_ops/resample.py:381-574), numerically torchaudio's
+ * Resample(orig_freq, new_freq) with float32 taps, accumulated in float64.
+ * Output m = l * new_step + j of a row is
+ *   y[m] = sum_k taps[j][k] x[l * orig_step + k - width],  x = 0 outside,
+ * for m < ceil(new_step * n_in / orig_step) (evaluated in float32).
+ * ------------------------------------------------------------------------- */
+typedef struct pesq_resampler pesq_resampler;
+
+typedef struct pesq_resample_desc {
+  int32_t abi_version;  /* PESQ_CUDA_ABI_VERSION */
+  int32_t orig_step;    /* orig_freq / gcd */
+  int32_t new_step;     /* new_freq / gcd */
+  int32_t width;        /* left zero padding of the input */
+  int32_t width_total;  /* taps per phase */
+  int32_t reserved0;
+  const double* taps;   /* [new_step * width_total], float32-valued */
+} pesq_resample_desc;
+
+/* Uploads the filter bank to the current device (replaces
+ * TritonResample.__init__, resample.py:490-528). */
+int pesq_resampler_create(const pesq_resample_desc* desc, pesq_resampler** out);
+int pesq_resampler_destroy(pesq_resampler* resampler);
+/* Output length for n_in input samples (resample.py:_target_length). */
+int pesq_resampler_length(const pesq_resampler* resampler, int64_t n_in, int64_t* n_out);
+/* y = A x for `rows` rows of n_in samples (row strides in elements; replaces
+ * _ResampleFunction.forward, resample.py:422-435). */
+int pesq_resample_forward(const pesq_resampler* resampler, void* stream, const float* x, int64_t ld_x,
+                          int64_t rows, int64_t n_in, float* y, int64_t ld_y);
+/* gx = A^T gy: the adjoint, a gather over input samples, deterministic
+ * (replaces _ResampleAdjoint.forward, resample.py:396-401).  n_in is the
+ * length of gx; gy has pesq_resampler_length(n_in) samples per row. */
+int pesq_resample_adjoint(const pesq_resampler* resampler, void* stream, const float* gy, int64_t ld_gy,
+                          int64_t rows, int64_t n_in, float* gx, int64_t ld_gx);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,100 @@
+"""Standalone resampler on the GPU against torchaudio's own resampling
+arithmetic in float64 with the same float32 filter bank (the reference's
+TritonResample tests, tests/test_triton_resample.py, compare against
+torchaudio.transforms.Resample the same way)."""
+
+import math
+
+import pytest
+import torch
+import torchaudio
+import torchaudio.functional.functional as TAF
+
+from triton_pesq_b200 import ResampleCuda
+
+pytestmark = pytest.mark.gpu
+
+RATES = [(44100, 16000), (48000, 16000), (8000, 16000), (22050, 16000), (16000, 48000), (16000, 44100)]
+
+
+def _reference64(x, module):
+    """torchaudio's polyphase convolution in float64 with the float32 taps."""
+
+    kernel = module.kernel.detach().cpu().double()[:, None, :]
+    return TAF._apply_sinc_resample_kernel(x.cpu().double(), module.orig_step, module.new_step, 1, kernel,
+                                           module.width)
+
+
+def _peak_err(got, want):
+    got = got.detach().double().cpu()
+    return float((got - want).abs().max() / max(want.abs().max(), 1e-30))
+
+
+@pytest.mark.parametrize("orig,new", RATES)
+@pytest.mark.parametrize("method", ["sinc_interp_hann", "sinc_interp_kaiser"])
+def test_forward_matches_torchaudio(cuda_device, orig, new, method):
+    g = torch.Generator().manual_seed(orig + new)
+    x = torch.randn(3, orig // 4 + 37, generator=g)
+    module = ResampleCuda(orig, new, resampling_method=method).to(cuda_device)
+    y = module(x.to(cuda_device))
+    want = _reference64(x, module)
+    assert y.shape == want.shape
+    # float64 accumulation of float32 products: one float32 rounding of the sum
+    assert _peak_err(y, want) < 1e-6
+    # and the float32 torchaudio module itself
+    ta = torchaudio.transforms.Resample(orig, new, resampling_method=method)(x)
+    assert _peak_err(y, ta.double()) < 1e-5
+
+
+def test_adjoint_and_double_backward(cuda_device):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 3000, generator=g, dtype=torch.float64)
+    module = ResampleCuda(44100, 16000).to(cuda_device)
+    xd = x.float().to(cuda_device).requires_grad_(True)
+    y = module(xd)
+    gy = torch.randn(y.shape, generator=g).to(cuda_device).requires_grad_(True)
+    (gx,) = torch.autograd.grad(y, xd, gy, create_graph=True)
+    # the gradient of torchaudio's float64 convolution with the same taps
+    xr = x.clone().requires_grad_(True)
+    (want,) = torch.autograd.grad(_reference64(xr, module), xr, gy.detach().double().cpu())
+    assert _peak_err(gx, want) < 1e-6
+    # double backward: d<gx, v>/d gy = A v, through the same kernels
+    v = torch.randn(x.shape, generator=g).to(cuda_device)
+    (ggy,) = torch.autograd.grad((gx * v).sum(), gy)
+    torch.testing.assert_close(ggy, module(v), rtol=0, atol=0)
+
+
+def test_leading_dims_strides_and_large_row_counts(cuda_device):
+    module = ResampleCuda(48000, 16000).to(cuda_device)
+    x = torch.randn(2, 3, 4800, device=cuda_device)
+    y = module(x)
+    assert y.shape == (2, 3, 1600)
+    torch.testing.assert_close(y[1, 2], module(x[1, 2][None])[0], rtol=0, atol=0)
+    wide = torch.randn(4, 9600, device=cuda_device)[:, ::2]  # strided samples
+    torch.testing.assert_close(module(wide), module(wide.contiguous()), rtol=0, atol=0)
+    many = torch.randn(70000, 30, device=cuda_device)  # more rows than grid y holds
+    out = module(many)
+    torch.testing.assert_close(out[69999], module(many[69999:])[0], rtol=0, atol=0)
+    assert module(torch.empty(0, 100, device=cuda_device)).shape == (0, 34)
+
+
+def test_short_inputs_and_determinism(cuda_device):
+    module = ResampleCuda(44100, 16000).to(cuda_device)
+    for n in (1, 5, 16, 17, 100):
+        x = torch.randn(2, n)
+        y = module(x.to(cuda_device))
+        assert _peak_err(y, _reference64(x, module)) < 1e-6
+    x = torch.randn(3, 50000, device=cuda_device).requires_grad_(True)
+    y1 = module(x)
+    g1 = torch.autograd.grad(y1.sum(), x)[0]
+    y2 = module(x)
+    g2 = torch.autograd.grad(y2.sum(), x)[0]
+    assert torch.equal(y1, y2) and torch.equal(g1, g2)
+
+
+def test_errors(cuda_device):
+    module = ResampleCuda(44100, 16000).to(cuda_device)
+    with pytest.raises(RuntimeError):
+        module(torch.randn(2, 100, device=cuda_device, dtype=torch.float64))
+    with pytest.raises(RuntimeError):
+        module(torch.randn(2, 100))

@@ -2,9 +2,12 @@
 
 ``PesqLossCuda`` is a drop-in for the reference's ``PesqLossTriton``
 (torch_pesq/triton_ops/loss.py) evaluated by hand-written sm_100a kernels
-through the C ABI of ``libpesq_cuda.so`` (``include/pesq_cuda.h``).
+through the C ABI of ``libpesq_cuda.so`` (``include/pesq_cuda.h``);
+``ResampleCuda`` is the reference's ``TritonResample`` (its polyphase sinc
+resampler as a standalone op) on the same library.
 """
 
 from .loss import PesqLossCuda
+from .resample import ResampleCuda
 
-__all__ = ["PesqLossCuda"]
+__all__ = ["PesqLossCuda", "ResampleCuda"]

@@ -77,6 +77,18 @@ class PlanDesc(ctypes.Structure):
     ]
 
 
+class ResampleDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("orig_step", ctypes.c_int32),
+        ("new_step", ctypes.c_int32),
+        ("width", ctypes.c_int32),
+        ("width_total", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("taps", ctypes.POINTER(ctypes.c_double)),
+    ]
+
+
 class Shape(ctypes.Structure):
     _fields_ = [("n16", ctypes.c_int64), ("frames", ctypes.c_int32), ("windows", ctypes.c_int32)]
 
@@ -130,6 +142,19 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p,
          ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64],
+    ),
+    "pesq_resampler_create": (ctypes.c_int, [ctypes.POINTER(ResampleDesc), ctypes.POINTER(ctypes.c_void_p)]),
+    "pesq_resampler_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "pesq_resampler_length": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]),
+    "pesq_resample_forward": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+         ctypes.c_void_p, ctypes.c_int64],
+    ),
+    "pesq_resample_adjoint": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+         ctypes.c_void_p, ctypes.c_int64],
     ),
     "pesq_forward_noalloc": (
         ctypes.c_int,
@@ -274,3 +299,21 @@ def query_shape(handle: int, n_src: int):
     shape = Shape()
     check(library().pesq_query_shape(ctypes.c_void_p(handle), int(n_src), ctypes.byref(shape)), "pesq_query_shape")
     return shape.n16, shape.frames, shape.windows
+
+
+def create_resampler(kernel) -> int:
+    """Upload a :class:`~triton_pesq_b200.tables.ResampleKernel` to the current
+    CUDA device; returns the resampler handle."""
+
+    lib = library()
+    taps = np.ascontiguousarray(kernel.taps, dtype=np.float64)
+    desc = ResampleDesc()
+    desc.abi_version = ABI_VERSION
+    desc.orig_step = int(kernel.orig_step)
+    desc.new_step = int(kernel.new_step)
+    desc.width = int(kernel.width)
+    desc.width_total = int(kernel.width_total)
+    desc.taps = _dptr(taps)
+    handle = ctypes.c_void_p()
+    check(lib.pesq_resampler_create(ctypes.byref(desc), ctypes.byref(handle)), "pesq_resampler_create")
+    return int(handle.value)

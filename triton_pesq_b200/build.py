@@ -26,7 +26,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpesq_cuda.so")
 OPS = os.path.join(HERE, "_pesq_torch_ops.so")
 
-CUDA_SOURCES = ["front.cu", "align.cu", "back.cu", "chain.cu", "resample.cu", "pesq_abi.cu", "noalloc.cu"]
+CUDA_SOURCES = ["front.cu", "align.cu", "back.cu", "chain.cu", "resample.cu", "pesq_abi.cu", "noalloc.cu",
+                "resample_abi.cu"]
 NVCC_FLAGS = [
     "-std=c++17",
     "-O3",

@@ -193,6 +193,27 @@ struct ResampleArgs {
   const int4* adj_entries; // (dl, phase, tap bits, 0)
 };
 
+// Device tables of one polyphase resampler: the compact nonzero taps of every
+// phase and the adjoint's per-residue gather lists, built on the host from
+// float32-valued taps [new_step][width_total].
+struct ResampleTables {
+  int orig_step = 0, new_step = 0, width = 0, max_count = 0;
+  float* taps = nullptr;        // [new_step][max_count]
+  int* first = nullptr;         // [new_step]
+  int* count = nullptr;         // [new_step]
+  int* adj_offset = nullptr;    // [orig_step + 1]
+  int4* adj_entries = nullptr;  // (frame offset, phase, tap bits, 0)
+};
+// Builds t on the current device; returns nullptr or a message.
+const char* build_resample_tables(int orig_step, int new_step, int width, int width_total, const double* taps,
+                                  ResampleTables& t);
+void free_resample_tables(ResampleTables& t);
+// Arguments of the resampler kernels for tables t, rows [row_begin, row_begin + rows).
+ResampleArgs resample_args(const ResampleTables& t, int64_t n_in, int64_t n_out);
+// Output length of the resampler: ceil(new_step * n / orig_step) evaluated
+// on a float32 scalar, as torchaudio does.
+int64_t resample_length(int orig_step, int new_step, int64_t n);
+
 // Launch configuration of one kernel; `pdl` adds programmatic stream
 // serialisation (the kernel may start while its predecessor on the stream
 // runs, see pdl_wait), `cluster` > 0 a thread block cluster dimension.

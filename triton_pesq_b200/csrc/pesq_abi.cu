@@ -37,14 +37,9 @@ struct pesq_plan {
   PreTab64 pre64;    // float64 tables: pre-emphasis of the front kernel
   DevTables* dtab;   // device copy
   DevTwiddle64* tw64;
-  // resampler
+  // resampler to 16 kHz (sample_rate != 16000)
   bool resample;
-  int orig_step, new_step, width, width_total, max_count;
-  float* taps;       // device [new_step][max_count]
-  int* first;        // device [new_step]
-  int* count;        // device [new_step]
-  int* adj_offset;   // device [orig_step + 1]
-  int4* adj_entries; // device
+  ResampleTables rs;
 };
 
 namespace {
@@ -129,8 +124,7 @@ void balance(int64_t n16, int max_frames, int& seg, int& nseg) {
 
 int64_t resampled_length(const pesq_plan* p, int64_t n) {
   if (!p->resample) return n;
-  const float q = (float)((double)p->new_step * (double)n / (double)p->orig_step);
-  return (int64_t)ceilf(q);
+  return resample_length(p->rs.orig_step, p->rs.new_step, n);
 }
 
 int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, Geometry& g) {
@@ -324,58 +318,9 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   // resampler tables
   p->resample = d->sample_rate != 16000;
   if (p->resample) {
-    const int os = d->rs_orig_step, ns = d->rs_new_step, wt = d->rs_width_total;
-    if (os <= 0 || ns <= 0 || wt <= 0 || d->rs_width < 0 || !d->rs_taps)
-      return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "invalid resampler description"));
-    p->orig_step = os;
-    p->new_step = ns;
-    p->width = d->rs_width;
-    p->width_total = wt;
-    std::vector<int> first(ns), count(ns);
-    int maxc = 1;
-    for (int j = 0; j < ns; ++j) {
-      int lo = -1, hi = -1;
-      for (int k = 0; k < wt; ++k)
-        if ((float)d->rs_taps[(size_t)j * wt + k] != 0.0f) {
-          if (lo < 0) lo = k;
-          hi = k;
-        }
-      first[j] = lo < 0 ? 0 : lo;
-      count[j] = lo < 0 ? 0 : hi + 1 - lo;
-      maxc = std::max(maxc, count[j]);
-    }
-    std::vector<float> taps((size_t)ns * maxc, 0.0f);
-    for (int j = 0; j < ns; ++j)
-      for (int i = 0; i < count[j]; ++i) taps[(size_t)j * maxc + i] = (float)d->rs_taps[(size_t)j * wt + first[j] + i];
-    p->max_count = maxc;
-    // adjoint: per residue rho = k mod orig_step the (k / orig_step, phase, tap) triples
-    std::vector<int> offs(os + 1, 0);
-    std::vector<int4> ents;
-    for (int rho = 0; rho < os; ++rho) {
-      offs[rho] = (int)ents.size();
-      for (int k = rho; k < wt; k += os)
-        for (int j = 0; j < ns; ++j) {
-          const float v = (float)d->rs_taps[(size_t)j * wt + k];
-          if (v != 0.0f) {
-            int bits;
-            memcpy(&bits, &v, 4);
-            ents.push_back(make_int4((k - rho) / os, j, bits, 0));
-          }
-        }
-    }
-    offs[os] = (int)ents.size();
-    if (ents.empty()) ents.push_back(make_int4(0, 0, 0, 0));
-    bool ok = cudaMalloc(&p->taps, taps.size() * 4) == cudaSuccess &&
-              cudaMalloc(&p->first, ns * 4) == cudaSuccess && cudaMalloc(&p->count, ns * 4) == cudaSuccess &&
-              cudaMalloc(&p->adj_offset, (os + 1) * 4) == cudaSuccess &&
-              cudaMalloc(&p->adj_entries, ents.size() * sizeof(int4)) == cudaSuccess;
-    ok = ok && cudaMemcpy(p->taps, taps.data(), taps.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(p->first, first.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(p->count, count.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(p->adj_offset, offs.data(), (os + 1) * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(p->adj_entries, ents.data(), ents.size() * sizeof(int4), cudaMemcpyHostToDevice) ==
-             cudaSuccess;
-    if (!ok) return bail(fail(PESQ_ERR_CUDA, "upload of the resampler tables failed"));
+    const char* msg = build_resample_tables(d->rs_orig_step, d->rs_new_step, d->rs_width, d->rs_width_total,
+                                            d->rs_taps, p->rs);
+    if (msg) return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "%s", msg));
   }
 
   cudaError_t e = configure_front();
@@ -394,11 +339,7 @@ int pesq_plan_destroy(pesq_plan* p) {
   if (!p) return PESQ_OK;
   cudaFree(p->dtab);
   cudaFree(p->tw64);
-  cudaFree(p->taps);
-  cudaFree(p->first);
-  cudaFree(p->count);
-  cudaFree(p->adj_offset);
-  cudaFree(p->adj_entries);
+  free_resample_tables(p->rs);
   delete p;
   return PESQ_OK;
 }
@@ -447,23 +388,12 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64
   if (g.resample) {
     float* x16 = at<float>(ws, g.x16);
     float* x16lo = at<float>(ws, g.x16lo);
-    ResampleArgs ra{};
+    ResampleArgs ra = resample_args(p->rs, n_src, g.n16);
     ra.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
     ra.dst = RowSink{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.dst_lo = RowSink{x16lo, x16lo + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.rows = (int)g.rows;
     ra.row_begin = 0;
-    ra.n_in = n_src;
-    ra.n_out = g.n16;
-    ra.orig_step = p->orig_step;
-    ra.new_step = p->new_step;
-    ra.width = p->width;
-    ra.taps = p->taps;
-    ra.first = p->first;
-    ra.count = p->count;
-    ra.max_count = p->max_count;
-    ra.adj_offset = p->adj_offset;
-    ra.adj_entries = p->adj_entries;
     PESQ_CUDA_TRY(launch_resample_fwd(ra, s), "resample kernel");
     src16 = RowSource{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
     lo16 = RowSource{x16lo, x16lo + batch * g.n16, g.n16, g.n16, (int)batch};
@@ -622,22 +552,11 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   PESQ_CUDA_TRY(launch_back(ba, p->pre, g.grad_end - g.grad_begin, s), "back kernel");
 
   if (g.resample) {
-    ResampleArgs ra{};
+    ResampleArgs ra = resample_args(p->rs, n_src, g.n16);
     ra.src = RowSource{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.dst = RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
     ra.rows = g.grad_end - g.grad_begin;
     ra.row_begin = g.grad_begin;
-    ra.n_in = n_src;
-    ra.n_out = g.n16;
-    ra.orig_step = p->orig_step;
-    ra.new_step = p->new_step;
-    ra.width = p->width;
-    ra.taps = p->taps;
-    ra.first = p->first;
-    ra.count = p->count;
-    ra.max_count = p->max_count;
-    ra.adj_offset = p->adj_offset;
-    ra.adj_entries = p->adj_entries;
     PESQ_CUDA_TRY(launch_resample_adj(ra, s), "resample adjoint kernel");
   }
   return PESQ_OK;

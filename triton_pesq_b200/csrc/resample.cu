@@ -11,6 +11,11 @@
 // every tap that reaches sample n has k = n + width (mod orig_step), so the
 // host lists, per residue, the (frame offset, phase, tap) triples that
 // contribute.  No atomics; the result is bitwise reproducible.
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
 #include "kernels.cuh"
 
 namespace pesq {
@@ -45,7 +50,7 @@ __global__ void __launch_bounds__(kResampleThreads) resample_fwd_kernel(const __
   }
   const float hi = (float)acc;
   p.dst.row(r)[m] = hi;
-  p.dst_lo.row(r)[m] = (float)(acc - (double)hi);
+  if (p.dst_lo.ref) p.dst_lo.row(r)[m] = (float)(acc - (double)hi);
 }
 
 __global__ void __launch_bounds__(kResampleThreads) resample_adj_kernel(const __grid_constant__ ResampleArgs p) {
@@ -69,18 +74,120 @@ __global__ void __launch_bounds__(kResampleThreads) resample_adj_kernel(const __
 
 }  // namespace
 
+// Rows go in grid y, at most kMaxGridRows per launch.
+constexpr int kMaxGridRows = 65535;
+
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s) {
   if (a.rows <= 0 || a.n_out <= 0) return cudaSuccess;
-  dim3 grid((unsigned)ceil_div(a.n_out, kResampleThreads), (unsigned)a.rows);
-  resample_fwd_kernel<<<grid, kResampleThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  for (int r0 = 0; r0 < a.rows; r0 += kMaxGridRows) {
+    ResampleArgs c = a;
+    c.row_begin = a.row_begin + r0;
+    c.rows = std::min(kMaxGridRows, a.rows - r0);
+    dim3 grid((unsigned)ceil_div(a.n_out, kResampleThreads), (unsigned)c.rows);
+    resample_fwd_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s) {
   if (a.rows <= 0 || a.n_in <= 0) return cudaSuccess;
-  dim3 grid((unsigned)ceil_div(a.n_in, kResampleThreads), (unsigned)a.rows);
-  resample_adj_kernel<<<grid, kResampleThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  for (int r0 = 0; r0 < a.rows; r0 += kMaxGridRows) {
+    ResampleArgs c = a;
+    c.row_begin = a.row_begin + r0;
+    c.rows = std::min(kMaxGridRows, a.rows - r0);
+    dim3 grid((unsigned)ceil_div(a.n_in, kResampleThreads), (unsigned)c.rows);
+    resample_adj_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+int64_t resample_length(int orig_step, int new_step, int64_t n) {
+  const float q = (float)((double)new_step * (double)n / (double)orig_step);
+  return (int64_t)ceilf(q);
+}
+
+const char* build_resample_tables(int os, int ns, int width, int wt, const double* d_taps, ResampleTables& t) {
+  if (os <= 0 || ns <= 0 || wt <= 0 || width < 0 || !d_taps) return "invalid resampler description";
+  t.orig_step = os;
+  t.new_step = ns;
+  t.width = width;
+  // compact taps: the nonzero range of every phase
+  std::vector<int> first(ns), count(ns);
+  int maxc = 1;
+  for (int j = 0; j < ns; ++j) {
+    int lo = -1, hi = -1;
+    for (int k = 0; k < wt; ++k)
+      if ((float)d_taps[(size_t)j * wt + k] != 0.0f) {
+        if (lo < 0) lo = k;
+        hi = k;
+      }
+    first[j] = lo < 0 ? 0 : lo;
+    count[j] = lo < 0 ? 0 : hi + 1 - lo;
+    maxc = std::max(maxc, count[j]);
+  }
+  std::vector<float> taps((size_t)ns * maxc, 0.0f);
+  for (int j = 0; j < ns; ++j)
+    for (int i = 0; i < count[j]; ++i) taps[(size_t)j * maxc + i] = (float)d_taps[(size_t)j * wt + first[j] + i];
+  t.max_count = maxc;
+  // adjoint: per residue rho = k mod orig_step the (k / orig_step, phase, tap) triples
+  std::vector<int> offs(os + 1, 0);
+  std::vector<int4> ents;
+  for (int rho = 0; rho < os; ++rho) {
+    offs[rho] = (int)ents.size();
+    for (int k = rho; k < wt; k += os)
+      for (int j = 0; j < ns; ++j) {
+        const float v = (float)d_taps[(size_t)j * wt + k];
+        if (v != 0.0f) {
+          int bits;
+          memcpy(&bits, &v, 4);
+          ents.push_back(make_int4((k - rho) / os, j, bits, 0));
+        }
+      }
+  }
+  offs[os] = (int)ents.size();
+  if (ents.empty()) ents.push_back(make_int4(0, 0, 0, 0));
+  bool ok = cudaMalloc(&t.taps, taps.size() * 4) == cudaSuccess && cudaMalloc(&t.first, ns * 4) == cudaSuccess &&
+            cudaMalloc(&t.count, ns * 4) == cudaSuccess && cudaMalloc(&t.adj_offset, (os + 1) * 4) == cudaSuccess &&
+            cudaMalloc(&t.adj_entries, ents.size() * sizeof(int4)) == cudaSuccess;
+  ok = ok && cudaMemcpy(t.taps, taps.data(), taps.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.first, first.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.count, count.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.adj_offset, offs.data(), (os + 1) * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.adj_entries, ents.data(), ents.size() * sizeof(int4), cudaMemcpyHostToDevice) == cudaSuccess;
+  if (!ok) {
+    free_resample_tables(t);
+    return "upload of the resampler tables failed";
+  }
+  return nullptr;
+}
+
+void free_resample_tables(ResampleTables& t) {
+  cudaFree(t.taps);
+  cudaFree(t.first);
+  cudaFree(t.count);
+  cudaFree(t.adj_offset);
+  cudaFree(t.adj_entries);
+  t = ResampleTables{};
+}
+
+ResampleArgs resample_args(const ResampleTables& t, int64_t n_in, int64_t n_out) {
+  ResampleArgs ra{};
+  ra.n_in = n_in;
+  ra.n_out = n_out;
+  ra.orig_step = t.orig_step;
+  ra.new_step = t.new_step;
+  ra.width = t.width;
+  ra.taps = t.taps;
+  ra.first = t.first;
+  ra.count = t.count;
+  ra.max_count = t.max_count;
+  ra.adj_offset = t.adj_offset;
+  ra.adj_entries = t.adj_entries;
+  return ra;
 }
 
 }  // namespace pesq

@@ -4,6 +4,8 @@
 // safe under CUDA graph capture), pick the current stream and forward to
 // pesq_forward / pesq_backward.  Plans are created from Python through the
 // same C ABI (ctypes) and passed in as an opaque integer handle.
+#include <algorithm>
+
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -117,6 +119,56 @@ std::tuple<at::Tensor, at::Tensor> pesq_backward_op(int64_t plan_handle, const a
   return {g_ref, g_deg};
 }
 
+const pesq_resampler* as_resampler(int64_t handle) {
+  TORCH_CHECK(handle != 0, "invalid resampler handle");
+  return reinterpret_cast<const pesq_resampler*>(static_cast<uintptr_t>(handle));
+}
+
+void check_rows(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "The CUDA resampler needs `", name, "` to live on a GPU.");
+  TORCH_CHECK(t.scalar_type() == at::kFloat, "The CUDA resampler only supports float32, `", name, "` is ",
+              t.scalar_type(), ".");
+  TORCH_CHECK(t.dim() == 2, "`", name, "` must be [rows, samples], got ", t.sizes());
+}
+
+// y = A x over the rows of x [rows, n_in]
+at::Tensor resample_op(int64_t handle, const at::Tensor& x_in) {
+  check_rows(x_in, "waveform");
+  const pesq_resampler* r = as_resampler(handle);
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const at::Tensor x = x_in.stride(1) == 1 ? x_in : x_in.contiguous();
+  const int64_t rows = x.size(0), n_in = x.size(1);
+  int64_t n_out = 0;
+  check_status(pesq_resampler_length(r, n_in, &n_out), "pesq_resampler_length");
+  at::Tensor y = at::empty({rows, n_out}, x.options());
+  if (rows == 0 || n_out == 0) return y;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(x.device().index());
+  check_status(pesq_resample_forward(r, stream, x.data_ptr<float>(), std::max<int64_t>(x.stride(0), n_in), rows,
+                                     n_in, y.data_ptr<float>(), n_out),
+               "pesq_resample_forward");
+  return y;
+}
+
+// gx = A^T gy, gx [rows, n_in]
+at::Tensor resample_adjoint_op(int64_t handle, const at::Tensor& g_in, int64_t n_in) {
+  check_rows(g_in, "grad");
+  const pesq_resampler* r = as_resampler(handle);
+  c10::cuda::CUDAGuard guard(g_in.device());
+  const at::Tensor g = g_in.stride(1) == 1 ? g_in : g_in.contiguous();
+  const int64_t rows = g.size(0);
+  int64_t n_out = 0;
+  check_status(pesq_resampler_length(r, n_in, &n_out), "pesq_resampler_length");
+  TORCH_CHECK_VALUE(g.size(1) == n_out, "gradient of ", g.size(1), " samples, the resampler produces ", n_out,
+                    " from ", n_in);
+  at::Tensor gx = at::empty({rows, n_in}, g.options());
+  if (rows == 0 || n_in == 0) return gx;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(g.device().index());
+  check_status(pesq_resample_adjoint(r, stream, g.data_ptr<float>(), std::max<int64_t>(g.stride(0), n_out), rows,
+                                     n_in, gx.data_ptr<float>(), n_in),
+               "pesq_resample_adjoint");
+  return gx;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(pesq_cuda, m) {
@@ -124,9 +176,13 @@ TORCH_LIBRARY(pesq_cuda, m) {
   m.def(
       "backward(int plan, Tensor ref, Tensor deg, int flags, Tensor workspace, Tensor? g_loss, Tensor? g_mos, "
       "Tensor? g_dsymm, Tensor? g_dasymm) -> (Tensor, Tensor)");
+  m.def("resample(int resampler, Tensor waveform) -> Tensor");
+  m.def("resample_adjoint(int resampler, Tensor grad, int n_in) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(pesq_cuda, CUDA, m) {
   m.impl("forward", &pesq_forward_op);
   m.impl("backward", &pesq_backward_op);
+  m.impl("resample", &resample_op);
+  m.impl("resample_adjoint", &resample_adjoint_op);
 }

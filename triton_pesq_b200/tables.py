@@ -30,6 +30,7 @@ from dataclasses import dataclass, field
 from typing import List, Optional, Tuple
 
 import numpy as np
+import torch
 
 # ---------------------------------------------------------------------------
 # ITU-T P.862 tables, 16 kHz (values as in torch_pesq/bark.py:11-76 and
@@ -320,26 +321,40 @@ class ResampleKernel:
         return int(self.taps.shape[1])
 
 
+RESAMPLING_METHODS = ("sinc_interp_hann", "sinc_interp_kaiser")
+#: default Kaiser window shape of torchaudio's resampler
+KAISER_BETA = 14.769656459379492
+
+
 def sinc_resample_kernel(
     orig_freq: int,
     new_freq: int,
     lowpass_filter_width: int = 6,
     rolloff: float = 0.99,
+    resampling_method: str = "sinc_interp_hann",
+    beta: Optional[float] = None,
 ) -> ResampleKernel:
-    """Hann-windowed sinc polyphase kernel, float32 taps.
+    """Windowed sinc polyphase kernel, float32 taps.
 
     Restates the published algorithm of torchaudio 2.x
-    ``torchaudio.functional.functional._get_sinc_resample_kernel`` (method
-    ``sinc_interp_hann``), which ``loss.py:76`` uses through
-    ``torchaudio.transforms.Resample``.  The phase offsets ``-j / new_step`` are
-    formed in float32 and everything after that in float64, matching the dtype
-    promotions of that implementation, so the float32 taps agree bit for bit.
+    ``torchaudio.functional.functional._get_sinc_resample_kernel`` (methods
+    ``sinc_interp_hann`` and ``sinc_interp_kaiser``), which ``loss.py:76`` uses
+    through ``torchaudio.transforms.Resample`` and the reference's
+    ``TritonResample`` (``triton_ops/resample.py:442-528``) designs its filter
+    bank with.  The phase offsets ``-j / new_step`` are formed in float32 and
+    everything after that in float64; the Kaiser window divides by ``i0`` of
+    the float32 shape parameter evaluated in float32 -- the dtype promotions of
+    that implementation, so the float32 taps agree bit for bit.
     """
 
     if orig_freq <= 0 or new_freq <= 0:
         raise ValueError("Original and desired frequency have to be positive.")
+    if int(orig_freq) != orig_freq or int(new_freq) != new_freq:
+        raise ValueError("Frequencies must be integers.")
     if lowpass_filter_width <= 0:
         raise ValueError("Low pass filter width should be positive.")
+    if resampling_method not in RESAMPLING_METHODS:
+        raise ValueError("Invalid resampling method: {}".format(resampling_method))
 
     gcd = math.gcd(int(orig_freq), int(new_freq))
     orig = int(orig_freq) // gcd
@@ -354,7 +369,12 @@ def sinc_resample_kernel(
     ).astype(np.float64)[:, None]
     t = (phase + idx) * base
     t = np.clip(t, -lowpass_filter_width, lowpass_filter_width)
-    window = np.cos(t * math.pi / lowpass_filter_width / 2) ** 2
+    if resampling_method == "sinc_interp_hann":
+        window = np.cos(t * math.pi / lowpass_filter_width / 2) ** 2
+    else:
+        shape = torch.tensor(float(KAISER_BETA if beta is None else beta))  # float32, as torchaudio
+        tt = torch.from_numpy(t)
+        window = (torch.i0(shape * torch.sqrt(1 - (tt / lowpass_filter_width) ** 2)) / torch.i0(shape)).numpy()
     t = t * math.pi
     scale = base / orig
     with np.errstate(invalid="ignore", divide="ignore"):
