@@ -319,6 +319,51 @@ def stage_times(model, ref, deg, dev, launches=40):
     return result
 
 
+def measure_resampler(dev, peak, launches=10):
+    """The standalone resampler (ResampleCuda, the reference's TritonResample)
+    on 256 rows of 4 s at 44.1 kHz -> 16 kHz (180 MB in, 65 MB out: beyond
+    L2), forward and adjoint each timed alone with CUDA events."""
+
+    import torch
+
+    from triton_pesq_b200 import ResampleCuda
+
+    rows, n_in = 256, 4 * 44100
+    module = ResampleCuda(44100, 16000).to(dev)
+    x = torch.randn(rows, n_in, device=dev)
+    handle = module._handle(dev)
+    y = torch.ops.pesq_cuda.resample(handle, x)
+    n_out = y.shape[1]
+    g = torch.randn_like(y)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(launches):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        return 1e3 * start.elapsed_time(stop) / launches
+
+    fwd_us = timed(lambda: torch.ops.pesq_cuda.resample(handle, x))
+    adj_us = timed(lambda: torch.ops.pesq_cuda.resample_adjoint(handle, g, n_in))
+    # compulsory traffic: read the input, write the output (and the reverse)
+    alg = 4 * rows * (n_in + n_out)
+    return {
+        "workload": f"{rows} rows x 4 s @44.1 kHz -> 16 kHz, float32, fp64 accumulation",
+        "forward_us": fwd_us,
+        "adjoint_us": adj_us,
+        "forward_gbs": alg / (fwd_us * 1e-6) / 1e9,
+        "adjoint_gbs": alg / (adj_us * 1e-6) / 1e9,
+        "forward_frac_of_measured_hbm": alg / (fwd_us * 1e-6) / 1e9 / peak,
+        "adjoint_frac_of_measured_hbm": alg / (adj_us * 1e-6) / 1e9 / peak,
+        "utterance_seconds_per_s_fwd_bwd": rows * 4.0 / ((fwd_us + adj_us) * 1e-6),
+    }
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
@@ -493,6 +538,7 @@ def run_cuda(args):
     front_us = stages["front"]
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
+    ops = {"resample_44k1_to_16k": measure_resampler(dev, peak)}
 
     if world > 1:
         graph.reset()
@@ -548,6 +594,7 @@ def run_cuda(args):
             "launch_us": front_us,
         },
         "stages_us": stages,
+        "ops": ops,
         "dominant_stage": dominant,
         "eager_ms_per_step": 1e3 * statistics.median(eager),
         "step_ms_min": min(step_ms),

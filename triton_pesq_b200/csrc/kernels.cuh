@@ -183,7 +183,7 @@ struct ResampleArgs {
   int row_begin;
   int64_t n_in;
   int64_t n_out;
-  int orig_step, new_step, width;
+  int orig_step, new_step, width, width_total;
   const float* taps;    // compact nonzero taps [new_step][max_count]
   const int* first;     // [new_step]
   const int* count;     // [new_step]
@@ -191,19 +191,32 @@ struct ResampleArgs {
   // adjoint gather lists per residue mod orig_step
   const int* adj_offset;   // [orig_step + 1]
   const int4* adj_entries; // (dl, phase, tap bits, 0)
+  // the same lists residue-major for the staged adjoint: entry e of residue
+  // rho at e * orig_step + rho, (dl << 24 | phase) or -1 past the end
+  const int* adj_code;
+  const float* adj_tap;
+  int max_entries, max_dl;
+  int fwd_staged, adj_staged;  // shared memory kernels (the tables fit)
+  int tpitch;                  // odd row pitch of the staged taps
 };
 
 // Device tables of one polyphase resampler: the compact nonzero taps of every
 // phase and the adjoint's per-residue gather lists, built on the host from
 // float32-valued taps [new_step][width_total].
 struct ResampleTables {
-  int orig_step = 0, new_step = 0, width = 0, max_count = 0;
+  int orig_step = 0, new_step = 0, width = 0, width_total = 0, max_count = 0;
   float* taps = nullptr;        // [new_step][max_count]
   int* first = nullptr;         // [new_step]
   int* count = nullptr;         // [new_step]
   int* adj_offset = nullptr;    // [orig_step + 1]
   int4* adj_entries = nullptr;  // (frame offset, phase, tap bits, 0)
+  int* adj_code = nullptr;      // [max_entries][orig_step]
+  float* adj_tap = nullptr;     // [max_entries][orig_step]
+  int max_entries = 0, max_dl = 0;
+  bool fwd_staged = false, adj_staged = false;
 };
+// Allows the staged resampler kernels their shared memory (once per process).
+cudaError_t configure_resample();
 // Builds t on the current device; returns nullptr or a message.
 const char* build_resample_tables(int orig_step, int new_step, int width, int width_total, const double* taps,
                                   ResampleTables& t);

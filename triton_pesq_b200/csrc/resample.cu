@@ -11,6 +11,11 @@
 // every tap that reaches sample n has k = n + width (mod orig_step), so the
 // host lists, per residue, the (frame offset, phase, tap) triples that
 // contribute.  No atomics; the result is bitwise reproducible.
+//
+// For the rate pairs whose tables fit (all the usual ones), both directions
+// run staged kernels: a few CTAs per row, each with the filter bank (the
+// gather lists) staged once and the input (gradient) window of each block of
+// 1024 outputs (inputs) staged before it, in shared memory.
 #include <string.h>
 
 #include <algorithm>
@@ -23,7 +28,35 @@ namespace pesq {
 namespace {
 
 constexpr int kResampleThreads = 256;
+// outputs (forward) / inputs (adjoint) per step of the staged kernels
+constexpr int kResampleBlock = 1024;
+// shared memory a staged CTA may use
+constexpr size_t kResampleSmemLimit = 96 * 1024;
+// CTAs the staged kernels aim for (several waves), split over the rows
+constexpr int kResampleTargetCtas = 16 * 148;
 
+// staged geometry shared by host and device
+__host__ __device__ inline int fwd_span(int os, int ns, int wt) { return ((kResampleBlock - 1) / ns + 1) * os + wt; }
+__host__ __device__ inline int tap_pitch(int max_count) { return max_count | 1; }
+__host__ __device__ inline int adj_span(int os, int ns, int max_dl) {
+  return ((kResampleBlock - 1) / os + 2 + max_dl) * ns;
+}
+size_t fwd_smem(int os, int ns, int wt, int max_count) {
+  return ((size_t)ns * tap_pitch(max_count) + fwd_span(os, ns, wt) + 2 * (size_t)ns) * 4;
+}
+size_t adj_smem(int os, int ns, int max_dl, int max_e) {
+  return ((size_t)adj_span(os, ns, max_dl) + 2 * (size_t)max_e * os) * 4;
+}
+// staged CTAs per row and the (block multiple) share of the row each handles
+void staged_split(int rows, int64_t n, int& ctas, int64_t& chunk) {
+  const int64_t blocks = ceil_div(n, (int64_t)kResampleBlock);
+  const int64_t want = std::max<int64_t>(1, ceil_div((int64_t)kResampleTargetCtas, (int64_t)std::max(rows, 1)));
+  const int64_t k = std::min(blocks, want);
+  chunk = ceil_div(blocks, k) * kResampleBlock;
+  ctas = (int)ceil_div(n, chunk);
+}
+
+// one output per thread, taps and input read from global memory (any ratio)
 __global__ void __launch_bounds__(kResampleThreads) resample_fwd_kernel(const __grid_constant__ ResampleArgs p) {
   const int r = p.row_begin + (int)blockIdx.y;
   const int64_t m = (int64_t)blockIdx.x * kResampleThreads + threadIdx.x;
@@ -53,6 +86,68 @@ __global__ void __launch_bounds__(kResampleThreads) resample_fwd_kernel(const __
   if (p.dst_lo.ref) p.dst_lo.row(r)[m] = (float)(acc - (double)hi);
 }
 
+// A CTA handles `chunk` consecutive outputs of a row in steps of
+// kResampleBlock: the filter bank (odd row pitch: the phases of consecutive
+// lanes hit distinct banks) is staged once, the input window of every step
+// before it.
+__global__ void __launch_bounds__(kResampleThreads)
+    resample_fwd_staged_kernel(const __grid_constant__ ResampleArgs p, int64_t chunk) {
+  extern __shared__ __align__(16) float rsm[];
+  const int os = p.orig_step, ns = p.new_step, tpitch = p.tpitch;
+  float* tp = rsm;                                               // [ns][tpitch]
+  float* xs = tp + (size_t)ns * tpitch;                          // input window
+  int* fi = reinterpret_cast<int*>(xs + fwd_span(os, ns, p.width_total));  // first [ns]
+  int* co = fi + ns;                                             // count [ns]
+  const int tid = threadIdx.x;
+  const int r = p.row_begin + (int)blockIdx.y;
+
+  for (int i = tid; i < ns * tpitch; i += kResampleThreads) {
+    const int j = i / tpitch, k = i - j * tpitch;
+    tp[i] = k < p.max_count ? __ldg(p.taps + j * p.max_count + k) : 0.0f;
+  }
+  for (int i = tid; i < ns; i += kResampleThreads) {
+    fi[i] = __ldg(p.first + i);
+    co[i] = __ldg(p.count + i);
+  }
+  const float* x = p.src.row(r);
+  float* y = p.dst.row(r);
+  const int64_t c0 = (int64_t)blockIdx.x * chunk;
+  const int64_t c1 = min(c0 + chunk, p.n_out);
+  for (int64_t m0 = c0; m0 < c1; m0 += kResampleBlock) {
+    const int64_t m_end = min(m0 + kResampleBlock, c1);
+    const int64_t l_first = m0 / ns;
+    const int64_t base = l_first * os - p.width;  // input index of xs[0]
+    const int span = (int)(((m_end - 1) / ns - l_first) * os + p.width_total);
+    __syncthreads();  // the previous step is done with xs
+    for (int i = tid; i < span; i += kResampleThreads) {
+      const int64_t g = base + i;
+      xs[i] = (g >= 0 && g < p.n_in) ? __ldg(x + g) : 0.0f;
+    }
+    __syncthreads();
+    for (int64_t m = m0 + tid; m < m_end; m += kResampleThreads) {
+      const int64_t l = m / ns;
+      const int j = (int)(m - l * ns);
+      const float* t = tp + j * tpitch;
+      const float* xv = xs + (l - l_first) * os + fi[j];
+      const int cnt = co[j];
+      // two partial sums halve the dependent chain of the tap loop
+      double acc0 = 0.0, acc1 = 0.0;
+      int i = 0;
+#pragma unroll 4
+      for (; i + 1 < cnt; i += 2) {
+        acc0 = fma((double)t[i], (double)xv[i], acc0);
+        acc1 = fma((double)t[i + 1], (double)xv[i + 1], acc1);
+      }
+      if (i < cnt) acc0 = fma((double)t[i], (double)xv[i], acc0);
+      const double acc = acc0 + acc1;
+      const float hi = (float)acc;
+      y[m] = hi;
+      if (p.dst_lo.ref) p.dst_lo.row(r)[m] = (float)(acc - (double)hi);
+    }
+  }
+}
+
+// one input sample per thread, per-residue gather lists from global memory
 __global__ void __launch_bounds__(kResampleThreads) resample_adj_kernel(const __grid_constant__ ResampleArgs p) {
   const int r = p.row_begin + (int)blockIdx.y;
   const int64_t n = (int64_t)blockIdx.x * kResampleThreads + threadIdx.x;
@@ -72,6 +167,59 @@ __global__ void __launch_bounds__(kResampleThreads) resample_adj_kernel(const __
   p.dst.row(r)[n] = acc;
 }
 
+// A CTA handles `chunk` consecutive input samples of a row in steps of
+// kResampleBlock: the residue-major gather lists are staged once (consecutive
+// samples have consecutive residues), the gradient window of every step
+// before it.
+__global__ void __launch_bounds__(kResampleThreads)
+    resample_adj_staged_kernel(const __grid_constant__ ResampleArgs p, int64_t chunk) {
+  extern __shared__ __align__(16) float rsm[];
+  const int os = p.orig_step, ns = p.new_step, ne = p.max_entries;
+  // entry e of residue rho: (window offset j - dl * ns, tap); unused entries
+  // have tap 0 and offset 0, so every lane runs the same ne iterations
+  int2* ent = reinterpret_cast<int2*>(rsm);
+  float* gs = reinterpret_cast<float*>(ent + (size_t)ne * os);  // gradient window
+  const int tid = threadIdx.x;
+  const int r = p.row_begin + (int)blockIdx.y;
+  for (int i = tid; i < ne * os; i += kResampleThreads) {
+    const int cd = __ldg(p.adj_code + i);
+    ent[i] = cd < 0 ? make_int2(0, 0)
+                    : make_int2((cd & 0xffffff) - (cd >> 24) * ns, __float_as_int(__ldg(p.adj_tap + i)));
+  }
+  const float* g = p.src.row(r);
+  float* out = p.dst.row(r);
+  const int64_t c0 = (int64_t)blockIdx.x * chunk;
+  const int64_t c1 = min(c0 + chunk, p.n_in);
+  for (int64_t n0 = c0; n0 < c1; n0 += kResampleBlock) {
+    const int64_t n_end = min(n0 + kResampleBlock, c1);
+    const int64_t l0_first = (n0 + p.width) / os;
+    const int64_t mbase = (l0_first - p.max_dl) * ns;  // gradient index of gs[0]
+    const int span = (int)(((n_end - 1 + p.width) / os - l0_first + 1 + p.max_dl) * ns);
+    __syncthreads();  // the previous step is done with gs
+    for (int i = tid; i < span; i += kResampleThreads) {
+      const int64_t m = mbase + i;
+      gs[i] = (m >= 0 && m < p.n_out) ? __ldg(g + m) : 0.0f;
+    }
+    __syncthreads();
+    for (int64_t n = n0 + tid; n < n_end; n += kResampleThreads) {
+      const int64_t pos = n + p.width;
+      const int64_t l0 = pos / os;
+      const int rho = (int)(pos - l0 * os);
+      // slot of (l0, phase 0) in the window; entry (dl, j) reads slot + j - dl * ns
+      const int slot = (int)((l0 - l0_first + p.max_dl) * ns);
+      float acc = 0.0f;
+      const int2* en = ent + rho;
+      const float* gw = gs + slot;
+#pragma unroll 4
+      for (int e = 0; e < ne; ++e) {
+        const int2 v = en[e * os];
+        acc = fmaf(__int_as_float(v.y), gw[v.x], acc);
+      }
+      out[n] = acc;
+    }
+  }
+}
+
 }  // namespace
 
 // Rows go in grid y, at most kMaxGridRows per launch.
@@ -83,8 +231,17 @@ cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s) {
     ResampleArgs c = a;
     c.row_begin = a.row_begin + r0;
     c.rows = std::min(kMaxGridRows, a.rows - r0);
-    dim3 grid((unsigned)ceil_div(a.n_out, kResampleThreads), (unsigned)c.rows);
-    resample_fwd_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    if (a.fwd_staged) {
+      int ctas;
+      int64_t chunk;
+      staged_split(a.rows, a.n_out, ctas, chunk);
+      dim3 grid((unsigned)ctas, (unsigned)c.rows);
+      const size_t smem = fwd_smem(a.orig_step, a.new_step, a.width_total, a.max_count);
+      resample_fwd_staged_kernel<<<grid, kResampleThreads, smem, s>>>(c, chunk);
+    } else {
+      dim3 grid((unsigned)ceil_div(a.n_out, kResampleThreads), (unsigned)c.rows);
+      resample_fwd_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -97,12 +254,29 @@ cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s) {
     ResampleArgs c = a;
     c.row_begin = a.row_begin + r0;
     c.rows = std::min(kMaxGridRows, a.rows - r0);
-    dim3 grid((unsigned)ceil_div(a.n_in, kResampleThreads), (unsigned)c.rows);
-    resample_adj_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    if (a.adj_staged) {
+      int ctas;
+      int64_t chunk;
+      staged_split(a.rows, a.n_in, ctas, chunk);
+      dim3 grid((unsigned)ctas, (unsigned)c.rows);
+      const size_t smem = adj_smem(a.orig_step, a.new_step, a.max_dl, a.max_entries);
+      resample_adj_staged_kernel<<<grid, kResampleThreads, smem, s>>>(c, chunk);
+    } else {
+      dim3 grid((unsigned)ceil_div(a.n_in, kResampleThreads), (unsigned)c.rows);
+      resample_adj_kernel<<<grid, kResampleThreads, 0, s>>>(c);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t configure_resample() {
+  cudaError_t e = cudaFuncSetAttribute(resample_fwd_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kResampleSmemLimit);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(resample_adj_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kResampleSmemLimit);
 }
 
 int64_t resample_length(int orig_step, int new_step, int64_t n) {
@@ -112,6 +286,7 @@ int64_t resample_length(int orig_step, int new_step, int64_t n) {
 
 const char* build_resample_tables(int os, int ns, int width, int wt, const double* d_taps, ResampleTables& t) {
   if (os <= 0 || ns <= 0 || wt <= 0 || width < 0 || !d_taps) return "invalid resampler description";
+  if (configure_resample() != cudaSuccess) return "configuring the resampler kernels failed";
   t.orig_step = os;
   t.new_step = ns;
   t.width = width;
@@ -149,15 +324,36 @@ const char* build_resample_tables(int os, int ns, int width, int wt, const doubl
       }
   }
   offs[os] = (int)ents.size();
+  // residue-major copy of the lists for the staged adjoint
+  int max_e = 0, max_dl = 0;
+  for (int rho = 0; rho < os; ++rho) max_e = std::max(max_e, offs[rho + 1] - offs[rho]);
+  for (const int4& e : ents) max_dl = std::max(max_dl, e.x);
+  t.max_entries = max_e;
+  t.max_dl = max_dl;
+  t.width_total = wt;
+  std::vector<int> code((size_t)std::max(max_e, 1) * os, -1);
+  std::vector<float> ctap((size_t)std::max(max_e, 1) * os, 0.0f);
+  for (int rho = 0; rho < os; ++rho)
+    for (int e = offs[rho]; e < offs[rho + 1]; ++e) {
+      const int slot = (e - offs[rho]) * os + rho;
+      code[slot] = (ents[e].x << 24) | ents[e].y;
+      memcpy(&ctap[slot], &ents[e].z, 4);
+    }
+  t.fwd_staged = fwd_smem(os, ns, wt, maxc) <= kResampleSmemLimit;
+  t.adj_staged = max_dl < 128 && ns < (1 << 24) && adj_smem(os, ns, max_dl, max_e) <= kResampleSmemLimit;
   if (ents.empty()) ents.push_back(make_int4(0, 0, 0, 0));
   bool ok = cudaMalloc(&t.taps, taps.size() * 4) == cudaSuccess && cudaMalloc(&t.first, ns * 4) == cudaSuccess &&
             cudaMalloc(&t.count, ns * 4) == cudaSuccess && cudaMalloc(&t.adj_offset, (os + 1) * 4) == cudaSuccess &&
-            cudaMalloc(&t.adj_entries, ents.size() * sizeof(int4)) == cudaSuccess;
+            cudaMalloc(&t.adj_entries, ents.size() * sizeof(int4)) == cudaSuccess &&
+            cudaMalloc(&t.adj_code, code.size() * 4) == cudaSuccess &&
+            cudaMalloc(&t.adj_tap, ctap.size() * 4) == cudaSuccess;
   ok = ok && cudaMemcpy(t.taps, taps.data(), taps.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
        cudaMemcpy(t.first, first.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
        cudaMemcpy(t.count, count.data(), ns * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
        cudaMemcpy(t.adj_offset, offs.data(), (os + 1) * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-       cudaMemcpy(t.adj_entries, ents.data(), ents.size() * sizeof(int4), cudaMemcpyHostToDevice) == cudaSuccess;
+       cudaMemcpy(t.adj_entries, ents.data(), ents.size() * sizeof(int4), cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.adj_code, code.data(), code.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(t.adj_tap, ctap.data(), ctap.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
   if (!ok) {
     free_resample_tables(t);
     return "upload of the resampler tables failed";
@@ -171,6 +367,8 @@ void free_resample_tables(ResampleTables& t) {
   cudaFree(t.count);
   cudaFree(t.adj_offset);
   cudaFree(t.adj_entries);
+  cudaFree(t.adj_code);
+  cudaFree(t.adj_tap);
   t = ResampleTables{};
 }
 
@@ -187,6 +385,14 @@ ResampleArgs resample_args(const ResampleTables& t, int64_t n_in, int64_t n_out)
   ra.max_count = t.max_count;
   ra.adj_offset = t.adj_offset;
   ra.adj_entries = t.adj_entries;
+  ra.width_total = t.width_total;
+  ra.adj_code = t.adj_code;
+  ra.adj_tap = t.adj_tap;
+  ra.max_entries = t.max_entries;
+  ra.max_dl = t.max_dl;
+  ra.fwd_staged = t.fwd_staged;
+  ra.adj_staged = t.adj_staged;
+  ra.tpitch = tap_pitch(t.max_count);
   return ra;
 }
 
