@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="do not time the other BASELINE configurations (cfg1, cfg3, cfg4, cfg5)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
@@ -364,6 +366,56 @@ def measure_resampler(dev, peak, launches=10):
     }
 
 
+def measure_configs(dev, flush, steps=10):
+    """Graph-replayed fwd+bwd (w.r.t. deg) step of the other BASELINE
+    configurations on one GPU (L2 flushed before each step): cfg1, cfg3, the
+    per-GPU share of cfg4 (8 of its 64 utterances) and cfg5."""
+
+    import torch
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.signals import workload
+
+    out = {}
+    for name, keep, secs in (("cfg1", 1, 1.0), ("cfg3", 16, 4.0), ("cfg4_per_gpu", 8, 10.0), ("cfg5", 512, 3.0)):
+        ref_c, deg_c, sr = workload(name.split("_")[0], seed=0)
+        ref = ref_c[:keep].to(dev)
+        deg = deg_c[:keep].to(dev).requires_grad_(True)
+        model = PesqLossCuda(1.0, sample_rate=sr)
+
+        def step():
+            loss = model(ref, deg)
+            (g,) = torch.autograd.grad(loss.sum(), [deg])
+            return loss, g
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        times = []
+        for k in range(steps + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            b.synchronize()
+            if k >= 3:
+                times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        out[name] = {"batch": keep, "seconds": secs, "sample_rate": sr, "ms_per_step": ms,
+                     "utterance_seconds_per_s": keep * secs / (ms * 1e-3)}
+        del graph
+    return out
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
@@ -539,6 +591,7 @@ def run_cuda(args):
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
     ops = {"resample_44k1_to_16k": measure_resampler(dev, peak)}
+    configs = measure_configs(dev, flush) if not args.skip_configs else None
 
     if world > 1:
         graph.reset()
@@ -595,6 +648,7 @@ def run_cuda(args):
         },
         "stages_us": stages,
         "ops": ops,
+        "other_configs": configs,
         "dominant_stage": dominant,
         "eager_ms_per_step": 1e3 * statistics.median(eager),
         "step_ms_min": min(step_ms),
