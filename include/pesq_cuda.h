@@ -236,6 +236,60 @@ int pesq_resample_forward(const pesq_resampler* resampler, void* stream, const f
 int pesq_resample_adjoint(const pesq_resampler* resampler, void* stream, const float* gy, int64_t ld_gy,
                           int64_t rows, int64_t n_in, float* gx, int64_t ld_gx);
 
+/* ---------------------------------------------------------------------------
+ * Standalone causal IIR filter: the reference's TritonIIR
+ * (torch_pesq/triton_ops/iir.py:1266-1482), lfilter(x, a, b, clamp=False) with
+ * zero initial state along every row, through a state space realisation
+ *   s[n+1] = A s[n] + B x[n],  y[n] = C s[n] + D x[n]
+ * chosen on the host in float64 (triton_pesq_b200/iir_design.py, which
+ * replaces iir.py:187-599).  The rows are split into chunks whose states are
+ * combined by an exact parallel scan (no truncation), single pass.
+ * ------------------------------------------------------------------------- */
+typedef struct pesq_iir pesq_iir;
+
+typedef struct pesq_iir_desc {
+  int32_t abi_version;   /* PESQ_CUDA_ABI_VERSION */
+  int32_t states;        /* P, 1 .. 24 */
+  const double* trans;   /* A, [P][P] row-major */
+  const double* input;   /* B, [P] */
+  const double* output;  /* C, [P] */
+  double feed;           /* D */
+} pesq_iir_desc;
+
+typedef struct pesq_iir_info {
+  int32_t states;         /* P of the realisation */
+  int32_t kernel_states;  /* state count of the kernel instantiation (>= P, zero padded) */
+  int32_t block_lower;    /* A is block lower triangular in 2 x 2 blocks (zero blocks skipped) */
+  int32_t chunk;          /* samples per thread chunk */
+  int32_t tile;           /* samples per tile of a long row */
+  int32_t reserved0;
+  double largest32;       /* largest entry of the float32 tables */
+  double largest64;       /* largest entry of the float64 tile chaining tables */
+} pesq_iir_info;
+
+/* flags of pesq_iir_filter */
+#define PESQ_IIR_REVERSE 1u /* filter each row back to front: the adjoint (iir.py:1232-1258) */
+#define PESQ_IIR_RERUN 2u   /* chunk outputs by re-running the recursion ("scan") instead of the
+                               impulse response product ("matmul", the default) */
+
+/* Builds the kernel tables (float64, then float32) on the current device
+ * (replaces TritonIIR.__init__'s table build, iir.py:602-667 and 1343-1397). */
+int pesq_iir_create(const pesq_iir_desc* desc, pesq_iir** out);
+int pesq_iir_destroy(pesq_iir* filter);
+int pesq_iir_query(const pesq_iir* filter, pesq_iir_info* info);
+/* Device workspace of one pesq_iir_filter call (0 when no row spans more than
+ * one tile); a workspace serves one call in flight at a time. */
+size_t pesq_iir_workspace_bytes(const pesq_iir* filter, int64_t rows, int64_t n);
+/* y = filter(x) over `rows` rows of n samples, row strides in elements; x and
+ * y must not overlap (replaces _launch, iir.py:1016-1161, and
+ * _IIRFunction, iir.py:1232-1263). */
+int pesq_iir_filter(const pesq_iir* filter, void* stream, const float* x, int64_t ld_x, int64_t rows, int64_t n,
+                    float* y, int64_t ld_y, uint32_t flags, void* workspace, size_t workspace_bytes);
+/* Synchronises `stream`, then reads and clears the filter's error word:
+ * nonzero when a tile of an earlier call stopped waiting for its predecessor
+ * (a bounded wait that ran out; its rows are then wrong). */
+int pesq_iir_check(pesq_iir* filter, void* stream, uint32_t* failed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,35 @@ class ResampleDesc(ctypes.Structure):
     ]
 
 
+class IirDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("states", ctypes.c_int32),
+        ("trans", ctypes.POINTER(ctypes.c_double)),
+        ("input", ctypes.POINTER(ctypes.c_double)),
+        ("output", ctypes.POINTER(ctypes.c_double)),
+        ("feed", ctypes.c_double),
+    ]
+
+
+class IirInfo(ctypes.Structure):
+    _fields_ = [
+        ("states", ctypes.c_int32),
+        ("kernel_states", ctypes.c_int32),
+        ("block_lower", ctypes.c_int32),
+        ("chunk", ctypes.c_int32),
+        ("tile", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("largest32", ctypes.c_double),
+        ("largest64", ctypes.c_double),
+    ]
+
+
+#: pesq_iir_filter flags
+IIR_REVERSE = 1
+IIR_RERUN = 2
+
+
 class Shape(ctypes.Structure):
     _fields_ = [("n16", ctypes.c_int64), ("frames", ctypes.c_int32), ("windows", ctypes.c_int32)]
 
@@ -156,6 +185,16 @@ SIGNATURES = {
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
          ctypes.c_void_p, ctypes.c_int64],
     ),
+    "pesq_iir_create": (ctypes.c_int, [ctypes.POINTER(IirDesc), ctypes.POINTER(ctypes.c_void_p)]),
+    "pesq_iir_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "pesq_iir_query": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(IirInfo)]),
+    "pesq_iir_workspace_bytes": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]),
+    "pesq_iir_filter": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t],
+    ),
+    "pesq_iir_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "pesq_forward_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
@@ -317,3 +356,41 @@ def create_resampler(kernel) -> int:
     handle = ctypes.c_void_p()
     check(lib.pesq_resampler_create(ctypes.byref(desc), ctypes.byref(handle)), "pesq_resampler_create")
     return int(handle.value)
+
+
+def create_iir(design) -> int:
+    """Build the kernel tables of an :class:`~triton_pesq_b200.iir_design.IIRDesign`
+    on the current CUDA device; returns the filter handle."""
+
+    lib = library()
+    keep = [np.ascontiguousarray(design.trans, dtype=np.float64),
+            np.ascontiguousarray(design.input, dtype=np.float64),
+            np.ascontiguousarray(design.output, dtype=np.float64)]
+    desc = IirDesc()
+    desc.abi_version = ABI_VERSION
+    desc.states = int(design.trans.shape[0])
+    desc.trans, desc.input, desc.output = (_dptr(k) for k in keep)
+    desc.feed = float(design.feed)
+    handle = ctypes.c_void_p()
+    check(lib.pesq_iir_create(ctypes.byref(desc), ctypes.byref(handle)), "pesq_iir_create")
+    return int(handle.value)
+
+
+def destroy_iir(handle: int) -> None:
+    if handle and _lib is not None:
+        _lib.pesq_iir_destroy(ctypes.c_void_p(handle))
+
+
+def iir_info(handle: int) -> IirInfo:
+    info = IirInfo()
+    check(library().pesq_iir_query(ctypes.c_void_p(handle), ctypes.byref(info)), "pesq_iir_query")
+    return info
+
+
+def iir_check(handle: int, stream: int = 0) -> int:
+    """Synchronise ``stream`` and return (and clear) the filter's error word."""
+
+    failed = ctypes.c_uint32(0)
+    check(library().pesq_iir_check(ctypes.c_void_p(handle), ctypes.c_void_p(stream), ctypes.byref(failed)),
+          "pesq_iir_check")
+    return int(failed.value)

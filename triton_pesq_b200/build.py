@@ -27,7 +27,8 @@ LIB = os.path.join(HERE, "libpesq_cuda.so")
 OPS = os.path.join(HERE, "_pesq_torch_ops.so")
 
 CUDA_SOURCES = ["front.cu", "align.cu", "back.cu", "chain.cu", "resample.cu", "pesq_abi.cu", "noalloc.cu",
-                "resample_abi.cu"]
+                "resample_abi.cu", "iir_abi.cu", "iir_ka.cu", "iir_kb.cu", "iir_kc.cu", "iir_kd.cu", "iir_ke.cu",
+                "iir_kf.cu"]
 NVCC_FLAGS = [
     "-std=c++17",
     "-O3",

@@ -1,0 +1,485 @@
+// Standalone causal IIR filter: an exact chunked scan over whole rows.
+//
+// The filter is a state space recursion s[n+1] = A s[n] + B x[n],
+// y[n] = C s[n] + D x[n] (realisation chosen on the host in float64,
+// triton_pesq_b200/iir_design.py), applied with zero initial state to every
+// row of a [rows, n] float32 array -- lfilter(x, a, b, clamp=False), as the
+// reference's TritonIIR (torch_pesq/triton_ops/iir.py:1266-1482).  With
+// `reverse` the rows are read and written back to front, which evaluates the
+// adjoint (the vector-Jacobian product) of the filter (iir.py:1232-1258).
+//
+// One CTA of kThreads threads filters one tile.  Thread c owns a chunk of kL
+// consecutive samples:
+//
+//   1. e_c = sum_k A^(kL-1-k) B x[k], the chunk's end state from zero (table W),
+//      and (impulse form) the chunk's zero-state outputs sum_k h[t-k] x[k];
+//   2. a segmented Kogge-Stone scan over the 32 chunks of a warp with the
+//      doubling steps M_i = A^(kL 2^i) (warp shuffles), restarted at every
+//      row start ("head");
+//   3. warp 0 chains the 8 warp totals in float64 with A^(32 kL) into the
+//      start state of every warp, from the tile's start state S;
+//   4. each chunk's start state is the warp-exclusive prefix plus
+//      A^(kL lane) times its warp's start state (lane table, shared memory);
+//   5. outputs: zero-state part + C A^t s (impulse form) or the recursion
+//      re-run from s (re-run form); staged through shared memory and stored
+//      coalesced.
+//
+// Tile geometry.  Rows of at most kThreads chunks are packed whole, several to
+// a tile (segments of cpr chunks, a head at each segment start): nothing
+// crosses a tile.  Longer rows are cut into tiles of kTile samples that are
+// chained by a decoupled look-back (single pass, 8 bytes of HBM traffic per
+// sample): a CTA takes its tile from a ticket counter (so every tile it waits
+// for belongs to a CTA that is already running), publishes its zero-start
+// aggregate, sums the aggregates of its predecessors with the powers
+// A^(k kTile) (float64) back to the first one that has published its
+// inclusive end state, and publishes its own inclusive state.  Nothing is
+// truncated: the result is exact for any stable or unstable filter.  Every
+// wait is bounded (kSpinLimit polls); a wait that gives up records an error
+// in the filter's error word and treats the predecessor as zero.
+#pragma once
+
+#include "common.cuh"
+
+namespace pesq {
+namespace iir {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kL = 33;                  // samples per thread chunk (coprime with the banks)
+constexpr int kLevels = 5;              // warp scan levels
+constexpr int kTile = kThreads * kL;    // 8448 samples per tile
+constexpr int kLook = 32;               // predecessors per look-back window
+constexpr int kMaxStates = 24;
+constexpr unsigned kSpinLimit = 1u << 21;
+
+// Per-filter constants in float32, passed as a kernel parameter (constant
+// bank operands of the FMAs).
+template <int P>
+struct Tab {
+  float h[kL];              // impulse response h[0..kL-1]
+  float G[kL][P];           // C A^t
+  float W[kL][P];           // A^(kL-1-k) B
+  float M[kLevels][P][P];   // A^(kL 2^i)
+  float A[P][P];
+  float B[P];
+  float C[P];
+  float D;
+};
+
+// Lane table pitch: A^(kL l) for lane l at l * lane_pitch(P) floats; odd, so
+// the per-lane reads of a warp never share a bank.
+__host__ __device__ constexpr int lane_pitch(int P) { return P * P + 1; }
+__host__ __device__ constexpr int lane_floats(int P) { return 32 * lane_pitch(P); }
+
+struct Args {
+  const float* x;
+  int64_t ld_x;
+  float* y;
+  int64_t ld_y;
+  int64_t rows;
+  int64_t n;
+  int reverse;
+  int cpr;                 // chunks per row (rows packed whole), else kThreads
+  int rows_per_tile;       // whole rows per tile (1 for chained rows)
+  int seg;                 // samples per segment: cpr * kL, or kTile
+  uint32_t seg_inv;        // ceil(2^32 / seg): q / seg == umulhi(q, seg_inv) for q < kTile
+  int64_t tiles_per_row;   // > 1: the tiles of a row are chained
+  int64_t tiles;
+  const float* lanes;      // [32][lane_pitch]  A^(kL l)
+  const double* wstep;     // [P][P]            A^(32 kL)
+  const double* look;      // [kLook + 1][P][P] A^(k kTile)
+  uint32_t* flags;         // [tiles + 1]: tile status (0, 1 aggregate, 2 inclusive), ticket counter
+  double* vals;            // [tiles][2][P]: aggregate, inclusive end state
+  uint32_t* err;
+};
+
+__host__ __device__ constexpr size_t smem_bytes(int P) {
+  return (size_t)kTile * 4 + (size_t)lane_floats(P) * 4 + (size_t)P * P * 8 + (size_t)kWarps * P * 8 +
+         (size_t)kWarps * P * 4;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int P, bool kLower>
+__device__ __forceinline__ bool skip(int i, int j) {
+  return kLower && (j >> 1) > (i >> 1);
+}
+
+// Warp 0: X_0 = x0 (lane i holds component i), X_{w+1} = head_w ? T_w :
+// A^(32 kL) X_w + T_w; stores X_w (float) for every warp and returns X_8,
+// the tile's end state.
+template <int P, bool kLower>
+__device__ __forceinline__ double chain_warps(double x0, const double* wstep, const double* tot, const int* whead,
+                                              float* start, int lane) {
+  const int i = lane < P ? lane : 0;
+  double xv = x0;
+#pragma unroll 1
+  for (int w = 0; w < kWarps; ++w) {
+    if (lane < P) start[w * P + lane] = (float)xv;
+    double nv = tot[w * P + i];
+    if (!whead[w]) {
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const double xj = __shfl_sync(0xffffffffu, xv, j);
+        if (!skip<P, kLower>(i, j)) nv = fma(wstep[i * P + j], xj, nv);
+      }
+    }
+    xv = lane < P ? nv : 0.0;
+  }
+  return xv;
+}
+
+// Warp 0: lane 0 stores the P components (lane i holds component i) into
+// vals[tile][slot] and then releases the tile's status.
+template <int P>
+__device__ __forceinline__ void publish(const Args& a, int64_t tile, int slot, double mine, uint32_t status,
+                                        int lane) {
+  double* dst = a.vals + (tile * 2 + slot) * P;
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const double v = __shfl_sync(0xffffffffu, mine, j);
+    if (lane == 0) __stcg(dst + j, v);
+  }
+  if (lane == 0) {
+    __threadfence();
+    st_release(a.flags + tile, status);
+  }
+  __syncwarp();
+}
+
+// Warp 0: start state of tile `tile` (its index in the row is tin >= 1), from
+// the published states of its predecessors; lane i returns component i.
+template <int P>
+__device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwin, int lane) {
+  double S[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) S[j] = 0.0;
+  bool first = true;
+  for (int64_t done = 0;; done += kLook) {
+    const int64_t k = done + lane;
+    const bool valid = k < tin;
+    const int64_t pred = tile - 1 - k;
+    uint32_t st = 0;
+    if (valid) {
+      unsigned it = 0;
+      while ((st = ld_acquire(a.flags + pred)) == 0u) {
+        if (++it > kSpinLimit) {
+          atomicOr(a.err, 1u);
+          st = 3u;  // give up: the predecessor counts as a zero inclusive state
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    const unsigned incl = __ballot_sync(0xffffffffu, valid && st >= 2u);
+    const int m = incl ? __ffs(incl) - 1 : kLook;
+    double v[P];
+    const bool take = valid && lane <= m && st != 3u;
+#pragma unroll
+    for (int j = 0; j < P; ++j) v[j] = 0.0;
+    if (take) {
+      const double* src = a.vals + (pred * 2 + (lane == m ? 1 : 0)) * P;
+#pragma unroll
+      for (int j = 0; j < P; ++j) v[j] = __ldcg(src + j);
+    }
+    // c = A^(lane kTile) v (the identity for lane 0)
+    double c[P];
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) c[i] = v[i];
+    } else {
+      const double* L = a.look + (size_t)lane * P * P;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        double acc = 0.0;
+#pragma unroll
+        for (int j = 0; j < P; ++j) acc = fma(__ldg(L + i * P + j), v[j], acc);
+        c[i] = take ? acc : 0.0;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) c[i] += __shfl_xor_sync(0xffffffffu, c[i], off);
+    }
+    if (first) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) S[i] = c[i];
+    } else {
+      // S += mwin c, mwin = A^(done kTile)
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        double acc = S[i];
+#pragma unroll
+        for (int j = 0; j < P; ++j) acc = fma(mwin[i * P + j], c[j], acc);
+        S[i] = acc;
+      }
+    }
+    if (m < kLook || done + kLook >= tin) break;
+    // the next window lies A^(kLook kTile) further back: mwin <- mwin A^(kLook kTile)
+    __syncwarp();
+    const double* step = a.look + (size_t)kLook * P * P;
+    double row[P];
+    if (lane < P) {
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        double acc = 0.0;
+#pragma unroll
+        for (int q = 0; q < P; ++q) acc = fma(first ? (lane == q ? 1.0 : 0.0) : mwin[lane * P + q], __ldg(step + q * P + j), acc);
+        row[j] = acc;
+      }
+    }
+    __syncwarp();
+    if (lane < P) {
+#pragma unroll
+      for (int j = 0; j < P; ++j) mwin[lane * P + j] = row[j];
+    }
+    __syncwarp();
+    first = false;
+  }
+  double mine = 0.0;
+#pragma unroll
+  for (int j = 0; j < P; ++j)
+    if (j == lane) mine = S[j];
+  return mine;
+}
+
+template <int P, bool kLower, bool kRerun>
+__global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const __grid_constant__ Args a,
+                                                        const __grid_constant__ Tab<P> tab) {
+  extern __shared__ __align__(16) float smem[];
+  float* xs = smem;                                                // kTile samples
+  float* lanes = xs + kTile;                                       // lane table
+  double* wstep = reinterpret_cast<double*>(lanes + lane_floats(P));  // A^(32 kL)
+  double* tot = wstep + P * P;                                     // [kWarps][P] warp totals
+  float* start = reinterpret_cast<float*>(tot + kWarps * P);       // [kWarps][P] warp start states
+  __shared__ int64_t s_tile;
+  __shared__ int s_whead[kWarps];
+  __shared__ double s_mwin[P * P];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool chained = a.tiles_per_row > 1;
+  if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.flags + a.tiles, 1u) : (int64_t)blockIdx.x;
+  copy_async<kThreads>(lanes, a.lanes, lane_floats(P) * 4);
+  copy_async<kThreads>(wstep, a.wstep, P * P * 8);
+  cp_async_commit();
+  __syncthreads();
+
+  // tile geometry: rows [row0, row0 + nrows), memory span [m0, m0 + seg) of each
+  const int64_t tile = s_tile;
+  const int seg = a.seg;
+  int64_t row0, tin, m0;
+  int nrows;
+  if (chained) {
+    row0 = tile / a.tiles_per_row;
+    tin = tile - row0 * a.tiles_per_row;
+    nrows = 1;
+    m0 = a.reverse ? a.n - (tin + 1) * (int64_t)kTile : tin * (int64_t)kTile;
+  } else {
+    row0 = tile * a.rows_per_tile;
+    tin = 0;
+    nrows = (int)min((int64_t)a.rows_per_tile, a.rows - row0);
+    m0 = a.reverse ? a.n - seg : 0;
+  }
+
+  // stage the tile in memory order (zeros outside the rows), 33 loads in flight per thread
+  {
+    float v[kL];
+#pragma unroll
+    for (int k = 0; k < kL; ++k) {
+      const int q = tid + k * kThreads;
+      const int r = (int)__umulhi((uint32_t)q, a.seg_inv);
+      const int64_t m = m0 + (q - r * seg);
+      v[k] = (r < nrows && m >= 0 && m < a.n) ? __ldg(a.x + (row0 + r) * a.ld_x + m) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kL; ++k) xs[tid + k * kThreads] = v[k];
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // this thread's chunk: segment r, chunk lc of the segment
+  const int r = chained ? 0 : tid / a.cpr;
+  const int lc = chained ? tid : tid - r * a.cpr;
+  const bool used = chained || r < nrows;
+  const bool head = chained ? (tin == 0 && tid == 0) : (!used || lc == 0);
+  const int sbase = r * seg;
+  const int p0 = lc * kL;
+  auto at = [&](int t) { return a.reverse ? sbase + seg - 1 - (p0 + t) : sbase + p0 + t; };
+
+  // (chunks past the last packed row hold no data and store nothing; their
+  // shared memory index could lie past the tile)
+  float x[kL];
+#pragma unroll
+  for (int k = 0; k < kL; ++k) x[k] = used ? xs[at(k)] : 0.0f;
+
+  // 1. end state from zero, and the zero-state outputs (in place, last first)
+  float e[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kL; ++k) acc = fmaf(tab.W[k][j], x[k], acc);
+    e[j] = acc;
+  }
+  // Every thread reads and writes only its own chunk's slots of the staged
+  // tile, so the zero-state outputs (impulse form) or the inputs (re-run form)
+  // wait there, not in registers, until the chunk's start state is known.
+  if constexpr (!kRerun) {
+#pragma unroll
+    for (int t = kL - 1; t >= 0; --t) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k <= t; ++k) acc = fmaf(tab.h[t - k], x[k], acc);
+      x[t] = acc;
+    }
+    if (used) {
+#pragma unroll
+      for (int t = 0; t < kL; ++t) xs[at(t)] = x[t];
+    }
+  }
+
+  // 2. segmented scan over the warp's chunks
+  bool f = head;
+#pragma unroll
+  for (int lv = 0; lv < kLevels; ++lv) {
+    const int d = 1 << lv;
+    float pv[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) pv[j] = __shfl_up_sync(0xffffffffu, e[j], d);
+    const bool pf = __shfl_up_sync(0xffffffffu, (int)f, d) != 0;
+    if (lane >= d) {
+      if (!f) {
+        float ne[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          float acc = e[i];
+#pragma unroll
+          for (int j = 0; j < P; ++j)
+            if (!skip<P, kLower>(i, j)) acc = fmaf(tab.M[lv][i][j], pv[j], acc);
+          ne[i] = acc;
+        }
+#pragma unroll
+        for (int i = 0; i < P; ++i) e[i] = ne[i];
+      }
+      f = f || pf;
+    }
+  }
+  // exclusive prefix within the warp, and whether a head precedes this lane
+  float ex[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const float v = __shfl_up_sync(0xffffffffu, e[j], 1);
+    ex[j] = lane == 0 ? 0.0f : v;
+  }
+  // (every lane takes part in the shuffle; lane 0 discards what it receives)
+  const int fup = __shfl_up_sync(0xffffffffu, (int)f, 1);
+  const bool fex = lane != 0 && fup != 0;
+  if (lane == 31) {
+#pragma unroll
+    for (int j = 0; j < P; ++j) tot[warp * P + j] = (double)e[j];
+    s_whead[warp] = f;
+  }
+  __syncthreads();
+
+  // 3. start state of every warp (warp 0), chaining the tiles of a row
+  if (warp == 0) {
+    const bool successor = chained && tin + 1 < a.tiles_per_row;
+    const double agg = chain_warps<P, kLower>(0.0, wstep, tot, s_whead, start, lane);
+    if (chained && tin == 0) {
+      if (successor) publish<P>(a, tile, 1, agg, 2u, lane);
+    } else if (chained) {
+      if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
+      const double sin = lookback<P>(a, tile, tin, s_mwin, lane);
+      if (successor) {
+        // inclusive end state: A^kTile S + aggregate
+        const int i = lane < P ? lane : 0;
+        const double* T1 = a.look + (size_t)P * P;
+        double acc = agg;
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+          const double sj = __shfl_sync(0xffffffffu, sin, j);
+          acc = fma(__ldg(T1 + i * P + j), sj, acc);
+        }
+        publish<P>(a, tile, 1, acc, 2u, lane);
+      }
+      chain_warps<P, kLower>(sin, wstep, tot, s_whead, start, lane);
+    }
+  }
+  __syncthreads();
+
+  // 4. start state of the chunk
+  float s[P];
+  {
+    float xw[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) xw[j] = start[warp * P + j];
+    const float* Lm = lanes + lane * lane_pitch(P);
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float acc = ex[i];
+      if (!fex) {
+#pragma unroll
+        for (int j = 0; j < P; ++j)
+          if (!skip<P, kLower>(i, j)) acc = fmaf(Lm[i * P + j], xw[j], acc);
+      }
+      s[i] = head ? 0.0f : acc;
+    }
+  }
+
+  // 5. outputs, back into the staged tile
+  if (!used) {
+    // no data in this chunk
+  } else if constexpr (kRerun) {
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      const float xt = xs[at(t)];
+      float yv = tab.D * xt;
+#pragma unroll
+      for (int j = 0; j < P; ++j) yv = fmaf(tab.C[j], s[j], yv);
+      float ns[P];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        float acc = tab.B[i] * xt;
+#pragma unroll
+        for (int j = 0; j < P; ++j)
+          if (!skip<P, kLower>(i, j)) acc = fmaf(tab.A[i][j], s[j], acc);
+        ns[i] = acc;
+      }
+#pragma unroll
+      for (int i = 0; i < P; ++i) s[i] = ns[i];
+      xs[at(t)] = yv;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < kL; ++t) {
+      float yv = xs[at(t)];
+#pragma unroll
+      for (int j = 0; j < P; ++j) yv = fmaf(tab.G[t][j], s[j], yv);
+      xs[at(t)] = yv;
+    }
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int k = 0; k < kL; ++k) {
+    const int q = tid + k * kThreads;
+    const int rr = (int)__umulhi((uint32_t)q, a.seg_inv);
+    const int64_t m = m0 + (q - rr * seg);
+    if (rr < nrows && m >= 0 && m < a.n) a.y[(row0 + rr) * a.ld_y + m] = xs[q];
+  }
+}
+
+// Launch of one instantiation (defined in iir_k*.cu).
+template <int P, bool kLower, bool kRerun>
+cudaError_t launch(const Args& a, const void* tab, cudaStream_t s);
+
+}  // namespace iir
+}  // namespace pesq

@@ -169,6 +169,35 @@ at::Tensor resample_adjoint_op(int64_t handle, const at::Tensor& g_in, int64_t n
   return gx;
 }
 
+const pesq_iir* as_iir(int64_t handle) {
+  TORCH_CHECK(handle != 0, "invalid IIR filter handle");
+  return reinterpret_cast<const pesq_iir*>(static_cast<uintptr_t>(handle));
+}
+
+// y = filter(x) along the rows of x [rows, n]; flags: PESQ_IIR_REVERSE (the
+// adjoint), PESQ_IIR_RERUN
+at::Tensor iir_op(int64_t handle, const at::Tensor& x_in, int64_t flags) {
+  TORCH_CHECK(x_in.is_cuda(), "The CUDA IIR filter needs `signal` to live on a GPU.");
+  TORCH_CHECK(x_in.scalar_type() == at::kFloat, "The CUDA IIR filter only supports float32, `signal` is ",
+              x_in.scalar_type(), ".");
+  TORCH_CHECK(x_in.dim() == 2, "The CUDA IIR filter needs a [batch, sample] tensor, got ", x_in.sizes(), ".");
+  const pesq_iir* f = as_iir(handle);
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const at::Tensor x = x_in.stride(1) == 1 ? x_in : x_in.contiguous();
+  const int64_t rows = x.size(0), n = x.size(1);
+  at::Tensor y = at::empty({rows, n}, x.options());
+  if (rows == 0 || n == 0) return y;
+  const size_t ws_bytes = pesq_iir_workspace_bytes(f, rows, n);
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(x.device().index());
+  check_status(pesq_iir_filter(f, stream, x.data_ptr<float>(), std::max<int64_t>(x.stride(0), n), rows, n,
+                               y.data_ptr<float>(), n, (uint32_t)flags, ws_bytes ? ws.data_ptr() : nullptr,
+                               ws_bytes),
+               "pesq_iir_filter");
+  return y;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(pesq_cuda, m) {
@@ -178,6 +207,7 @@ TORCH_LIBRARY(pesq_cuda, m) {
       "Tensor? g_dsymm, Tensor? g_dasymm) -> (Tensor, Tensor)");
   m.def("resample(int resampler, Tensor waveform) -> Tensor");
   m.def("resample_adjoint(int resampler, Tensor grad, int n_in) -> Tensor");
+  m.def("iir(int filter, Tensor signal, int flags) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(pesq_cuda, CUDA, m) {
@@ -185,4 +215,5 @@ TORCH_LIBRARY_IMPL(pesq_cuda, CUDA, m) {
   m.impl("backward", &pesq_backward_op);
   m.impl("resample", &resample_op);
   m.impl("resample_adjoint", &resample_adjoint_op);
+  m.impl("iir", &iir_op);
 }
