@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
+    ap.add_argument("--op", choices=["iir"], default=None,
+                    help="time only a standalone op on its large case (one JSON line; for profiling)")
     args = ap.parse_args()
     global BATCH, SECONDS
     BATCH, SECONDS = WORKLOADS[args.workload]
@@ -366,6 +368,63 @@ def measure_resampler(dev, peak, launches=10):
     }
 
 
+def measure_iir(dev, peak, launches=20, large_only=False):
+    """The standalone IIR filter (IIRCuda, the reference's TritonIIR) with the
+    order 10 PESQ band pass: the reference's own benchmark shapes [8, 16000]
+    and [8, 64000] (per call, eager, CUDA events; forward and forward plus
+    backward through autograd), and [64, 480000] (123 MB in, 123 MB out:
+    beyond L2) for the HBM roofline of the kernel, with the order 2
+    pre-emphasis filter beside it."""
+
+    import torch
+
+    from triton_pesq_b200 import IIRCuda
+    from triton_pesq_b200.tables import power_filter, pre_filter
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, n=launches):
+        for _ in range(3):
+            fn()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(n):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        return 1e3 * start.elapsed_time(stop) / n
+
+    out = {}
+    band = IIRCuda(*power_filter()).to(dev)
+    for rows, n in (() if large_only else ((8, 16000), (8, 64000))):
+        x = torch.randn(rows, n, device=dev)
+        out[f"order10_fwd_{rows}x{n}_us"] = timed(lambda: band(x))
+        leaf = x.clone().requires_grad_(True)
+        g = torch.randn_like(x)
+        out[f"order10_fwd_bwd_{rows}x{n}_us"] = timed(
+            lambda: torch.autograd.grad(band(leaf), leaf, g))
+    large = (((64, 480000), "order10", band), ((64, 480000), "order2", IIRCuda(*pre_filter()).to(dev)),
+             ((30720, 1000), "order10", band))
+    for (rows, n), label, module in large:
+        x = torch.randn(rows, n, device=dev)
+        alg = 8.0 * rows * n  # read every sample once, write every output once
+        fwd = timed(lambda: module(x))
+        handle = module._handle(dev)
+        rev = timed(lambda: torch.ops.pesq_cuda.iir(handle, x, module._flags(True)))
+        out[f"{label}_{rows}x{n}"] = {
+            "forward_us": fwd, "reverse_us": rev,
+            "forward_gbs": alg / (fwd * 1e-6) / 1e9, "reverse_gbs": alg / (rev * 1e-6) / 1e9,
+            "forward_frac_of_measured_hbm": alg / (fwd * 1e-6) / 1e9 / peak,
+            "gsamples_per_s": rows * n / (fwd * 1e-6) / 1e9,
+        }
+    out["note"] = ("per call, eager (allocation and launch included) for the reference's shapes; "
+                   "the reference quotes 83 / 153 us forward and 387 us forward plus backward on a GTX 1080 Ti")
+    errors = band.check_errors()
+    if errors:
+        raise RuntimeError(f"IIR look-back wait gave up (error word {errors})")
+    return out
+
+
 def measure_configs(dev, flush, steps=10):
     """Graph-replayed fwd+bwd (w.r.t. deg) step of the other BASELINE
     configurations on one GPU (L2 flushed before each step): cfg1, cfg3, the
@@ -590,7 +649,7 @@ def run_cuda(args):
     front_us = stages["front"]
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
-    ops = {"resample_44k1_to_16k": measure_resampler(dev, peak)}
+    ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)}
     configs = measure_configs(dev, flush) if not args.skip_configs else None
 
     if world > 1:
@@ -660,9 +719,23 @@ def run_cuda(args):
     print(json.dumps(line), flush=True)
 
 
+def run_op(args):
+    """Only the large case of a standalone op, e.g. as the target of a
+    profiler capture."""
+
+    import torch
+
+    dev = torch.device("cuda", 0)
+    peak, _ = measured_peaks()
+    print(json.dumps({"op": args.op, "measurements": measure_iir(dev, peak, launches=args.steps,
+                                                                  large_only=True)}))
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.op is not None:
+        run_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_cuda(args)
