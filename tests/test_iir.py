@@ -75,8 +75,8 @@ def test_conditioning_covers_every_table(name):
 
     d = D.design(*ALL[name])
     tabs = d.tables()
-    largest = max(np.abs(t).max() for t in (tabs.carry, tabs.drive, tabs.steps, tabs.lanes, tabs.trans,
-                                            tabs.input, tabs.output))
+    largest = max(np.abs(t).max() for t in (tabs.carry, tabs.drive, tabs.steps, tabs.lanes, tabs.warp_powers,
+                                            tabs.trans, tabs.input, tabs.output))
     assert d.entry >= largest * (1.0 - 1e-12)
     assert d.score >= d.entry * D.FLOAT32_EPS
 
@@ -113,7 +113,7 @@ def test_degraded_filter_warns():
 
 def test_kernel_tables_are_consistent():
     """h[t] = C A^(t-1) B, the chunk step is A^33, the lane table its powers,
-    the warp step A^(32*33) and the look-back table the powers of A^8448."""
+    the warp powers those of A^(32*33) and the look-back table those of A^8448."""
 
     d = D.design(*FILTERS["order10"])
     t = d.tables()
@@ -122,7 +122,8 @@ def test_kernel_tables_are_consistent():
     np.testing.assert_allclose(t.steps[0], step, rtol=1e-12, atol=1e-15)
     np.testing.assert_allclose(t.steps[3], np.linalg.matrix_power(step, 8), rtol=1e-10, atol=1e-15)
     np.testing.assert_allclose(t.lanes[5], np.linalg.matrix_power(step, 5), rtol=1e-10, atol=1e-15)
-    np.testing.assert_allclose(t.warp_step, np.linalg.matrix_power(step, 32), rtol=1e-9, atol=1e-15)
+    np.testing.assert_allclose(t.warp_powers[1], np.linalg.matrix_power(step, 32), rtol=1e-9, atol=1e-15)
+    np.testing.assert_allclose(t.warp_powers[8], t.lookback[1], rtol=1e-9, atol=1e-15)
     np.testing.assert_allclose(t.lookback[1], np.linalg.matrix_power(A, D.IIR_TILE), rtol=1e-8, atol=1e-15)
     for k in (1, 7, 20):
         np.testing.assert_allclose(t.impulse[k], C @ np.linalg.matrix_power(A, k - 1) @ B, rtol=1e-12)

@@ -16,8 +16,9 @@
 //   2. a segmented Kogge-Stone scan over the 32 chunks of a warp with the
 //      doubling steps M_i = A^(kL 2^i) (warp shuffles), restarted at every
 //      row start ("head");
-//   3. warp 0 chains the 8 warp totals in float64 with A^(32 kL) into the
-//      start state of every warp, from the tile's start state S;
+//   3. every warp forms its own start state from the totals of the warps
+//      before it and the warp powers A^(32 kL k), back to the last head or
+//      to the tile's start state S (no serial chain across the warps);
 //   4. each chunk's start state is the warp-exclusive prefix plus
 //      A^(kL lane) times its warp's start state (lane table, shared memory);
 //   5. outputs: zero-state part + C A^t s (impulse form) or the recursion
@@ -36,6 +37,9 @@
 // truncated: the result is exact for any stable or unstable filter.  Every
 // wait is bounded (kSpinLimit polls); a wait that gives up records an error
 // in the filter's error word and treats the predecessor as zero.
+//
+// Every warp-collective operation (shuffle, ballot) is executed by all 32
+// lanes of the warp: a lane that skips one leaves the others waiting forever.
 #pragma once
 
 #include "common.cuh"
@@ -70,6 +74,8 @@ struct Tab {
 // the per-lane reads of a warp never share a bank.
 __host__ __device__ constexpr int lane_pitch(int P) { return P * P + 1; }
 __host__ __device__ constexpr int lane_floats(int P) { return 32 * lane_pitch(P); }
+// Warp powers A^(32 kL k), k = 0..kWarps.
+__host__ __device__ constexpr int wpow_floats(int P) { return (kWarps + 1) * P * P; }
 
 struct Args {
   const float* x;
@@ -86,7 +92,7 @@ struct Args {
   int64_t tiles_per_row;   // > 1: the tiles of a row are chained
   int64_t tiles;
   const float* lanes;      // [32][lane_pitch]  A^(kL l)
-  const double* wstep;     // [P][P]            A^(32 kL)
+  const float* wpow;       // [kWarps + 1][P][P] A^(32 kL k)
   const double* look;      // [kLook + 1][P][P] A^(k kTile)
   uint32_t* flags;         // [tiles + 1]: tile status (0, 1 aggregate, 2 inclusive), ticket counter
   double* vals;            // [tiles][2][P]: aggregate, inclusive end state
@@ -94,8 +100,8 @@ struct Args {
 };
 
 __host__ __device__ constexpr size_t smem_bytes(int P) {
-  return (size_t)kTile * 4 + (size_t)lane_floats(P) * 4 + (size_t)P * P * 8 + (size_t)kWarps * P * 8 +
-         (size_t)kWarps * P * 4;
+  return (size_t)kTile * 4 + (size_t)lane_floats(P) * 4 + (size_t)wpow_floats(P) * 4 +
+         (size_t)kWarps * P * 4 + (size_t)P * 4 + 16;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
@@ -106,34 +112,17 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 __device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// 4-byte asynchronous copy global -> shared that writes zero (and reads
+// nothing) when `valid` is false; `src` must still be a valid address.
+__device__ __forceinline__ void cp_async4_zfill(float* dst, const float* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
 
 template <int P, bool kLower>
 __device__ __forceinline__ bool skip(int i, int j) {
   return kLower && (j >> 1) > (i >> 1);
-}
-
-// Warp 0: X_0 = x0 (lane i holds component i), X_{w+1} = head_w ? T_w :
-// A^(32 kL) X_w + T_w; stores X_w (float) for every warp and returns X_8,
-// the tile's end state.
-template <int P, bool kLower>
-__device__ __forceinline__ double chain_warps(double x0, const double* wstep, const double* tot, const int* whead,
-                                              float* start, int lane) {
-  const int i = lane < P ? lane : 0;
-  double xv = x0;
-#pragma unroll 1
-  for (int w = 0; w < kWarps; ++w) {
-    if (lane < P) start[w * P + lane] = (float)xv;
-    double nv = tot[w * P + i];
-    if (!whead[w]) {
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        const double xj = __shfl_sync(0xffffffffu, xv, j);
-        if (!skip<P, kLower>(i, j)) nv = fma(wstep[i * P + j], xj, nv);
-      }
-    }
-    xv = lane < P ? nv : 0.0;
-  }
-  return xv;
 }
 
 // Warp 0: lane 0 stores the P components (lane i holds component i) into
@@ -175,7 +164,7 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
           st = 3u;  // give up: the predecessor counts as a zero inclusive state
           break;
         }
-        __nanosleep(128);
+        __nanosleep(64);
       }
     }
     const unsigned incl = __ballot_sync(0xffffffffu, valid && st >= 2u);
@@ -191,7 +180,7 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
     }
     // c = A^(lane kTile) v (the identity for lane 0)
     double c[P];
-    if (lane == 0) {
+    if (lane == 0 || !take) {
 #pragma unroll
       for (int i = 0; i < P; ++i) c[i] = v[i];
     } else {
@@ -201,7 +190,7 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
         double acc = 0.0;
 #pragma unroll
         for (int j = 0; j < P; ++j) acc = fma(__ldg(L + i * P + j), v[j], acc);
-        c[i] = take ? acc : 0.0;
+        c[i] = acc;
       }
     }
 #pragma unroll
@@ -232,7 +221,8 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
       for (int j = 0; j < P; ++j) {
         double acc = 0.0;
 #pragma unroll
-        for (int q = 0; q < P; ++q) acc = fma(first ? (lane == q ? 1.0 : 0.0) : mwin[lane * P + q], __ldg(step + q * P + j), acc);
+        for (int q = 0; q < P; ++q)
+          acc = fma(first ? (lane == q ? 1.0 : 0.0) : mwin[lane * P + q], __ldg(step + q * P + j), acc);
         row[j] = acc;
       }
     }
@@ -251,15 +241,30 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
   return mine;
 }
 
+// Lane i < P: component i of sum_{v = v0}^{v1 - 1} A^(32 kL (v1 - 1 - v)) T_v
+// (warp totals T in shared memory).
+template <int P, bool kLower>
+__device__ __forceinline__ float warp_sum(const float* wpow, const float* tot, int v0, int v1, int i) {
+  float acc = 0.0f;
+  for (int v = v0; v < v1; ++v) {
+    const float* Wm = wpow + (v1 - 1 - v) * P * P + i * P;
+    const float* T = tot + v * P;
+#pragma unroll
+    for (int j = 0; j < P; ++j)
+      if (!skip<P, kLower>(i, j)) acc = fmaf(Wm[j], T[j], acc);
+  }
+  return acc;
+}
+
 template <int P, bool kLower, bool kRerun>
 __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const __grid_constant__ Args a,
-                                                        const __grid_constant__ Tab<P> tab) {
+                                                                        const __grid_constant__ Tab<P> tab) {
   extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                                                // kTile samples
-  float* lanes = xs + kTile;                                       // lane table
-  double* wstep = reinterpret_cast<double*>(lanes + lane_floats(P));  // A^(32 kL)
-  double* tot = wstep + P * P;                                     // [kWarps][P] warp totals
-  float* start = reinterpret_cast<float*>(tot + kWarps * P);       // [kWarps][P] warp start states
+  float* xs = smem;                              // kTile samples
+  float* lanes = xs + kTile;                     // lane table
+  float* wpow = lanes + lane_floats(P);          // warp powers
+  float* tot = wpow + wpow_floats(P);            // [kWarps][P] warp totals
+  float* sin_s = tot + kWarps * P;               // [P] start state of the tile
   __shared__ int64_t s_tile;
   __shared__ int s_whead[kWarps];
   __shared__ double s_mwin[P * P];
@@ -268,8 +273,7 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
   const bool chained = a.tiles_per_row > 1;
   if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.flags + a.tiles, 1u) : (int64_t)blockIdx.x;
   copy_async<kThreads>(lanes, a.lanes, lane_floats(P) * 4);
-  copy_async<kThreads>(wstep, a.wstep, P * P * 8);
-  cp_async_commit();
+  copy_async<kThreads>(wpow, a.wpow, wpow_floats(P) * 4);
   __syncthreads();
 
   // tile geometry: rows [row0, row0 + nrows), memory span [m0, m0 + seg) of each
@@ -288,39 +292,49 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
     nrows = (int)min((int64_t)a.rows_per_tile, a.rows - row0);
     m0 = a.reverse ? a.n - seg : 0;
   }
+  // a whole, 16-byte aligned tile of one row moves in 16-byte pieces
+  const float* xrow = a.x + row0 * a.ld_x;
+  float* yrow = a.y + row0 * a.ld_y;
+  const bool full = chained && m0 >= 0 && m0 + kTile <= a.n;
+  const bool vec_in = full && ((reinterpret_cast<uintptr_t>(xrow + m0) & 15) == 0);
+  const bool vec_out = full && ((reinterpret_cast<uintptr_t>(yrow + m0) & 15) == 0);
 
-  // stage the tile in memory order (zeros outside the rows), 33 loads in flight per thread
-  {
-    float v[kL];
-#pragma unroll
+  // stage the tile in memory order (zeros outside the rows)
+  if (vec_in) {
+    for (int i = tid; i < kTile / 4; i += kThreads) cp_async16(xs + 4 * i, xrow + m0 + 4 * i);
+  } else {
+#pragma unroll 11
     for (int k = 0; k < kL; ++k) {
       const int q = tid + k * kThreads;
-      const int r = (int)__umulhi((uint32_t)q, a.seg_inv);
+      const int r = chained ? 0 : (int)__umulhi((uint32_t)q, a.seg_inv);
       const int64_t m = m0 + (q - r * seg);
-      v[k] = (r < nrows && m >= 0 && m < a.n) ? __ldg(a.x + (row0 + r) * a.ld_x + m) : 0.0f;
+      const bool valid = r < nrows && m >= 0 && m < a.n;
+      cp_async4_zfill(xs + q, valid ? xrow + r * a.ld_x + m : a.x, valid);
     }
-#pragma unroll
-    for (int k = 0; k < kL; ++k) xs[tid + k * kThreads] = v[k];
   }
+  cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
 
-  // this thread's chunk: segment r, chunk lc of the segment
+  // this thread's chunk: segment r, chunk lc of the segment; its sample t
+  // sits at xs[base + dir * t]
   const int r = chained ? 0 : tid / a.cpr;
   const int lc = chained ? tid : tid - r * a.cpr;
   const bool used = chained || r < nrows;
   const bool head = chained ? (tin == 0 && tid == 0) : (!used || lc == 0);
-  const int sbase = r * seg;
-  const int p0 = lc * kL;
-  auto at = [&](int t) { return a.reverse ? sbase + seg - 1 - (p0 + t) : sbase + p0 + t; };
+  const int dir = a.reverse ? -1 : 1;
+  const int base = a.reverse ? r * seg + seg - 1 - lc * kL : r * seg + lc * kL;
 
   // (chunks past the last packed row hold no data and store nothing; their
   // shared memory index could lie past the tile)
   float x[kL];
 #pragma unroll
-  for (int k = 0; k < kL; ++k) x[k] = used ? xs[at(k)] : 0.0f;
+  for (int k = 0; k < kL; ++k) x[k] = used ? xs[base + dir * k] : 0.0f;
 
-  // 1. end state from zero, and the zero-state outputs (in place, last first)
+  // 1. end state from zero, and the zero-state outputs (in place, last first).
+  // Every thread reads and writes only its own chunk's slots of the staged
+  // tile, so the zero-state outputs (impulse form) or the inputs (re-run form)
+  // wait there, not in registers, until the chunk's start state is known.
   float e[P];
 #pragma unroll
   for (int j = 0; j < P; ++j) {
@@ -329,9 +343,6 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
     for (int k = 0; k < kL; ++k) acc = fmaf(tab.W[k][j], x[k], acc);
     e[j] = acc;
   }
-  // Every thread reads and writes only its own chunk's slots of the staged
-  // tile, so the zero-state outputs (impulse form) or the inputs (re-run form)
-  // wait there, not in registers, until the chunk's start state is known.
   if constexpr (!kRerun) {
 #pragma unroll
     for (int t = kL - 1; t >= 0; --t) {
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
     }
     if (used) {
 #pragma unroll
-      for (int t = 0; t < kL; ++t) xs[at(t)] = x[t];
+      for (int t = 0; t < kL; ++t) xs[base + dir * t] = x[t];
     }
   }
 
@@ -379,48 +390,60 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
     const float v = __shfl_up_sync(0xffffffffu, e[j], 1);
     ex[j] = lane == 0 ? 0.0f : v;
   }
-  // (every lane takes part in the shuffle; lane 0 discards what it receives)
   const int fup = __shfl_up_sync(0xffffffffu, (int)f, 1);
   const bool fex = lane != 0 && fup != 0;
   if (lane == 31) {
 #pragma unroll
-    for (int j = 0; j < P; ++j) tot[warp * P + j] = (double)e[j];
+    for (int j = 0; j < P; ++j) tot[warp * P + j] = e[j];
     s_whead[warp] = f;
   }
   __syncthreads();
 
-  // 3. start state of every warp (warp 0), chaining the tiles of a row
-  if (warp == 0) {
-    const bool successor = chained && tin + 1 < a.tiles_per_row;
-    const double agg = chain_warps<P, kLower>(0.0, wstep, tot, s_whead, start, lane);
-    if (chained && tin == 0) {
-      if (successor) publish<P>(a, tile, 1, agg, 2u, lane);
-    } else if (chained) {
-      if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
-      const double sin = lookback<P>(a, tile, tin, s_mwin, lane);
-      if (successor) {
-        // inclusive end state: A^kTile S + aggregate
-        const int i = lane < P ? lane : 0;
-        const double* T1 = a.look + (size_t)P * P;
-        double acc = agg;
+  // 3. start state of this warp: back to the last warp with a head, or to
+  //    the tile's start state (lane i < P holds component i)
+  int h = -1;
+  for (int v = 0; v < warp; ++v)
+    if (s_whead[v]) h = v;
+  const int ci = lane < P ? lane : 0;
+  float xw = warp_sum<P, kLower>(wpow, tot, h < 0 ? 0 : h, warp, ci);
+  if (chained) {
+    const bool successor = tin + 1 < a.tiles_per_row;
+    if (tin == 0) {
+      if (warp == 0 && successor)
+        publish<P>(a, tile, 1, (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci), 2u, lane);
+    } else {
+      if (warp == 0) {
+        const double agg = (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci);
+        if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
+        const double sv = lookback<P>(a, tile, tin, s_mwin, lane);
+        if (successor) {
+          // inclusive end state: A^kTile S + aggregate
+          const double* T1 = a.look + (size_t)P * P;
+          double acc = agg;
 #pragma unroll
-        for (int j = 0; j < P; ++j) {
-          const double sj = __shfl_sync(0xffffffffu, sin, j);
-          acc = fma(__ldg(T1 + i * P + j), sj, acc);
+          for (int j = 0; j < P; ++j) {
+            const double sj = __shfl_sync(0xffffffffu, sv, j);
+            acc = fma(__ldg(T1 + ci * P + j), sj, acc);
+          }
+          publish<P>(a, tile, 1, acc, 2u, lane);
         }
-        publish<P>(a, tile, 1, acc, 2u, lane);
+        if (lane < P) sin_s[lane] = (float)sv;
       }
-      chain_warps<P, kLower>(sin, wstep, tot, s_whead, start, lane);
+      __syncthreads();
+      // no head in a tile after the first of its row: add A^(32 kL warp) S
+      const float* Wm = wpow + warp * P * P + ci * P;
+#pragma unroll
+      for (int j = 0; j < P; ++j)
+        if (!skip<P, kLower>(ci, j)) xw = fmaf(Wm[j], sin_s[j], xw);
     }
   }
-  __syncthreads();
 
   // 4. start state of the chunk
   float s[P];
   {
-    float xw[P];
+    float xv[P];
 #pragma unroll
-    for (int j = 0; j < P; ++j) xw[j] = start[warp * P + j];
+    for (int j = 0; j < P; ++j) xv[j] = __shfl_sync(0xffffffffu, xw, j);
     const float* Lm = lanes + lane * lane_pitch(P);
 #pragma unroll
     for (int i = 0; i < P; ++i) {
@@ -428,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
       if (!fex) {
 #pragma unroll
         for (int j = 0; j < P; ++j)
-          if (!skip<P, kLower>(i, j)) acc = fmaf(Lm[i * P + j], xw[j], acc);
+          if (!skip<P, kLower>(i, j)) acc = fmaf(Lm[i * P + j], xv[j], acc);
       }
       s[i] = head ? 0.0f : acc;
     }
@@ -440,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
   } else if constexpr (kRerun) {
 #pragma unroll
     for (int t = 0; t < kL; ++t) {
-      const float xt = xs[at(t)];
+      const float xt = xs[base + dir * t];
       float yv = tab.D * xt;
 #pragma unroll
       for (int j = 0; j < P; ++j) yv = fmaf(tab.C[j], s[j], yv);
@@ -455,25 +478,31 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
       }
 #pragma unroll
       for (int i = 0; i < P; ++i) s[i] = ns[i];
-      xs[at(t)] = yv;
+      xs[base + dir * t] = yv;
     }
   } else {
 #pragma unroll
     for (int t = 0; t < kL; ++t) {
-      float yv = xs[at(t)];
+      float yv = xs[base + dir * t];
 #pragma unroll
       for (int j = 0; j < P; ++j) yv = fmaf(tab.G[t][j], s[j], yv);
-      xs[at(t)] = yv;
+      xs[base + dir * t] = yv;
     }
   }
   __syncthreads();
 
-#pragma unroll
-  for (int k = 0; k < kL; ++k) {
-    const int q = tid + k * kThreads;
-    const int rr = (int)__umulhi((uint32_t)q, a.seg_inv);
-    const int64_t m = m0 + (q - rr * seg);
-    if (rr < nrows && m >= 0 && m < a.n) a.y[(row0 + rr) * a.ld_y + m] = xs[q];
+  if (vec_out) {
+    float4* dst = reinterpret_cast<float4*>(yrow + m0);
+    const float4* src = reinterpret_cast<const float4*>(xs);
+    for (int i = tid; i < kTile / 4; i += kThreads) dst[i] = src[i];
+  } else {
+#pragma unroll 11
+    for (int k = 0; k < kL; ++k) {
+      const int q = tid + k * kThreads;
+      const int rr = chained ? 0 : (int)__umulhi((uint32_t)q, a.seg_inv);
+      const int64_t m = m0 + (q - rr * seg);
+      if (rr < nrows && m >= 0 && m < a.n) yrow[rr * a.ld_y + m] = xs[q];
+    }
   }
 }
 

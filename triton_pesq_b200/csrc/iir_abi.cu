@@ -50,7 +50,7 @@ struct pesq_iir {
   bool lower = false;     // A block lower triangular in 2 x 2 blocks
   std::vector<float> tab; // Tab<kstates> image
   float* lanes = nullptr;
-  double* wstep = nullptr;
+  float* wpow = nullptr;
   double* look = nullptr;
   uint32_t* err = nullptr;
   double largest32 = 0.0, largest64 = 0.0;
@@ -114,11 +114,11 @@ struct TabLayout {
 
 void free_tables(pesq_iir* f) {
   cudaFree(f->lanes);
-  cudaFree(f->wstep);
+  cudaFree(f->wpow);
   cudaFree(f->look);
   cudaFree(f->err);
   f->lanes = nullptr;
-  f->wstep = nullptr;
+  f->wpow = nullptr;
   f->look = nullptr;
   f->err = nullptr;
 }
@@ -237,8 +237,10 @@ int pesq_iir_create(const pesq_iir_desc* d, pesq_iir** out) {
     cur = mul(chunk_step, cur, P);
   }
   const Mat wstep = cur;  // A^(32 L)
-  Mat tile_step = eye(P);
-  for (int w = 0; w < kWarps; ++w) tile_step = mul(wstep, tile_step, P);
+  std::vector<Mat> wp(kWarps + 1);  // A^(32 L k), k = 0..kWarps
+  wp[0] = eye(P);
+  for (int w = 1; w <= kWarps; ++w) wp[w] = mul(wstep, wp[w - 1], P);
+  const Mat tile_step = wp[kWarps];
   std::vector<double> look((size_t)(kLook + 1) * P * P);
   cur = eye(P);
   for (int k = 0; k <= kLook; ++k) {
@@ -278,19 +280,24 @@ int pesq_iir_create(const pesq_iir_desc* d, pesq_iir** out) {
     for (size_t q = 0; q < (size_t)P * P; ++q) lane_img[(size_t)l * lane_pitch(P) + q] = (float)lanes[l][q];
     big32 = std::fmax(big32, absmax(lanes[l]));
   }
+  std::vector<float> wpow_img((size_t)wpow_floats(P), 0.0f);
+  for (int w = 0; w <= kWarps; ++w) {
+    for (size_t q = 0; q < (size_t)P * P; ++q) wpow_img[(size_t)w * P * P + q] = (float)wp[w][q];
+    big32 = std::fmax(big32, absmax(wp[w]));
+  }
   f->largest32 = big32;
-  f->largest64 = std::fmax(absmax(wstep), absmax(look));
+  f->largest64 = absmax(look);
   if (!std::isfinite(f->largest32) || !std::isfinite(f->largest64)) {
     delete f;
     return set_error(PESQ_ERR_INVALID_ARGUMENT, "the realisation's tables overflow");
   }
 
   cudaError_t e = cudaMalloc(&f->lanes, lane_img.size() * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&f->wstep, sizeof(double) * P * P);
+  if (e == cudaSuccess) e = cudaMalloc(&f->wpow, wpow_img.size() * 4);
   if (e == cudaSuccess) e = cudaMalloc(&f->look, sizeof(double) * look.size());
   if (e == cudaSuccess) e = cudaMalloc(&f->err, 16);
   if (e == cudaSuccess) e = cudaMemcpy(f->lanes, lane_img.data(), lane_img.size() * 4, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemcpy(f->wstep, wstep.data(), sizeof(double) * P * P, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(f->wpow, wpow_img.data(), wpow_img.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(f->look, look.data(), sizeof(double) * look.size(), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(f->err, 0, 16);
   if (e != cudaSuccess) {
@@ -360,7 +367,7 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   a.tiles_per_row = g.tiles_per_row;
   a.tiles = g.tiles;
   a.lanes = f->lanes;
-  a.wstep = f->wstep;
+  a.wpow = f->wpow;
   a.look = f->look;
   a.err = f->err;
   if (g.chained()) {

@@ -24,7 +24,7 @@ own impulse response already is from the difference equation's) and its
 with, times the float32 unit round-off), as in iir.py:436-517.  The tables are
 the ones of the sm_100a kernel (``csrc/iir.cuh``), whose geometry differs from
 the reference's Triton tiles: 33-sample thread chunks, a 5 level warp scan, a
-lane table, a per-warp step and a per-tile look-back table.  Selection,
+lane table, warp powers and a per-tile look-back table.  Selection,
 rejection (predicted peak relative error above ``1e5`` round-offs) and the
 warning threshold (``1e3`` round-offs) follow iir.py:520-599.
 """
@@ -261,16 +261,6 @@ def _block_lower(trans: np.ndarray) -> bool:
     return True
 
 
-def _matpow(m: np.ndarray, e: int) -> np.ndarray:
-    out = np.eye(m.shape[0])
-    base = m.copy()
-    while e:
-        if e & 1:
-            out = out @ base
-        base = base @ base
-        e >>= 1
-    return out
-
 
 @dataclass
 class KernelTables:
@@ -281,9 +271,9 @@ class KernelTables:
     ``y[t] = sum_k impulse[t-k] x[k] + carry[t] . S`` and the end state is
     ``A^L S + sum_k drive[k] x[k]``; ``steps[i] = A^(L 2^i)`` drive the warp
     scan, ``lanes[l] = A^(L l)`` carry a warp's start state to its lanes,
-    ``warp_step = A^(32 L)`` chains the warps of a tile and
-    ``lookback[k] = A^(k T)`` (``T`` samples per tile) chains the tiles of a
-    row.
+    ``warp_powers[k] = A^(32 L k)`` (k = 0..8) give every warp its start state
+    from the totals of the warps before it, and ``lookback[k] = A^(k T)``
+    (``T`` samples per tile, float64) chains the tiles of a row.
     """
 
     order: int
@@ -295,7 +285,7 @@ class KernelTables:
     drive: np.ndarray  # [L, P]
     steps: np.ndarray  # [levels, P, P]
     lanes: np.ndarray  # [32, P, P]
-    warp_step: np.ndarray  # [P, P]
+    warp_powers: np.ndarray  # [9, P, P]
     lookback: np.ndarray  # [33, P, P]
     trans: np.ndarray
     input: np.ndarray
@@ -308,13 +298,13 @@ class KernelTables:
         of the filter rather than the realisation, excluded as iir.py:768-823)."""
 
         return float(max(np.abs(t).max() for t in (self.carry, self.drive, self.steps, self.lanes,
-                                                   self.trans, self.input, self.output)))
+                                                   self.warp_powers, self.trans, self.input, self.output)))
 
     @property
     def largest64(self) -> float:
         """Largest entry of the float64 tables (tile chaining)."""
 
-        return float(max(np.abs(self.warp_step).max(), np.abs(self.lookback).max()))
+        return float(np.abs(self.lookback).max())
 
 
 def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> KernelTables:
@@ -356,7 +346,12 @@ def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> Kern
         lanes[l] = cur
         cur = chunk_step @ cur
     warp_step = cur  # A^(32 L)
-    tile_step = _matpow(warp_step, IIR_WARPS)  # A^T
+    warp_powers = np.zeros((IIR_WARPS + 1, p, p))
+    cur = np.eye(p)
+    for k in range(IIR_WARPS + 1):
+        warp_powers[k] = cur
+        cur = warp_step @ cur
+    tile_step = warp_powers[IIR_WARPS]  # A^T
     lookback = np.zeros((IIR_LOOKBACK + 1, p, p))
     cur = np.eye(p)
     with np.errstate(over="ignore", invalid="ignore"):
@@ -366,7 +361,7 @@ def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> Kern
 
     return KernelTables(order=order if order is not None else realised, realised_states=realised, states=p,
                         lower=_block_lower(A), impulse=impulse, carry=carry, drive=drive_tab, steps=steps,
-                        lanes=lanes, warp_step=warp_step, lookback=lookback, trans=A, input=B, output=C,
+                        lanes=lanes, warp_powers=warp_powers, lookback=lookback, trans=A, input=B, output=C,
                         feed=float(feed))
 
 
