@@ -475,6 +475,82 @@ def measure_configs(dev, flush, steps=10):
     return out
 
 
+def measure_fused(dev, flush, steps=10):
+    """The loss inside a caller's mixed-precision training step: the headline
+    8 x 8 s fwd+bwd with bfloat16 inputs (graph replay, L2 flushed), and the
+    same step on a side stream overlapping a chain of bf16 GEMMs on the
+    default stream (a stand-in for the model's backward), against the two
+    run back to back."""
+
+    import torch
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.signals import workload
+
+    ref_c, deg_c, sr = workload("cfg2", seed=0)
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+
+    def capture(ref, deg):
+        model = PesqLossCuda(1.0, sample_rate=sr)
+
+        def step():
+            loss = model(ref, deg)
+            torch.autograd.grad(loss.sum(), [deg])
+
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        main.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        return graph
+
+    def timed(fn):
+        times = []
+        for k in range(steps + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(main)
+            fn()
+            b.record(main)
+            b.synchronize()
+            if k >= 3:
+                times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    out = {}
+    g16 = capture(ref_c.to(dev, torch.bfloat16), deg_c.to(dev, torch.bfloat16).requires_grad_(True))
+    out["bf16_inputs_ms_per_step"] = timed(g16.replay)
+    g32 = capture(ref_c.to(dev), deg_c.to(dev).requires_grad_(True))
+    out["fp32_inputs_ms_per_step"] = timed(g32.replay)
+    a = torch.randn(4096, 4096, device=dev, dtype=torch.bfloat16)
+
+    def gemms():
+        c = a
+        for _ in range(4):
+            c = c @ a
+
+    def both():
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            g32.replay()
+        gemms()
+        main.wait_stream(side)
+
+    out["gemm_chain_ms"] = timed(gemms)
+    out["serial_ms"] = out["gemm_chain_ms"] + out["fp32_inputs_ms_per_step"]
+    out["overlapped_ms"] = timed(both)
+    out["hidden_fraction_of_loss_step"] = (out["serial_ms"] - out["overlapped_ms"]) / out["fp32_inputs_ms_per_step"]
+    out["note"] = "gemm chain: 4 bf16 4096^3 products on the default stream; the loss step on a side stream"
+    del g16, g32
+    return out
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
@@ -651,6 +727,7 @@ def run_cuda(args):
     traffic = profiled_traffic()
     ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)}
     configs = measure_configs(dev, flush) if not args.skip_configs else None
+    fused = measure_fused(dev, flush) if not args.skip_configs else None
 
     if world > 1:
         graph.reset()
@@ -708,6 +785,7 @@ def run_cuda(args):
         "stages_us": stages,
         "ops": ops,
         "other_configs": configs,
+        "in_training_step": fused,
         "dominant_stage": dominant,
         "eager_ms_per_step": 1e3 * statistics.median(eager),
         "step_ms_min": min(step_ms),

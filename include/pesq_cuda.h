@@ -50,6 +50,13 @@ typedef enum pesq_status {
  * g_dasymm) points to ONE value shared by every utterance of the batch, as
  * the gradient of a sum or mean over the batch is; saves materialising it */
 #define PESQ_UPSTREAM_SCALAR 4u
+/* forward: element type of ref / deg (float32 without either flag).  Each
+ * sample is widened to float as the first kernel reads it; everything after
+ * runs in float32 / float64 exactly as for float32 inputs of the same values,
+ * and the gradients of the backward are float32.  (The reference accepts
+ * float32 only; this serves a caller training in mixed precision.) */
+#define PESQ_INPUT_BF16 8u
+#define PESQ_INPUT_F16 16u
 
 typedef struct pesq_plan pesq_plan;
 
@@ -130,10 +137,11 @@ int pesq_query_shape(const pesq_plan* plan, int64_t n_src, pesq_shape* shape);
 int pesq_workspace_size(const pesq_plan* plan, int64_t batch, int64_t n_src, uint32_t flags, size_t* bytes);
 
 /* Forward pass of `batch` utterance pairs.  ref / deg: [batch, n_src] rows
- * with row strides ld_ref / ld_deg (elements, >= n_src).  Any of the four
+ * with row strides ld_ref / ld_deg (elements, >= n_src) of float32, or of
+ * bf16 / fp16 with PESQ_INPUT_BF16 / PESQ_INPUT_F16.  Any of the four
  * outputs ([batch] each) may be NULL.  Replaces PesqLossTriton.raw / mos /
  * forward (triton_ops/loss.py:104-147, 203-215). */
-int pesq_forward(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+int pesq_forward(const pesq_plan* plan, void* stream, const void* ref, int64_t ld_ref, const void* deg,
                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
                  size_t workspace_bytes, float* d_symm, float* d_asymm, float* mos, float* loss);
 
@@ -156,7 +164,7 @@ int pesq_backward(const pesq_plan* plan, void* stream, const float* ref, int64_t
  *          (replaces triton_ops/loss.py:133-143: peak_normalize .. spectral)
  *   chain: perceptual model, distances, MOS and loss
  *          (replaces triton_ops/loss.py:145-147 and elementwise.py:683-747) */
-int pesq_forward_front(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+int pesq_forward_front(const pesq_plan* plan, void* stream, const void* ref, int64_t ld_ref, const void* deg,
                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
                        size_t workspace_bytes);
 int pesq_forward_chain(const pesq_plan* plan, void* stream, int64_t batch, int64_t n_src, uint32_t flags,

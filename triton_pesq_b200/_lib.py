@@ -23,6 +23,8 @@ ABI_VERSION = 2
 GRAD_REF = 1
 GRAD_DEG = 2
 UPSTREAM_SCALAR = 4
+INPUT_BF16 = 8
+INPUT_F16 = 16
 
 PESQ_OK = 0
 PESQ_ERR_INVALID_ARGUMENT = 1

@@ -1,6 +1,7 @@
 // Shared constants and small device helpers of the PESQ engine (sm_100a).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -250,6 +251,27 @@ __device__ __forceinline__ void stage_span(float* dst, const float* src, int64_t
   }
 #pragma unroll
   for (int k = 0; k < kPer; ++k) dst[threadIdx.x + k * kThreads] = v[k];
+}
+
+// stage_span over a row of 16-bit elements (type 1: bf16, 2: fp16), widened
+// to float; type 0 is stage_span itself.
+__device__ __forceinline__ void stage_span_any(float* dst, const void* src, int64_t base, int64_t n, int type) {
+  if (type == 0) {
+    stage_span(dst, static_cast<const float*>(src), base, n);
+    return;
+  }
+  constexpr int kPer = kSpan / kThreads;
+  const unsigned short* s = static_cast<const unsigned short*>(src);
+  unsigned short v[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int64_t g = base + threadIdx.x + k * kThreads;
+    v[k] = (g >= 0 && g < n) ? __ldg(s + g) : (unsigned short)0;
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k)
+    dst[threadIdx.x + k * kThreads] =
+        type == 1 ? __uint_as_float((unsigned)v[k] << 16) : __half2float(__ushort_as_half(v[k]));
 }
 
 // dst[k * pitch + t] = src[k * src_pitch + t] for k < rows, t < cnt, by a CTA

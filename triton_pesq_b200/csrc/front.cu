@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t a = (int64_t)seg * p.seg_frames * kHop;
   const int64_t send = min(a + (int64_t)p.seg_frames * kHop, n_row);
   const int64_t base = a - kHorizon;
-  const float* xr = p.src.row(row);
+  const void* xr = p.src.row_any(row);  // the caller's rows (any element type)
   const bool grad_row = row >= p.spec_begin && row < p.spec_end;
   PESQ_SPAN_BEGIN(g_span_front, 0);
   PESQ_CTA_BEGIN(g_cta_front);
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
   // On gradient rows fb first holds f = H x (below), the low part only after.
   const bool has_lo = p.src_lo.ref != nullptr;
-  stage_span(xs, xr, base, n_row);
+  stage_span_any(xs, xr, base, n_row, p.src.type);
   if (has_lo && !grad_row) stage_span(fb, p.src_lo.row(row), base, n_row);
   cp_async_wait_all();
   __syncthreads();

@@ -37,16 +37,36 @@ struct alignas(16) DevTables {
 using DevTwiddle64 = FftTwiddles<double>;
 
 // Rows of one call: ref rows are 0..B-1, deg rows B..2B-1.
+// Element type of a caller's input rows; every buffer of the engine itself is
+// float32.
+enum InputType : int { kInF32 = 0, kInBF16 = 1, kInF16 = 2 };
+
 struct RowSource {
   const float* ref;
   const float* deg;
-  int64_t ld_ref;
+  int64_t ld_ref;  // row strides in elements
   int64_t ld_deg;
   int batch;
+  int type = kInF32;  // caller rows only: bf16 / fp16 rows are widened to float as they are read
+  // float rows
   __device__ __forceinline__ const float* row(int r) const {
     return r < batch ? ref + (int64_t)r * ld_ref : deg + (int64_t)(r - batch) * ld_deg;
   }
+  // rows of any element type (read through load_elem)
+  __device__ __forceinline__ const void* row_any(int r) const {
+    const char* base = reinterpret_cast<const char*>(r < batch ? ref : deg);
+    const int64_t off = r < batch ? (int64_t)r * ld_ref : (int64_t)(r - batch) * ld_deg;
+    return base + off * (type == kInF32 ? 4 : 2);
+  }
 };
+
+// Element i of a row of the given type, widened to float (exact for bf16 and
+// fp16).
+__device__ __forceinline__ float load_elem(const void* p, int64_t i, int type) {
+  if (type == kInF32) return __ldg(static_cast<const float*>(p) + i);
+  const unsigned short u = __ldg(static_cast<const unsigned short*>(p) + i);
+  return type == kInBF16 ? __uint_as_float((unsigned)u << 16) : __half2float(__ushort_as_half(u));
+}
 
 struct RowSink {
   float* ref;

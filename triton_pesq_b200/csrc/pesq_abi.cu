@@ -128,8 +128,10 @@ int64_t resampled_length(const pesq_plan* p, int64_t n) {
 }
 
 int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, Geometry& g) {
-  if (flags & ~(PESQ_GRAD_REF | PESQ_GRAD_DEG | PESQ_UPSTREAM_SCALAR))
+  if (flags & ~(PESQ_GRAD_REF | PESQ_GRAD_DEG | PESQ_UPSTREAM_SCALAR | PESQ_INPUT_BF16 | PESQ_INPUT_F16))
     return fail(PESQ_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if ((flags & PESQ_INPUT_BF16) && (flags & PESQ_INPUT_F16))
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "PESQ_INPUT_BF16 and PESQ_INPUT_F16 together");
   if (batch < 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "negative batch %lld", (long long)batch);
   if (n_src <= 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "signals need at least one sample");
   g.batch = batch;
@@ -370,8 +372,12 @@ int pesq_workspace_size(const pesq_plan* p, int64_t batch, int64_t n_src, uint32
   return PESQ_OK;
 }
 
-int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int64_t ld_ref, const void* deg_in,
                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes) {
+  // the caller's rows; 16-bit rows are widened to float as the first kernel reads them
+  const float* ref = static_cast<const float*>(ref_in);
+  const float* deg = static_cast<const float*>(deg_in);
+  const int in_type = (flags & PESQ_INPUT_BF16) ? kInBF16 : (flags & PESQ_INPUT_F16) ? kInF16 : kInF32;
   if (!p) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL plan");
   Geometry g;
   int rc = geometry(p, batch, n_src, flags, g);
@@ -383,13 +389,13 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const float* ref, int64
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch};
+  RowSource src16{ref, deg, ld_ref, ld_deg, (int)batch, in_type};
   RowSource lo16{nullptr, nullptr, 0, 0, (int)batch};
   if (g.resample) {
     float* x16 = at<float>(ws, g.x16);
     float* x16lo = at<float>(ws, g.x16lo);
     ResampleArgs ra = resample_args(p->rs, n_src, g.n16);
-    ra.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch};
+    ra.src = RowSource{ref, deg, ld_ref, ld_deg, (int)batch, in_type};
     ra.dst = RowSink{x16, x16 + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.dst_lo = RowSink{x16lo, x16lo + batch * g.n16, g.n16, g.n16, (int)batch};
     ra.rows = (int)g.rows;
@@ -451,7 +457,7 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   return PESQ_OK;
 }
 
-int pesq_forward(const pesq_plan* p, void* stream, const float* ref, int64_t ld_ref, const float* deg,
+int pesq_forward(const pesq_plan* p, void* stream, const void* ref, int64_t ld_ref, const void* deg,
                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes,
                  float* d_symm, float* d_asymm, float* mos, float* loss) {
   const int rc = pesq_forward_front(p, stream, ref, ld_ref, deg, ld_deg, batch, n_src, flags, ws, ws_bytes);

@@ -65,19 +65,28 @@ __global__ void __launch_bounds__(kResampleThreads) resample_fwd_kernel(const __
   const int j = (int)(m - l * p.new_step);
   const int cnt = p.count[j];
   const float* taps = p.taps + (int64_t)j * p.max_count;
-  const float* x = p.src.row(r);
   const int64_t s0 = l * p.orig_step + p.first[j] - p.width;
   // accumulated in double and returned as a float hi/lo pair: the resampled
   // signal feeds the double precision pre-emphasis and spectrum of the front
   // kernel, and near-silent bands make the loss gradient sensitive to its
   // rounding
   double acc = 0.0;
-  if (s0 >= 0 && s0 + cnt <= p.n_in) {
-    for (int i = 0; i < cnt; ++i) acc = fma((double)taps[i], (double)__ldg(x + s0 + i), acc);
+  if (p.src.type == kInF32) {
+    const float* x = p.src.row(r);
+    if (s0 >= 0 && s0 + cnt <= p.n_in) {
+      for (int i = 0; i < cnt; ++i) acc = fma((double)taps[i], (double)__ldg(x + s0 + i), acc);
+    } else {
+      for (int i = 0; i < cnt; ++i) {
+        const int64_t s = s0 + i;
+        const float v = (s >= 0 && s < p.n_in) ? __ldg(x + s) : 0.0f;
+        acc = fma((double)taps[i], (double)v, acc);
+      }
+    }
   } else {
+    const void* x = p.src.row_any(r);
     for (int i = 0; i < cnt; ++i) {
       const int64_t s = s0 + i;
-      const float v = (s >= 0 && s < p.n_in) ? __ldg(x + s) : 0.0f;
+      const float v = (s >= 0 && s < p.n_in) ? load_elem(x, s, p.src.type) : 0.0f;
       acc = fma((double)taps[i], (double)v, acc);
     }
   }
@@ -109,7 +118,8 @@ __global__ void __launch_bounds__(kResampleThreads)
     fi[i] = __ldg(p.first + i);
     co[i] = __ldg(p.count + i);
   }
-  const float* x = p.src.row(r);
+  const void* x = p.src.row_any(r);  // the caller's rows (any element type)
+  const int xtype = p.src.type;
   float* y = p.dst.row(r);
   const int64_t c0 = (int64_t)blockIdx.x * chunk;
   const int64_t c1 = min(c0 + chunk, p.n_out);
@@ -119,9 +129,17 @@ __global__ void __launch_bounds__(kResampleThreads)
     const int64_t base = l_first * os - p.width;  // input index of xs[0]
     const int span = (int)(((m_end - 1) / ns - l_first) * os + p.width_total);
     __syncthreads();  // the previous step is done with xs
-    for (int i = tid; i < span; i += kResampleThreads) {
-      const int64_t g = base + i;
-      xs[i] = (g >= 0 && g < p.n_in) ? __ldg(x + g) : 0.0f;
+    if (xtype == kInF32) {
+      const float* xf = static_cast<const float*>(x);
+      for (int i = tid; i < span; i += kResampleThreads) {
+        const int64_t g = base + i;
+        xs[i] = (g >= 0 && g < p.n_in) ? __ldg(xf + g) : 0.0f;
+      }
+    } else {
+      for (int i = tid; i < span; i += kResampleThreads) {
+        const int64_t g = base + i;
+        xs[i] = (g >= 0 && g < p.n_in) ? load_elem(x, g, xtype) : 0.0f;
+      }
     }
     __syncthreads();
     for (int64_t m = m0 + tid; m < m_end; m += kResampleThreads) {

@@ -26,10 +26,20 @@ void check_status(int status, const char* what) {
 
 void check_signal(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), "The CUDA PESQ backend needs `", name, "` to live on a GPU.");
-  TORCH_CHECK(t.scalar_type() == at::kFloat, "The CUDA PESQ backend only supports float32, `", name, "` is ",
+  TORCH_CHECK(t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf,
+              "The CUDA PESQ backend supports float32 (and bfloat16 / float16 inputs), `", name, "` is ",
               t.scalar_type(), ".");
   TORCH_CHECK(t.dim() == 2, "`", name, "` must be [batch, sample], got ", t.sizes());
   TORCH_CHECK(t.stride(1) == 1, "`", name, "` rows must be contiguous");
+}
+
+// PESQ_INPUT_* flag of the inputs' element type
+uint32_t input_flag(const at::Tensor& ref, const at::Tensor& deg) {
+  TORCH_CHECK_VALUE(ref.scalar_type() == deg.scalar_type(), "ref and deg must have the same dtype, got ",
+                    ref.scalar_type(), " and ", deg.scalar_type(), ".");
+  if (ref.scalar_type() == at::kBFloat16) return PESQ_INPUT_BF16;
+  if (ref.scalar_type() == at::kHalf) return PESQ_INPUT_F16;
+  return 0u;
 }
 
 const pesq_plan* as_plan(int64_t handle) {
@@ -49,14 +59,15 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> pesq_forw
   const pesq_plan* plan = as_plan(plan_handle);
   c10::cuda::CUDAGuard guard(ref.device());
   const int64_t batch = ref.size(0), n = ref.size(1);
+  flags |= input_flag(ref, deg);
   size_t bytes = 0;
   check_status(pesq_workspace_size(plan, batch, n, (uint32_t)flags, &bytes), "pesq_workspace_size");
-  auto opts = ref.options();
+  auto opts = ref.options().dtype(at::kFloat);
   at::Tensor ws = at::empty({(int64_t)((bytes + 3) / 4)}, opts);
   at::Tensor d_symm = at::empty({batch}, opts), d_asymm = at::empty({batch}, opts);
   at::Tensor mos = at::empty({batch}, opts), loss = at::empty({batch}, opts);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index());
-  check_status(pesq_forward(plan, stream, ref.data_ptr<float>(), ref.stride(0), deg.data_ptr<float>(),
+  check_status(pesq_forward(plan, stream, ref.data_ptr(), ref.stride(0), deg.data_ptr(),
                             deg.stride(0), batch, n, (uint32_t)flags, ws.data_ptr(), bytes,
                             d_symm.data_ptr<float>(), d_asymm.data_ptr<float>(), mos.data_ptr<float>(),
                             loss.data_ptr<float>()),
@@ -104,18 +115,27 @@ std::tuple<at::Tensor, at::Tensor> pesq_backward_op(int64_t plan_handle, const a
   const pesq_plan* plan = as_plan(plan_handle);
   c10::cuda::CUDAGuard guard(ref.device());
   const int64_t batch = ref.size(0), n = ref.size(1);
-  // a gradient that was not asked for comes back as an empty tensor
-  at::Tensor g_ref = (flags & PESQ_GRAD_REF) ? at::empty({batch, n}, ref.options()) : at::empty({0}, ref.options());
-  at::Tensor g_deg = (flags & PESQ_GRAD_DEG) ? at::empty({batch, n}, deg.options()) : at::empty({0}, deg.options());
+  flags |= input_flag(ref, deg);
+  // a gradient that was not asked for comes back as an empty tensor; the
+  // engine writes float32 gradients, returned in the inputs' dtype
+  const auto fopts = ref.options().dtype(at::kFloat);
+  at::Tensor g_ref = (flags & PESQ_GRAD_REF) ? at::empty({batch, n}, fopts) : at::empty({0}, ref.options());
+  at::Tensor g_deg = (flags & PESQ_GRAD_DEG) ? at::empty({batch, n}, fopts) : at::empty({0}, deg.options());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index());
   const c10::optional<at::Tensor>* g[4] = {&g_loss, &g_mos, &g_dsymm, &g_dasymm};
   const Upstream up(g, batch);
-  check_status(pesq_backward(plan, stream, ref.data_ptr<float>(), ref.stride(0), deg.data_ptr<float>(),
-                             deg.stride(0), batch, n, (uint32_t)flags | up.flag, ws.data_ptr(),
+  // (ref / deg are not read by the backward)
+  check_status(pesq_backward(plan, stream, static_cast<const float*>(ref.data_ptr()), ref.stride(0),
+                             static_cast<const float*>(deg.data_ptr()), deg.stride(0), batch, n,
+                             (uint32_t)flags | up.flag, ws.data_ptr(),
                              (size_t)ws.numel() * 4, up.ptr[0], up.ptr[1], up.ptr[2], up.ptr[3],
                              (flags & PESQ_GRAD_REF) ? g_ref.data_ptr<float>() : nullptr, n,
                              (flags & PESQ_GRAD_DEG) ? g_deg.data_ptr<float>() : nullptr, n),
                "pesq_backward");
+  if (ref.scalar_type() != at::kFloat) {
+    if (flags & PESQ_GRAD_REF) g_ref = g_ref.to(ref.scalar_type());
+    if (flags & PESQ_GRAD_DEG) g_deg = g_deg.to(deg.scalar_type());
+  }
   return {g_ref, g_deg};
 }
 

@@ -77,9 +77,17 @@ def _check_signal(t: torch.Tensor, name: str) -> torch.Tensor:
         raise TypeError(f"`{name}` must be a torch.Tensor")
     if not t.is_cuda:
         raise RuntimeError(f"The CUDA PESQ backend needs `{name}` to live on a GPU.")
-    if t.dtype != torch.float32:
-        raise RuntimeError(f"The CUDA PESQ backend only supports float32, `{name}` is {t.dtype}.")
+    if t.dtype not in _INPUT_DTYPES:
+        raise RuntimeError(
+            f"The CUDA PESQ backend supports float32 (and bfloat16 / float16 inputs), `{name}` is {t.dtype}.")
     return t
+
+
+#: input dtypes: float32 as the reference, plus bfloat16 / float16 for callers
+#: training in mixed precision (each sample is widened to float as the first
+#: kernel reads it; the whole path then runs as for float32 inputs of the same
+#: values; losses are float32, gradients come back in the inputs' dtype)
+_INPUT_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 
 class PesqLossCuda(torch.nn.Module):
@@ -91,7 +99,12 @@ class PesqLossCuda(torch.nn.Module):
 
     Inputs are float32 CUDA tensors ``[batch, sample]`` (``[sample]`` is promoted
     to a batch of one); rows may have any stride.  Gradients flow to whichever
-    input requires one.
+    input requires one.  bfloat16 / float16 inputs are accepted too (both of
+    the same dtype): they are widened to float as they are read and evaluated
+    exactly as float32 inputs of the same values; the outputs are float32 and
+    the gradients come back in the inputs' dtype.  Every launch goes to the
+    current stream, so a caller overlaps the loss with other work (e.g. the
+    model's backward) by evaluating it under ``torch.cuda.stream``.
 
     Attributes
     ----------
