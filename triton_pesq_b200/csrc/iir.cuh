@@ -88,7 +88,6 @@ struct Args {
   int cpr;                 // chunks per row (rows packed whole), else kThreads
   int rows_per_tile;       // whole rows per tile (1 for chained rows)
   int seg;                 // samples per segment: cpr * kL, or kTile
-  uint32_t seg_inv;        // ceil(2^32 / seg): q / seg == umulhi(q, seg_inv) for q < kTile
   int64_t tiles_per_row;   // > 1: the tiles of a row are chained
   int64_t tiles;
   const float* lanes;      // [32][lane_pitch]  A^(kL l)
@@ -99,9 +98,10 @@ struct Args {
   uint32_t* err;
 };
 
+__host__ __device__ constexpr int kNearPowers = 4;  // A^(k kTile), k < 4, staged for the look-back
 __host__ __device__ constexpr size_t smem_bytes(int P) {
-  return (size_t)kTile * 4 + (size_t)lane_floats(P) * 4 + (size_t)wpow_floats(P) * 4 +
-         (size_t)kWarps * P * 4 + (size_t)P * 4 + 16;
+  return (size_t)kTile * 4 + (size_t)kNearPowers * P * P * 8 + (size_t)lane_floats(P) * 4 +
+         (size_t)wpow_floats(P) * 4 + (size_t)kWarps * P * 4 + (size_t)P * 4 + 16;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
@@ -136,17 +136,19 @@ __device__ __forceinline__ void publish(const Args& a, int64_t tile, int slot, d
     const double v = __shfl_sync(0xffffffffu, mine, j);
     if (lane == 0) __stcg(dst + j, v);
   }
-  if (lane == 0) {
-    __threadfence();
-    st_release(a.flags + tile, status);
-  }
+  // (the release store orders lane 0's value stores before the status)
+  if (lane == 0) st_release(a.flags + tile, status);
   __syncwarp();
 }
 
 // Warp 0: start state of tile `tile` (its index in the row is tin >= 1), from
 // the published states of its predecessors; lane i returns component i.
+// Powers A^(k kTile) for k < kNearPowers are staged in shared memory
+// (`near`); the look-back usually resolves within them.
+constexpr int kNear = kNearPowers;
+
 template <int P>
-__device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwin, int lane) {
+__device__ double lookback(const Args& a, int64_t tile, int64_t tin, const double* near, double* mwin, int lane) {
   double S[P];
 #pragma unroll
   for (int j = 0; j < P; ++j) S[j] = 0.0;
@@ -184,12 +186,18 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, double* mwi
 #pragma unroll
       for (int i = 0; i < P; ++i) c[i] = v[i];
     } else {
-      const double* L = a.look + (size_t)lane * P * P;
+      const bool staged = done == 0 && lane < kNear;
+      const double* L = staged ? near + (size_t)lane * P * P : a.look + (size_t)lane * P * P;
 #pragma unroll
       for (int i = 0; i < P; ++i) {
         double acc = 0.0;
+        if (staged) {
 #pragma unroll
-        for (int j = 0; j < P; ++j) acc = fma(__ldg(L + i * P + j), v[j], acc);
+          for (int j = 0; j < P; ++j) acc = fma(L[i * P + j], v[j], acc);
+        } else {
+#pragma unroll
+          for (int j = 0; j < P; ++j) acc = fma(__ldg(L + i * P + j), v[j], acc);
+        }
         c[i] = acc;
       }
     }
@@ -257,11 +265,12 @@ __device__ __forceinline__ float warp_sum(const float* wpow, const float* tot, i
 }
 
 template <int P, bool kLower, bool kRerun>
-__global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const __grid_constant__ Args a,
+__global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan_kernel(const __grid_constant__ Args a,
                                                                         const __grid_constant__ Tab<P> tab) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;                              // kTile samples
-  float* lanes = xs + kTile;                     // lane table
+  double* near = reinterpret_cast<double*>(xs + kTile);  // A^(k kTile), k < kNearPowers
+  float* lanes = reinterpret_cast<float*>(near + kNearPowers * P * P);  // lane table
   float* wpow = lanes + lane_floats(P);          // warp powers
   float* tot = wpow + wpow_floats(P);            // [kWarps][P] warp totals
   float* sin_s = tot + kWarps * P;               // [P] start state of the tile
@@ -274,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
   if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.flags + a.tiles, 1u) : (int64_t)blockIdx.x;
   copy_async<kThreads>(lanes, a.lanes, lane_floats(P) * 4);
   copy_async<kThreads>(wpow, a.wpow, wpow_floats(P) * 4);
+  if (chained) copy_async<kThreads>(near, a.look, kNearPowers * P * P * 8);
   __syncthreads();
 
   // tile geometry: rows [row0, row0 + nrows), memory span [m0, m0 + seg) of each
@@ -302,14 +312,31 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
   // stage the tile in memory order (zeros outside the rows)
   if (vec_in) {
     for (int i = tid; i < kTile / 4; i += kThreads) cp_async16(xs + 4 * i, xrow + m0 + 4 * i);
-  } else {
+  } else if (chained) {
 #pragma unroll 11
     for (int k = 0; k < kL; ++k) {
       const int q = tid + k * kThreads;
-      const int r = chained ? 0 : (int)__umulhi((uint32_t)q, a.seg_inv);
-      const int64_t m = m0 + (q - r * seg);
-      const bool valid = r < nrows && m >= 0 && m < a.n;
-      cp_async4_zfill(xs + q, valid ? xrow + r * a.ld_x + m : a.x, valid);
+      const int64_t m = m0 + q;
+      const bool valid = m >= 0 && m < a.n;
+      cp_async4_zfill(xs + q, valid ? xrow + m : a.x, valid);
+    }
+  } else {
+    // packed rows: warp w stages rows w, w + kWarps, ... (segments of seg
+    // samples, the row's n samples at the front or, reversed, at the back)
+    const int n = (int)a.n;
+    const int lead = a.reverse ? seg - n : 0;
+    for (int rr = warp; rr < a.rows_per_tile; rr += kWarps) {
+      float* dst = xs + rr * seg;
+      if (rr < nrows) {
+        const float* src = xrow + rr * a.ld_x;
+        for (int i = lane; i < seg; i += 32) {
+          const int m = i - lead;
+          const bool valid = m >= 0 && m < n;
+          cp_async4_zfill(dst + i, valid ? src + m : a.x, valid);
+        }
+      } else {
+        for (int i = lane; i < seg; i += 32) dst[i] = 0.0f;
+      }
     }
   }
   cp_async_commit();
@@ -415,15 +442,15 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
       if (warp == 0) {
         const double agg = (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci);
         if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
-        const double sv = lookback<P>(a, tile, tin, s_mwin, lane);
+        const double sv = lookback<P>(a, tile, tin, near, s_mwin, lane);
         if (successor) {
           // inclusive end state: A^kTile S + aggregate
-          const double* T1 = a.look + (size_t)P * P;
+          const double* T1 = near + P * P;
           double acc = agg;
 #pragma unroll
           for (int j = 0; j < P; ++j) {
             const double sj = __shfl_sync(0xffffffffu, sv, j);
-            acc = fma(__ldg(T1 + ci * P + j), sj, acc);
+            acc = fma(T1[ci * P + j], sj, acc);
           }
           publish<P>(a, tile, 1, acc, 2u, lane);
         }
@@ -495,13 +522,20 @@ __global__ void __launch_bounds__(kThreads, P <= 10 ? 2 : 1) scan_kernel(const _
     float4* dst = reinterpret_cast<float4*>(yrow + m0);
     const float4* src = reinterpret_cast<const float4*>(xs);
     for (int i = tid; i < kTile / 4; i += kThreads) dst[i] = src[i];
-  } else {
+  } else if (chained) {
 #pragma unroll 11
     for (int k = 0; k < kL; ++k) {
       const int q = tid + k * kThreads;
-      const int rr = chained ? 0 : (int)__umulhi((uint32_t)q, a.seg_inv);
-      const int64_t m = m0 + (q - rr * seg);
-      if (rr < nrows && m >= 0 && m < a.n) yrow[rr * a.ld_y + m] = xs[q];
+      const int64_t m = m0 + q;
+      if (m >= 0 && m < a.n) yrow[m] = xs[q];
+    }
+  } else {
+    const int n = (int)a.n;
+    const int lead = a.reverse ? seg - n : 0;
+    for (int rr = warp; rr < nrows; rr += kWarps) {
+      float* dst = yrow + rr * a.ld_y;
+      const float* src = xs + rr * seg + lead;
+      for (int i = lane; i < n; i += 32) dst[i] = src[i];
     }
   }
 }

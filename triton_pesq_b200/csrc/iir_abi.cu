@@ -363,7 +363,6 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   a.cpr = g.cpr;
   a.rows_per_tile = g.rows_per_tile;
   a.seg = g.seg;
-  a.seg_inv = (uint32_t)((((uint64_t)1 << 32) + (uint64_t)g.seg - 1) / (uint64_t)g.seg);
   a.tiles_per_row = g.tiles_per_row;
   a.tiles = g.tiles;
   a.lanes = f->lanes;
