@@ -59,7 +59,7 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
-    ap.add_argument("--op", choices=["iir"], default=None,
+    ap.add_argument("--op", choices=["iir", "resample"], default=None,
                     help="time only a standalone op on its large case (one JSON line; for profiling)")
     args = ap.parse_args()
     global BATCH, SECONDS
@@ -805,8 +805,11 @@ def run_op(args):
 
     dev = torch.device("cuda", 0)
     peak, _ = measured_peaks()
-    print(json.dumps({"op": args.op, "measurements": measure_iir(dev, peak, launches=args.steps,
-                                                                  large_only=True)}))
+    if args.op == "resample":
+        result = measure_resampler(dev, peak, launches=args.steps)
+    else:
+        result = measure_iir(dev, peak, launches=args.steps, large_only=True)
+    print(json.dumps({"op": args.op, "measurements": result}))
 
 
 def main():

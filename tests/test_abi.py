@@ -14,12 +14,14 @@ HEADER = os.path.join(ROOT, "include", "pesq_cuda.h")
 
 def declared_functions():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(pesq_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(pesq_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_entry_points():
     names = declared_functions()
-    for want in ("pesq_plan_create", "pesq_forward", "pesq_backward", "pesq_workspace_size", "pesq_last_error"):
+    for want in ("pesq_plan_create", "pesq_forward", "pesq_backward", "pesq_workspace_size", "pesq_last_error",
+                 "pesq_resampler_create", "pesq_resample_forward", "pesq_iir_create", "pesq_iir_workspace_bytes",
+                 "pesq_iir_filter", "pesq_forward_noalloc"):
         assert want in names
 
 
