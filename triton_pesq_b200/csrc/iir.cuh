@@ -52,7 +52,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kL = 33;                  // samples per thread chunk (coprime with the banks)
 constexpr int kLevels = 5;              // warp scan levels
 constexpr int kTile = kThreads * kL;    // 8448 samples per tile
-constexpr int kLook = 32;               // predecessors per look-back window
+constexpr int kLook = 32;               // predecessors per look-back window (a warp)
+constexpr int kFar = 256;               // predecessors the look-back reaches (8 windows)
 constexpr int kMaxStates = 24;
 constexpr unsigned kSpinLimit = 1u << 21;
 
@@ -92,7 +93,7 @@ struct Args {
   int64_t tiles;
   const float* lanes;      // [32][lane_pitch]  A^(kL l)
   const float* wpow;       // [kWarps + 1][P][P] A^(32 kL k)
-  const double* look;      // [kLook + 1][P][P] A^(k kTile)
+  const double* look;      // [kFar + 1][P][P] A^(k kTile)
   uint32_t* flags;         // [tiles + 1]: tile status (0, 1 aggregate, 2 inclusive), ticket counter
   double* vals;            // [tiles][2][P]: aggregate, inclusive end state
   uint32_t* err;
@@ -143,24 +144,25 @@ __device__ __forceinline__ void publish(const Args& a, int64_t tile, int slot, d
 
 // Warp 0: start state of tile `tile` (its index in the row is tin >= 1), from
 // the published states of its predecessors; lane i returns component i.
-// Powers A^(k kTile) for k < kNearPowers are staged in shared memory
-// (`near`); the look-back usually resolves within them.
-constexpr int kNear = kNearPowers;
-
+// Windows of 32 predecessors, lane k of a window the one k + done back: the
+// aggregates before the first inclusive state, and that state, each times
+// A^(distance kTile) from the table (k < kNearPowers from shared memory,
+// `near`).  The last lane of the last window (256 back) waits for an
+// inclusive state, so at most 8 windows are read.
 template <int P>
-__device__ double lookback(const Args& a, int64_t tile, int64_t tin, const double* near, double* mwin, int lane) {
+__device__ double lookback(const Args& a, int64_t tile, int64_t tin, const double* near, int lane) {
   double S[P];
 #pragma unroll
   for (int j = 0; j < P; ++j) S[j] = 0.0;
-  bool first = true;
   for (int64_t done = 0;; done += kLook) {
     const int64_t k = done + lane;
     const bool valid = k < tin;
     const int64_t pred = tile - 1 - k;
+    const uint32_t need = (done + kLook >= kFar && lane == kLook - 1) ? 2u : 1u;
     uint32_t st = 0;
     if (valid) {
       unsigned it = 0;
-      while ((st = ld_acquire(a.flags + pred)) == 0u) {
+      while ((st = ld_acquire(a.flags + pred)) < need) {
         if (++it > kSpinLimit) {
           atomicOr(a.err, 1u);
           st = 3u;  // give up: the predecessor counts as a zero inclusive state
@@ -171,8 +173,8 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
     }
     const unsigned incl = __ballot_sync(0xffffffffu, valid && st >= 2u);
     const int m = incl ? __ffs(incl) - 1 : kLook;
-    double v[P];
     const bool take = valid && lane <= m && st != 3u;
+    double v[P];
 #pragma unroll
     for (int j = 0; j < P; ++j) v[j] = 0.0;
     if (take) {
@@ -180,14 +182,14 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
 #pragma unroll
       for (int j = 0; j < P; ++j) v[j] = __ldcg(src + j);
     }
-    // c = A^(lane kTile) v (the identity for lane 0)
+    // c = A^(k kTile) v (the identity for k = 0)
     double c[P];
-    if (lane == 0 || !take) {
+    if (k == 0 || !take) {
 #pragma unroll
       for (int i = 0; i < P; ++i) c[i] = v[i];
     } else {
-      const bool staged = done == 0 && lane < kNear;
-      const double* L = staged ? near + (size_t)lane * P * P : a.look + (size_t)lane * P * P;
+      const bool staged = k < kNearPowers;
+      const double* L = staged ? near + (size_t)k * P * P : a.look + (size_t)k * P * P;
 #pragma unroll
       for (int i = 0; i < P; ++i) {
         double acc = 0.0;
@@ -205,42 +207,9 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
     for (int i = 0; i < P; ++i) {
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) c[i] += __shfl_xor_sync(0xffffffffu, c[i], off);
-    }
-    if (first) {
-#pragma unroll
-      for (int i = 0; i < P; ++i) S[i] = c[i];
-    } else {
-      // S += mwin c, mwin = A^(done kTile)
-#pragma unroll
-      for (int i = 0; i < P; ++i) {
-        double acc = S[i];
-#pragma unroll
-        for (int j = 0; j < P; ++j) acc = fma(mwin[i * P + j], c[j], acc);
-        S[i] = acc;
-      }
+      S[i] += c[i];
     }
     if (m < kLook || done + kLook >= tin) break;
-    // the next window lies A^(kLook kTile) further back: mwin <- mwin A^(kLook kTile)
-    __syncwarp();
-    const double* step = a.look + (size_t)kLook * P * P;
-    double row[P];
-    if (lane < P) {
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        double acc = 0.0;
-#pragma unroll
-        for (int q = 0; q < P; ++q)
-          acc = fma(first ? (lane == q ? 1.0 : 0.0) : mwin[lane * P + q], __ldg(step + q * P + j), acc);
-        row[j] = acc;
-      }
-    }
-    __syncwarp();
-    if (lane < P) {
-#pragma unroll
-      for (int j = 0; j < P; ++j) mwin[lane * P + j] = row[j];
-    }
-    __syncwarp();
-    first = false;
   }
   double mine = 0.0;
 #pragma unroll
@@ -276,7 +245,6 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
   float* sin_s = tot + kWarps * P;               // [P] start state of the tile
   __shared__ int64_t s_tile;
   __shared__ int s_whead[kWarps];
-  __shared__ double s_mwin[P * P];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool chained = a.tiles_per_row > 1;
@@ -442,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
       if (warp == 0) {
         const double agg = (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci);
         if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
-        const double sv = lookback<P>(a, tile, tin, near, s_mwin, lane);
+        const double sv = lookback<P>(a, tile, tin, near, lane);
         if (successor) {
           // inclusive end state: A^kTile S + aggregate
           const double* T1 = near + P * P;

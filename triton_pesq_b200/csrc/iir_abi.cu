@@ -241,9 +241,9 @@ int pesq_iir_create(const pesq_iir_desc* d, pesq_iir** out) {
   wp[0] = eye(P);
   for (int w = 1; w <= kWarps; ++w) wp[w] = mul(wstep, wp[w - 1], P);
   const Mat tile_step = wp[kWarps];
-  std::vector<double> look((size_t)(kLook + 1) * P * P);
+  std::vector<double> look((size_t)(kFar + 1) * P * P);
   cur = eye(P);
-  for (int k = 0; k <= kLook; ++k) {
+  for (int k = 0; k <= kFar; ++k) {
     std::memcpy(look.data() + (size_t)k * P * P, cur.data(), sizeof(double) * P * P);
     cur = mul(tile_step, cur, P);
   }

@@ -89,6 +89,8 @@ IIR_LEVELS = 5
 IIR_WARPS = IIR_THREADS // IIR_LANES
 IIR_TILE = IIR_THREADS * IIR_CHUNK
 IIR_LOOKBACK = 32
+#: Predecessor tiles the look-back reaches (its table of tile powers).
+IIR_FAR = 256
 
 
 def as_coeffs(values: Union[Sequence[float], np.ndarray, "torch.Tensor"]) -> np.ndarray:  # noqa: F821
@@ -286,7 +288,7 @@ class KernelTables:
     steps: np.ndarray  # [levels, P, P]
     lanes: np.ndarray  # [32, P, P]
     warp_powers: np.ndarray  # [9, P, P]
-    lookback: np.ndarray  # [33, P, P]
+    lookback: np.ndarray  # [257, P, P]
     trans: np.ndarray
     input: np.ndarray
     output: np.ndarray
@@ -352,10 +354,10 @@ def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> Kern
         warp_powers[k] = cur
         cur = warp_step @ cur
     tile_step = warp_powers[IIR_WARPS]  # A^T
-    lookback = np.zeros((IIR_LOOKBACK + 1, p, p))
+    lookback = np.zeros((IIR_FAR + 1, p, p))
     cur = np.eye(p)
     with np.errstate(over="ignore", invalid="ignore"):
-        for k in range(IIR_LOOKBACK + 1):
+        for k in range(IIR_FAR + 1):
             lookback[k] = cur
             cur = tile_step @ cur
 
