@@ -33,7 +33,8 @@
 // for belongs to a CTA that is already running), publishes its zero-start
 // aggregate, sums the aggregates of its predecessors with the powers
 // A^(k kTile) (float64) back to the first one that has published its
-// inclusive end state, and publishes its own inclusive state.  Nothing is
+// inclusive end state, and publishes its own inclusive state.  Published
+// states are self-validating tagged words (no memory fences, see publish).  Nothing is
 // truncated: the result is exact for any stable or unstable filter.  Every
 // wait is bounded (kSpinLimit polls); a wait that gives up records an error
 // in the filter's error word and treats the predecessor as zero.
@@ -94,25 +95,17 @@ struct Args {
   const float* lanes;      // [32][lane_pitch]  A^(kL l)
   const float* wpow;       // [kWarps + 1][P][P] A^(32 kL k)
   const double* look;      // [kFar + 1][P][P] A^(k kTile)
-  uint32_t* flags;         // [tiles + 1]: tile status (0, 1 aggregate, 2 inclusive), ticket counter
-  double* vals;            // [tiles][2][P]: aggregate, inclusive end state
+  uint32_t* ticket;        // tile counter (zero before the launch)
+  unsigned long long* slots;  // [tiles][2][P][2]: aggregate / inclusive state, zero before the launch
   uint32_t* err;
 };
 
-__host__ __device__ constexpr int kNearPowers = 4;  // A^(k kTile), k < 4, staged for the look-back
+constexpr int kNearPowers = 4;  // A^(k kTile), k < 4, staged for the look-back
 __host__ __device__ constexpr size_t smem_bytes(int P) {
   return (size_t)kTile * 4 + (size_t)kNearPowers * P * P * 8 + (size_t)lane_floats(P) * 4 +
          (size_t)wpow_floats(P) * 4 + (size_t)kWarps * P * 4 + (size_t)P * 4 + 16;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 // 4-byte asynchronous copy global -> shared that writes zero (and reads
 // nothing) when `valid` is false; `src` must still be a valid address.
 __device__ __forceinline__ void cp_async4_zfill(float* dst, const float* src, bool valid) {
@@ -121,25 +114,67 @@ __device__ __forceinline__ void cp_async4_zfill(float* dst, const float* src, bo
                : "memory");
 }
 
+#ifdef PESQ_PHASE_PROBE
+// [tile][phase] globaltimer of the first 1024 tiles of a launch (probe builds
+// only; one copy per translation unit, read by the unit's own reader)
+static __device__ unsigned long long g_iir_probe[1024 * 8];
+#define PESQ_IIR_STAMP(tile, i)                                                      \
+  do {                                                                               \
+    if (threadIdx.x == 0 && (tile) < 1024) g_iir_probe[(tile) * 8 + (i)] = pesq_globaltimer(); \
+  } while (0)
+#else
+#define PESQ_IIR_STAMP(tile, i) \
+  do {                          \
+  } while (0)
+#endif
+
 template <int P, bool kLower>
 __device__ __forceinline__ bool skip(int i, int j) {
   return kLower && (j >> 1) > (i >> 1);
 }
 
-// Warp 0: lane 0 stores the P components (lane i holds component i) into
-// vals[tile][slot] and then releases the tile's status.
+// Published states need no fences: component i of a tile's aggregate (slot
+// 0) or inclusive end state (slot 1) is the float pair (hi, lo) with
+// hi + lo = the float64 value to ~48 bits, each in its own 64-bit word with
+// the tag 1 in its upper half.  A naturally aligned 64-bit access is
+// single-copy atomic, so a reader that sees every word of a slot tagged has
+// the whole state, whatever order the words became visible in.
+__device__ __forceinline__ unsigned long long slot_word(float v) {
+  return (1ull << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void st_relaxed64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Warp 0: lanes i < P publish component i (lane i holds it).
 template <int P>
-__device__ __forceinline__ void publish(const Args& a, int64_t tile, int slot, double mine, uint32_t status,
-                                        int lane) {
-  double* dst = a.vals + (tile * 2 + slot) * P;
+__device__ __forceinline__ void publish(const Args& a, int64_t tile, int slot, double mine, int lane) {
+  if (lane < P) {
+    unsigned long long* dst = a.slots + ((tile * 2 + slot) * P + lane) * 2;
+    const float hi = (float)mine;
+    st_relaxed64(dst, slot_word(hi));
+    st_relaxed64(dst + 1, slot_word((float)(mine - (double)hi)));
+  }
+}
+
+// Reads slot `slot` of tile `t`: true (and its P components in v) when every
+// word is tagged.
+template <int P>
+__device__ __forceinline__ bool read_slot(const Args& a, int64_t t, int slot, double (&v)[P]) {
+  const unsigned long long* src = a.slots + (t * 2 + slot) * P * 2;
+  bool ok = true;
 #pragma unroll
   for (int j = 0; j < P; ++j) {
-    const double v = __shfl_sync(0xffffffffu, mine, j);
-    if (lane == 0) __stcg(dst + j, v);
+    const unsigned long long hi = ld_relaxed64(src + 2 * j), lo = ld_relaxed64(src + 2 * j + 1);
+    ok = ok && (hi >> 32) == 1u && (lo >> 32) == 1u;
+    v[j] = (double)__uint_as_float((unsigned)hi) + (double)__uint_as_float((unsigned)lo);
   }
-  // (the release store orders lane 0's value stores before the status)
-  if (lane == 0) st_release(a.flags + tile, status);
-  __syncwarp();
+  return ok;
 }
 
 // Warp 0: start state of tile `tile` (its index in the row is tin >= 1), from
@@ -159,10 +194,22 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
     const bool valid = k < tin;
     const int64_t pred = tile - 1 - k;
     const uint32_t need = (done + kLook >= kFar && lane == kLook - 1) ? 2u : 1u;
+    // st: 0 nothing yet, 1 aggregate, 2 inclusive (v holds it), 3 gave up
     uint32_t st = 0;
+    double v[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) v[j] = 0.0;
     if (valid) {
       unsigned it = 0;
-      while ((st = ld_acquire(a.flags + pred)) < need) {
+      for (;;) {
+        if (read_slot<P>(a, pred, 1, v)) {
+          st = 2u;
+          break;
+        }
+        if (need == 1u && read_slot<P>(a, pred, 0, v)) {
+          st = 1u;
+          break;
+        }
         if (++it > kSpinLimit) {
           atomicOr(a.err, 1u);
           st = 3u;  // give up: the predecessor counts as a zero inclusive state
@@ -174,17 +221,14 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
     const unsigned incl = __ballot_sync(0xffffffffu, valid && st >= 2u);
     const int m = incl ? __ffs(incl) - 1 : kLook;
     const bool take = valid && lane <= m && st != 3u;
-    double v[P];
-#pragma unroll
-    for (int j = 0; j < P; ++j) v[j] = 0.0;
-    if (take) {
-      const double* src = a.vals + (pred * 2 + (lane == m ? 1 : 0)) * P;
-#pragma unroll
-      for (int j = 0; j < P; ++j) v[j] = __ldcg(src + j);
-    }
+    // (a lane before m holds its predecessor's aggregate: that one had no
+    // inclusive state when it was read)
     // c = A^(k kTile) v (the identity for k = 0)
     double c[P];
-    if (k == 0 || !take) {
+    if (!take) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) c[i] = 0.0;
+    } else if (k == 0) {
 #pragma unroll
       for (int i = 0; i < P; ++i) c[i] = v[i];
     } else {
@@ -222,15 +266,17 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
 // (warp totals T in shared memory).
 template <int P, bool kLower>
 __device__ __forceinline__ float warp_sum(const float* wpow, const float* tot, int v0, int v1, int i) {
-  float acc = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent chains, one per warp mod 4
   for (int v = v0; v < v1; ++v) {
     const float* Wm = wpow + (v1 - 1 - v) * P * P + i * P;
     const float* T = tot + v * P;
+    float part = 0.0f;
 #pragma unroll
     for (int j = 0; j < P; ++j)
-      if (!skip<P, kLower>(i, j)) acc = fmaf(Wm[j], T[j], acc);
+      if (!skip<P, kLower>(i, j)) part = fmaf(Wm[j], T[j], part);
+    acc[v & 3] += part;
   }
-  return acc;
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 template <int P, bool kLower, bool kRerun>
@@ -248,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool chained = a.tiles_per_row > 1;
-  if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.flags + a.tiles, 1u) : (int64_t)blockIdx.x;
+  if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.ticket, 1u) : (int64_t)blockIdx.x;
   copy_async<kThreads>(lanes, a.lanes, lane_floats(P) * 4);
   copy_async<kThreads>(wpow, a.wpow, wpow_floats(P) * 4);
   if (chained) copy_async<kThreads>(near, a.look, kNearPowers * P * P * 8);
@@ -256,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
 
   // tile geometry: rows [row0, row0 + nrows), memory span [m0, m0 + seg) of each
   const int64_t tile = s_tile;
+  PESQ_IIR_STAMP(tile, 0);
   const int seg = a.seg;
   int64_t row0, tin, m0;
   int nrows;
@@ -310,6 +357,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
+  PESQ_IIR_STAMP(tile, 1);
 
   // this thread's chunk: segment r, chunk lc of the segment; its sample t
   // sits at xs[base + dir * t]
@@ -393,6 +441,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
     s_whead[warp] = f;
   }
   __syncthreads();
+  PESQ_IIR_STAMP(tile, 2);
 
   // 3. start state of this warp: back to the last warp with a head, or to
   //    the tile's start state (lane i < P holds component i)
@@ -405,12 +454,14 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
     const bool successor = tin + 1 < a.tiles_per_row;
     if (tin == 0) {
       if (warp == 0 && successor)
-        publish<P>(a, tile, 1, (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci), 2u, lane);
+        publish<P>(a, tile, 1, (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci), lane);
     } else {
       if (warp == 0) {
         const double agg = (double)warp_sum<P, kLower>(wpow, tot, 0, kWarps, ci);
-        if (successor) publish<P>(a, tile, 0, agg, 1u, lane);
+        if (successor) publish<P>(a, tile, 0, agg, lane);
+        PESQ_IIR_STAMP(tile, 5);
         const double sv = lookback<P>(a, tile, tin, near, lane);
+        PESQ_IIR_STAMP(tile, 6);
         if (successor) {
           // inclusive end state: A^kTile S + aggregate
           const double* T1 = near + P * P;
@@ -420,11 +471,13 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
             const double sj = __shfl_sync(0xffffffffu, sv, j);
             acc = fma(T1[ci * P + j], sj, acc);
           }
-          publish<P>(a, tile, 1, acc, 2u, lane);
+          publish<P>(a, tile, 1, acc, lane);
         }
+        PESQ_IIR_STAMP(tile, 7);
         if (lane < P) sin_s[lane] = (float)sv;
       }
       __syncthreads();
+      PESQ_IIR_STAMP(tile, 3);
       // no head in a tile after the first of its row: add A^(32 kL warp) S
       const float* Wm = wpow + warp * P * P + ci * P;
 #pragma unroll
@@ -486,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan
   }
   __syncthreads();
 
+  PESQ_IIR_STAMP(tile, 4);
   if (vec_out) {
     float4* dst = reinterpret_cast<float4*>(yrow + m0);
     const float4* src = reinterpret_cast<const float4*>(xs);

@@ -148,11 +148,11 @@ Geometry geometry(int64_t rows, int64_t n) {
   return g;
 }
 
-size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
-
+// chained rows: the tile ticket (16 bytes) and two published states of P
+// components per tile, two tagged 64-bit words each; all zero before a launch
 size_t workspace_bytes(const pesq_iir* f, const Geometry& g) {
   if (!g.chained()) return 0;
-  return align16((size_t)(g.tiles + 1) * 4) + (size_t)g.tiles * 2 * f->kstates * 8;
+  return 16 + (size_t)g.tiles * 2 * f->kstates * 2 * 8;
 }
 
 template <int P>
@@ -371,9 +371,9 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   a.err = f->err;
   if (g.chained()) {
     char* w = static_cast<char*>(workspace);
-    a.flags = reinterpret_cast<uint32_t*>(w);
-    a.vals = reinterpret_cast<double*>(w + align16((size_t)(g.tiles + 1) * 4));
-    const cudaError_t e = cudaMemsetAsync(a.flags, 0, (size_t)(g.tiles + 1) * 4, s);
+    a.ticket = reinterpret_cast<uint32_t*>(w);
+    a.slots = reinterpret_cast<unsigned long long*>(w + 16);
+    const cudaError_t e = cudaMemsetAsync(w, 0, need, s);
     if (e != cudaSuccess) return set_error(PESQ_ERR_CUDA, cudaGetErrorString(e));
   }
   const bool rerun = (flags & PESQ_IIR_RERUN) != 0;
