@@ -280,7 +280,7 @@ __device__ __forceinline__ float warp_sum(const float* wpow, const float* tot, i
 }
 
 template <int P, bool kLower, bool kRerun>
-__global__ void __launch_bounds__(kThreads, P <= 2 ? 3 : (P <= 10 ? 2 : 1)) scan_kernel(const __grid_constant__ Args a,
+__global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan_kernel(const __grid_constant__ Args a,
                                                                         const __grid_constant__ Tab<P> tab) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;                              // kTile samples
