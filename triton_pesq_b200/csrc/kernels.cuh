@@ -218,6 +218,7 @@ struct ResampleArgs {
   int max_entries, max_dl;
   int fwd_staged, adj_staged;  // shared memory kernels (the tables fit)
   int tpitch;                  // odd row pitch of the staged taps
+  uint32_t inv_os, inv_ns;     // ceil(2^32 / orig_step), ceil(2^32 / new_step): 32-bit divisions
 };
 
 // Device tables of one polyphase resampler: the compact nonzero taps of every

@@ -35,6 +35,12 @@ constexpr size_t kResampleSmemLimit = 96 * 1024;
 // CTAs the staged kernels aim for (several waves), split over the rows
 constexpr int kResampleTargetCtas = 16 * 148;
 
+// q / d for 0 <= q < 2^32 / d from inv = ceil(2^32 / d) (d >= 2), or q for d = 1
+__device__ __forceinline__ uint32_t div_small(uint32_t q, uint32_t d, uint32_t inv) {
+  return d == 1u ? q : __umulhi(q, inv);
+}
+inline uint32_t div_inverse(int d) { return d <= 1 ? 0u : (uint32_t)((((uint64_t)1 << 32) + (uint64_t)d - 1) / (uint64_t)d); }
+
 // staged geometry shared by host and device
 __host__ __device__ inline int fwd_span(int os, int ns, int wt) { return ((kResampleBlock - 1) / ns + 1) * os + wt; }
 __host__ __device__ inline int tap_pitch(int max_count) { return max_count | 1; }
@@ -142,11 +148,14 @@ __global__ void __launch_bounds__(kResampleThreads)
       }
     }
     __syncthreads();
+    const int j0 = (int)(m0 - l_first * ns);  // phase of m0
     for (int64_t m = m0 + tid; m < m_end; m += kResampleThreads) {
-      const int64_t l = m / ns;
-      const int j = (int)(m - l * ns);
+      // frame and phase of m relative to the step (32-bit, no 64-bit division)
+      const uint32_t tq = (uint32_t)(j0 + (m - m0));
+      const int dl = (int)div_small(tq, (uint32_t)ns, p.inv_ns);
+      const int j = (int)tq - dl * ns;
       const float* t = tp + j * tpitch;
-      const float* xv = xs + (l - l_first) * os + fi[j];
+      const float* xv = xs + dl * os + fi[j];
       const int cnt = co[j];
       // two partial sums halve the dependent chain of the tap loop
       double acc0 = 0.0, acc1 = 0.0;
@@ -219,12 +228,14 @@ __global__ void __launch_bounds__(kResampleThreads)
       gs[i] = (m >= 0 && m < p.n_out) ? __ldg(g + m) : 0.0f;
     }
     __syncthreads();
+    const int r0 = (int)(n0 + p.width - l0_first * os);  // residue of n0
     for (int64_t n = n0 + tid; n < n_end; n += kResampleThreads) {
-      const int64_t pos = n + p.width;
-      const int64_t l0 = pos / os;
-      const int rho = (int)(pos - l0 * os);
+      // frame and residue of n relative to the step (32-bit, no 64-bit division)
+      const uint32_t tq = (uint32_t)(r0 + (n - n0));
+      const int dl0 = (int)div_small(tq, (uint32_t)os, p.inv_os);
+      const int rho = (int)tq - dl0 * os;
       // slot of (l0, phase 0) in the window; entry (dl, j) reads slot + j - dl * ns
-      const int slot = (int)((l0 - l0_first + p.max_dl) * ns);
+      const int slot = (dl0 + p.max_dl) * ns;
       float acc = 0.0f;
       const int2* en = ent + rho;
       const float* gw = gs + slot;
@@ -411,6 +422,8 @@ ResampleArgs resample_args(const ResampleTables& t, int64_t n_in, int64_t n_out)
   ra.fwd_staged = t.fwd_staged;
   ra.adj_staged = t.adj_staged;
   ra.tpitch = tap_pitch(t.max_count);
+  ra.inv_os = div_inverse(t.orig_step);
+  ra.inv_ns = div_inverse(t.new_step);
   return ra;
 }
 
