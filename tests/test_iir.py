@@ -21,6 +21,7 @@ EXTRA = {
     "cheby1": tuple(np.asarray(c) for c in cheby1(4, 1, [325, 3250], fs=16000, btype="band")),
     "ellip": tuple(np.asarray(c) for c in ellip(4, 1, 60, [325, 3250], fs=16000, btype="band")),
     "bp16": tuple(np.asarray(c) for c in butter(8, [325, 3250], fs=16000, btype="band")),
+    "lp24": tuple(np.asarray(c) for c in butter(24, 3000, fs=16000)),
 }
 ALL = {**FILTERS, **DEGENERATE, **EXTRA}
 
@@ -78,7 +79,36 @@ def test_conditioning_covers_every_table(name):
     largest = max(np.abs(t).max() for t in (tabs.carry, tabs.drive, tabs.steps, tabs.lanes, tabs.warp_powers,
                                             tabs.trans, tabs.input, tabs.output))
     assert d.entry >= largest * (1.0 - 1e-12)
-    assert d.score >= d.entry * D.FLOAT32_EPS
+    assert d.score >= D.emulated_error(tabs, *ALL[name]) * (1.0 - 1e-12)
+
+
+@pytest.mark.parametrize("name", ["order2", "order10", "lp24", "bp16"])
+@pytest.mark.parametrize("samples", [100, D.IIR_TILE, D.IIR_TILE + 4321, 2 * D.IIR_TILE])
+def test_emulation_in_float64_is_the_filter(name, samples):
+    """The kernel emulation that scores the realisations computes the filter:
+    in float64 arithmetic it agrees with the realisation's own recursion to
+    rounding, in both output
+    forms, over one and two tiles (so its float32 error is rounding alone)."""
+
+    d = D.design(*ALL[name])
+    x = np.random.default_rng(samples).standard_normal(samples)
+    truth, state = np.empty(samples), np.zeros(d.trans.shape[0])
+    for k in range(samples):  # the realisation's own recursion
+        truth[k] = d.output @ state + d.feed * x[k]
+        state = d.trans @ state + d.input * x[k]
+    for y in D.emulate(d.tables(), x, dtype=np.float64):
+        assert np.abs(y - truth).max() <= 1e-9 * np.abs(truth).max()
+
+
+def test_high_order_low_pass_avoids_the_companion_form():
+    """The companion form of an order 24 low pass has small table entries
+    yet loses every digit in float32; the emulated error sees it and the
+    cascade (large entries, seven digits) is taken."""
+
+    d = D.design(*EXTRA["lp24"])
+    assert d.basis == "cascade" and d.score < D.ERROR_WARN
+    assert d.candidates["companion"][0] > 0.1
+    assert d.candidates["companion"][1] < d.candidates["cascade"][1]
 
 
 @pytest.mark.parametrize("name", list(DEGENERATE))

@@ -490,3 +490,66 @@ def test_cuda_graph_replay(modules, shape):
         torch.cuda.synchronize()
         assert torch.equal(out, module(fresh))
     assert module.check_errors() == 0
+
+
+def _spread(order: int, radius: float = 0.85):
+    """Order `order` filter with poles of one radius spread over the band and
+    zeros on the unit circle beside them (well conditioned in every basis)."""
+
+    th = np.linspace(0.15, 2.9, order // 2)
+    poles = np.concatenate([radius * np.exp(1j * th), radius * np.exp(-1j * th)])
+    zeros = np.concatenate([np.exp(1j * (th + 0.07)), np.exp(-1j * (th + 0.07))])
+    return np.poly(zeros).real / order, np.poly(poles).real
+
+
+WIDE = {
+    "lp20": (lambda: butter(20, 3000, fs=16000), 20),
+    "lp23": (lambda: butter(23, 3000, fs=16000), 24),
+    "lp24": (lambda: butter(24, 3000, fs=16000), 24),
+    "bp22": (lambda: butter(11, [325, 3250], fs=16000, btype="band"), 24),
+    "spread20": (lambda: _spread(20), 20),
+    "spread24": (lambda: _spread(24), 24),
+}
+
+
+@pytest.mark.parametrize("name,dense", [(name, False) for name in WIDE] +
+                         [(name, True) for name in WIDE if name.startswith("spread")])
+@pytest.mark.parametrize("method", ["matmul", "scan"])
+def test_widest_kernels(cuda_device, name, dense, method):
+    """The 20- and 24-state kernel instantiations, block lower (the selected
+    cascade) and dense (the same realisation in a random orthonormal basis),
+    both output forms, forward and adjoint, chained rows: within a small
+    multiple of the error the float32 emulation of the kernel predicts.  The
+    high order low passes only have an accurate block lower realisation (any
+    dense basis mixes their unbalanced states), so the dense kernels run on
+    the well conditioned `spread` filters."""
+
+    import dataclasses
+    import warnings
+
+    coeffs, states = WIDE[name]
+    b, a = (np.asarray(c) for c in coeffs())
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", RuntimeWarning)
+        design = D.design(b, a)
+    if dense:
+        n = design.trans.shape[0]
+        q = np.linalg.qr(np.random.default_rng(n).standard_normal((n, n)))[0]
+        design = dataclasses.replace(design, trans=q.T @ design.trans @ q, input=q.T @ design.input,
+                                     output=design.output @ q, basis="dense")
+    tabs = design.tables()
+    assert tabs.states == states and tabs.lower == (not dense)
+    bound = max(TOL, 4 * D.emulated_error(tabs, b, a))
+    signal = noise(2, 20000, seed=len(name) + states)
+    upstream = noise(2, 20000, seed=7 + states)
+    flags = _lib.IIR_RERUN if method == "scan" else 0
+    handle = _lib.create_iir(design)
+    try:
+        out = torch.ops.pesq_cuda.iir(handle, signal, flags)
+        grad = torch.ops.pesq_cuda.iir(handle, upstream, flags | _lib.IIR_REVERSE)
+        assert _lib.iir_check(handle, torch.cuda.current_stream().cuda_stream) == 0
+    finally:
+        torch.cuda.synchronize()
+        _lib.destroy_iir(handle)
+    assert peak_error(out, exact(signal, b, a)) < bound
+    assert peak_error(grad, exact_vjp(signal, upstream, b, a)) < bound

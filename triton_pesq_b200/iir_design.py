@@ -19,9 +19,11 @@ decides the float32 accuracy, so three are built here and scored
     the per-section companion blocks of the reference.
 
 The score of a realisation is the larger of its float64 *fidelity* (how far its
-own impulse response already is from the difference equation's) and its
+own impulse response already is from the difference equation's), its
 *conditioning* (the largest entry of any table the CUDA kernel multiplies data
-with, times the float32 unit round-off), as in iir.py:436-517.  The tables are
+with, times the float32 unit round-off), as in iir.py:436-517, and the error of
+its recursion run in float32 on seeded white noise (which the reference leaves
+to the user: table entries do not see how the recursion amplifies rounding).  The tables are
 the ones of the sm_100a kernel (``csrc/iir.cuh``), whose geometry differs from
 the reference's Triton tiles: 33-sample thread chunks, a 5 level warp scan, a
 lane table, warp powers and a per-tile look-back table.  Selection,
@@ -55,6 +57,8 @@ __all__ = [
     "realised_response",
     "KernelTables",
     "kernel_tables",
+    "emulate",
+    "emulated_error",
     "score",
     "IIRDesign",
     "design",
@@ -75,6 +79,13 @@ FLOAT32_LIMIT = 1e5
 FLOAT32_WARN = 1e3
 ERROR_LIMIT = FLOAT32_LIMIT * FLOAT32_EPS
 ERROR_WARN = FLOAT32_WARN * FLOAT32_EPS
+#: Realisations in the order they are preferred, and the factor within which
+#: two predicted errors count as equal.
+PREFERENCE = ("cascade", "modal", "companion")
+SCORE_TIE = 2.0
+#: Realisations with a larger float32 table entry are not used: a product of
+#: it with a moderate sample already nears the float32 range.
+FLOAT32_MAX_ENTRY = 1e24
 
 #: State counts the CUDA kernel is instantiated for; a realisation is zero
 #: padded to the next one.
@@ -367,10 +378,100 @@ def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> Kern
                         feed=float(feed))
 
 
-def score(trans, drive, read, feed, reference: np.ndarray, scale: float) -> Tuple[float, float]:
+def emulate(tabs: KernelTables, x: np.ndarray, dtype=np.float32) -> Tuple[np.ndarray, np.ndarray]:
+    """The CUDA kernel's float32 arithmetic (``dtype``) on one row of up to two tiles,
+    step by step as csrc/iir.cuh (scan_kernel) runs it: chunk end states from
+    zero, the warp's doubling scan, the warp start states from the warp
+    totals, the second tile's start state (float64 look-back, rounded to
+    float32), the chunk start states from the lane table, and the outputs in
+    the impulse form and in the re-run form.  Returns both output rows."""
+
+    f = dtype
+    p, L, T = tabs.states, IIR_CHUNK, IIR_TILE
+    h, G, W = tabs.impulse.astype(f), tabs.carry.astype(f), tabs.drive.astype(f)
+    M, A = tabs.steps.astype(f), tabs.trans.astype(f)
+    Bv, C, D = tabs.input.astype(f), tabs.output.astype(f), f(tabs.feed)
+    lanes, wpow = tabs.lanes.astype(f), tabs.warp_powers.astype(f)
+    n = x.size
+    tiles = -(-n // T)
+    if tiles > 2:
+        raise ValueError("emulate() covers one or two tiles")
+    xp = np.zeros(tiles * T, f)
+    xp[:n] = x
+    chunks = xp.reshape(tiles, IIR_WARPS, IIR_LANES, L)
+    # 1. chunk end states from zero
+    e = chunks @ W
+    # 2. doubling scan within each warp
+    lane = np.arange(IIR_LANES)[None, None, :, None]
+    for lv in range(IIR_LEVELS):
+        d = 1 << lv
+        pv = np.zeros_like(e)
+        pv[:, :, d:] = e[:, :, :-d]
+        e = np.where(lane >= d, e + pv @ M[lv].T, e)
+    ex = np.zeros_like(e)
+    ex[:, :, 1:] = e[:, :, :-1]
+    tot = e[:, :, -1]  # [tiles, warps, p]
+    # 3. warp start states (tile-local), the tile aggregate, the start state
+    # of the second tile
+    xw = np.zeros((tiles, IIR_WARPS, p), f)
+    for w in range(IIR_WARPS):
+        for v in range(w):
+            xw[:, w] += tot[:, v] @ wpow[w - 1 - v].T
+    if tiles == 2:
+        agg = np.zeros(p, f)
+        for v in range(IIR_WARPS):
+            agg += wpow[IIR_WARPS - 1 - v] @ tot[0, v]
+        start = agg.astype(f)  # the first tile's inclusive state: its aggregate
+        xw[1] += np.einsum("wij,j->wi", wpow[:IIR_WARPS], start).astype(f)
+    # 4. chunk start states; the row's first chunk starts from zero
+    s = ex + np.einsum("lij,twj->twli", lanes, xw).astype(f)
+    s[0, 0, 0] = 0.0
+    s = s.reshape(-1, p)
+    xc = chunks.reshape(-1, L)
+    # 5. outputs
+    zero = np.stack([xc[:, :t + 1] @ h[t::-1] for t in range(L)], axis=1)
+    impulse_form = zero + s @ G.T
+    rerun = np.empty_like(xc)
+    st = s.copy()
+    for t in range(L):
+        rerun[:, t] = st @ C + D * xc[:, t]
+        st = st @ A.T + np.outer(xc[:, t], Bv)
+    return impulse_form.reshape(-1)[:n], rerun.reshape(-1)[:n]
+
+
+def emulated_error(tabs: KernelTables, b: np.ndarray, a: np.ndarray) -> float:
+    """Peak relative error of the kernel's float32 arithmetic (both output
+    forms) on two tiles of seeded white noise, against a float64 lfilter of
+    the coefficients.
+
+    The reference predicts the error from the largest table entry alone
+    (iir.py:468-517) and documents that this underestimates it by up to two
+    orders of magnitude.  Table entries bound the rounding of one product, not
+    how the state magnitudes amplify it: the companion form of an order 24
+    low pass has entries below 1e4 and returns noise, while its cascade has
+    entries near 1e7 and keeps seven digits.  Running the arithmetic itself
+    measures both."""
+
+    from scipy.signal import lfilter
+
+    x = np.random.default_rng(0).standard_normal(2 * IIR_TILE).astype(np.float32)
+    truth = lfilter(np.asarray(b, np.float64), np.asarray(a, np.float64), x.astype(np.float64))
+    scale = float(np.abs(truth).max())
+    if not (math.isfinite(scale) and scale > 0.0):
+        return math.inf
+    with np.errstate(over="ignore", invalid="ignore"):
+        worst = max(float(np.abs(y.astype(np.float64) - truth).max()) for y in emulate(tabs, x))
+    err = worst / scale
+    return err if math.isfinite(err) else math.inf
+
+
+def score(trans, drive, read, feed, reference: np.ndarray, scale: float, b=None, a=None) -> Tuple[float, float]:
     """Predicted peak relative error of a realisation and its largest float32
-    table entry (iir.py:468-517): the larger of the float64 fidelity of its
-    impulse response and the conditioning of the kernel's tables."""
+    table entry: the larger of the float64 fidelity of its impulse response
+    and the conditioning of its float64 tables (iir.py:468-517) and, given the
+    coefficients, the error of the kernel's own float32 arithmetic
+    (emulated_error; without them, the reference's estimate from the largest
+    float32 table entry)."""
 
     with np.errstate(over="ignore", invalid="ignore"):
         response = realised_response(trans, drive, read, feed, reference.size)
@@ -379,9 +480,12 @@ def score(trans, drive, read, feed, reference: np.ndarray, scale: float) -> Tupl
             return math.inf, math.inf
         tabs = kernel_tables(trans, drive, read, feed)
         entry32, entry64 = tabs.largest32, tabs.largest64
-    if not (math.isfinite(entry32) and math.isfinite(entry64)):
+    if not (math.isfinite(entry32) and math.isfinite(entry64)) or entry32 > FLOAT32_MAX_ENTRY:
         return math.inf, math.inf
-    return max(fidelity, entry32 * FLOAT32_EPS, entry64 * FLOAT64_EPS), entry32
+    predicted = max(fidelity, entry64 * FLOAT64_EPS)
+    if b is None:
+        return max(predicted, entry32 * FLOAT32_EPS), entry32
+    return max(predicted, emulated_error(tabs, b, a)), entry32
 
 
 @dataclass
@@ -430,15 +534,20 @@ def design(b, a, taps: int = DEFAULT_CHUNK, stacklevel: int = 3) -> IIRDesign:
     if c is not None:
         candidates.append(("cascade",) + tuple(c))
 
-    best, best_score, best_entry, scores = None, math.inf, math.inf, {}
+    scores = {}
     for name, A, B, C, D in candidates:
-        if A.shape[0] > KERNEL_STATES[-1]:
-            scores[name] = (math.inf, math.inf)
-            continue
-        s, e = score(A, B, C, D, reference, scale)
-        scores[name] = (s, e)
-        if s < best_score:
+        scores[name] = (math.inf, math.inf) if A.shape[0] > KERNEL_STATES[-1] else \
+            score(A, B, C, D, reference, scale, b, a)
+    # the emulated errors of two good realisations differ by rounding noise:
+    # take the first in the order cascade, modal, companion (the block lower
+    # ones skip the zero blocks of their tables) within SCORE_TIE of the best
+    lowest = min(s for s, _ in scores.values())
+    best, best_score, best_entry = None, math.inf, math.inf
+    for name, A, B, C, D in sorted(candidates, key=lambda c: PREFERENCE.index(c[0])):
+        s, e = scores[name]
+        if math.isfinite(s) and s <= SCORE_TIE * lowest:
             best, best_score, best_entry = (name, A, B, C, D), s, e
+            break
 
     if best is None or not math.isfinite(best_score):
         if order > KERNEL_STATES[-1]:
