@@ -83,13 +83,13 @@ typedef struct pesq_scan_desc {
 typedef struct pesq_plan_desc {
   int32_t abi_version; /* PESQ_CUDA_ABI_VERSION */
   int32_t sample_rate; /* input rate; 16000 skips the resampler */
-  int32_t n_fft;       /* 512 */
-  int32_t hop_length;  /* 256 */
+  int32_t n_fft;       /* power of two in [32, 4096]; 512 runs the fused default path */
+  int32_t hop_length;  /* >= 1; other than 256 (or n_fft other than 512) runs the spectrum kernels */
   int32_t nbarks;      /* 1 .. 64 (49 for P.862) */
   int32_t reserved0;
   double factor;       /* loss = factor * (0.1 d_symm + 0.0309 d_asymm) */
   const double* window;      /* [n_fft] analysis window, centred, zero padded */
-  const int32_t* band_start; /* [nbarks] first bin of each Bark band */
+  const int32_t* band_start; /* [nbarks] first bin of each Bark band (bands sorted, disjoint, below n_fft / 2) */
   const int32_t* band_end;   /* [nbarks] one past the last bin */
   const double* band_corr;   /* [nbarks] power density correction */
   const double* threshold;   /* [nbarks] absolute hearing threshold */

@@ -10,6 +10,14 @@ if ROOT not in sys.path:
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 
+def golden_geometry(z) -> dict:
+    """Frame geometry of a golden fixture (``PesqLoss`` keyword arguments);
+    empty for the default n_fft 512 / hop 256 / window 512."""
+
+    keys = ("n_fft", "hop_length", "win_length")
+    return {k: int(z[k]) for k in keys if k in z.files}
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built extension")
 

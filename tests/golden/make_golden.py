@@ -22,7 +22,8 @@ Per case the fixture holds the float32 inputs and
 thresholds, exponents, correction, widths, window, filter coefficients and the
 resampling kernels of several rates).
 
-Usage: ``python tests/golden/make_golden.py`` from the repository root.
+Usage: ``python tests/golden/make_golden.py [case ...]`` from the repository
+root (all cases and the constants when no case is named).
 """
 
 import copy
@@ -78,14 +79,25 @@ def speech_pair(batch, n, sr, seed, snr_db):
     return ref.astype(np.float32), deg.astype(np.float32)
 
 
+DEFAULT_GEOMETRY = (512, 256, 512)  # n_fft, hop_length, win_length
+
 CASES = [
-    # name, batch, samples, sample_rate, seed, snr_db, factor
+    # name, batch, samples, sample_rate, seed, snr_db, factor[, (n_fft, hop_length, win_length)]
     ("sr16k_b2_n6000", 2, 6000, 16000, 1, 10.0, 0.5),
     ("sr16k_b1_n8192", 1, 8192, 16000, 2, 3.0, 1.0),
     ("sr16k_b3_n7001", 3, 7001, 16000, 3, 20.0, 1.0),
     ("sr48k_b1_n18000", 1, 18000, 48000, 4, 10.0, 1.0),
     ("sr44k_b1_n16540", 1, 16540, 44100, 5, 10.0, 1.0),
     ("sr8k_b1_n3200", 1, 3200, 8000, 6, 15.0, 1.0),
+    # other frame geometries of PesqLoss(..., win_length, n_fft, hop_length)
+    ("sr16k_fft256_hop128_b2_n6000", 2, 6000, 16000, 11, 10.0, 1.0, (256, 128, 256)),
+    ("sr16k_fft1024_hop512_b1_n20000", 1, 20000, 16000, 12, 5.0, 1.0, (1024, 512, 1024)),
+    ("sr16k_fft512_hop200_win400_b1_n9000", 1, 9000, 16000, 13, 15.0, 1.0, (512, 200, 400)),
+    ("sr16k_fft512_hop256_win400_b1_n8000", 1, 8000, 16000, 14, 10.0, 1.0, (512, 256, 400)),
+    ("sr16k_fft64_hop32_b1_n4000", 1, 4000, 16000, 15, 10.0, 1.0, (64, 32, 64)),
+    ("sr16k_fft4096_hop1024_b1_n28000", 1, 28000, 16000, 16, 10.0, 1.0, (4096, 1024, 4096)),
+    ("sr16k_fft512_hop600_b1_n16000", 1, 16000, 16000, 17, 10.0, 1.0, (512, 600, 512)),
+    ("sr48k_fft256_hop128_b1_n18000", 1, 18000, 48000, 18, 10.0, 1.0, (256, 128, 256)),
 ]
 
 
@@ -93,10 +105,16 @@ def main():
     PesqLoss, ref_pipeline = _import_reference()
     torch.manual_seed(0)
 
-    for name, batch, n, sr, seed, snr, factor in CASES:
-        model = PesqLoss(factor, sample_rate=sr)
+    only = set(sys.argv[1:])  # case names to (re)generate; all when empty
+    for name, batch, n, sr, seed, snr, factor, *rest in CASES:
+        if only and name not in only:
+            continue
+        n_fft, hop, win = rest[0] if rest else DEFAULT_GEOMETRY
+        model = PesqLoss(factor, sample_rate=sr, n_fft=n_fft, hop_length=hop, win_length=win)
         ref_np, deg_np = speech_pair(batch, n, sr, seed, snr)
         out = {"ref": ref_np, "deg": deg_np, "factor": np.float64(factor), "sample_rate": np.int64(sr)}
+        if rest:
+            out.update(n_fft=np.int64(n_fft), hop_length=np.int64(hop), win_length=np.int64(win))
 
         ref = torch.from_numpy(ref_np).requires_grad_(True)
         deg = torch.from_numpy(deg_np).requires_grad_(True)
@@ -124,6 +142,8 @@ def main():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print(name, out["f64_d_symm"], out["f64_d_asymm"], out["ref32_d_symm"])
 
+    if only:
+        return
     model = PesqLoss(1.0, sample_rate=16000)
     const = {
         "fbank": model.fbank.fbank.detach().numpy(),

@@ -12,10 +12,11 @@ F64_RTOL = 1e-5
 GRAD_RTOL = 1e-4
 
 
-def oracle_grads(ref, deg, factor, sample_rate):
-    """float64 distances and gradients of ``factor*(0.1 ds + 0.0309 da)``."""
+def oracle_grads(ref, deg, factor, sample_rate, **geometry):
+    """float64 distances and gradients of ``factor*(0.1 ds + 0.0309 da)``
+    (``geometry``: n_fft / hop_length / win_length of ``PesqLoss``)."""
 
-    p = O.OracleParams(factor=factor, sample_rate=sample_rate)
+    p = O.OracleParams(factor=factor, sample_rate=sample_rate, **geometry)
     r = ref.detach().cpu().double().requires_grad_(True)
     d = deg.detach().cpu().double().requires_grad_(True)
     ds, da = O.raw(r, d, p, "float64")

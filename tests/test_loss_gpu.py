@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN
+from conftest import GOLDEN, golden_geometry
 from gpu_helpers import F64_RTOL, GRAD_RTOL, oracle_grads, peak_rel_err, rel_err
 from triton_pesq_b200 import PesqLossCuda
 from triton_pesq_b200.signals import add_noise, speech_like
@@ -30,11 +30,13 @@ def _grads(model, ref, deg, which=(True, True)):
 
 @pytest.mark.parametrize("path", CASES, ids=[os.path.basename(c)[:-4] for c in CASES])
 def test_golden_vectors(cuda_device, path):
-    """Distances and gradients against the reference's own float64 pipeline."""
+    """Distances and gradients against the reference's own float64 pipeline
+    (default and other frame geometries: n_fft 64..4096, hops shorter and
+    longer than the frame, a window shorter than n_fft)."""
 
     z = np.load(path)
     factor, sr = float(z["factor"]), int(z["sample_rate"])
-    model = PesqLossCuda(factor, sample_rate=sr)
+    model = PesqLossCuda(factor, sample_rate=sr, **golden_geometry(z))
     ref = torch.from_numpy(z["ref"]).to(cuda_device)
     deg = torch.from_numpy(z["deg"]).to(cuda_device)
     ds, da = model.raw(ref, deg)
@@ -62,6 +64,61 @@ def test_matches_float64(cuda_device, batch, samples, sample_rate, snr):
     _, (g_ref, g_deg) = _grads(model, ref, deg)
     assert peak_rel_err(g_ref.cpu(), gr64) < GRAD_RTOL
     assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL
+
+
+GEOMETRIES = [  # n_fft, hop_length, win_length
+    (256, 128, 256), (1024, 256, 1024), (128, 100, 96), (32, 16, 32), (2048, 512, 2048),
+    (512, 128, 512), (512, 300, 512), (512, 256, 320), (256, 512, 256),
+]
+GEOMETRY_CASES = ([g + (3, 20000, 16000) for g in GEOMETRIES] + [g + (2, 33075, 44100) for g in GEOMETRIES] +
+                  [(4096, 512, 3000, 2, 20000, 16000), (4096, 1024, 4096, 1, 96000, 48000)])
+
+
+@pytest.mark.parametrize("n_fft,hop,win,batch,samples,sample_rate", GEOMETRY_CASES)
+def test_frame_geometries(cuda_device, n_fft, hop, win, batch, samples, sample_rate):
+    """PesqLoss(..., win_length, n_fft, hop_length) with the spectrum kernels
+    (every geometry but 512 / 256) and the fused path with a shorter window:
+    distances and both gradients against the float64 oracle."""
+
+    geometry = dict(n_fft=n_fft, hop_length=hop, win_length=win)
+    ref = speech_like(batch, samples, sample_rate, seed=n_fft + hop + batch)
+    deg = add_noise(ref, 8.0, seed=win)
+    ds64, da64, gr64, gd64 = oracle_grads(ref, deg, 1.0, sample_rate, **geometry)
+    model = PesqLossCuda(1.0, sample_rate=sample_rate, **geometry)
+    ref, deg = ref.to(cuda_device), deg.to(cuda_device)
+    ds, da = model.raw(ref, deg)
+    assert rel_err(ds.cpu(), ds64) < F64_RTOL
+    assert rel_err(da.cpu(), da64) < F64_RTOL
+    _, (g_ref, g_deg) = _grads(model, ref, deg)
+    assert peak_rel_err(g_ref.cpu(), gr64) < GRAD_RTOL
+    assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL
+    # one-sided gradients agree with the two-sided ones
+    _, (g_deg_only,) = _grads(model, ref, deg, which=(False, True))
+    assert torch.equal(g_deg_only, g_deg)
+
+
+def test_frame_geometry_graph_replay_is_bit_exact(cuda_device):
+    """The spectrum kernels are deterministic and capturable: a graphed step
+    replays bitwise equal to the eager one."""
+
+    ref = speech_like(2, 16000, 16000, seed=5).to(cuda_device).requires_grad_(True)
+    deg = add_noise(ref.detach().cpu(), 5.0, seed=6).to(cuda_device).requires_grad_(True)
+    model = PesqLossCuda(1.0, sample_rate=16000, n_fft=256, hop_length=128, win_length=256)
+    eager = model(ref, deg)
+    eager_grads = torch.autograd.grad(eager.sum(), [ref, deg])
+    graphed = model.graphed(ref, deg)
+    for _ in range(2):
+        captured = graphed(ref, deg)
+        captured_grads = torch.autograd.grad(captured.sum(), [ref, deg])
+        assert torch.equal(captured, eager)
+        for want, got in zip(eager_grads, captured_grads):
+            assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("n_fft", [40, 48, 96, 1000, 16, 8192])
+def test_rejects_unsupported_n_fft(n_fft):
+    with pytest.raises(ValueError):
+        PesqLossCuda(1.0, sample_rate=16000, n_fft=n_fft, win_length=min(n_fft, 16))
 
 
 def test_outputs_are_consistent(cuda_device):

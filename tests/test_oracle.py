@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN
+from conftest import GOLDEN, golden_geometry
 from oracle import pesq_oracle as O
 
 CASES = sorted(glob.glob(os.path.join(GOLDEN, "sr*.npz")))
@@ -15,7 +15,7 @@ CASES = sorted(glob.glob(os.path.join(GOLDEN, "sr*.npz")))
 
 def _load(path):
     z = np.load(path)
-    p = O.OracleParams(factor=float(z["factor"]), sample_rate=int(z["sample_rate"]))
+    p = O.OracleParams(factor=float(z["factor"]), sample_rate=int(z["sample_rate"]), **golden_geometry(z))
     return z, p
 
 

@@ -91,3 +91,31 @@ def test_frame_and_window_counts():
     assert T.frame_count(64000) == 249
     assert T.frame_count(160000) == 624
     assert T.psqm_windows(499) == 48
+
+
+@pytest.mark.parametrize("n_fft", [40, 48, 96, 1000, 16])
+def test_rejects_non_power_of_two_n_fft(n_fft):
+    """n_fft must be a power of two of at least 32, as for the reference's
+    spectral op (test_triton_spectral.py:237-255)."""
+
+    with pytest.raises(ValueError, match="power of two"):
+        T.PlanConfig.build(1.0, 16000, n_fft=n_fft, win_length=min(n_fft, 16))
+
+
+@pytest.mark.parametrize("kw", [dict(n_fft=8192), dict(hop_length=0), dict(win_length=600)])
+def test_rejects_other_frame_geometries(kw):
+    with pytest.raises(ValueError):
+        T.PlanConfig.build(1.0, 16000, **kw)
+
+
+@pytest.mark.parametrize("n_fft", [32, 64, 128, 256, 1024, 2048, 4096])
+def test_bark_bands_segment_every_frame_length(n_fft):
+    """The filterbank of every supported n_fft is a sorted, disjoint
+    segmentation of the n_fft / 2 bins (test_triton_spectral.py:178-195), as
+    the spectrum kernels' band table assumes."""
+
+    lay = T.bark_layout(n_fft // 2, 49)
+    prev = 0
+    for s, e in zip(lay.starts, lay.ends):
+        assert prev <= s <= e <= n_fft // 2
+        prev = e

@@ -26,7 +26,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpesq_cuda.so")
 OPS = os.path.join(HERE, "_pesq_torch_ops.so")
 
-CUDA_SOURCES = ["front.cu", "align.cu", "back.cu", "chain.cu", "resample.cu", "pesq_abi.cu", "noalloc.cu",
+CUDA_SOURCES = ["front.cu", "align.cu", "back.cu", "spectrum.cu", "chain.cu", "resample.cu", "pesq_abi.cu", "noalloc.cu",
                 "resample_abi.cu", "iir_abi.cu", "iir_ka.cu", "iir_kb.cu", "iir_kc.cu", "iir_kd.cu", "iir_ke.cu",
                 "iir_kf.cu"]
 NVCC_FLAGS = [
@@ -128,7 +128,12 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
 
 def build(force: bool = False, verbose: bool = False) -> None:
     build_library(force=force, verbose=verbose)
-    build_torch_ops(force=force, verbose=verbose)
+    if force or _stale(OPS, _deps() + [LIB]):
+        # cpp_extension.load() registers the ops from its build directory:
+        # compile in a child process so that this one can still load the
+        # in-tree copy (a namespace may be registered only once per process)
+        code = f"from triton_pesq_b200.build import build_torch_ops; build_torch_ops(force=True, verbose={verbose!r})"
+        subprocess.run([sys.executable, "-c", code], check=True, cwd=os.path.dirname(HERE))
 
 
 if __name__ == "__main__":

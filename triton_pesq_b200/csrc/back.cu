@@ -35,6 +35,9 @@ constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps
                                kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4 +
                                kBackFrames * kMaxBands * 4;
 
+// kGather: general frame geometry, dL/dy is gathered from the frame gradients
+// of the spectrum kernel (spectrum.cu) instead of the fused transforms
+template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     back_kernel(const __grid_constant__ BackArgs p, const __grid_constant__ PreTab pre) {
   extern __shared__ __align__(16) float smem[];
@@ -58,6 +61,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_CTA_BEGIN(g_cta_back);
   PESQ_STAMP(g_phase_back, 0);
 
+  if constexpr (kGather) {
+    // dL/dy on [a, send + kHorizon): sum over the frames covering each sample
+    // (frame order), z staged in the background
+    const float* zr = p.z + (int64_t)row * n_row;
+    for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
+    cp_async_commit();
+    const float* fg = p.frame_grad + (int64_t)(row - p.row_begin) * p.frames * p.nfft;
+    const int top_g = kHop + kHorizon + (int)(send - a);
+    for (int i = tid; i < kSpan; i += kThreads) {
+      const int64_t n = base + i;
+      float acc = 0.0f;
+      if (i >= kHop && i < top_g && n < n_row) {
+        const int t_hi = (int)min((int64_t)p.frames - 1, n / p.hop);
+        const int t_lo = n >= p.nfft ? (int)((n - p.nfft) / p.hop) + 1 : 0;
+        for (int t = t_lo; t <= t_hi; ++t) acc += __ldg(fg + (int64_t)t * p.nfft + (n - (int64_t)t * p.hop));
+      }
+      gy[i] = acc;
+    }
+    __syncthreads();
+  } else {
   // frames that touch [a, send + kHorizon)
   const int nb = p.nb;
   const int t0 = seg * p.seg_frames;
@@ -82,7 +105,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   PESQ_STAMP(g_phase_back, 1);
 
-  const float kappa = p.kappa[row];
   Cx<float>* sh = fft + warp * FftLayout<float>::kSlots;
   float* gbw = gb + warp * kMaxBands;
   int band_of[8];  // band of bin lane + 32 m (-1: none)
@@ -130,6 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
   }
+  }
+  const float kappa = p.kappa[row];
   PESQ_STAMP(g_phase_back, 2);
 
   // pre-emphasis adjoint on [a, send): backwards in time from send + kHorizon;
@@ -169,11 +193,15 @@ cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStre
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
   LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(), s, false);
-  return cudaLaunchKernelEx(&l.cfg, back_kernel, a, pre);
+  if (a.frame_grad) return cudaLaunchKernelEx(&l.cfg, back_kernel<true>, a, pre);
+  return cudaLaunchKernelEx(&l.cfg, back_kernel<false>, a, pre);
 }
 
 cudaError_t configure_back() {
-  return cudaFuncSetAttribute(back_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)back_smem_bytes());
+  const cudaError_t e =
+      cudaFuncSetAttribute(back_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)back_smem_bytes());
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(back_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)back_smem_bytes());
 }
 
 }  // namespace pesq

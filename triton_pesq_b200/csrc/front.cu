@@ -41,6 +41,9 @@ constexpr int kFrontScratchFloats =
 constexpr int kFrontSmemBytes = 2 * kSpan * 4 + kFrontScratchFloats * 4 + (int)sizeof(DevTables) +
                                 (int)sizeof(DevTwiddle64) + kWarps * 8;
 
+// kSignal: general frame geometry, y is written to p.y64 and the frames are
+// left to the spectrum kernel (spectrum.cu)
+template <bool kSignal>
 __global__ void __launch_bounds__(kThreads, 1)
     front_kernel(const __grid_constant__ FrontArgs p, const __grid_constant__ PowTab pow,
                  const __grid_constant__ PreTab64 pre) {
@@ -141,6 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   PESQ_STAMP(g_phase_front, 3);
 
+  if constexpr (kSignal) {
+    double* yo = p.y64 + (int64_t)row * n_row;
+    for (int i = tid; i < (int)(send - a); i += kThreads) yo[a + i] = yd[kHorizon + i];
+  } else {
   // 4. frames starting in this segment: window, rfft, power, Bark segment sums
   const int nb = tab->nb;
   const int t0 = seg * p.seg_frames;
@@ -177,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   }
+  }
   PESQ_STAMP(g_phase_front, 4);
   PESQ_CTA_END(g_cta_front);
   PESQ_SPAN_END(g_span_front, 0);
@@ -187,14 +195,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 size_t front_smem_bytes() { return (size_t)kFrontSmemBytes; }
 
 cudaError_t configure_front() {
-  return cudaFuncSetAttribute(front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
+  const cudaError_t e =
+      cudaFuncSetAttribute(front_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(front_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
 }
 
 cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
   LaunchShape l((unsigned)blocks, kThreads, front_smem_bytes(), s, false);
-  return cudaLaunchKernelEx(&l.cfg, front_kernel, a, pow, pre);
+  if (a.y64) return cudaLaunchKernelEx(&l.cfg, front_kernel<true>, a, pow, pre);
+  return cudaLaunchKernelEx(&l.cfg, front_kernel<false>, a, pow, pre);
 }
 
 }  // namespace pesq

@@ -95,6 +95,39 @@ struct FrontArgs {
   Cx<float>* spec;   // [rows][T][256]  rfft bins 0..255 of every frame
   float* fpow;       // [rows][n]       f = H x, written for the rows that save the spectrum
   uint32_t* err;
+  // general frame geometry (n_fft / hop other than 512 / 256): the kernel
+  // writes the pre-emphasised rows y here instead of evaluating the frames
+  double* y64;       // [rows][n], or nullptr
+};
+
+// Frame geometry other than n_fft 512 / hop 256 (spectrum.cu): a warp per
+// frame, an n_fft-point complex FFT in shared memory.
+constexpr int kGenMinFft = 32;
+constexpr int kGenMaxFft = 4096;
+constexpr int kGenThreads = 256;
+
+struct GenTables {
+  int nfft, log2n, hop, nfreq;   // nfreq = n_fft / 2 bins (the Nyquist bin is never used)
+  const float* window;           // [nfft] analysis window, zero padded/centred
+  const Cx<double>* tw;          // [nfft / 2] exp(-2 pi i k / nfft)
+  const int* bin_band;           // [nfreq] band owning bin f, -1 if none (bin 0 never has one)
+};
+
+struct SpecArgs {
+  GenTables g;
+  const DevTables* tab;
+  int64_t n;           // samples per row
+  int frames;          // T
+  int rows;            // rows (frames) of this launch: rows [row_begin, row_begin + rows)
+  int row_begin;
+  // forward: y -> Bark spectrum, and X on rows [spec_begin, spec_end)
+  const double* y;     // [all rows][n]
+  float* bark;         // [all rows][T][nb]
+  Cx<float>* spec;     // [all rows][T][nfreq]
+  int spec_begin, spec_end;
+  // adjoint: dL/dBark and X -> windowed frame gradients
+  const float* g_bark;  // [all rows][T][nb]
+  float* frame_grad;    // [rows][T][nfft], row r at r - row_begin
 };
 
 struct AlignArgs {
@@ -120,6 +153,10 @@ struct BackArgs {
   const Cx<float>* spec;  // [rows][T][256] saved by the front kernel
   RowSink out;          // gradient rows (16 kHz)
   uint32_t* err;
+  // general frame geometry: dL/dy is the overlap-add (a gather, in frame
+  // order) of these windowed frame gradients instead of the fused transforms
+  const float* frame_grad;  // [rows - row_begin][T][nfft], or nullptr
+  int nfft, hop;
 };
 
 // Chain state saved by the forward for the backward, per utterance.
@@ -284,6 +321,9 @@ cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStre
 // preceding kernel on the stream runs, and completes after it
 cudaError_t launch_align(const AlignArgs& a, const PowTab& pow, int rows, cudaStream_t s);
 cudaError_t configure_align();
+cudaError_t launch_stft(const SpecArgs& a, cudaStream_t s);
+cudaError_t launch_istft(const SpecArgs& a, cudaStream_t s);
+cudaError_t configure_spectrum();
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t configure_chain();

@@ -37,6 +37,12 @@ struct pesq_plan {
   PreTab64 pre64;    // float64 tables: pre-emphasis of the front kernel
   DevTables* dtab;   // device copy
   DevTwiddle64* tw64;
+  // frame geometry; `general` when it is not n_fft 512 / hop 256 (the
+  // spectrum kernels with the tables in `gen_buf`)
+  int nfft, hop;
+  bool general;
+  void* gen_buf;
+  GenTables gen;
   // resampler to 16 kHz (sample_rate != 16000)
   bool resample;
   ResampleTables rs;
@@ -108,11 +114,13 @@ struct Geometry {
   int seg, nseg;  // segmentation of a row
   int cluster;
   bool fwd_staged, fwd_stage_cells, bwd_staged;
-  bool resample, grad;
+  bool resample, grad, general;
+  int nfreq;  // spectrum bins saved per frame
   int grad_begin, grad_end;
   ChainLayout lay;
   // byte offsets
-  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, err, total;
+  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, y64, fgrad, err,
+      total;
   int64_t cell_stride;  // floats between the fields of the chain's adjoint coefficients
 };
 
@@ -139,8 +147,9 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.n_src = n_src;
   g.resample = p->resample;
   g.n16 = resampled_length(p, n_src);
+  // loss.py:191-192 pads by N % 256 whatever the hop; torch.stft, center=False
   const int64_t padded = g.n16 + g.n16 % 256;
-  g.T = padded < kNfft ? 0 : (int)(1 + (padded - kNfft) / kHop);
+  g.T = padded < p->nfft ? 0 : (int)std::min<int64_t>(INT32_MAX, 1 + (padded - p->nfft) / p->hop);
   if (g.T < 20)
     return fail(PESQ_ERR_INVALID_ARGUMENT,
                 "The PESQ chain needs at least 20 frames for the overlapping sums, got %d (%lld samples at 16 kHz).",
@@ -148,8 +157,12 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   if (g.n16 > (int64_t)1 << 31 || g.rows > 65535)
     return fail(PESQ_ERR_INVALID_ARGUMENT, "signal or batch too large (%lld samples, %lld rows)",
                 (long long)g.n16, (long long)g.rows);
+  if ((int64_t)g.T * p->nfft > (int64_t)1 << 33)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "%d frames of %d samples: too many for one call", g.T, p->nfft);
   g.L = (g.T - 20) / 10 + 1;
   g.nb = p->nb;
+  g.general = p->general;
+  g.nfreq = p->general ? p->gen.nfreq : kBins;
   balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
   // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
@@ -178,7 +191,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.bark = take(rows * (size_t)g.T * g.nb * 4);
   g.fpow = take(g.grad ? rows * g.n16 * 4 : 0);
   g.z = take(g.grad ? rows * g.n16 * 4 : 0);
-  g.spec = take(g.grad ? rows * (size_t)g.T * kBins * 8 : 0);
+  g.spec = take(g.grad ? rows * (size_t)g.T * g.nfreq * 8 : 0);
   g.saved = take((size_t)batch * g.lay.stride * 4);
   g.cell_stride = (int64_t)batch * g.cluster * cell_block(g.T, g.cluster, g.nb);
   g.cells = take(g.grad ? (size_t)kCellFields * g.cell_stride * 4 : 0);
@@ -186,6 +199,8 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.kappa = take(g.grad ? rows * 4 : 0);
   g.cscratch = take(g.grad ? (size_t)batch * 2 * g.T * 4 : 0);
   g.gx16 = take(g.grad && g.resample ? rows * g.n16 * 4 : 0);
+  g.y64 = take(g.general ? rows * g.n16 * 8 : 0);
+  g.fgrad = take(g.grad && g.general ? (size_t)(g.grad_end - g.grad_begin) * g.T * p->nfft * 4 : 0);
   g.err = take(16);
   g.total = o;
   return PESQ_OK;
@@ -228,9 +243,10 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   *out = nullptr;
   if (d->abi_version != PESQ_CUDA_ABI_VERSION)
     return fail(PESQ_ERR_UNSUPPORTED, "ABI version %d, library has %d", d->abi_version, PESQ_CUDA_ABI_VERSION);
-  if (d->n_fft != kNfft || d->hop_length != kHop)
-    return fail(PESQ_ERR_UNSUPPORTED, "n_fft %d / hop %d: the kernels implement n_fft 512, hop 256", d->n_fft,
-                d->hop_length);
+  if (d->n_fft < kGenMinFft || d->n_fft > kGenMaxFft || (d->n_fft & (d->n_fft - 1)) != 0)
+    return fail(PESQ_ERR_UNSUPPORTED, "n_fft %d: the kernels implement powers of two from %d to %d", d->n_fft,
+                kGenMinFft, kGenMaxFft);
+  if (d->hop_length < 1) return fail(PESQ_ERR_INVALID_ARGUMENT, "hop_length %d must be positive", d->hop_length);
   if (d->nbarks < 1 || d->nbarks > kMaxBands)
     return fail(PESQ_ERR_UNSUPPORTED, "%d Bark bands, the kernels support 1..%d", d->nbarks, kMaxBands);
   if (d->sample_rate <= 0) return fail(PESQ_ERR_INVALID_ARGUMENT, "sample rate must be positive");
@@ -246,6 +262,10 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (cudaGetDevice(&p->device) != cudaSuccess) return bail(fail(PESQ_ERR_CUDA, "no CUDA device"));
   p->sample_rate = d->sample_rate;
   p->nb = d->nbarks;
+  p->nfft = d->n_fft;
+  p->hop = d->hop_length;
+  p->general = d->n_fft != kNfft || d->hop_length != kHop;
+  const int nfreq = d->n_fft / 2;
   p->factor = d->factor;
   int rc = fill_scan(p->pow, d->power_filter, "power filter");
   if (rc) return bail(rc);
@@ -265,7 +285,8 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   // constant tables
   DevTables h;
   memset(&h, 0, sizeof(h));
-  for (int k = 0; k < kNfft; ++k) h.window[k] = (float)d->window[k];
+  if (!p->general)
+    for (int k = 0; k < kNfft; ++k) h.window[k] = (float)d->window[k];
   DevTwiddle64 h64;
   // exp(-2 pi i k / n); the argument reduction k mod n, k / n is exact in double
   auto root = [](int k, int n, Cx<double>& w64, Cx<float>& w32) {
@@ -286,13 +307,14 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   int prev_end = 0;
   for (int b = 0; b < d->nbarks; ++b) {
     const int s = d->band_start[b], e = d->band_end[b];
-    if (s < 0 || e < s || e > kBins || s < prev_end)
+    if (s < 0 || e < s || e > nfreq || s < prev_end)
       return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "band %d covers [%d, %d): bands must be sorted, disjoint and below bin %d",
-                       b, s, e, kBins));
+                       b, s, e, nfreq));
     prev_end = e;
     h.band_start[b] = s;
     h.band_end[b] = e;
-    for (int f = std::max(s, 1); f < e; ++f) h.bin_band[f] = b;
+    if (!p->general)
+      for (int f = std::max(s, 1); f < e; ++f) h.bin_band[f] = b;
     const double th = d->threshold[b], ex = d->exponent[b];
     if (!(th > 0.0)) return bail(fail(PESQ_ERR_INVALID_ARGUMENT, "hearing thresholds must be positive"));
     h.band_corr[b] = (float)d->band_corr[b];
@@ -317,6 +339,39 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
       cudaMemcpy(p->tw64, &h64, sizeof(h64), cudaMemcpyHostToDevice) != cudaSuccess)
     return bail(fail(PESQ_ERR_CUDA, "upload of the twiddle tables failed"));
 
+  // general frame geometry: window, twiddles exp(-2 pi i k / n_fft) and the
+  // band of every bin, in one device buffer
+  if (p->general) {
+    const int n = d->n_fft;
+    const size_t tw_bytes = (size_t)(n / 2) * sizeof(Cx<double>), win_bytes = (size_t)n * 4;
+    const size_t band_bytes = (size_t)nfreq * 4;
+    std::vector<char> host(tw_bytes + win_bytes + band_bytes);
+    Cx<double>* tw = reinterpret_cast<Cx<double>*>(host.data());
+    float* win = reinterpret_cast<float*>(host.data() + tw_bytes);
+    int* band = reinterpret_cast<int*>(host.data() + tw_bytes + win_bytes);
+    for (int k = 0; k < n / 2; ++k) {
+      const double t = -2.0 * M_PI * ((double)k / (double)n);
+      tw[k].x = cos(t);
+      tw[k].y = sin(t);
+    }
+    for (int k = 0; k < n; ++k) win[k] = (float)d->window[k];
+    for (int f = 0; f < nfreq; ++f) band[f] = -1;
+    for (int b = 0; b < d->nbarks; ++b)
+      for (int f = std::max(d->band_start[b], 1); f < d->band_end[b]; ++f) band[f] = b;
+    if (cudaMalloc(&p->gen_buf, host.size()) != cudaSuccess ||
+        cudaMemcpy(p->gen_buf, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(PESQ_ERR_CUDA, "upload of the spectrum tables failed"));
+    char* dev = static_cast<char*>(p->gen_buf);
+    p->gen.nfft = n;
+    p->gen.log2n = 0;
+    while ((1 << p->gen.log2n) < n) ++p->gen.log2n;
+    p->gen.hop = d->hop_length;
+    p->gen.nfreq = nfreq;
+    p->gen.tw = reinterpret_cast<const Cx<double>*>(dev);
+    p->gen.window = reinterpret_cast<const float*>(dev + tw_bytes);
+    p->gen.bin_band = reinterpret_cast<const int*>(dev + tw_bytes + win_bytes);
+  }
+
   // resampler tables
   p->resample = d->sample_rate != 16000;
   if (p->resample) {
@@ -333,6 +388,8 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the chain kernels"));
   e = configure_align();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the align kernel"));
+  e = configure_spectrum();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the spectrum kernels"));
   *out = p;
   return PESQ_OK;
 }
@@ -341,6 +398,7 @@ int pesq_plan_destroy(pesq_plan* p) {
   if (!p) return PESQ_OK;
   cudaFree(p->dtab);
   cudaFree(p->tw64);
+  cudaFree(p->gen_buf);
   free_resample_tables(p->rs);
   delete p;
   return PESQ_OK;
@@ -421,7 +479,23 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int
   fa.spec = at<Cx<float>>(ws, g.spec);
   fa.fpow = at<float>(ws, g.fpow);
   fa.err = at<uint32_t>(ws, g.err);
+  fa.y64 = g.general ? at<double>(ws, g.y64) : nullptr;
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
+  if (g.general) {
+    SpecArgs sa{};
+    sa.g = p->gen;
+    sa.tab = p->dtab;
+    sa.n = g.n16;
+    sa.frames = g.T;
+    sa.rows = (int)g.rows;
+    sa.row_begin = 0;
+    sa.y = fa.y64;
+    sa.bark = fa.bark;
+    sa.spec = fa.spec;
+    sa.spec_begin = fa.spec_begin;
+    sa.spec_end = fa.spec_end;
+    PESQ_CUDA_TRY(launch_stft(sa, s), "spectrum kernel");
+  }
   return PESQ_OK;
 }
 
@@ -555,6 +629,22 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ba.out = g.resample ? RowSink{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch}
                       : RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
   ba.err = at<uint32_t>(ws, g.err);
+  if (g.general) {
+    SpecArgs sa{};
+    sa.g = p->gen;
+    sa.tab = p->dtab;
+    sa.n = g.n16;
+    sa.frames = g.T;
+    sa.rows = g.grad_end - g.grad_begin;
+    sa.row_begin = g.grad_begin;
+    sa.spec = ba.spec ? const_cast<Cx<float>*>(ba.spec) : nullptr;
+    sa.g_bark = ba.g_bark;
+    sa.frame_grad = at<float>(ws, g.fgrad);
+    PESQ_CUDA_TRY(launch_istft(sa, s), "spectrum adjoint kernel");
+    ba.frame_grad = sa.frame_grad;
+    ba.nfft = p->nfft;
+    ba.hop = p->hop;
+  }
   PESQ_CUDA_TRY(launch_back(ba, p->pre, g.grad_end - g.grad_begin, s), "back kernel");
 
   if (g.resample) {

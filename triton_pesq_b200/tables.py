@@ -116,6 +116,10 @@ PRE_FILTER_A = (1.0, -1.9444777, 0.94597794)
 #: The frames are laid out after padding by ``length % PAD_MODULUS`` zeros
 #: (``loss.py:191-192``); the modulus is fixed, independent of the hop.
 PAD_MODULUS = 256
+#: Frame lengths (n_fft) the CUDA kernels implement: powers of two in this
+#: range (512 runs the fused default path, the others the spectrum kernels).
+MIN_FFT = 32
+MAX_FFT = 4096
 
 #: Overlapping sums of the disturbance, 20 frames with stride 10 (``loss.py:258-266``).
 PSQM_WINDOW = 20
@@ -666,8 +670,16 @@ class PlanConfig:
             raise ValueError(
                 f"PesqLoss evaluates its loudness model with 49 bands only, got nbarks={nbarks}."
             )
-        if win_length > n_fft:
-            raise ValueError(f"win_length ({win_length}) must not exceed n_fft ({n_fft}).")
+        n_fft, hop_length, win_length = int(n_fft), int(hop_length), int(win_length)
+        if n_fft < MIN_FFT or n_fft & (n_fft - 1):
+            # the reference's spectral op rejects these too (spectral.py, test_triton_spectral.py:237-255)
+            raise ValueError(f"n_fft ({n_fft}) must be a power of two of at least {MIN_FFT}.")
+        if n_fft > MAX_FFT:
+            raise ValueError(f"n_fft ({n_fft}): the CUDA kernels implement frames of up to {MAX_FFT} samples.")
+        if hop_length < 1:
+            raise ValueError(f"hop_length ({hop_length}) must be positive.")
+        if not 1 <= win_length <= n_fft:
+            raise ValueError(f"win_length ({win_length}) must be in [1, n_fft ({n_fft})].")
         layout = bark_layout(n_fft // 2, nbarks)
         power_b, power_a = power_filter()
         pre_b, pre_a = pre_filter()
