@@ -59,7 +59,7 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
-    ap.add_argument("--op", choices=["iir", "resample"], default=None,
+    ap.add_argument("--op", choices=["iir", "resample", "triton-reference"], default=None,
                     help="time only a standalone op on its large case (one JSON line; for profiling)")
     args = ap.parse_args()
     global BATCH, SECONDS
@@ -438,40 +438,68 @@ def measure_configs(dev, flush, steps=10):
     out = {}
     for name, keep, secs in (("cfg1", 1, 1.0), ("cfg3", 16, 4.0), ("cfg4_per_gpu", 8, 10.0), ("cfg5", 512, 3.0)):
         ref_c, deg_c, sr = workload(name.split("_")[0], seed=0)
-        ref = ref_c[:keep].to(dev)
-        deg = deg_c[:keep].to(dev).requires_grad_(True)
-        model = PesqLossCuda(1.0, sample_rate=sr)
-
-        def step():
-            loss = model(ref, deg)
-            (g,) = torch.autograd.grad(loss.sum(), [deg])
-            return loss, g
-
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                step()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        torch.cuda.synchronize()
-        times = []
-        for k in range(steps + 3):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            graph.replay()
-            b.record()
-            b.synchronize()
-            if k >= 3:
-                times.append(a.elapsed_time(b))
-        ms = statistics.median(times)
+        ms = _graphed_step_ms(PesqLossCuda(1.0, sample_rate=sr), ref_c[:keep].to(dev), deg_c[:keep].to(dev), flush,
+                              steps)
         out[name] = {"batch": keep, "seconds": secs, "sample_rate": sr, "ms_per_step": ms,
                      "utterance_seconds_per_s": keep * secs / (ms * 1e-3)}
-        del graph
+    return out
+
+
+def _graphed_step_ms(model, ref, deg, flush, steps):
+    """Median device time of a graph-replayed fwd+bwd (w.r.t. deg) step, L2
+    flushed before each replay."""
+
+    import torch
+
+    deg = deg.detach().requires_grad_(True)
+
+    def step():
+        loss = model(ref, deg)
+        (g,) = torch.autograd.grad(loss.sum(), [deg])
+        return loss, g
+
+    dev = ref.device
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for k in range(steps + 3):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        if k >= 3:
+            times.append(a.elapsed_time(b))
+    del graph
+    return statistics.median(times)
+
+
+def measure_geometries(dev, flush, steps=10):
+    """The cfg2 step (8 x 8 s at 16 kHz, fwd+bwd w.r.t. deg, graph replay) with
+    other frame geometries of PesqLoss (n_fft, hop_length, win_length): the
+    spectrum kernels instead of the fused 512 / 256 transforms."""
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.signals import workload
+
+    ref_c, deg_c, sr = workload("cfg2", seed=0)
+    ref, deg = ref_c.to(dev), deg_c.to(dev)
+    out = {}
+    for n_fft, hop, win in ((512, 256, 512), (256, 128, 256), (1024, 512, 1024), (512, 128, 512), (2048, 512, 2048)):
+        model = PesqLossCuda(1.0, sample_rate=sr, n_fft=n_fft, hop_length=hop, win_length=win)
+        ms = _graphed_step_ms(model, ref, deg, flush, steps)
+        out[f"n_fft{n_fft}_hop{hop}"] = {"ms_per_step": ms,
+                                         "utterance_seconds_per_s": ref.shape[0] * ref.shape[1] / sr / (ms * 1e-3)}
     return out
 
 
@@ -741,6 +769,7 @@ def run_cuda(args):
     ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)}
     configs = measure_configs(dev, flush) if not args.skip_configs else None
     fused = measure_fused(dev, flush) if not args.skip_configs else None
+    geometries = measure_geometries(dev, flush) if not args.skip_configs else None
 
     if world > 1:
         graph.reset()
@@ -800,6 +829,7 @@ def run_cuda(args):
         "ops": ops,
         "other_configs": configs,
         "in_training_step": fused,
+        "frame_geometries": geometries,
         "dominant_stage": dominant,
         "eager_ms_per_step": 1e3 * statistics.median(eager),
         "step_ms_min": min(step_ms),
@@ -811,14 +841,121 @@ def run_cuda(args):
     print(json.dumps(line), flush=True)
 
 
+REFERENCE_INSTALL = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+
+
+def _import_reference_gpu():
+    """``PesqLossTriton`` of the reference installed in baseline/_ref by
+    ``pip install --no-index --no-deps --target baseline/_ref <reference>``.
+    Two import shims, neither of which changes a computation: ``torchtyping``
+    is absent (``TensorType[...]`` becomes ``torch.Tensor``) and the installed
+    typeguard 4.x cannot evaluate the reference's string dimensions
+    (``typechecked`` becomes the identity)."""
+
+    import types
+
+    import torch
+
+    if not os.path.isdir(os.path.join(REFERENCE_INSTALL, "torch_pesq")):
+        raise ImportError("the reference is not installed in baseline/_ref")
+    shim = types.ModuleType("torchtyping")
+
+    class _TensorType:
+        def __class_getitem__(cls, item):
+            return torch.Tensor
+
+    shim.TensorType = _TensorType
+    sys.modules.setdefault("torchtyping", shim)
+    import typeguard
+
+    typeguard.typechecked = lambda fn: fn
+    sys.path.insert(0, REFERENCE_INSTALL)
+    from torch_pesq import PesqLossTriton
+
+    return PesqLossTriton
+
+
+def measure_triton_reference(dev, flush, steps):
+    """The reference's own GPU path (``PesqLossTriton``, Triton kernels) on the
+    headline workload, timed like this engine: the whole fwd+bwd (w.r.t. deg)
+    step captured in one CUDA graph, L2 flushed, CUDA events; plus its own
+    ``graphed`` callable and the eager step."""
+
+    import torch
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.signals import workload
+
+    PesqLossTriton = _import_reference_gpu()
+    ref_c, deg_c, sr = workload("cfg2", seed=0)
+    ref, deg = ref_c.to(dev), deg_c.to(dev)
+    utt_s = ref.shape[0] * ref.shape[1] / sr
+    model = PesqLossTriton(1.0, sample_rate=sr).to(dev)
+    out = {"workload": "cfg2: 8 x 8 s at 16 kHz, fwd + bwd w.r.t. deg"}
+
+    def timed(fn, n):
+        times = []
+        for k in range(n + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            if k >= 3:
+                times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    d = deg.detach().requires_grad_(True)
+
+    def eager():
+        loss = model(ref, d)
+        torch.autograd.grad(loss.sum(), [d])
+
+    out["eager_ms_per_step"] = timed(eager, steps)
+    graphed = model.graphed(ref, d)
+
+    def replay():
+        loss = graphed(ref, d)
+        torch.autograd.grad(loss.sum(), [d])
+
+    out["graphed_callable_ms_per_step"] = timed(replay, steps)
+    try:
+        out["step_graph_ms_per_step"] = _graphed_step_ms(model, ref, deg, flush, steps)
+    except Exception as exc:  # a host synchronisation inside the step breaks the capture
+        out["step_graph_ms_per_step"] = None
+        out["step_graph_error"] = f"{type(exc).__name__}: {exc}"[:200]
+    best = min(v for v in (out["graphed_callable_ms_per_step"], out["step_graph_ms_per_step"]) if v)
+    out["utterance_seconds_per_s"] = utt_s / (best * 1e-3)
+    # this engine, same workload and timing
+    mine = _graphed_step_ms(PesqLossCuda(1.0, sample_rate=sr), ref, deg, flush, steps)
+    out["this_engine_ms_per_step"] = mine
+    out["speedup"] = best / mine
+    # the two agree (float32 reference path vs this engine): relative distance gap
+    with torch.no_grad():
+        ds_r, da_r = model.raw(ref, deg)
+        ds_m, da_m = PesqLossCuda(1.0, sample_rate=sr).raw(ref, deg)
+    out["max_rel_diff_d_symm"] = float(((ds_r - ds_m).abs() / ds_m.abs()).max())
+    out["max_rel_diff_d_asymm"] = float(((da_r - da_m).abs() / da_m.abs()).max())
+    return out
+
+
 def run_op(args):
     """Only the large case of a standalone op, e.g. as the target of a
-    profiler capture."""
+    profiler capture; or the reference's own GPU path."""
 
     import torch
 
     dev = torch.device("cuda", 0)
     peak, _ = measured_peaks()
+    if args.op == "triton-reference":
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        try:
+            result = measure_triton_reference(dev, flush, args.steps)
+        except ImportError as exc:
+            result = {"unavailable": str(exc)}
+        print(json.dumps({"op": args.op, "measurements": result}))
+        return
     if args.op == "resample":
         result = measure_resampler(dev, peak, launches=args.steps)
     else:
