@@ -887,6 +887,7 @@ def measure_triton_reference(dev, flush, steps):
     from triton_pesq_b200.signals import workload
 
     PesqLossTriton = _import_reference_gpu()
+    out_ops = _measure_reference_ops(dev)
     ref_c, deg_c, sr = workload("cfg2", seed=0)
     ref, deg = ref_c.to(dev), deg_c.to(dev)
     utt_s = ref.shape[0] * ref.shape[1] / sr
@@ -937,6 +938,69 @@ def measure_triton_reference(dev, flush, steps):
         ds_m, da_m = PesqLossCuda(1.0, sample_rate=sr).raw(ref, deg)
     out["max_rel_diff_d_symm"] = float(((ds_r - ds_m).abs() / ds_m.abs()).max())
     out["max_rel_diff_d_asymm"] = float(((da_r - da_m).abs() / da_m.abs()).max())
+    out["ops"] = out_ops
+    return out
+
+
+def _measure_reference_ops(dev, launches=20):
+    """The reference's standalone ``TritonIIR`` and ``TritonResample`` and this
+    engine's ``IIRCuda`` / ``ResampleCuda`` on the same shapes, each call
+    timed the same way (eager, CUDA events over ``launches`` calls after 3
+    warm-up calls)."""
+
+    import torch
+
+    from torch_pesq.triton_ops.iir import TritonIIR
+    from torch_pesq.triton_ops.resample import TritonResample
+
+    from triton_pesq_b200 import IIRCuda, ResampleCuda
+    from triton_pesq_b200.tables import power_filter, pre_filter
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(launches):
+            fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        return 1e3 * start.elapsed_time(stop) / launches
+
+    out = {}
+    for label, (b, a) in (("order10", power_filter()), ("order2", pre_filter())):
+        theirs = TritonIIR(torch.tensor(b, dtype=torch.float32), torch.tensor(a, dtype=torch.float32)).to(dev)
+        mine = IIRCuda(b, a).to(dev)
+        shapes = ((8, 16000), (8, 64000), (64, 480000), (30720, 1000)) if label == "order10" else ((64, 480000),)
+        for rows, n in shapes:
+            x = torch.randn(rows, n, device=dev)
+            row = {"reference_fwd_us": timed(lambda: theirs(x)), "this_fwd_us": timed(lambda: mine(x))}
+            if rows * n <= 512000:
+                leaf = x.clone().requires_grad_(True)
+                g = torch.randn_like(x)
+                row["reference_fwd_bwd_us"] = timed(lambda: torch.autograd.grad(theirs(leaf), leaf, g))
+                row["this_fwd_bwd_us"] = timed(lambda: torch.autograd.grad(mine(leaf), leaf, g))
+            with torch.no_grad():
+                y_t, y_m = theirs(x), mine(x)
+                row["max_abs_diff_over_peak"] = float((y_t - y_m).abs().max() / y_m.abs().max())
+            row["speedup_fwd"] = row["reference_fwd_us"] / row["this_fwd_us"]
+            out[f"iir_{label}_{rows}x{n}"] = row
+    theirs = TritonResample(44100, 16000).to(dev)
+    mine = ResampleCuda(44100, 16000).to(dev)
+    x = torch.randn(256, 4 * 44100, device=dev)
+    leaf = x.clone().requires_grad_(True)
+    y = mine(x)
+    g = torch.randn_like(y)
+    row = {"reference_fwd_us": timed(lambda: theirs(x)), "this_fwd_us": timed(lambda: mine(x)),
+           "reference_fwd_bwd_us": timed(lambda: torch.autograd.grad(theirs(leaf), leaf, g)),
+           "this_fwd_bwd_us": timed(lambda: torch.autograd.grad(mine(leaf), leaf, g))}
+    with torch.no_grad():
+        row["max_abs_diff_over_peak"] = float((theirs(x) - y).abs().max() / y.abs().max())
+    row["speedup_fwd"] = row["reference_fwd_us"] / row["this_fwd_us"]
+    row["speedup_fwd_bwd"] = row["reference_fwd_bwd_us"] / row["this_fwd_bwd_us"]
+    out["resample_44100_to_16000_256x176400"] = row
     return out
 
 
