@@ -59,7 +59,7 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
-    ap.add_argument("--op", choices=["iir", "resample", "triton-reference"], default=None,
+    ap.add_argument("--op", choices=["iir", "resample", "geometry", "triton-reference"], default=None,
                     help="time only a standalone op on its large case (one JSON line; for profiling)")
     args = ap.parse_args()
     global BATCH, SECONDS
@@ -1019,6 +1019,10 @@ def run_op(args):
         except ImportError as exc:
             result = {"unavailable": str(exc)}
         print(json.dumps({"op": args.op, "measurements": result}))
+        return
+    if args.op == "geometry":
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        print(json.dumps({"op": args.op, "measurements": measure_geometries(dev, flush, steps=args.steps)}))
         return
     if args.op == "resample":
         result = measure_resampler(dev, peak, launches=args.steps)

@@ -116,6 +116,7 @@ struct GenTables {
 struct SpecArgs {
   GenTables g;
   const DevTables* tab;
+  const FftTwiddles<double>* tw512;  // n_fft 512: twiddles of the forward transform (the plan's)
   int64_t n;           // samples per row
   int frames;          // T
   int rows;            // rows (frames) of this launch: rows [row_begin, row_begin + rows)

@@ -485,6 +485,7 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int
     SpecArgs sa{};
     sa.g = p->gen;
     sa.tab = p->dtab;
+    sa.tw512 = p->tw64;
     sa.n = g.n16;
     sa.frames = g.T;
     sa.rows = (int)g.rows;
@@ -633,6 +634,7 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
     SpecArgs sa{};
     sa.g = p->gen;
     sa.tab = p->dtab;
+    sa.tw512 = p->tw64;
     sa.n = g.n16;
     sa.frames = g.T;
     sa.rows = g.grad_end - g.grad_begin;

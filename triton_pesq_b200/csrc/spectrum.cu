@@ -14,39 +14,61 @@
 //             dL/du_k = 2 Re sum_f conj(V_f) exp(-2 pi i f k / n_fft)        float32
 //             G_t[k] = w_k dL/du_k                                          -> frame gradients
 //
-// both with an in-place radix-2 transform of n_fft complex points in the
-// warp's slice of shared memory (inputs stored at bit-reversed positions,
-// log2 n_fft butterfly stages separated by __syncwarp, twiddles from a float64
-// table).  The back kernel overlap-adds the frame gradients by a gather in
-// frame order (no atomics, bitwise reproducible).  The default geometry keeps
-// the fused warp FFTs of the front and back kernels.
+// n_fft 512 (the PESQ frame with another hop or window) uses the register /
+// shared-memory transposed 512-point real transform of the fused path
+// (fft.cuh).  Every other n_fft uses an in-place radix-2 transform of n_fft
+// complex points in the warp's slice of shared memory, instantiated per
+// log2 n_fft so that its loops unroll: inputs stored at bit-reversed
+// positions, log2 n_fft butterfly stages separated by __syncwarp, twiddles
+// from a table the CTA stages in shared memory.  The back kernel overlap-adds
+// the frame gradients by a gather in frame order (no atomics, bitwise
+// reproducible).
 #include "kernels.cuh"
 
 namespace pesq {
 
 namespace {
 
-// warps per CTA: up to 8, as many n_fft-point frames as fit in 192 KB
+constexpr int kSmemBudget = 226 * 1024;
+
+// warps per CTA of the generic transform: up to 8, as many n_fft-point frames
+// as fit next to the CTA's twiddle table
 __host__ __device__ constexpr int gen_warps(int nfft, int elem_bytes) {
-  const int w = (192 * 1024) / (nfft * elem_bytes);
+  const int w = (kSmemBudget - (nfft / 2) * elem_bytes) / (nfft * elem_bytes);
   return w < 1 ? 1 : (w > kGenThreads / 32 ? kGenThreads / 32 : w);
 }
+__host__ __device__ constexpr size_t gen_smem(int nfft, int elem_bytes) {
+  return (size_t)(gen_warps(nfft, elem_bytes) * nfft + nfft / 2) * elem_bytes;
+}
 
-// In-place decimation-in-time FFT of 2^log2n points (input in bit-reversed
-// order, output in natural order), twiddle w^k = exp(-2 pi i k / 2^log2n).
-template <class R>
-__device__ __forceinline__ void warp_fft(Cx<R>* z, int log2n, const Cx<double>* tw, int lane) {
-  const int half_n = 1 << (log2n - 1);
-  for (int s = 0; s < log2n; ++s) {
+// The 512-point path: per warp the transposes' scratch, per CTA the twiddles.
+constexpr int kWarps512 = kGenThreads / 32;
+constexpr size_t kStft512Smem = sizeof(FftTwiddles<double>) + (size_t)kWarps512 * FftLayout<double>::kSlots * 16;
+constexpr size_t kIstft512Smem = sizeof(FftTwiddles<float>) + (size_t)kWarps512 * FftLayout<float>::kSlots * 8;
+
+__device__ __forceinline__ int bit_reverse(int k, int log2n) { return (int)(__brev((unsigned)k) >> (32 - log2n)); }
+
+// CTA copy of `bytes` (a multiple of 16) global -> shared
+__device__ __forceinline__ void stage_table(void* dst, const void* src, int bytes) {
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
+}
+
+// In-place decimation-in-time FFT of 2^LOG2N points (input in bit-reversed
+// order, output in natural order), tw[k] = exp(-2 pi i k / 2^LOG2N), k < N/2.
+template <int LOG2N, class R>
+__device__ __forceinline__ void warp_fft(Cx<R>* z, const Cx<R>* tw, int lane) {
+  constexpr int kHalfN = 1 << (LOG2N - 1);
+#pragma unroll
+  for (int s = 0; s < LOG2N; ++s) {
     const int half = 1 << s;
-    const int shift = log2n - 1 - s;  // butterfly k of this stage uses w^(k 2^shift)
-    for (int i = lane; i < half_n; i += 32) {
+    const int shift = LOG2N - 1 - s;  // butterfly k of this stage uses w^(k 2^shift)
+#pragma unroll 4
+    for (int i = lane; i < kHalfN; i += 32) {
       const int k = i & (half - 1);
       const int j = ((i >> s) << (s + 1)) + k;
-      const double2 wd = __ldg(reinterpret_cast<const double2*>(tw) + (k << shift));
-      const Cx<R> w = mk((R)wd.x, (R)wd.y);
       const Cx<R> a = z[j];
-      const Cx<R> b = c_mul(z[j + half], w);
+      const Cx<R> b = c_mul(z[j + half], tw[k << shift]);
       z[j] = c_add(a, b);
       z[j + half] = c_sub(a, b);
     }
@@ -54,110 +76,237 @@ __device__ __forceinline__ void warp_fft(Cx<R>* z, int log2n, const Cx<double>* 
   }
 }
 
-__device__ __forceinline__ int bit_reverse(int k, int log2n) { return (int)(__brev((unsigned)k) >> (32 - log2n)); }
+struct Frame {
+  int row, t;
+  bool valid;
+};
 
-__global__ void __launch_bounds__(kGenThreads) stft_kernel(const __grid_constant__ SpecArgs p) {
-  extern __shared__ __align__(16) double smem_d[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int warps = blockDim.x >> 5;
-  const int64_t item = (int64_t)blockIdx.x * warps + warp;
-  if (item >= (int64_t)p.rows * p.frames) return;  // whole warps only: no CTA barrier below
-  const int row = p.row_begin + (int)(item / p.frames);
-  const int t = (int)(item - (int64_t)(row - p.row_begin) * p.frames);
-  const int nfft = p.g.nfft, log2n = p.g.log2n, nfreq = p.g.nfreq;
-  Cx<double>* z = reinterpret_cast<Cx<double>*>(smem_d) + (size_t)warp * nfft;
+__device__ __forceinline__ Frame frame_of(const SpecArgs& p, int warp) {
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  Frame f;
+  f.valid = item < (int64_t)p.rows * p.frames;
+  const int local = f.valid ? (int)(item / p.frames) : 0;
+  f.row = p.row_begin + local;
+  f.t = f.valid ? (int)(item - (int64_t)local * p.frames) : 0;
+  return f;
+}
 
-  const double* yr = p.y + (int64_t)row * p.n;
-  const int64_t start = (int64_t)t * p.g.hop;
-  for (int k = lane; k < nfft; k += 32) {
-    const int64_t m = start + k;
-    const double v = m < p.n ? __ldg(yr + m) * (double)__ldg(p.g.window + k) : 0.0;
-    z[bit_reverse(k, log2n)] = mk(v, 0.0);
-  }
-  __syncwarp();
-  warp_fft<double>(z, log2n, p.g.tw, lane);
-
-  if (row >= p.spec_begin && row < p.spec_end) {
-    Cx<float>* out = p.spec + ((int64_t)row * p.frames + t) * nfreq;
-    for (int f = lane; f < nfreq; f += 32) out[f] = mk((float)z[f].x, (float)z[f].y);
-  }
-  // power in place (the DC bin is dropped), then the Bark segment sums
-  for (int f = lane; f < nfreq; f += 32) {
-    const Cx<double> X = z[f];
-    z[f].x = f == 0 ? 0.0 : fma(X.x, X.x, X.y * X.y);
-  }
-  __syncwarp();
+// Bark segment sums of the power spectrum pw (bin 0 already dropped)
+__device__ __forceinline__ void bark_sums(const SpecArgs& p, const double* pw, int row, int t, int lane) {
   const DevTables* tab = p.tab;
   const int nb = tab->nb;
   float* bark = p.bark + ((int64_t)row * p.frames + t) * nb;
   for (int b = lane; b < nb; b += 32) {
+    const int f0 = tab->band_start[b], f1 = tab->band_end[b];
     double acc = 0.0;
-    for (int f = tab->band_start[b]; f < tab->band_end[b]; ++f) acc += z[f].x;
+    for (int f = f0; f < f1; ++f) acc += pw[f];
     bark[b] = (float)(acc * (double)tab->band_corr[b]);
   }
 }
 
-__global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constant__ SpecArgs p) {
+template <int LOG2N>
+__global__ void __launch_bounds__(kGenThreads) stft_kernel(const __grid_constant__ SpecArgs p) {
+  constexpr int kN = 1 << LOG2N, kBinsN = kN / 2;
   extern __shared__ __align__(16) double smem_d[];
+  Cx<double>* tw = reinterpret_cast<Cx<double>*>(smem_d);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int warps = blockDim.x >> 5;
-  const int64_t item = (int64_t)blockIdx.x * warps + warp;
-  if (item >= (int64_t)p.rows * p.frames) return;
-  const int local = (int)(item / p.frames);
-  const int row = p.row_begin + local;
-  const int t = (int)(item - (int64_t)local * p.frames);
-  const int nfft = p.g.nfft, log2n = p.g.log2n, nfreq = p.g.nfreq;
-  Cx<float>* z = reinterpret_cast<Cx<float>*>(smem_d) + (size_t)warp * nfft;
+  stage_table(tw, p.g.tw, kBinsN * 16);
+  __syncthreads();
+  const Frame fr = frame_of(p, warp);
+  if (!fr.valid) return;  // whole warps only: no CTA barrier below
+  Cx<double>* z = tw + kBinsN + (size_t)warp * kN;
+
+  const double* yr = p.y + (int64_t)fr.row * p.n;
+  const int64_t start = (int64_t)fr.t * p.g.hop;
+#pragma unroll 4
+  for (int k = lane; k < kN; k += 32) {
+    const int64_t m = start + k;
+    const double v = m < p.n ? __ldg(yr + m) * (double)__ldg(p.g.window + k) : 0.0;
+    z[bit_reverse(k, LOG2N)] = mk(v, 0.0);
+  }
+  __syncwarp();
+  warp_fft<LOG2N, double>(z, tw, lane);
+
+  if (fr.row >= p.spec_begin && fr.row < p.spec_end) {
+    Cx<float>* out = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBinsN;
+    for (int f = lane; f < kBinsN; f += 32) out[f] = mk((float)z[f].x, (float)z[f].y);
+  }
+  // the power of bin f goes over the upper half of z (bins >= n_fft / 2 are not used)
+  double* pw = reinterpret_cast<double*>(z + kBinsN);
+  for (int f = lane; f < kBinsN; f += 32) {
+    const Cx<double> X = z[f];
+    pw[f] = f == 0 ? 0.0 : fma(X.x, X.x, X.y * X.y);
+  }
+  __syncwarp();
+  bark_sums(p, pw, fr.row, fr.t, lane);
+}
+
+template <int LOG2N>
+__global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constant__ SpecArgs p) {
+  constexpr int kN = 1 << LOG2N, kBinsN = kN / 2;
+  extern __shared__ __align__(16) double smem_d[];
+  Cx<float>* tw = reinterpret_cast<Cx<float>*>(smem_d);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int k = threadIdx.x; k < kBinsN; k += blockDim.x) {
+    const double2 w = __ldg(reinterpret_cast<const double2*>(p.g.tw) + k);
+    tw[k] = mk((float)w.x, (float)w.y);
+  }
+  __syncthreads();
+  const Frame fr = frame_of(p, warp);
+  if (!fr.valid) return;
+  const int local = fr.row - p.row_begin;
+  Cx<float>* z = tw + kBinsN + (size_t)warp * kN;
 
   const DevTables* tab = p.tab;
-  const Cx<float>* X = p.spec + ((int64_t)row * p.frames + t) * nfreq;
-  const float* g = p.g_bark + ((int64_t)row * p.frames + t) * tab->nb;
-  for (int f = lane; f < nfft; f += 32) {
+  const Cx<float>* X = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBinsN;
+  const float* g = p.g_bark + ((int64_t)fr.row * p.frames + fr.t) * tab->nb;
+#pragma unroll 4
+  for (int f = lane; f < kN; f += 32) {
     Cx<float> v = mk(0.0f, 0.0f);
-    const int b = f < nfreq ? __ldg(p.g.bin_band + f) : -1;
+    const int b = f < kBinsN ? __ldg(p.g.bin_band + f) : -1;
     if (b >= 0) {
       const float scale = g[b] * tab->band_corr[b];
       const Cx<float> x = X[f];
       v = mk(x.x * scale, -x.y * scale);  // conj(V_f)
     }
-    z[bit_reverse(f, log2n)] = v;
+    z[bit_reverse(f, LOG2N)] = v;
   }
   __syncwarp();
-  warp_fft<float>(z, log2n, p.g.tw, lane);
-  float* out = p.frame_grad + ((int64_t)local * p.frames + t) * nfft;
-  for (int k = lane; k < nfft; k += 32) out[k] = 2.0f * z[k].x * __ldg(p.g.window + k);
+  warp_fft<LOG2N, float>(z, tw, lane);
+  float* out = p.frame_grad + ((int64_t)local * p.frames + fr.t) * kN;
+#pragma unroll 4
+  for (int k = lane; k < kN; k += 32) out[k] = 2.0f * z[k].x * __ldg(p.g.window + k);
 }
 
-size_t stft_smem(int nfft) { return (size_t)gen_warps(nfft, 16) * nfft * 16; }
-size_t istft_smem(int nfft) { return (size_t)gen_warps(nfft, 8) * nfft * 8; }
+// n_fft 512: the transposed warp transforms of fft.cuh
+__global__ void __launch_bounds__(kGenThreads) stft512_kernel(const __grid_constant__ SpecArgs p) {
+  extern __shared__ __align__(16) double smem_d[];
+  FftTwiddles<double>* tw = reinterpret_cast<FftTwiddles<double>*>(smem_d);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  stage_table(tw, p.tw512, (int)sizeof(FftTwiddles<double>));
+  __syncthreads();
+  const Frame fr = frame_of(p, warp);
+  if (!fr.valid) return;
+  Cx<double>* sh = reinterpret_cast<Cx<double>*>(tw + 1) + (size_t)warp * FftLayout<double>::kSlots;
+
+  const double* yr = p.y + (int64_t)fr.row * p.n;
+  const int64_t start = (int64_t)fr.t * p.g.hop;
+  Cx<double> v[8], X[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int k = 2 * (lane + 32 * m);
+    const int64_t s0 = start + k;
+    const double y0 = s0 < p.n ? __ldg(yr + s0) : 0.0;
+    const double y1 = s0 + 1 < p.n ? __ldg(yr + s0 + 1) : 0.0;
+    const float2 w = __ldg(reinterpret_cast<const float2*>(p.g.window + k));
+    v[m] = mk(y0 * (double)w.x, y1 * (double)w.y);
+  }
+  warp_rfft512<double>(v, sh, *tw, lane, X);
+  if (fr.row >= p.spec_begin && fr.row < p.spec_end) {
+    Cx<float>* out = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBins;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) out[lane + 32 * m] = mk((float)X[m].x, (float)X[m].y);
+  }
+  double* pw = reinterpret_cast<double*>(sh);
+  __syncwarp();
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int f = lane + 32 * m;
+    pw[f] = f == 0 ? 0.0 : fma(X[m].x, X[m].x, X[m].y * X[m].y);
+  }
+  __syncwarp();
+  bark_sums(p, pw, fr.row, fr.t, lane);
+}
+
+__global__ void __launch_bounds__(kGenThreads) istft512_kernel(const __grid_constant__ SpecArgs p) {
+  extern __shared__ __align__(16) double smem_d[];
+  FftTwiddles<float>* tw = reinterpret_cast<FftTwiddles<float>*>(smem_d);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  stage_table(tw, &p.tab->fft, (int)sizeof(FftTwiddles<float>));
+  __syncthreads();
+  const Frame fr = frame_of(p, warp);
+  if (!fr.valid) return;
+  const int local = fr.row - p.row_begin;
+  Cx<float>* sh = reinterpret_cast<Cx<float>*>(tw + 1) + (size_t)warp * FftLayout<float>::kSlots;
+
+  const DevTables* tab = p.tab;
+  const Cx<float>* X = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBins;
+  const float* g = p.g_bark + ((int64_t)fr.row * p.frames + fr.t) * tab->nb;
+  Cx<float> V[8], gr[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int f = lane + 32 * m;
+    const int b = __ldg(p.g.bin_band + f);
+    V[m] = b >= 0 ? c_scale(X[f], g[b] * tab->band_corr[b]) : mk(0.0f, 0.0f);
+  }
+  warp_irfft512_adjoint(V, sh, *tw, lane, gr);
+  float* out = p.frame_grad + ((int64_t)local * p.frames + fr.t) * 512;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int k = 2 * (lane + 32 * m);
+    const float2 w = __ldg(reinterpret_cast<const float2*>(p.g.window + k));
+    *reinterpret_cast<float2*>(out + k) = make_float2(w.x * gr[m].x, w.y * gr[m].y);
+  }
+}
 
 template <class Kernel>
-cudaError_t launch_frames(Kernel kernel, const SpecArgs& a, int elem_bytes, cudaStream_t s) {
+cudaError_t launch_frames(Kernel kernel, const SpecArgs& a, int warps, size_t smem, cudaStream_t s) {
   const int64_t items = (int64_t)a.rows * a.frames;
   if (items <= 0) return cudaSuccess;
-  const int warps = gen_warps(a.g.nfft, elem_bytes);
   const int64_t blocks = (items + warps - 1) / warps;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  LaunchShape l((unsigned)blocks, (unsigned)(warps * 32), (size_t)warps * a.g.nfft * elem_bytes, s, false);
+  LaunchShape l((unsigned)blocks, (unsigned)(warps * 32), smem, s, false);
   return cudaLaunchKernelEx(&l.cfg, kernel, a);
+}
+
+template <int LOG2N>
+cudaError_t configure_log2() {
+  cudaError_t e = cudaFuncSetAttribute(stft_kernel<LOG2N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gen_smem(1 << LOG2N, 16));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(istft_kernel<LOG2N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)gen_smem(1 << LOG2N, 8));
+}
+
+template <int LOG2N>
+cudaError_t launch_log2(const SpecArgs& a, bool adjoint, cudaStream_t s) {
+  constexpr int kN = 1 << LOG2N;
+  if (adjoint) return launch_frames(istft_kernel<LOG2N>, a, gen_warps(kN, 8), gen_smem(kN, 8), s);
+  return launch_frames(stft_kernel<LOG2N>, a, gen_warps(kN, 16), gen_smem(kN, 16), s);
+}
+
+cudaError_t launch_spectrum(const SpecArgs& a, bool adjoint, cudaStream_t s) {
+  switch (a.g.log2n) {
+    case 5: return launch_log2<5>(a, adjoint, s);
+    case 6: return launch_log2<6>(a, adjoint, s);
+    case 7: return launch_log2<7>(a, adjoint, s);
+    case 8: return launch_log2<8>(a, adjoint, s);
+    case 9:
+      if (adjoint) return launch_frames(istft512_kernel, a, kWarps512, kIstft512Smem, s);
+      return launch_frames(stft512_kernel, a, kWarps512, kStft512Smem, s);
+    case 10: return launch_log2<10>(a, adjoint, s);
+    case 11: return launch_log2<11>(a, adjoint, s);
+    case 12: return launch_log2<12>(a, adjoint, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
 
 cudaError_t configure_spectrum() {
-  cudaError_t e = cudaFuncSetAttribute(stft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)stft_smem(kGenMaxFft));
+  cudaError_t e = cudaSuccess;
+  if ((e = configure_log2<5>()) != cudaSuccess || (e = configure_log2<6>()) != cudaSuccess ||
+      (e = configure_log2<7>()) != cudaSuccess || (e = configure_log2<8>()) != cudaSuccess ||
+      (e = configure_log2<10>()) != cudaSuccess || (e = configure_log2<11>()) != cudaSuccess ||
+      (e = configure_log2<12>()) != cudaSuccess)
+    return e;
+  e = cudaFuncSetAttribute(stft512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStft512Smem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(istft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)istft_smem(kGenMaxFft));
+  return cudaFuncSetAttribute(istft512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kIstft512Smem);
 }
 
-cudaError_t launch_stft(const SpecArgs& a, cudaStream_t s) {
-  return launch_frames(stft_kernel, a, 16, s);
-}
+cudaError_t launch_stft(const SpecArgs& a, cudaStream_t s) { return launch_spectrum(a, false, s); }
 
-cudaError_t launch_istft(const SpecArgs& a, cudaStream_t s) {
-  return launch_frames(istft_kernel, a, 8, s);
-}
+cudaError_t launch_istft(const SpecArgs& a, cudaStream_t s) { return launch_spectrum(a, true, s); }
 
 }  // namespace pesq
