@@ -73,8 +73,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t n = base + i;
       float acc = 0.0f;
       if (i >= kHop && i < top_g && n < n_row) {
-        const int t_hi = (int)min((int64_t)p.frames - 1, n / p.hop);
-        const int t_lo = n >= p.nfft ? (int)((n - p.nfft) / p.hop) + 1 : 0;
+        // rows hold at most 2^31 samples: 32-bit divisions
+        const unsigned un = (unsigned)n, hop = (unsigned)p.hop, nfft = (unsigned)p.nfft;
+        const int t_hi = min(p.frames - 1, (int)(un / hop));
+        const int t_lo = un >= nfft ? (int)((un - nfft) / hop) + 1 : 0;
         for (int t = t_lo; t <= t_hi; ++t) acc += __ldg(fg + (int64_t)t * p.nfft + (n - (int64_t)t * p.hop));
       }
       gy[i] = acc;

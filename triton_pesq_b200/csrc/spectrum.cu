@@ -16,11 +16,13 @@
 //
 // n_fft 512 (the PESQ frame with another hop or window) uses the register /
 // shared-memory transposed 512-point real transform of the fused path
-// (fft.cuh).  Every other n_fft uses an in-place radix-2 transform of n_fft
-// complex points in the warp's slice of shared memory, instantiated per
-// log2 n_fft so that its loops unroll: inputs stored at bit-reversed
-// positions, log2 n_fft butterfly stages separated by __syncwarp, twiddles
-// from a table the CTA stages in shared memory.  The back kernel overlap-adds
+// (fft.cuh).  Every other n_fft packs the real frame into n_fft / 2 complex
+// points (even samples real, odd imaginary) and runs an in-place radix-2
+// transform of those in the warp's slice of shared memory, instantiated per
+// log2 n_fft so that its loops unroll (inputs stored at bit-reversed
+// positions, butterfly stages separated by __syncwarp, twiddles from a table
+// the CTA stages in shared memory); the even / odd split of the result gives
+// the real spectrum, and its adjoint the inverse.  The back kernel overlap-adds
 // the frame gradients by a gather in frame order (no atomics, bitwise
 // reproducible).
 #include "kernels.cuh"
@@ -31,14 +33,15 @@ namespace {
 
 constexpr int kSmemBudget = 226 * 1024;
 
-// warps per CTA of the generic transform: up to 8, as many n_fft-point frames
-// as fit next to the CTA's twiddle table
+// warps per CTA of the generic transform: up to 8, as many frames (n_fft / 2
+// packed complex points each) as fit next to the CTA's twiddle table of
+// n_fft / 2 entries
 __host__ __device__ constexpr int gen_warps(int nfft, int elem_bytes) {
-  const int w = (kSmemBudget - (nfft / 2) * elem_bytes) / (nfft * elem_bytes);
+  const int w = (kSmemBudget - (nfft / 2) * elem_bytes) / ((nfft / 2) * elem_bytes);
   return w < 1 ? 1 : (w > kGenThreads / 32 ? kGenThreads / 32 : w);
 }
 __host__ __device__ constexpr size_t gen_smem(int nfft, int elem_bytes) {
-  return (size_t)(gen_warps(nfft, elem_bytes) * nfft + nfft / 2) * elem_bytes;
+  return (size_t)(gen_warps(nfft, elem_bytes) + 1) * (nfft / 2) * elem_bytes;
 }
 
 // The 512-point path: per warp the transposes' scratch, per CTA the twiddles.
@@ -54,17 +57,19 @@ __device__ __forceinline__ void stage_table(void* dst, const void* src, int byte
     reinterpret_cast<float4*>(dst)[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
 }
 
-// In-place decimation-in-time FFT of 2^LOG2N points (input in bit-reversed
-// order, output in natural order), tw[k] = exp(-2 pi i k / 2^LOG2N), k < N/2.
-template <int LOG2N, class R>
+// In-place decimation-in-time FFT of M = 2^LOG2M points (input in
+// bit-reversed order, output in natural order) with twiddles
+// exp(-2 pi i k / M) = tw[k << TWS] from a table of a 2^TWS times longer
+// transform.
+template <int LOG2M, int TWS, class R>
 __device__ __forceinline__ void warp_fft(Cx<R>* z, const Cx<R>* tw, int lane) {
-  constexpr int kHalfN = 1 << (LOG2N - 1);
+  constexpr int kHalfM = 1 << (LOG2M - 1);
 #pragma unroll
-  for (int s = 0; s < LOG2N; ++s) {
+  for (int s = 0; s < LOG2M; ++s) {
     const int half = 1 << s;
-    const int shift = LOG2N - 1 - s;  // butterfly k of this stage uses w^(k 2^shift)
+    const int shift = LOG2M - 1 - s + TWS;  // butterfly k of this stage uses exp(-2 pi i k / (2 half))
 #pragma unroll 4
-    for (int i = lane; i < kHalfN; i += 32) {
+    for (int i = lane; i < kHalfM; i += 32) {
       const int k = i & (half - 1);
       const int j = ((i >> s) << (s + 1)) + k;
       const Cx<R> a = z[j];
@@ -74,6 +79,15 @@ __device__ __forceinline__ void warp_fft(Cx<R>* z, const Cx<R>* tw, int lane) {
     }
     __syncwarp();
   }
+}
+
+// Bin of a real n_fft-point frame from the n_fft/2-point transform Z of its
+// packed samples z[n] = u[2n] + i u[2n+1]: with Zc = conj Z[n_fft/2 - f],
+// X_f = (Z_f + Zc) / 2 + w^f (-i) (Z_f - Zc) / 2, w = exp(-2 pi i / n_fft).
+__device__ __forceinline__ Cx<double> real_bin(Cx<double> zf, Cx<double> zc, Cx<double> w) {
+  const Cx<double> e = c_scale(c_add(zf, zc), 0.5);
+  const Cx<double> o = c_scale(c_rot90<-1>(c_sub(zf, zc)), 0.5);
+  return c_add(e, c_mul(w, o));
 }
 
 struct Frame {
@@ -91,7 +105,8 @@ __device__ __forceinline__ Frame frame_of(const SpecArgs& p, int warp) {
   return f;
 }
 
-// Bark segment sums of the power spectrum pw (bin 0 already dropped)
+// Bark segment sums of the power spectrum pw[f * STRIDE] (bin 0 already dropped)
+template <int STRIDE>
 __device__ __forceinline__ void bark_sums(const SpecArgs& p, const double* pw, int row, int t, int lane) {
   const DevTables* tab = p.tab;
   const int nb = tab->nb;
@@ -99,55 +114,63 @@ __device__ __forceinline__ void bark_sums(const SpecArgs& p, const double* pw, i
   for (int b = lane; b < nb; b += 32) {
     const int f0 = tab->band_start[b], f1 = tab->band_end[b];
     double acc = 0.0;
-    for (int f = f0; f < f1; ++f) acc += pw[f];
+    for (int f = f0; f < f1; ++f) acc += pw[f * STRIDE];
     bark[b] = (float)(acc * (double)tab->band_corr[b]);
   }
 }
 
 template <int LOG2N>
 __global__ void __launch_bounds__(kGenThreads) stft_kernel(const __grid_constant__ SpecArgs p) {
-  constexpr int kN = 1 << LOG2N, kBinsN = kN / 2;
+  constexpr int kLog2M = LOG2N - 1, kM = 1 << kLog2M;  // packed complex points = bins
   extern __shared__ __align__(16) double smem_d[];
-  Cx<double>* tw = reinterpret_cast<Cx<double>*>(smem_d);
+  Cx<double>* tw = reinterpret_cast<Cx<double>*>(smem_d);  // exp(-2 pi i k / n_fft), k < kM
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  stage_table(tw, p.g.tw, kBinsN * 16);
+  stage_table(tw, p.g.tw, kM * 16);
   __syncthreads();
   const Frame fr = frame_of(p, warp);
   if (!fr.valid) return;  // whole warps only: no CTA barrier below
-  Cx<double>* z = tw + kBinsN + (size_t)warp * kN;
+  Cx<double>* z = tw + kM + (size_t)warp * kM;
 
   const double* yr = p.y + (int64_t)fr.row * p.n;
   const int64_t start = (int64_t)fr.t * p.g.hop;
 #pragma unroll 4
-  for (int k = lane; k < kN; k += 32) {
-    const int64_t m = start + k;
-    const double v = m < p.n ? __ldg(yr + m) * (double)__ldg(p.g.window + k) : 0.0;
-    z[bit_reverse(k, LOG2N)] = mk(v, 0.0);
+  for (int k = lane; k < kM; k += 32) {
+    const int64_t m = start + 2 * k;
+    const double y0 = m < p.n ? __ldg(yr + m) : 0.0;
+    const double y1 = m + 1 < p.n ? __ldg(yr + m + 1) : 0.0;
+    const float2 w = __ldg(reinterpret_cast<const float2*>(p.g.window + 2 * k));
+    z[bit_reverse(k, kLog2M)] = mk(y0 * (double)w.x, y1 * (double)w.y);
   }
   __syncwarp();
-  warp_fft<LOG2N, double>(z, tw, lane);
+  warp_fft<kLog2M, 1, double>(z, tw, lane);
 
-  if (fr.row >= p.spec_begin && fr.row < p.spec_end) {
-    Cx<float>* out = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBinsN;
-    for (int f = lane; f < kBinsN; f += 32) out[f] = mk((float)z[f].x, (float)z[f].y);
-  }
-  // the power of bin f goes over the upper half of z (bins >= n_fft / 2 are not used)
-  double* pw = reinterpret_cast<double*>(z + kBinsN);
-  for (int f = lane; f < kBinsN; f += 32) {
-    const Cx<double> X = z[f];
-    pw[f] = f == 0 ? 0.0 : fma(X.x, X.x, X.y * X.y);
+  // bins f and kM - f from the same two values (one lane owns both slots):
+  // the spectrum, then the power in place of the real part (bin 0 dropped)
+  const bool save = fr.row >= p.spec_begin && fr.row < p.spec_end;
+  Cx<float>* out = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kM;
+  for (int f = lane; f <= kM / 2; f += 32) {
+    const int g = (kM - f) & (kM - 1);
+    const Cx<double> zf = z[f], zg = z[g];
+    const Cx<double> xf = real_bin(zf, c_conj(zg), tw[f]);
+    const Cx<double> xg = real_bin(zg, c_conj(zf), tw[g]);
+    if (save) {
+      out[f] = mk((float)xf.x, (float)xf.y);
+      if (g != f) out[g] = mk((float)xg.x, (float)xg.y);
+    }
+    z[f].x = f == 0 ? 0.0 : fma(xf.x, xf.x, xf.y * xf.y);
+    if (g != f) z[g].x = fma(xg.x, xg.x, xg.y * xg.y);
   }
   __syncwarp();
-  bark_sums(p, pw, fr.row, fr.t, lane);
+  bark_sums<2>(p, reinterpret_cast<const double*>(z), fr.row, fr.t, lane);
 }
 
 template <int LOG2N>
 __global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constant__ SpecArgs p) {
-  constexpr int kN = 1 << LOG2N, kBinsN = kN / 2;
+  constexpr int kLog2M = LOG2N - 1, kM = 1 << kLog2M;
   extern __shared__ __align__(16) double smem_d[];
   Cx<float>* tw = reinterpret_cast<Cx<float>*>(smem_d);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int k = threadIdx.x; k < kBinsN; k += blockDim.x) {
+  for (int k = threadIdx.x; k < kM; k += blockDim.x) {
     const double2 w = __ldg(reinterpret_cast<const double2*>(p.g.tw) + k);
     tw[k] = mk((float)w.x, (float)w.y);
   }
@@ -155,27 +178,36 @@ __global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constan
   const Frame fr = frame_of(p, warp);
   if (!fr.valid) return;
   const int local = fr.row - p.row_begin;
-  Cx<float>* z = tw + kBinsN + (size_t)warp * kN;
+  Cx<float>* z = tw + kM + (size_t)warp * kM;
 
+  // V_f = corr_b dL/dB_b X_f (0 for bin 0 and bins outside every band);
+  // the frame gradient g_k = sum_f U_f exp(+2 pi i f k / n_fft) over the
+  // Hermitian extension U of V is, packed as g_2n + i g_2n+1, the inverse
+  // kM-point transform of Z'_f = (V_f + conj V_{kM-f}) + i conj(w^f) (V_f - conj V_{kM-f})
+  // (V_kM = 0), evaluated as conj(DFT(conj Z')).
   const DevTables* tab = p.tab;
-  const Cx<float>* X = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kBinsN;
-  const float* g = p.g_bark + ((int64_t)fr.row * p.frames + fr.t) * tab->nb;
+  const Cx<float>* X = p.spec + ((int64_t)fr.row * p.frames + fr.t) * kM;
+  const float* gb = p.g_bark + ((int64_t)fr.row * p.frames + fr.t) * tab->nb;
+  auto vbin = [&](int f) {
+    const int b = f < kM ? __ldg(p.g.bin_band + f) : -1;
+    return b >= 0 ? c_scale(X[f], gb[b] * tab->band_corr[b]) : mk(0.0f, 0.0f);
+  };
 #pragma unroll 4
-  for (int f = lane; f < kN; f += 32) {
-    Cx<float> v = mk(0.0f, 0.0f);
-    const int b = f < kBinsN ? __ldg(p.g.bin_band + f) : -1;
-    if (b >= 0) {
-      const float scale = g[b] * tab->band_corr[b];
-      const Cx<float> x = X[f];
-      v = mk(x.x * scale, -x.y * scale);  // conj(V_f)
-    }
-    z[bit_reverse(f, LOG2N)] = v;
+  for (int f = lane; f < kM; f += 32) {
+    const Cx<float> v = vbin(f);
+    const Cx<float> vc = c_conj(vbin(kM - f));
+    const Cx<float> d = c_mul(c_conj(tw[f]), c_sub(v, vc));
+    z[bit_reverse(f, kLog2M)] = c_conj(c_add(c_add(v, vc), c_rot90<1>(d)));
   }
   __syncwarp();
-  warp_fft<LOG2N, float>(z, tw, lane);
-  float* out = p.frame_grad + ((int64_t)local * p.frames + fr.t) * kN;
+  warp_fft<kLog2M, 1, float>(z, tw, lane);
+  float* out = p.frame_grad + ((int64_t)local * p.frames + fr.t) * (2 * kM);
 #pragma unroll 4
-  for (int k = lane; k < kN; k += 32) out[k] = 2.0f * z[k].x * __ldg(p.g.window + k);
+  for (int n = lane; n < kM; n += 32) {
+    const Cx<float> r = z[n];
+    const float2 w = __ldg(reinterpret_cast<const float2*>(p.g.window + 2 * n));
+    *reinterpret_cast<float2*>(out + 2 * n) = make_float2(w.x * r.x, -w.y * r.y);
+  }
 }
 
 // n_fft 512: the transposed warp transforms of fft.cuh
@@ -215,7 +247,7 @@ __global__ void __launch_bounds__(kGenThreads) stft512_kernel(const __grid_const
     pw[f] = f == 0 ? 0.0 : fma(X[m].x, X[m].x, X[m].y * X[m].y);
   }
   __syncwarp();
-  bark_sums(p, pw, fr.row, fr.t, lane);
+  bark_sums<1>(p, pw, fr.row, fr.t, lane);
 }
 
 __global__ void __launch_bounds__(kGenThreads) istft512_kernel(const __grid_constant__ SpecArgs p) {
