@@ -248,7 +248,7 @@ def test_cuda_graph_is_bit_exact(cuda_device):
         assert torch.equal(got, want)
 
 
-@pytest.mark.parametrize("sample_rate,seconds", [(48000, 12.0), (16000, 30.0)])
+@pytest.mark.parametrize("sample_rate,seconds", [(48000, 12.0), (16000, 15.0), (16000, 30.0)])
 def test_long_signal(cuda_device, sample_rate, seconds):
     n = int(sample_rate * seconds)
     ref = speech_like(1, n, sample_rate, seed=41)

@@ -810,7 +810,28 @@ cudaError_t configure_chain() {
   cudaError_t e = cudaFuncSetAttribute(chain_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kChainSmemLimit);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmemLimit);
+  e = cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmemLimit);
+  if (e != cudaSuccess) return e;
+  // clusters of up to 16 CTAs (beyond the portable 8) for long utterances
+  e = cudaFuncSetAttribute(chain_fwd_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+int chain_active_clusters(int cluster) {
+  // clusters of `cluster` CTAs of both chain kernels that the current device
+  // runs at once with the full shared memory allocation (0: none)
+  int fewest = 1 << 30;
+  for (const void* k : {reinterpret_cast<const void*>(chain_fwd_kernel), reinterpret_cast<const void*>(chain_bwd_kernel)}) {
+    LaunchShape l((unsigned)cluster, kChainThreads, kChainSmemLimit, nullptr, false, cluster);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k, &l.cfg) != cudaSuccess) {
+      cudaGetLastError();  // a refused query leaves no error behind
+      return 0;
+    }
+    fewest = clusters < fewest ? clusters : fewest;
+  }
+  return fewest;
 }
 
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s) {

@@ -328,6 +328,7 @@ cudaError_t configure_spectrum();
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s);
 cudaError_t configure_chain();
+int chain_active_clusters(int cluster);  // chain clusters of that size the current device runs at once
 // frames of the largest cluster slice, and the dynamic shared memory of the
 // staged forward / backward chain kernels for it
 int chain_slice_frames(int T, int cluster);

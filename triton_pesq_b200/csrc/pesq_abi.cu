@@ -42,6 +42,7 @@ struct pesq_plan {
   int nfft, hop;
   bool general;
   void* gen_buf;
+  int active_clusters[17];  // [c]: chain clusters of c CTAs the plan's device runs at once (c = 8..16)
   GenTables gen;
   // resampler to 16 kHz (sample_rate != 16000)
   bool resample;
@@ -166,6 +167,21 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
   // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
+  // a long utterance whose 8-CTA slices do not fit the chain backward's
+  // shared memory layout takes the smallest larger cluster (up to 16) whose
+  // slices fit, unless the device runs fewer of those at once than it
+  // needs for the batch in as many waves as with 8
+  if (g.cluster == 8 && chain_bwd_smem_bytes(chain_slice_frames(g.T, 8), p->nb) > chain_smem_limit()) {
+    const int64_t waves8 = ceil_div(std::max<int64_t>(batch, 1), std::max(1, p->active_clusters[8]));
+    for (int c = 9; c <= 16; ++c) {
+      if (p->active_clusters[c] < 1 ||
+          chain_bwd_smem_bytes(chain_slice_frames(g.T, c), p->nb) > chain_smem_limit() ||
+          ceil_div(std::max<int64_t>(batch, 1), p->active_clusters[c]) > waves8)
+        continue;
+      g.cluster = c;
+      break;
+    }
+  }
   {
     const int slice = chain_slice_frames(g.T, g.cluster);
     g.fwd_staged = chain_fwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
@@ -386,6 +402,7 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the back kernel"));
   e = configure_chain();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the chain kernels"));
+  for (int c = 8; c <= 16; ++c) p->active_clusters[c] = chain_active_clusters(c);
   e = configure_align();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the align kernel"));
   e = configure_spectrum();
