@@ -94,6 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n >= a && n < send) ssq = fma((double)y, (double)y, ssq);
         if (grad_row) fb[q] = y;
       });
+  PESQ_STAMP(g_phase_front, 2);
   ssq = warp_sum(ssq);
   if (lane == 0) red[warp] = ssq;
   __syncthreads();
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
   }
+  PESQ_STAMP(g_phase_front, 3);
   // x = xs + fb from here on (fb = 0 for a 16 kHz input)
   if (!has_lo)
     for (int i = tid; i < kSpan; i += kThreads) fb[i] = 0.0f;
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
-  PESQ_STAMP(g_phase_front, 2);
+  PESQ_STAMP(g_phase_front, 4);
 
   // 3. pre-emphasis in double precision, y written as doubles over the
   //    (xs, fb) pair (every thread reads all of its inputs before the scan's
@@ -142,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pre, reinterpret_cast<double*>(scratch), [&](int q) { return (double)xs[q] + (double)fb[q]; },
       [&](int q, double y) { yd[q] = q < q_end ? y : 0.0; });
   __syncthreads();
-  PESQ_STAMP(g_phase_front, 3);
+  PESQ_STAMP(g_phase_front, 5);
 
   if constexpr (kSignal) {
     double* yo = p.y64 + (int64_t)row * n_row;
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
   }
-  PESQ_STAMP(g_phase_front, 4);
+  PESQ_STAMP(g_phase_front, 6);
   PESQ_CTA_END(g_cta_front);
   PESQ_SPAN_END(g_span_front, 0);
 }
