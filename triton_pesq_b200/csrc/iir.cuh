@@ -279,7 +279,9 @@ __device__ __forceinline__ float warp_sum(const float* wpow, const float* tot, i
   return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
-template <int P, bool kLower, bool kRerun>
+// kRev: the rows are filtered back to front (a.reverse; a compile-time
+// direction turns every staged-tile index into a constant offset)
+template <int P, bool kLower, bool kRerun, bool kRev>
 __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan_kernel(const __grid_constant__ Args a,
                                                                         const __grid_constant__ Tab<P> tab) {
   extern __shared__ __align__(16) float smem[];
@@ -310,12 +312,12 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
     row0 = tile / a.tiles_per_row;
     tin = tile - row0 * a.tiles_per_row;
     nrows = 1;
-    m0 = a.reverse ? a.n - (tin + 1) * (int64_t)kTile : tin * (int64_t)kTile;
+    m0 = kRev ? a.n - (tin + 1) * (int64_t)kTile : tin * (int64_t)kTile;
   } else {
     row0 = tile * a.rows_per_tile;
     tin = 0;
     nrows = (int)min((int64_t)a.rows_per_tile, a.rows - row0);
-    m0 = a.reverse ? a.n - seg : 0;
+    m0 = kRev ? a.n - seg : 0;
   }
   // a whole, 16-byte aligned tile of one row moves in 16-byte pieces
   const float* xrow = a.x + row0 * a.ld_x;
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
     // packed rows: warp w stages rows w, w + kWarps, ... (segments of seg
     // samples, the row's n samples at the front or, reversed, at the back)
     const int n = (int)a.n;
-    const int lead = a.reverse ? seg - n : 0;
+    const int lead = kRev ? seg - n : 0;
     for (int rr = warp; rr < a.rows_per_tile; rr += kWarps) {
       float* dst = xs + rr * seg;
       if (rr < nrows) {
@@ -365,8 +367,8 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
   const int lc = chained ? tid : tid - r * a.cpr;
   const bool used = chained || r < nrows;
   const bool head = chained ? (tin == 0 && tid == 0) : (!used || lc == 0);
-  const int dir = a.reverse ? -1 : 1;
-  const int base = a.reverse ? r * seg + seg - 1 - lc * kL : r * seg + lc * kL;
+  constexpr int dir = kRev ? -1 : 1;
+  const int base = kRev ? r * seg + seg - 1 - lc * kL : r * seg + lc * kL;
 
   // (chunks past the last packed row hold no data and store nothing; their
   // shared memory index could lie past the tile)
@@ -553,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
     }
   } else {
     const int n = (int)a.n;
-    const int lead = a.reverse ? seg - n : 0;
+    const int lead = kRev ? seg - n : 0;
     for (int rr = warp; rr < nrows; rr += kWarps) {
       float* dst = yrow + rr * a.ld_y;
       const float* src = xs + rr * seg + lead;

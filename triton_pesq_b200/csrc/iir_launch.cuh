@@ -12,7 +12,7 @@ cudaError_t launch(const Args& a, const void* tab, cudaStream_t s) {
   static_assert(sizeof(Tab<P>) == sizeof(float) * (kL + 2 * kL * P + (kLevels + 1) * P * P + 2 * P + 1),
                 "Tab<P> is a packed array of floats");
   const size_t smem = smem_bytes(P);
-  auto kern = scan_kernel<P, kLower, kRerun>;
+  auto kern = a.reverse ? scan_kernel<P, kLower, kRerun, true> : scan_kernel<P, kLower, kRerun, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<(unsigned)a.tiles, kThreads, smem, s>>>(a, *static_cast<const Tab<P>*>(tab));
