@@ -71,7 +71,10 @@ GEOMETRIES = [  # n_fft, hop_length, win_length
     (512, 128, 512), (512, 300, 512), (512, 256, 320), (256, 512, 256),
 ]
 GEOMETRY_CASES = ([g + (3, 20000, 16000) for g in GEOMETRIES] + [g + (2, 33075, 44100) for g in GEOMETRIES] +
-                  [(4096, 512, 3000, 2, 20000, 16000), (4096, 1024, 4096, 1, 96000, 48000)])
+                  [(4096, 512, 3000, 2, 20000, 16000), (4096, 1024, 4096, 1, 96000, 48000),
+                   # 8 x 8 s at hop 128: T = 999, the chain backward stages its slices
+                   # but reads the forward's coefficients from L2
+                   (512, 128, 512, 8, 128000, 16000)])
 
 
 @pytest.mark.parametrize("n_fft,hop,win,batch,samples,sample_rate", GEOMETRY_CASES)

@@ -69,13 +69,13 @@ size_t chain_fwd_smem_bytes(int slice, int nb, bool cells) {
   const size_t cblk = ((size_t)slice * nb + 3) & ~(size_t)3;
   return (spectra + (cells ? (size_t)kCellFields * cblk : 0)) * sizeof(float);
 }
-// Bark spectra and their gradient accumulators (4 slices), the forward's
-// adjoint coefficients of the slice (kCellFields slices), the ten per-frame
-// saved arrays and two per-frame gradients of frames c_lo..c_hi, and the two
-// window arrays over the slice
-size_t chain_bwd_smem_bytes(int slice, int nb) {
+// Bark spectra and their gradient accumulators (4 slices), with `cells` the
+// forward's adjoint coefficients of the slice (kCellFields slices), the ten
+// per-frame saved arrays and two per-frame gradients of frames c_lo..c_hi, and
+// the two window arrays over the slice
+size_t chain_bwd_smem_bytes(int slice, int nb, bool cells) {
   const size_t cblk = ((size_t)slice * nb + 3) & ~(size_t)3;
-  return ((size_t)kCellFields * cblk + (size_t)4 * slice * nb + (size_t)12 * (slice + 1) +
+  return ((cells ? (size_t)kCellFields * cblk : 0) + (size_t)4 * slice * nb + (size_t)12 * (slice + 1) +
           (size_t)2 * (slice / 10 + 4)) *
          sizeof(float);
 }
@@ -542,12 +542,16 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   float* fs = nullptr;   // [kFrameArrays][fpitch]
   float* gfs = nullptr;  // [2][fpitch]: dL/dfpr, dL/dh of the slice's frames
   float* ws = nullptr;   // [2][wpitch]: psqm_s, psqm_a of windows l_min..l_max
+  const bool cells_staged = p.staged && p.stage_cells;
   if (p.staged) {
     const int n = (sl.c_hi - sl.c_lo) * nb;
-    cs = dsm;  // first: 16-byte aligned
-    for (int f = 0; f < kCellFields; ++f)
-      copy_async<kChainThreads>(cs + f * cpitch, cells + f * p.cell_stride, ((n + 3) & ~3) * 4);
-    float* sr = cs + kCellFields * cpitch;
+    float* sr = dsm;  // 16-byte aligned
+    if (cells_staged) {
+      cs = dsm;  // first
+      for (int f = 0; f < kCellFields; ++f)
+        copy_async<kChainThreads>(cs + f * cpitch, cells + f * p.cell_stride, ((n + 3) & ~3) * 4);
+      sr = cs + kCellFields * cpitch;
+    }
     float* sd = sr + n;
     stage_rows_async<kChainThreads>(sr, n, Fr + (int64_t)sl.c_lo * nb, Fd - Fr, 2, n);
     fr = sr;
@@ -570,7 +574,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   };
   auto CELL = [&](int f, int t, int k) -> float {
     const int i = (t - sl.c_lo) * nb + k;
-    return p.staged ? cs[f * cpitch + i] : __ldg(cells + f * p.cell_stride + i);
+    return cells_staged ? cs[f * cpitch + i] : __ldg(cells + f * p.cell_stride + i);
   };
   auto PQ = [&](int side, int l) -> float {
     return p.staged ? ws[side * wpitch + (l - l_min)] : __ldg(sv + (side ? p.lay.psqm_a : p.lay.psqm_s) + l);
@@ -842,7 +846,7 @@ cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s)
 
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s) {
   const int slice = chain_slice_frames(a.lay.T, cluster);
-  const size_t smem = a.staged ? chain_bwd_smem_bytes(slice, a.lay.nb) : 0;
+  const size_t smem = a.staged ? chain_bwd_smem_bytes(slice, a.lay.nb, a.stage_cells != 0) : 0;
   return launch_cluster(chain_bwd_kernel, a, a.batch, cluster, smem, s);
 }
 

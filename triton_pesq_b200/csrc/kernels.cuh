@@ -231,6 +231,7 @@ struct ChainBwdArgs {
   int staged;               // Bark slice and its gradients live in shared memory
   const float* cells;       // the forward's adjoint coefficients (see CellField)
   int64_t cell_stride;
+  int stage_cells;          // (staged) the slice's coefficients are staged too, else read from L2
 };
 
 struct ResampleArgs {
@@ -333,7 +334,7 @@ int chain_active_clusters(int cluster);  // chain clusters of that size the curr
 // staged forward / backward chain kernels for it
 int chain_slice_frames(int T, int cluster);
 size_t chain_fwd_smem_bytes(int slice, int nb, bool cells);
-size_t chain_bwd_smem_bytes(int slice, int nb);
+size_t chain_bwd_smem_bytes(int slice, int nb, bool cells = true);
 size_t chain_smem_limit();
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);

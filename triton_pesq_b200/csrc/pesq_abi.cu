@@ -114,7 +114,7 @@ struct Geometry {
   int T, L, nb;
   int seg, nseg;  // segmentation of a row
   int cluster;
-  bool fwd_staged, fwd_stage_cells, bwd_staged;
+  bool fwd_staged, fwd_stage_cells, bwd_staged, bwd_stage_cells;
   bool resample, grad, general;
   int nfreq;  // spectrum bins saved per frame
   int grad_begin, grad_end;
@@ -186,7 +186,8 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     const int slice = chain_slice_frames(g.T, g.cluster);
     g.fwd_staged = chain_fwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
     g.fwd_stage_cells = chain_fwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
-    g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb) <= chain_smem_limit();
+    g.bwd_stage_cells = chain_bwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
+    g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
   }
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
   g.grad_begin = (flags & PESQ_GRAD_REF) ? 0 : (int)batch;
@@ -587,6 +588,7 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   cb.g_bark = at<float>(ws, g.gbark);
   cb.kappa = at<float>(ws, g.kappa);
   cb.staged = g.bwd_staged;
+  cb.stage_cells = g.bwd_stage_cells;
   cb.cells = at<float>(ws, g.cells);
   cb.cell_stride = g.cell_stride;
   PESQ_CUDA_TRY(launch_chain_bwd(cb, g.cluster, static_cast<cudaStream_t>(stream)), "chain backward kernel");
