@@ -589,6 +589,11 @@ def run_cuda(args):
     world, rank, local = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # libraries print banners (NCCL's version line) on file descriptor 1: send
+    # it to stderr until the JSON line, so that stdout carries that line only
+    sys.stdout.flush()
+    stdout_fd = os.dup(1)
+    os.dup2(2, 1)
     if world > 1:
         import datetime
 
@@ -838,6 +843,9 @@ def run_cuda(args):
     }
     if not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    sys.stdout.flush()
+    os.dup2(stdout_fd, 1)
+    os.close(stdout_fd)
     print(json.dumps(line), flush=True)
 
 
