@@ -43,6 +43,23 @@ def test_half_inputs_match_float32_of_the_same_values(cuda_device, dtype, sample
     assert torch.isfinite(gd_h.float()).all()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n_fft,hop,sample_rate", [(256, 128, 16000), (1024, 400, 44100)])
+def test_half_inputs_with_other_frame_geometries(cuda_device, dtype, n_fft, hop, sample_rate):
+    """The spectrum kernels' path (general n_fft / hop) reads 16-bit rows the
+    same way: bitwise the float32 evaluation of the rounded values."""
+
+    ref = speech_like(2, 2 * sample_rate, sample_rate, seed=65)
+    deg = add_noise(ref, 6.0, seed=66)
+    ref_h, deg_h = ref.to(cuda_device, dtype), deg.to(cuda_device, dtype)
+    model = PesqLossCuda(1.0, sample_rate=sample_rate, n_fft=n_fft, hop_length=hop, win_length=n_fft)
+    loss_h, ds_h, da_h, gr_h, gd_h = _eval(model, ref_h, deg_h)
+    loss_f, ds_f, da_f, gr_f, gd_f = _eval(model, ref_h.float(), deg_h.float())
+    assert torch.equal(loss_h, loss_f)
+    assert torch.equal(ds_h, ds_f) and torch.equal(da_h, da_f)
+    assert torch.equal(gr_h, gr_f.to(dtype)) and torch.equal(gd_h, gd_f.to(dtype))
+
+
 def test_half_inputs_strided_and_graphed(cuda_device):
     ref = speech_like(2, 40000, 16000, seed=63)
     deg = add_noise(ref, 5.0, seed=64)
