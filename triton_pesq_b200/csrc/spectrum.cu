@@ -34,14 +34,14 @@ namespace {
 constexpr int kSmemBudget = 226 * 1024;
 
 // warps per CTA of the generic transform: up to 8, as many frames (n_fft / 2
-// packed complex points each) as fit next to the CTA's twiddle table of
-// n_fft / 2 entries
+// packed complex points each) as fit next to the CTA's two twiddle tables of
+// n_fft / 2 entries (the real split's, and the butterfly stages')
 __host__ __device__ constexpr int gen_warps(int nfft, int elem_bytes) {
-  const int w = (kSmemBudget - (nfft / 2) * elem_bytes) / ((nfft / 2) * elem_bytes);
+  const int w = (kSmemBudget - 2 * (nfft / 2) * elem_bytes) / ((nfft / 2) * elem_bytes);
   return w < 1 ? 1 : (w > kGenThreads / 32 ? kGenThreads / 32 : w);
 }
 __host__ __device__ constexpr size_t gen_smem(int nfft, int elem_bytes) {
-  return (size_t)(gen_warps(nfft, elem_bytes) + 1) * (nfft / 2) * elem_bytes;
+  return (size_t)(gen_warps(nfft, elem_bytes) + 2) * (nfft / 2) * elem_bytes;
 }
 
 // The 512-point path: per warp the transposes' scratch, per CTA the twiddles.
@@ -58,22 +58,21 @@ __device__ __forceinline__ void stage_table(void* dst, const void* src, int byte
 }
 
 // In-place decimation-in-time FFT of M = 2^LOG2M points (input in
-// bit-reversed order, output in natural order) with twiddles
-// exp(-2 pi i k / M) = tw[k << TWS] from a table of a 2^TWS times longer
-// transform.
-template <int LOG2M, int TWS, class R>
-__device__ __forceinline__ void warp_fft(Cx<R>* z, const Cx<R>* tw, int lane) {
+// bit-reversed order, output in natural order).  The twiddles of each
+// butterfly stage lie contiguously, ts[half - 1 + k] = exp(-2 pi i k / (2 half)),
+// k < half, so that the lanes of a stage read consecutive entries (or one).
+template <int LOG2M, class R>
+__device__ __forceinline__ void warp_fft(Cx<R>* z, const Cx<R>* ts, int lane) {
   constexpr int kHalfM = 1 << (LOG2M - 1);
 #pragma unroll
   for (int s = 0; s < LOG2M; ++s) {
     const int half = 1 << s;
-    const int shift = LOG2M - 1 - s + TWS;  // butterfly k of this stage uses exp(-2 pi i k / (2 half))
 #pragma unroll 4
     for (int i = lane; i < kHalfM; i += 32) {
       const int k = i & (half - 1);
       const int j = ((i >> s) << (s + 1)) + k;
       const Cx<R> a = z[j];
-      const Cx<R> b = c_mul(z[j + half], tw[k << shift]);
+      const Cx<R> b = c_mul(z[j + half], ts[half - 1 + k]);
       z[j] = c_add(a, b);
       z[j + half] = c_sub(a, b);
     }
@@ -88,6 +87,19 @@ __device__ __forceinline__ Cx<double> real_bin(Cx<double> zf, Cx<double> zc, Cx<
   const Cx<double> e = c_scale(c_add(zf, zc), 0.5);
   const Cx<double> o = c_scale(c_rot90<-1>(c_sub(zf, zc)), 0.5);
   return c_add(e, c_mul(w, o));
+}
+
+// Stage twiddles of an M = 2^LOG2M point transform from the n_fft = 2M
+// table tw[k] = exp(-2 pi i k / n_fft): ts[half - 1 + k] = tw[k << (LOG2M - s)]
+template <int LOG2M, class R, class Src>
+__device__ __forceinline__ void stage_twiddles(Cx<R>* ts, const Src* tw) {
+  constexpr int kM = 1 << LOG2M;
+  for (int idx = threadIdx.x; idx < kM - 1; idx += blockDim.x) {
+    const int s = 31 - __clz(idx + 1), half = 1 << s;
+    const int k = idx + 1 - half;
+    const Src w = tw[k << (LOG2M - s)];
+    ts[idx] = mk((R)w.x, (R)w.y);
+  }
 }
 
 struct Frame {
@@ -124,12 +136,14 @@ __global__ void __launch_bounds__(kGenThreads) stft_kernel(const __grid_constant
   constexpr int kLog2M = LOG2N - 1, kM = 1 << kLog2M;  // packed complex points = bins
   extern __shared__ __align__(16) double smem_d[];
   Cx<double>* tw = reinterpret_cast<Cx<double>*>(smem_d);  // exp(-2 pi i k / n_fft), k < kM
+  Cx<double>* ts = tw + kM;                                   // the butterfly stages' twiddles
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   stage_table(tw, p.g.tw, kM * 16);
+  stage_twiddles<kLog2M, double>(ts, p.g.tw);
   __syncthreads();
   const Frame fr = frame_of(p, warp);
   if (!fr.valid) return;  // whole warps only: no CTA barrier below
-  Cx<double>* z = tw + kM + (size_t)warp * kM;
+  Cx<double>* z = ts + kM + (size_t)warp * kM;
 
   const double* yr = p.y + (int64_t)fr.row * p.n;
   const int64_t start = (int64_t)fr.t * p.g.hop;
@@ -142,7 +156,7 @@ __global__ void __launch_bounds__(kGenThreads) stft_kernel(const __grid_constant
     z[bit_reverse(k, kLog2M)] = mk(y0 * (double)w.x, y1 * (double)w.y);
   }
   __syncwarp();
-  warp_fft<kLog2M, 1, double>(z, tw, lane);
+  warp_fft<kLog2M, double>(z, ts, lane);
 
   // bins f and kM - f from the same two values (one lane owns both slots):
   // the spectrum, then the power in place of the real part (bin 0 dropped)
@@ -169,16 +183,18 @@ __global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constan
   constexpr int kLog2M = LOG2N - 1, kM = 1 << kLog2M;
   extern __shared__ __align__(16) double smem_d[];
   Cx<float>* tw = reinterpret_cast<Cx<float>*>(smem_d);
+  Cx<float>* ts = tw + kM;  // the butterfly stages' twiddles
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < kM; k += blockDim.x) {
     const double2 w = __ldg(reinterpret_cast<const double2*>(p.g.tw) + k);
     tw[k] = mk((float)w.x, (float)w.y);
   }
+  stage_twiddles<kLog2M, float>(ts, reinterpret_cast<const double2*>(p.g.tw));
   __syncthreads();
   const Frame fr = frame_of(p, warp);
   if (!fr.valid) return;
   const int local = fr.row - p.row_begin;
-  Cx<float>* z = tw + kM + (size_t)warp * kM;
+  Cx<float>* z = ts + kM + (size_t)warp * kM;
 
   // V_f = corr_b dL/dB_b X_f (0 for bin 0 and bins outside every band);
   // the frame gradient g_k = sum_f U_f exp(+2 pi i f k / n_fft) over the
@@ -200,7 +216,7 @@ __global__ void __launch_bounds__(kGenThreads) istft_kernel(const __grid_constan
     z[bit_reverse(f, kLog2M)] = c_conj(c_add(c_add(v, vc), c_rot90<1>(d)));
   }
   __syncwarp();
-  warp_fft<kLog2M, 1, float>(z, tw, lane);
+  warp_fft<kLog2M, float>(z, ts, lane);
   float* out = p.frame_grad + ((int64_t)local * p.frames + fr.t) * (2 * kM);
 #pragma unroll 4
   for (int n = lane; n < kM; n += 32) {
