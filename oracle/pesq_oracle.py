@@ -205,9 +205,16 @@ def _weighted_norm(t: torch.Tensor, w: torch.Tensor, total: float, p: float) -> 
     return total * (w * t / total ** (1 / p))[:, :, 1:].norm(p, dim=2)
 
 
-def chain(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams) -> Tuple[torch.Tensor, torch.Tensor]:
+def chain(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams, census: dict = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Perceptual model from the Bark spectra to both distances,
-    ``loss.py:205-268``."""
+    ``loss.py:205-268``.
+
+    ``census``, when given a dict, receives per utterance the fraction of the
+    values each clamp of the chain acts on (``band_ratio``: bands of the
+    band power ratio outside [0.01, 100]; ``frame_ratio``: frames of the
+    frame power ratio outside [3e-4, 5]; ``symm_45`` / ``asymm_45``: frames
+    whose weighted disturbance exceeds 45) -- the regime of a test input.
+    """
 
     dt = ref.dtype
     thr = torch.as_tensor(p.threshs, dtype=dt)
@@ -220,14 +227,18 @@ def chain(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams) -> Tuple[torch.
     mean_deg = (deg * ((deg > thr * 100.0) * keep)).mean(dim=1)
     mean_ref = (ref * ((ref > thr * 100.0) * keep)).mean(dim=1)
 
-    band_ratio = ((mean_deg + 1000) / (mean_ref + 1000)).unsqueeze(1).clamp(min=0.01, max=100.0)
+    band_ratio = ((mean_deg + 1000) / (mean_ref + 1000)).unsqueeze(1)
+    if census is not None:
+        census["band_ratio"] = ((band_ratio < 0.01) | (band_ratio > 100.0)).double().mean(dim=(1, 2))
+    band_ratio = band_ratio.clamp(min=0.01, max=100.0)
     equ_ref = band_ratio * ref
 
     taer = _total_audible(equ_ref, thr, 1.0)
     frame_ratio = (taer + 5e3) / (_total_audible(deg, thr, 1.0) + 5e3)
-    frame_ratio = torch.cat(
-        [frame_ratio[:, :1], frame_ratio[:, 1:] * 0.8 + frame_ratio[:, :-1] * 0.2], dim=1
-    ).clamp(min=3e-4, max=5.0)
+    frame_ratio = torch.cat([frame_ratio[:, :1], frame_ratio[:, 1:] * 0.8 + frame_ratio[:, :-1] * 0.2], dim=1)
+    if census is not None:
+        census["frame_ratio"] = ((frame_ratio < 3e-4) | (frame_ratio > 5.0)).double().mean(dim=1)
+    frame_ratio = frame_ratio.clamp(min=3e-4, max=5.0)
     equ_deg = frame_ratio.unsqueeze(2) * deg
 
     deg_loud = _loudness(equ_deg, thr, e)
@@ -244,6 +255,9 @@ def chain(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams) -> Tuple[torch.
     asymm = _weighted_norm(dist * asym, w, total, 1).clamp(min=1e-20)
 
     h = ((taer + 1e5) / 1e7) ** 0.04
+    if census is not None:
+        census["symm_45"] = (symm / h > 45.0).double().mean(dim=1)
+        census["asymm_45"] = (asymm / h > 45.0).double().mean(dim=1)
     symm = (symm / h).clamp(max=45.0)
     asymm = (asymm / h).clamp(max=45.0)
 
@@ -255,11 +269,11 @@ def chain(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams) -> Tuple[torch.
     return pool(symm), pool(asymm)
 
 
-def raw(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams, mode: str = "float64"):
+def raw(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams, mode: str = "float64", census: dict = None):
     """Symmetric and asymmetric distance, ``loss.py:172-268``.
 
     ``mode`` is ``"float64"`` (ground truth) or ``"reference"`` (the dtype
-    behaviour of ``PesqLoss`` on float32 input).
+    behaviour of ``PesqLoss`` on float32 input); ``census``: see ``chain``.
     """
 
     if mode == "float64":
@@ -283,7 +297,7 @@ def raw(ref: torch.Tensor, deg: torch.Tensor, p: OracleParams, mode: str = "floa
 
     ref_bark = stft_bark(ref, p, chain_dtype)
     deg_bark = stft_bark(deg, p, chain_dtype)
-    return chain(ref_bark, deg_bark, p)
+    return chain(ref_bark, deg_bark, p, census)
 
 
 def epilogue(d_symm, d_asymm, factor):

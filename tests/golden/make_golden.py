@@ -1,8 +1,9 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-Runs only where the reference checkout is present (it imports ``torch_pesq``
-from ``REFERENCE_ROOT``, default ``/root/reference``); the ``.npz`` files it
-writes are committed so that the tests never need the reference at run time.
+Runs only where the reference checkout is present: it imports ``torch_pesq``
+from the directory named by the ``REFERENCE_ROOT`` environment variable (the
+root of a LarocheC/triton-pesq checkout).  The ``.npz`` files it writes are
+committed so that the tests never need the reference at run time.
 
 Two shims make the reference importable with this image's packages:
 ``torchtyping`` is absent (``TensorType[...]`` is replaced by ``torch.Tensor``)
@@ -22,8 +23,19 @@ Per case the fixture holds the float32 inputs and
 thresholds, exponents, correction, widths, window, filter coefficients and the
 resampling kernels of several rates).
 
-Usage: ``python tests/golden/make_golden.py [case ...]`` from the repository
-root (all cases and the constants when no case is named).
+Signals (all seeded): ``speech`` -- a voiced harmonic stack with a broadband
+term plus white noise, the regime the loss is used in; ``harmonic`` -- the
+harmonic stack alone plus white noise, which pins the asymmetric distance to
+its 45.0 clamp in every frame (the saturated regime the reference's own test
+signals are built to avoid, ``tests/test_triton_loss.py:60-76``);
+``dropout`` -- speech with a 150 ms dropout and a 50 ms burst 18 dB louder in
+the degraded signal, which drives the frame power ratio into both of its
+clamps; ``fir`` -- speech through a seeded random 64-tap low pass FIR
+(4 kHz) plus white noise, the degradation of the 44.1 kHz workload.  ``snr``
+may be one value per row.
+
+Usage: ``REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py [case ...]``
+from the repository root (all cases and the constants when no case is named).
 """
 
 import copy
@@ -35,10 +47,10 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
-
-
 def _import_reference():
+    root = os.environ.get("REFERENCE_ROOT")
+    if not root or not os.path.isdir(os.path.join(root, "torch_pesq")):
+        raise SystemExit("set REFERENCE_ROOT to the root of a LarocheC/triton-pesq checkout")
     shim = types.ModuleType("torchtyping")
 
     class _TensorType:
@@ -50,15 +62,17 @@ def _import_reference():
     import typeguard
 
     typeguard.typechecked = lambda fn: fn
-    sys.path.insert(0, REFERENCE_ROOT)
+    sys.path.insert(0, root)
     from torch_pesq import PesqLoss
     from torch_pesq.triton_ops.reference import ref_pipeline
 
     return PesqLoss, ref_pipeline
 
 
-def speech_pair(batch, n, sr, seed, snr_db):
-    """Seeded speech-like reference and a noisy degraded copy (float32)."""
+def speech_pair(batch, n, sr, seed, snr_db, broadband=True):
+    """Seeded speech-like reference and a noisy degraded copy (float32);
+    ``broadband=False`` leaves out the broadband term (the harmonic stack
+    alone)."""
 
     rng = np.random.default_rng(seed)
     t = np.arange(n) / sr
@@ -71,18 +85,55 @@ def speech_pair(batch, n, sr, seed, snr_db):
             if f0 * k < sr / 2
         )
         sig = sig * 0.5 * (1 + np.sin(2 * np.pi * 4 * t))
-        sig = sig + 0.3 * rng.standard_normal(n) * 0.5 * (1 + np.sin(2 * np.pi * 3 * t))
+        if broadband:
+            sig = sig + 0.3 * rng.standard_normal(n) * 0.5 * (1 + np.sin(2 * np.pi * 3 * t))
         ref[b] = 0.3 * sig / np.abs(sig).max()
-    noise = rng.standard_normal((batch, n))
-    power = (ref**2).mean(axis=1, keepdims=True)
-    deg = ref + noise * np.sqrt(power / 10 ** (snr_db / 10))
-    return ref.astype(np.float32), deg.astype(np.float32)
+    return ref.astype(np.float32), _noisy(ref, rng, snr_db)
+
+
+def _noisy(ref, rng, snr_db):
+    noise = rng.standard_normal(ref.shape)
+    snr = np.broadcast_to(np.asarray(snr_db, np.float64).reshape(-1, 1), (ref.shape[0], 1))
+    power = (ref.astype(np.float64) ** 2).mean(axis=1, keepdims=True)
+    return (ref + noise * np.sqrt(power / 10 ** (snr / 10))).astype(np.float32)
+
+
+def dropout_pair(batch, n, sr, seed, snr_db):
+    """Speech whose degraded copy loses 150 ms (zeros) and carries a 50 ms
+    burst at 8x amplitude."""
+
+    ref, deg = speech_pair(batch, n, sr, seed, snr_db)
+    deg = deg.astype(np.float64)
+    rng = np.random.default_rng(seed + 100)
+    for b in range(batch):
+        a = int(rng.uniform(0.2, 0.4) * n)
+        deg[b, a : a + int(0.15 * sr)] = 0.0
+        c = int(rng.uniform(0.6, 0.8) * n)
+        deg[b, c : c + int(0.05 * sr)] *= 8.0
+    return ref, deg.astype(np.float32)
+
+
+def fir_pair(batch, n, sr, seed, snr_db, taps=64, cutoff=4000.0):
+    """Speech through a seeded random low pass FIR (windowed sinc with
+    +-10 % jitter on the taps), plus white noise."""
+
+    ref, _ = speech_pair(batch, n, sr, seed, snr_db)
+    rng = np.random.default_rng(seed + 200)
+    k = np.arange(taps) - (taps - 1) / 2
+    h = 2 * cutoff / sr * np.sinc(2 * cutoff / sr * k) * np.hanning(taps) * (1 + 0.2 * (rng.uniform(size=taps) - 0.5))
+    h = h / h.sum()
+    low = np.stack([np.convolve(r.astype(np.float64), h)[:n] for r in ref])
+    return ref, _noisy(low, rng, snr_db)
+
+
+SIGNALS = {"speech": speech_pair, "harmonic": lambda *a: speech_pair(*a, broadband=False),
+           "dropout": dropout_pair, "fir": fir_pair}
 
 
 DEFAULT_GEOMETRY = (512, 256, 512)  # n_fft, hop_length, win_length
 
 CASES = [
-    # name, batch, samples, sample_rate, seed, snr_db, factor[, (n_fft, hop_length, win_length)]
+    # name, batch, samples, sample_rate, seed, snr_db, factor[, (n_fft, hop_length, win_length)[, signal]]
     ("sr16k_b2_n6000", 2, 6000, 16000, 1, 10.0, 0.5),
     ("sr16k_b1_n8192", 1, 8192, 16000, 2, 3.0, 1.0),
     ("sr16k_b3_n7001", 3, 7001, 16000, 3, 20.0, 1.0),
@@ -98,6 +149,15 @@ CASES = [
     ("sr16k_fft4096_hop1024_b1_n28000", 1, 28000, 16000, 16, 10.0, 1.0, (4096, 1024, 4096)),
     ("sr16k_fft512_hop600_b1_n16000", 1, 16000, 16000, 17, 10.0, 1.0, (512, 600, 512)),
     ("sr48k_fft256_hop128_b1_n18000", 1, 18000, 48000, 18, 10.0, 1.0, (256, 128, 256)),
+    # the clamps of the perceptual chain: saturated asymmetric distance (45.0
+    # in every frame), the frame power ratio clamped at both ends, and the
+    # degradations of the 44.1 kHz and 48 kHz workloads (a -5 dB row beside a
+    # 25 dB row)
+    ("sr16k_sat_b2_n16000", 2, 16000, 16000, 21, 10.0, 1.0, DEFAULT_GEOMETRY, "harmonic"),
+    ("sr48k_sat_b1_n24000", 1, 24000, 48000, 22, 10.0, 1.0, DEFAULT_GEOMETRY, "harmonic"),
+    ("sr16k_clamp_b2_n16000", 2, 16000, 16000, 23, 15.0, 1.0, DEFAULT_GEOMETRY, "dropout"),
+    ("sr44k_fir_b1_n22050", 1, 22050, 44100, 24, 5.0, 1.0, DEFAULT_GEOMETRY, "fir"),
+    ("sr48k_mix_b2_n24000", 2, 24000, 48000, 25, (-5.0, 25.0), 1.0, DEFAULT_GEOMETRY, "speech"),
 ]
 
 
@@ -110,10 +170,11 @@ def main():
         if only and name not in only:
             continue
         n_fft, hop, win = rest[0] if rest else DEFAULT_GEOMETRY
+        kind = rest[1] if len(rest) > 1 else "speech"
         model = PesqLoss(factor, sample_rate=sr, n_fft=n_fft, hop_length=hop, win_length=win)
-        ref_np, deg_np = speech_pair(batch, n, sr, seed, snr)
+        ref_np, deg_np = SIGNALS[kind](batch, n, sr, seed, snr)
         out = {"ref": ref_np, "deg": deg_np, "factor": np.float64(factor), "sample_rate": np.int64(sr)}
-        if rest:
+        if rest and rest[0] != DEFAULT_GEOMETRY:
             out.update(n_fft=np.int64(n_fft), hop_length=np.int64(hop), win_length=np.int64(win))
 
         ref = torch.from_numpy(ref_np).requires_grad_(True)

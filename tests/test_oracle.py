@@ -93,3 +93,45 @@ def test_oracle_tolerance_is_not_vacuous():
         np.abs(b.numpy() - g.numpy()).max() / np.abs(g.numpy()).max() for g, b in zip(good, bad)
     )
     assert moved > 1e-4
+
+
+SATURATED_CASES = ["sr16k_sat_b2_n16000", "sr48k_sat_b1_n24000"]
+
+
+@pytest.mark.parametrize("name", SATURATED_CASES)
+def test_saturated_fixtures_hit_the_clamp(name):
+    """The saturated fixtures really sit at the 45.0 clamp: the reference's
+    float32 and float64 asymmetric distances are 45.0, and the oracle finds
+    (nearly) every frame clamped -- so comparing them is not comparing two
+    unrelated constants by accident, and it is not vacuous either: the
+    symmetric distance and the gradients still vary."""
+
+    z, p = _load(os.path.join(GOLDEN, name + ".npz"))
+    np.testing.assert_allclose(z["ref32_d_asymm"], 45.0, rtol=1e-6)
+    np.testing.assert_allclose(z["f64_d_asymm"], 45.0, rtol=1e-6)
+    census = {}
+    O.raw(torch.from_numpy(z["ref"]).double(), torch.from_numpy(z["deg"]).double(), p, census=census)
+    assert float(census["asymm_45"].min()) > 0.95
+    assert np.all(z["f64_d_symm"] < 45.0)
+    assert np.abs(z["f64_grad_deg"]).max() > 0
+
+
+def test_clamp_fixture_hits_every_clamp():
+    """The dropout / burst fixture drives the frame power ratio into its
+    [3e-4, 5] clamp, the band power ratio into [0.01, 100] and both weighted
+    disturbances into the 45.0 clamp in some (not all) frames."""
+
+    z, p = _load(os.path.join(GOLDEN, "sr16k_clamp_b2_n16000.npz"))
+    census = {}
+    O.raw(torch.from_numpy(z["ref"]).double(), torch.from_numpy(z["deg"]).double(), p, census=census)
+    for key in ("frame_ratio", "band_ratio", "symm_45", "asymm_45"):
+        assert 0.0 < float(census[key].min()) and float(census[key].max()) < 0.5, key
+
+
+def test_mixed_snr_fixture_regimes():
+    """The 48 kHz -5 dB / 25 dB pair: the -5 dB row clamps far more frames."""
+
+    z, p = _load(os.path.join(GOLDEN, "sr48k_mix_b2_n24000.npz"))
+    census = {}
+    O.raw(torch.from_numpy(z["ref"]).double(), torch.from_numpy(z["deg"]).double(), p, census=census)
+    assert float(census["asymm_45"][0]) > 0.3 > float(census["asymm_45"][1])

@@ -1,0 +1,112 @@
+"""Parity of PesqLossCuda on the benchmark workloads themselves and against
+the reference's own float32 ``PesqLoss``.
+
+* The inputs the benchmark times (``signals.workload``: cfg2 whole, cfg3
+  whole, four rows of cfg4 -- two at -5 dB SNR, where the asymmetric
+  distance runs into its 45.0 clamp, and two at 25 dB -- and a 32-utterance
+  slice of cfg5) against the float64 oracle: 1e-5 relative on the
+  distances, 1e-4 of the peak on both gradients.
+* Every golden fixture against the outputs of the reference's float32
+  ``PesqLoss`` stored in it (``ref32_*``): within the reference's documented
+  float32 ``lfilter`` error -- at most 4e-3 relative on the distances, the
+  loss and the MOS (``README.md:89-92``, ``docs/triton.md:165-168``), and
+  1e-6 where a distance is saturated at the 45.0 clamp
+  (``torch_pesq/loss.py:252-255``); gradients within 1.5e-2 of their peak,
+  the documented backward error of that float32 ``lfilter``
+  (``triton_ops/iir.py:77-82``), or -- where the reference's own float32
+  gradient is further than that from float64 -- no further from it than
+  float64 is.  That happens on the saturated fixtures: their harmonic
+  references have no energy between the partials, and there the reference's
+  float32 gradient w.r.t. the reference signal is 25-35 % of its peak away
+  from the float64 one (0.3-6 % w.r.t. the degraded signal), while this
+  engine stays within 1e-4 of float64 (``test_golden_vectors``).
+"""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden_geometry
+from gpu_helpers import F64_RTOL, GRAD_RTOL, oracle_grads, peak_rel_err, rel_err
+from oracle import pesq_oracle as O
+from triton_pesq_b200 import PesqLossCuda
+from triton_pesq_b200.signals import workload
+
+pytestmark = pytest.mark.gpu
+
+#: the reference's float32 PesqLoss against float64 (documented bounds)
+REF32_RTOL = 4e-3
+REF32_SATURATED_RTOL = 1e-6
+REF32_GRAD_RTOL = 1.5e-2
+SATURATED = 45.0
+
+WORKLOAD_CASES = [
+    ("cfg2", None),
+    ("cfg3", None),
+    ("cfg4", [0, 1, 32, 33]),
+    ("cfg5", list(range(32))),
+]
+
+
+def _both_grads(model, ref, deg):
+    r = ref.detach().clone().requires_grad_(True)
+    d = deg.detach().clone().requires_grad_(True)
+    loss = model(r, d)
+    g_ref, g_deg = torch.autograd.grad(loss.sum(), [r, d])
+    return loss, g_ref, g_deg
+
+
+@pytest.mark.parametrize("name,rows", WORKLOAD_CASES, ids=[c[0] for c in WORKLOAD_CASES])
+def test_benchmark_workloads_match_float64(cuda_device, name, rows):
+    ref, deg, sr = workload(name, seed=0, rows=rows)
+    ds64, da64, gr64, gd64 = oracle_grads(ref, deg, 1.0, sr)
+    model = PesqLossCuda(1.0, sample_rate=sr)
+    ds, da = model.raw(ref.to(cuda_device), deg.to(cuda_device))
+    assert rel_err(ds.cpu(), ds64) < F64_RTOL
+    assert rel_err(da.cpu(), da64) < F64_RTOL
+    _, g_ref, g_deg = _both_grads(model, ref.to(cuda_device), deg.to(cuda_device))
+    assert peak_rel_err(g_ref.cpu(), gr64) < GRAD_RTOL
+    assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL
+    if name == "cfg4":
+        # the -5 dB rows are in the clamp-saturated regime the bench includes:
+        # a good part of their frames sit at the 45.0 clamp, so the check
+        # above covers the clamped frames and not only the free ones
+        census = {}
+        O.raw(ref.double(), deg.double(), O.OracleParams(1.0, sr), census=census)
+        assert float(census["asymm_45"][:2].min()) > 0.2
+        assert float(census["asymm_45"][2:].max()) < float(census["asymm_45"][:2].min())
+
+
+CASES = sorted(glob.glob(os.path.join(GOLDEN, "sr*.npz")))
+
+
+@pytest.mark.parametrize("path", CASES, ids=[os.path.basename(c)[:-4] for c in CASES])
+def test_matches_reference_float32(cuda_device, path):
+    z = np.load(path)
+    factor, sr = float(z["factor"]), int(z["sample_rate"])
+    model = PesqLossCuda(factor, sample_rate=sr, **golden_geometry(z))
+    ref = torch.from_numpy(z["ref"]).to(cuda_device)
+    deg = torch.from_numpy(z["deg"]).to(cuda_device)
+    ds, da = (t.cpu().double().numpy() for t in model.raw(ref, deg))
+    for got, want in ((ds, z["ref32_d_symm"]), (da, z["ref32_d_asymm"])):
+        assert rel_err(got, want) < REF32_RTOL
+        saturated = want >= SATURATED
+        if saturated.any():
+            assert rel_err(got[saturated], want[saturated]) < REF32_SATURATED_RTOL
+    assert rel_err(model.mos(ref, deg).cpu(), z["ref32_mos"]) < REF32_RTOL
+    loss, g_ref, g_deg = _both_grads(model, ref, deg)
+    assert rel_err(loss.detach().cpu(), z["ref32_loss"]) < REF32_RTOL
+    for got, key in ((g_ref, "grad_ref"), (g_deg, "grad_deg")):
+        ref32_err = peak_rel_err(z["ref32_" + key], z["f64_" + key])
+        assert peak_rel_err(got.cpu(), z["ref32_" + key]) < max(REF32_GRAD_RTOL, ref32_err + GRAD_RTOL)
+
+
+def test_saturated_fixtures_are_covered():
+    """The saturated fixtures are among the cases above (the glob would
+    silently drop a renamed file)."""
+
+    names = {os.path.basename(c) for c in CASES}
+    assert {"sr16k_sat_b2_n16000.npz", "sr48k_sat_b1_n24000.npz", "sr16k_clamp_b2_n16000.npz"} <= names
