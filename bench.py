@@ -3,10 +3,14 @@
 
 Workload (the configuration the headline metric is quoted on): batch 8 x 8 s
 at 16 kHz per GPU, speech-like seeded synthetic signals with f0 ~ U[90, 250]
-Hz and SNR ~ U[0, 20] dB, forward + backward w.r.t. the degraded signal,
-CUDA-graph replayed.  With N GPUs every rank runs its own batch (weak
-scaling, batch sharding) and the mean loss is all-reduced over NCCL each
-step, the only collective of the path.
+Hz and SNR ~ U[0, 20] dB, forward + backward w.r.t. the degraded signal of
+the global mean loss, CUDA-graph replayed.  With N GPUs every rank runs its
+own batch (weak scaling, batch sharding) and the global mean loss is
+all-reduced over NCCL inside the captured step, on a side stream that
+overlaps the backward: the only collective of the path.  Beside it the
+north star's scaling configuration (512 x 3 s at 16 kHz as one global batch
+sharded over the N ranks, strong scaling) and the 64 x 10 s at 48 kHz batch
+sharded the same way.
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
 on the launching stream; the L2 is flushed (a 256 MiB write) between steps
@@ -15,13 +19,15 @@ loop is bracketed by a barrier and synchronize; the reported time is the sum
 of the K step times, maximum over ranks.
 
 Also reported: e2e (same metric through the public API, ``PesqLossCuda.graphed``,
-with the inputs copied from pinned host memory and the loss read back every
-step), eager latency, per-stage kernel times, the roofline of the dominant
-kernel and the reference's CPU path (the oracle port, reference dtype mode)
-timed on this host.
+with the inputs copied from pinned host memory and the losses and the
+global mean read back every step), eager latency, per-stage kernel times,
+the roofline of the dominant kernel and the reference's CPU path (its own
+``PesqLoss`` from the offline install in baseline/_ref, with the oracle port
+beside it) timed on this host.
 
-``--impl reference`` times the reference CPU implementation of the path (the
-oracle port in the reference's dtype mode) on this host's cores instead.
+``--impl reference`` times the reference CPU implementation of the path (its
+``PesqLoss``; the oracle port in the reference's dtype mode where the
+reference is not installed) on this host's cores instead.
 """
 
 from __future__ import annotations
@@ -153,9 +159,9 @@ class ClockSampler:
         }
 
 
-def cpu_reference_step(ref, deg, params):
-    """One forward + backward (w.r.t. deg) of the reference CPU path: the
-    oracle port in the reference's dtype mode (float32 signal stages, float64
+def cpu_port_step(ref, deg, params):
+    """One forward + backward (w.r.t. deg) of the oracle port of the reference
+    CPU path in the reference's dtype mode (float32 signal stages, float64
     perceptual chain, as PesqLoss evaluates on the CPU)."""
 
     import torch
@@ -168,7 +174,45 @@ def cpu_reference_step(ref, deg, params):
     return loss, g
 
 
+def reference_cpu_model(sample_rate):
+    """The reference's own ``PesqLoss`` (``torch_pesq/loss.py``) from the
+    offline install in baseline/_ref, or None when it is not installed."""
+
+    try:
+        return _reference_package().PesqLoss(1.0, sample_rate=sample_rate)
+    except ImportError:
+        return None
+
+
+def reference_cpu_step(model, ref, deg):
+    """One forward + backward (w.r.t. deg) through the reference's
+    ``PesqLoss`` on the CPU: its float32 torchaudio signal path and float64
+    perceptual chain (``loss.py:300-322``)."""
+
+    import torch
+
+    d = deg.detach().clone().requires_grad_(True)
+    loss = model(ref, d)
+    (g,) = torch.autograd.grad(loss.sum(), [d])
+    return loss, g
+
+
+def _time_cpu(step, budget_s, min_steps=2):
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= budget_s and steps >= min_steps:
+            return steps, elapsed
+
+
 def cpu_baseline(budget_s: float):
+    """The reference's CPU path on this host's cores, on the whole cfg2 batch
+    (8 x 8 s at 16 kHz, fwd + bwd w.r.t. deg) for about ``budget_s`` seconds:
+    the reference's own ``PesqLoss`` when it is installed (kind "reference"),
+    with the oracle port beside it; the port alone otherwise."""
+
     import torch
 
     from oracle import pesq_oracle as O
@@ -177,24 +221,25 @@ def cpu_baseline(budget_s: float):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ref, deg, sr = workload("cfg2", seed=0)
-    params = O.OracleParams(factor=1.0, sample_rate=sr)
-    cpu_reference_step(ref[:1], deg[:1], params)  # warm-up
-    steps, t0 = 0, time.perf_counter()
-    while True:
-        cpu_reference_step(ref, deg, params)
-        steps += 1
-        elapsed = time.perf_counter() - t0
-        if elapsed >= budget_s and steps >= 2:
-            break
     b, secs = WORKLOADS["cfg2"]
-    utt_s = steps * b * secs
-    return {
-        "value": utt_s / elapsed,
-        "unit": UNIT,
-        "cores": threads,
-        "kind": "port",
+    params = O.OracleParams(factor=1.0, sample_rate=sr)
+    cpu_port_step(ref[:1], deg[:1], params)  # warm-up
+    steps, elapsed = _time_cpu(lambda: cpu_port_step(ref, deg, params), budget_s / 2)
+    port = {
+        "value": steps * b * secs / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
         "sample": f"{steps} x forward+backward(deg) of the full 8 x 8 s @16 kHz batch, {elapsed:.1f} s, "
-                  f"oracle port in the reference dtype mode (float32 signal path, float64 chain)",
+                  "oracle port in the reference dtype mode (float32 signal path, float64 chain)",
+    }
+    model = reference_cpu_model(sr)
+    if model is None:
+        return port
+    reference_cpu_step(model, ref[:1], deg[:1])  # warm-up
+    steps, elapsed = _time_cpu(lambda: reference_cpu_step(model, ref, deg), budget_s)
+    return {
+        "value": steps * b * secs / elapsed, "unit": UNIT, "cores": threads, "kind": "reference",
+        "sample": f"{steps} x forward+backward(deg) of the full 8 x 8 s @16 kHz batch, {elapsed:.1f} s, "
+                  "the reference's PesqLoss (torch_pesq/loss.py) from baseline/_ref",
+        "port": port,
     }
 
 
@@ -204,6 +249,11 @@ def cpu_baseline(budget_s: float):
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path on this host: its own
+    ``PesqLoss`` forward + backward (w.r.t. deg) on the whole headline batch
+    each step, all host threads; the oracle port in the reference's dtype
+    mode when the reference is not installed."""
+
     world, rank, _ = dist_env()
     if rank != 0:
         return
@@ -215,19 +265,31 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ref, deg, sr = workload("cfg2", seed=0)
-    params = O.OracleParams(factor=1.0, sample_rate=sr)
-    # each step is a bounded sample of the workload: 2 of the 8 utterances
-    sample = 2
+    model = reference_cpu_model(sr)
+    if model is not None:
+        kind = "reference"
+        what = "the reference's PesqLoss (torch_pesq/loss.py, offline install in baseline/_ref)"
+
+        def step():
+            reference_cpu_step(model, ref, deg)
+    else:
+        kind = "port"
+        what = ("oracle port of PesqLoss in the reference dtype mode (float32 signal path, float64 chain); "
+                "the reference is not installed in baseline/_ref")
+        params = O.OracleParams(factor=1.0, sample_rate=sr)
+
+        def step():
+            cpu_port_step(ref, deg, params)
+
     for _ in range(args.warmup):
-        cpu_reference_step(ref[:sample], deg[:sample], params)
+        step()
     times = []
-    for k in range(args.steps):
-        lo = (2 * k) % BATCH
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_reference_step(ref[lo:lo + sample], deg[lo:lo + sample], params)
+        step()
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = args.steps * sample * SECONDS / total
+    value = args.steps * BATCH * SECONDS / total
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -242,11 +304,10 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "8x8s@16k fwd+bwd(deg)", "sample_per_step": f"{sample} x 8 s utterances",
-                   "global_batch": BATCH, "seconds": SECONDS, "sample_rate": RATE},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sample} of the 8 utterances per step, oracle port in the reference "
-                                   "dtype mode (float32 signal path, float64 chain)"},
+        "config": {"workload": f"{BATCH}x{SECONDS:g}s@16k fwd+bwd(deg)", "global_batch": BATCH, "seconds": SECONDS,
+                   "sample_rate": RATE, "sample_per_step": f"the whole batch: {BATCH} x {SECONDS:g} s utterances"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"the whole {BATCH} x {SECONDS:g} s batch per step, {what}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -579,11 +640,153 @@ def measure_fused(dev, flush, steps=10):
     return out
 
 
+def numa_local_cores(local: int):
+    """Pin this process to the host cores NVML names as nearest to its GPU,
+    so that the pinned host buffers allocated afterwards land in that NUMA
+    node's memory (first touch) and the host-to-device copies of the ranks of
+    one box do not cross the socket interconnect.  Changes only this
+    process's CPU affinity; returns the cores, or None when NVML cannot say."""
+
+    try:
+        import pynvml
+        import torch
+
+        props = torch.cuda.get_device_properties(local)
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(
+                f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cores = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cores &= os.sched_getaffinity(0)
+        if not cores:
+            return None
+        os.sched_setaffinity(0, cores)
+        return sorted(cores)
+    except Exception:
+        return None
+
+
+def capture_step(model, ref, deg, global_batch: int, group=None):
+    """One data-parallel fwd+bwd step captured in a CUDA graph.
+
+    Forward of this rank's utterances; the global mean loss (this rank's sum
+    and count, all-reduced over NCCL when a process group exists) on a side
+    stream that overlaps the backward; the backward of the global mean w.r.t.
+    the degraded signals.  Returns ``(graph, (loss, grad, mean))``."""
+
+    import torch
+
+    from triton_pesq_b200.distributed import GlobalMean
+
+    dev = ref.device
+    deg_p = deg.detach().clone().requires_grad_(True)
+    mean_op = GlobalMean(dev, group)
+    side = torch.cuda.Stream(dev)
+    # d(global mean)/d(loss_u) = 1 / global batch for every utterance: the
+    # upstream gradient autograd forms for loss.sum() / global_batch, passed
+    # as the broadcast value it is (the engine takes it as one scalar)
+    upstream = torch.full((1,), 1.0 / global_batch, device=dev).expand(ref.shape[0])
+
+    def step():
+        main = torch.cuda.current_stream(dev)
+        loss, loss_sum = model.forward_sum(ref, deg_p)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            mean = mean_op(loss, loss_sum)
+        (g,) = torch.autograd.grad(loss, [deg_p], grad_outputs=upstream)
+        main.wait_stream(side)
+        return loss, g, mean
+
+    warm = torch.cuda.Stream(dev)
+    warm.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(warm):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(warm)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = step()
+    torch.cuda.synchronize()
+    return graph, out
+
+
+def timed_replays(graph, steps: int, warmup: int, flush, world: int, clocks=None):
+    """Replay a captured step ``warmup`` times untimed, then ``steps`` times,
+    each bracketed by CUDA events on the launching stream with the L2 flushed
+    before it (outside the events); barrier + synchronize around the timed
+    loop.  Returns (per-step ms of this rank, total seconds max over ranks,
+    wall seconds of the timed loop)."""
+
+    import torch
+    import torch.distributed as dist
+
+    dev = flush.device
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        flush.zero_()
+        graph.replay()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for k in range(steps):
+        flush.zero_()
+        events[k][0].record(stream)
+        graph.replay()
+        events[k][1].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in events]
+    total = torch.tensor([sum(step_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    return step_ms, float(total.item()) / 1e3, wall
+
+
+def measure_sharded(name: str, global_batch: int, steps: int, warmup: int, flush, world: int, rank: int):
+    """A BASELINE configuration with a fixed global batch sharded over the
+    ranks (strong scaling): rank r evaluates its contiguous slice of the
+    utterances, the step (fwd+bwd of the global mean, its all-reduce inside)
+    is graph-replayed; time = max over ranks of the summed step times."""
+
+    import torch
+
+    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.distributed import shard_bounds
+    from triton_pesq_b200.signals import WORKLOADS, workload
+
+    dev = flush.device
+    lo, hi = shard_bounds(global_batch, rank, world)
+    ref_c, deg_c, sr = workload(name, seed=0, rows=range(lo, hi))
+    model = PesqLossCuda(1.0, sample_rate=sr)
+    graph, _ = capture_step(model, ref_c.to(dev), deg_c.to(dev), global_batch)
+    step_ms, total_s, _ = timed_replays(graph, steps, warmup, flush, world)
+    del graph
+    seconds = WORKLOADS[name][1] / sr
+    return {
+        "global_batch": global_batch, "per_rank_batch": hi - lo, "seconds": seconds, "sample_rate": sr,
+        "scaling": "strong", "steps": steps,
+        "ms_per_step": 1e3 * total_s / steps,
+        "utterance_seconds_per_s": global_batch * seconds * steps / total_s,
+        "step": "graph replay of fwd + bwd(deg) of the global mean loss, NCCL all-reduce of [sum, count] "
+                "on a side stream overlapping the backward (none at N = 1)",
+    }
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
 
     from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200.distributed import GlobalMean
     from triton_pesq_b200.signals import workload
 
     world, rank, local = dist_env()
@@ -594,6 +797,7 @@ def run_cuda(args):
     sys.stdout.flush()
     stdout_fd = os.dup(1)
     os.dup2(2, 1)
+    cores = numa_local_cores(local) if world > 1 else None
     if world > 1:
         import datetime
 
@@ -604,81 +808,46 @@ def run_cuda(args):
     ref = ref_cpu.to(dev)
     deg = deg_cpu.to(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    global_batch = BATCH * world
 
-    # ---- graph-replayed forward + backward (the headline value)
-    deg_p = deg.detach().clone().requires_grad_(True)
-
-    def step():
-        loss = model(ref, deg_p)
-        (g,) = torch.autograd.grad(loss.sum(), [deg_p])
-        return loss, g
-
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for _ in range(3):
-            step()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        loss_g, grad_g = step()
-    torch.cuda.synchronize()
-
-    # utterances are independent: every rank replays its own shard and no data
-    # crosses ranks inside a step (the ranks meet only at the barriers around
-    # the timed region and in the max-over-ranks of the timings)
-    def replay():
-        graph.replay()
-
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        replay()
-        flush.zero_()
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    wall0 = time.perf_counter()
+    # ---- graph-replayed forward + backward (the headline value): each rank
+    # evaluates its own utterances; the global mean loss is all-reduced over
+    # NCCL inside the step, overlapping the backward
+    graph, (loss_g, grad_g, mean_g) = capture_step(model, ref, deg, global_batch)
     with ClockSampler(local) as clocks:
-        for k in range(args.steps):
-            flush.zero_()
-            events[k][0].record(stream)
-            replay()
-            events[k][1].record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - wall0
-    step_ms = [a.elapsed_time(b) for a, b in events]
-    total_ms = torch.tensor([sum(step_ms)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
-    total_s = float(total_ms.item()) / 1e3
+        step_ms, total_s, wall = timed_replays(graph, args.steps, args.warmup, flush, world)
     utt_per_step = BATCH * SECONDS * world
     value = utt_per_step * args.steps / total_s
+    # the all-reduced mean agrees with the losses of every rank
+    check = torch.stack([loss_g.detach().double().sum(), torch.tensor(float(BATCH), device=dev, dtype=torch.float64)])
+    if world > 1:
+        dist.all_reduce(check)
+    mean_ok = bool(torch.isclose(mean_g, check[0] / check[1], rtol=1e-12, atol=0).item())
 
     # ---- eager latency (host dispatch included)
+    deg_e = deg.detach().clone().requires_grad_(True)
     eager = []
     for k in range(max(5, args.steps // 5)):
         flush.zero_()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        step()
+        out = model(ref, deg_e)
+        torch.autograd.grad(out.sum(), [deg_e])
         torch.cuda.synchronize()
         eager.append(time.perf_counter() - t0)
 
     # ---- end to end through the public API with host buffers
     # Every step copies its inputs from pinned host memory and reads its loss
-    # back.  The loop is double buffered as a training input pipeline is: the
-    # copy of step k + 1 (on a copy stream, into the second of two graphed
-    # input sets) overlaps the compute of step k; a set is overwritten only
-    # after the step that used it has finished.  The serial variant (copy,
-    # compute, read back, wait) is reported beside it.
+    # (and the global mean) back.  The loop is double buffered as a training
+    # input pipeline is: the copy of step k + 1 (on a copy stream, into the
+    # second of two graphed input sets) overlaps the compute of step k; a set
+    # is overwritten only after the step that used it has finished.  The
+    # serial variant (copy, compute, read back, wait) is reported beside it.
+    # With several ranks per box each process first moves to the cores of its
+    # GPU's NUMA node (numa_local_cores), so that its pinned buffers are local.
     ref_h = ref_cpu.pin_memory()
     deg_h = deg_cpu.pin_memory()
-    loss_h = [torch.empty(BATCH, pin_memory=True) for _ in range(2)]
+    loss_h = [torch.empty(BATCH + 1, dtype=torch.float64, pin_memory=True) for _ in range(2)]
     # (graphed() rebinds the module's forward, as PesqLossTriton.graphed does,
     # so each input set gets its own module instance)
     sets = []
@@ -688,20 +857,24 @@ def run_cuda(args):
         with torch.no_grad():
             ref_d.copy_(ref)
             deg_d.copy_(deg)
-        sets.append((ref_d, deg_d, PesqLossCuda(1.0, sample_rate=RATE).graphed(ref_d, deg_d)))
+        sets.append((ref_d, deg_d, PesqLossCuda(1.0, sample_rate=RATE).graphed(ref_d, deg_d),
+                     torch.empty(BATCH + 1, dtype=torch.float64, device=dev)))
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    mean_op = GlobalMean(dev)
+    upstream = torch.full((1,), 1.0 / global_batch, device=dev).expand(BATCH)
     # the reference and the degraded signal are copied on two copy streams
     # (two DMA engines in flight) when `split`, else one after the other
     copy_streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
-    copy_stream = copy_streams[0]
     copied = [[torch.cuda.Event(), torch.cuda.Event()] for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     split = [True]
 
     def issue_copy(k):
-        ref_d, deg_d, _ = sets[k % 2]
+        ref_d, deg_d, _, _ = sets[k % 2]
         pairs = ((ref_d, ref_h), (deg_d, deg_h))
         for i, (dst, src) in enumerate(pairs):
-            cs = copy_streams[i] if split[0] else copy_stream
+            cs = copy_streams[i] if split[0] else copy_streams[0]
             with torch.cuda.stream(cs):
                 cs.wait_event(consumed[k % 2])
                 with torch.no_grad():
@@ -709,13 +882,20 @@ def run_cuda(args):
                 copied[k % 2][i].record(cs)
 
     def run_step(k):
-        ref_d, deg_d, graphed = sets[k % 2]
+        ref_d, deg_d, graphed, result = sets[k % 2]
         stream.wait_event(copied[k % 2][0])
         stream.wait_event(copied[k % 2][1])
         out = graphed(ref_d, deg_d)
-        torch.autograd.grad(out.sum(), [deg_d])
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            mean = mean_op(out)
+        torch.autograd.grad(out, [deg_d], grad_outputs=upstream)
         consumed[k % 2].record(stream)
-        loss_h[k % 2].copy_(out.detach(), non_blocking=True)
+        stream.wait_stream(side)
+        with torch.no_grad():
+            result[:BATCH].copy_(out.detach())
+            result[BATCH:].copy_(mean.reshape(1))
+        loss_h[k % 2].copy_(result, non_blocking=True)
 
     def pipelined(n):
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -731,33 +911,64 @@ def run_cuda(args):
         stop.synchronize()
         return start.elapsed_time(stop)
 
+    if world > 1:
+        dist.barrier()
     split[0] = False
     pipelined(4)  # warm-up
     torch.cuda.synchronize()
-    one_stream_ms = pipelined(args.steps) / args.steps
+    one_stream = torch.tensor([pipelined(args.steps)], device=dev, dtype=torch.float64)
     split[0] = True
     pipelined(4)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     e2e_total = torch.tensor([pipelined(args.steps)], device=dev, dtype=torch.float64)
+
+    # host-to-device copy rate of this rank alone (the inputs of one step)
+    h2d = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        with torch.no_grad():
+            sets[0][0].copy_(ref_h, non_blocking=True)
+            sets[0][1].copy_(deg_h, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        h2d.append(a.elapsed_time(b))
+    h2d_gbs = 2 * ref.numel() * 4 / (statistics.median(h2d) * 1e-3) / 1e9
 
     serial_ms = []
     for k in range(max(5, args.steps // 5)):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ref_d, deg_d, graphed = sets[0]
+        ref_d, deg_d, graphed, result = sets[0]
         a.record(stream)
         with torch.no_grad():
             ref_d.copy_(ref_h, non_blocking=True)
             deg_d.copy_(deg_h, non_blocking=True)
         out = graphed(ref_d, deg_d)
-        torch.autograd.grad(out.sum(), [deg_d])
-        loss_h[0].copy_(out.detach(), non_blocking=True)
+        mean = mean_op(out)
+        torch.autograd.grad(out, [deg_d], grad_outputs=upstream)
+        with torch.no_grad():
+            result[:BATCH].copy_(out.detach())
+            result[BATCH:].copy_(mean.reshape(1))
+        loss_h[0].copy_(result, non_blocking=True)
         b.record(stream)
         b.synchronize()
         serial_ms.append(a.elapsed_time(b))
     if world > 1:
         dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+        dist.all_reduce(one_stream, op=dist.ReduceOp.MAX)
     e2e_ms_total = float(e2e_total.item())
     e2e_value = utt_per_step * args.steps / (e2e_ms_total / 1e3)
+    one_stream_ms = float(one_stream.item()) / args.steps
+
+    # ---- the north star's scaling configuration: 512 x 3 s at 16 kHz as one
+    # global batch sharded over the ranks, and the 64 x 10 s at 48 kHz batch
+    # (half of it at -5 dB SNR) sharded the same way
+    sharded = {}
+    if not args.skip_configs:
+        sharded["cfg5_scaling"] = measure_sharded("cfg5", 512, min(args.steps, 20), args.warmup, flush, world, rank)
+        sharded["cfg4_sharded"] = measure_sharded("cfg4", 64, min(args.steps, 10), args.warmup, flush, world, rank)
 
     # ---- stage kernels alone, roofline of the dominant one
     stages = stage_times(model, ref, deg, dev)
@@ -771,13 +982,14 @@ def run_cuda(args):
     front_us = stages["front"]
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
-    ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)}
-    configs = measure_configs(dev, flush) if not args.skip_configs else None
-    fused = measure_fused(dev, flush) if not args.skip_configs else None
-    geometries = measure_geometries(dev, flush) if not args.skip_configs else None
+    single = world == 1 and not args.skip_configs
+    ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)} if world == 1 else None
+    configs = measure_configs(dev, flush) if single else None
+    fused = measure_fused(dev, flush) if single else None
+    geometries = measure_geometries(dev, flush) if single else None
 
     if world > 1:
-        graph.reset()
+        del graph
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -796,11 +1008,14 @@ def run_cuda(args):
         "dtype": "f32",
         "data": "synthetic",
         "config": {
-            "workload": f"{BATCH}x{SECONDS:g}s@16k fwd+bwd(deg), CUDA-graph replay ({args.workload})",
-            "global_batch": BATCH * world,
+            "workload": f"{BATCH}x{SECONDS:g}s@16k fwd+bwd(deg) of the global mean loss, CUDA-graph replay "
+                        f"({args.workload})",
+            "global_batch": global_batch,
             "seconds": SECONDS,
             "sample_rate": RATE,
             "parallelism": f"dp{world}",
+            "collective": "NCCL all-reduce of the [sum, count] of the losses inside the captured step, on a side "
+                          "stream overlapping the backward" if world > 1 else "none (one rank)",
             "l2": "flushed between steps (256 MiB write, outside the step events)",
         },
         "clocks": clocks.summary(),
@@ -808,16 +1023,19 @@ def run_cuda(args):
             "value": e2e_value,
             "unit": UNIT,
             "h2d_bytes_per_step": int(ref.numel() * 4 * 2),
-            "d2h_bytes_per_step": int(BATCH * 4),
+            "d2h_bytes_per_step": int((BATCH + 1) * 8),
             "api": "PesqLossCuda.graphed (two instances, one per input set), inputs copied from pinned host memory "
                    "every step (reference and degraded signal on two copy streams) overlapping the previous "
-                   "step's compute, loss read back every step",
+                   "step's compute, global mean all-reduced, losses and mean read back every step",
             "ms_per_step": e2e_ms_total / args.steps,
             "one_copy_stream_ms_per_step": one_stream_ms,
             "serial_ms_per_step": statistics.median(serial_ms),
+            "h2d_gbs_alone": h2d_gbs,
+            "numa_local_cores": f"{len(cores)} cores" if cores else None,
         },
         # front + chain forward, chain adjoint + align + back per step
         "gpu_launches": 5 * args.steps,
+        "mean_allreduce_ok": mean_ok,
         "roofline": {
             "bound": "hbm",
             "kernel": "front",
@@ -831,6 +1049,7 @@ def run_cuda(args):
             "launch_us": front_us,
         },
         "stages_us": stages,
+        **sharded,
         "ops": ops,
         "other_configs": configs,
         "in_training_step": fused,
@@ -852,8 +1071,8 @@ def run_cuda(args):
 REFERENCE_INSTALL = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
 
 
-def _import_reference_gpu():
-    """``PesqLossTriton`` of the reference installed in baseline/_ref by
+def _reference_package():
+    """The reference package ``torch_pesq`` installed in baseline/_ref by
     ``pip install --no-index --no-deps --target baseline/_ref <reference>``.
     Two import shims, neither of which changes a computation: ``torchtyping``
     is absent (``TensorType[...]`` becomes ``torch.Tensor``) and the installed
@@ -877,10 +1096,17 @@ def _import_reference_gpu():
     import typeguard
 
     typeguard.typechecked = lambda fn: fn
-    sys.path.insert(0, REFERENCE_INSTALL)
-    from torch_pesq import PesqLossTriton
+    if REFERENCE_INSTALL not in sys.path:
+        sys.path.insert(0, REFERENCE_INSTALL)
+    import torch_pesq
 
-    return PesqLossTriton
+    return torch_pesq
+
+
+def _import_reference_gpu():
+    """``PesqLossTriton`` of the reference installed in baseline/_ref."""
+
+    return _reference_package().PesqLossTriton
 
 
 def measure_triton_reference(dev, flush, steps):

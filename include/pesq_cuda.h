@@ -145,6 +145,17 @@ int pesq_forward(const pesq_plan* plan, void* stream, const void* ref, int64_t l
                  int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* workspace,
                  size_t workspace_bytes, float* d_symm, float* d_asymm, float* mos, float* loss);
 
+/* Byte offset in the workspace of two doubles that pesq_forward leaves there:
+ * the sum over the batch of the losses (factor * (0.1 d_symm + 0.0309
+ * d_asymm), whether or not `loss` was requested) and the batch size, summed in
+ * a fixed order by the last utterance's cluster of the chain forward (the
+ * numerator and denominator of the global mean a data-parallel caller
+ * all-reduces; there is no collective in the reference, whose callers take
+ * loss.mean() of the [batch] loss, triton_ops/loss.py:210-215).  Valid after
+ * a pesq_forward (or pesq_forward_front followed by one pesq_forward_chain)
+ * with batch >= 1, until the workspace is reused. */
+int pesq_loss_sum_offset(const pesq_plan* plan, int64_t batch, int64_t n_src, uint32_t flags, size_t* offset);
+
 /* Backward of the preceding pesq_forward with the same inputs, flags and
  * workspace.  Upstream gradients g_loss / g_mos / g_dsymm / g_dasymm ([batch],
  * any may be NULL = zero) are summed.  Writes dL/dref into g_ref (row stride
@@ -202,8 +213,11 @@ int pesq_backward_back(const pesq_plan* plan, void* stream, int64_t batch, int64
  * device this entry point has been used on; the first call on a device looks
  * up that array and should come before any stream capture; calls sharing a
  * device must not overlap on the GPU (they share the array).  Batches needing
- * more than 16 MiB of scratch get PESQ_ERR_WORKSPACE.  This entry point has
- * no counterpart in the reference. */
+ * more than 16 MiB of scratch get PESQ_ERR_WORKSPACE.  The array's address
+ * is cached per device for the runtime's primary context: do not call this
+ * after cudaDeviceReset in the same process, nor with a context of your own
+ * (driver API) current.  This entry point has no counterpart in the
+ * reference. */
 int pesq_forward_noalloc(const pesq_plan* plan, void* stream, const float* ref, int64_t ld_ref, const float* deg,
                          int64_t ld_deg, int64_t batch, int64_t n_src, float* d_symm, float* d_asymm, float* mos,
                          float* loss);

@@ -231,7 +231,7 @@ def test_upstream_gradients(cuda_device):
     ds, da = model.raw(ref, deg.detach())
     m = 4.5 - 0.1 * ds - 0.0309 * da
     dmos_dloss = -4 * 1.3669 * torch.exp(-1.3669 * m + 3.8224) / (1 + torch.exp(-1.3669 * m + 3.8224)) ** 2 / 0.5
-    _, _, mos, loss = model._evaluate(ref, deg)  # one call, two differentiated outputs
+    _, _, mos, loss, _ = model._evaluate(ref, deg)  # one call, two differentiated outputs
     (g_both,) = torch.autograd.grad((mos + loss).sum(), [deg])
     want = g_arr * (1.0 + dmos_dloss)[:, None]
     torch.testing.assert_close(g_both, want, rtol=1e-4, atol=1e-4 * float(want.abs().max()))
@@ -263,3 +263,61 @@ def test_long_signal(cuda_device, sample_rate, seconds):
     assert rel_err(da.cpu(), da64) < F64_RTOL
     _, (g_deg,) = _grads(model, ref.to(cuda_device), deg.to(cuda_device), (False, True))
     assert peak_rel_err(g_deg.cpu(), gd64) < GRAD_RTOL
+
+
+def test_batch_beyond_grid_y(cuda_device):
+    """33000 utterance pairs (66000 rows, more than a grid dimension y
+    holds) at 8 kHz through the resampler: rows on either side of the 65535
+    boundary get exactly what they get in a batch of their own (the
+    reference folds the batch onto grid x for the same reason,
+    triton_ops/resample.py:40-47)."""
+
+    batch, n = 33000, 2700
+    gen = torch.Generator(device=cuda_device).manual_seed(91)
+    ref = torch.randn(batch, n, device=cuda_device, generator=gen)
+    deg = (ref + 0.3 * torch.randn(batch, n, device=cuda_device, generator=gen)).requires_grad_(True)
+    model = PesqLossCuda(1.0, sample_rate=8000)
+    loss = model(ref, deg)
+    (g,) = torch.autograd.grad(loss.sum(), [deg])
+    for rows in ([0, 1], [32766, 32767, 32768], [batch - 2, batch - 1]):
+        r, d = ref[rows], deg.detach()[rows].clone().requires_grad_(True)
+        alone = model(r, d)
+        (g_alone,) = torch.autograd.grad(alone.sum(), [d])
+        assert torch.equal(alone, loss[rows])
+        assert torch.equal(g_alone, g[rows])
+
+
+@pytest.mark.parametrize("batch", [1, 5, 40])
+def test_loss_sum_of_the_chain_kernel(cuda_device, batch):
+    """forward_sum's [sum, count] pair (summed by the chain forward's last
+    cluster, in a fixed order) against the losses it returns; bitwise the
+    same on a repeat call, and inside a CUDA graph replay."""
+
+    ref = speech_like(batch, 8000, 16000, seed=95 + batch).to(cuda_device)
+    deg = add_noise(ref.cpu(), 7.0, seed=96).to(cuda_device)
+    model = PesqLossCuda(0.5, sample_rate=16000)
+    loss, pair = model.forward_sum(ref, deg)
+    assert pair.dtype == torch.float64 and pair.shape == (2,)
+    assert float(pair[1]) == batch
+    assert float(pair[0]) == pytest.approx(float(loss.double().sum()), rel=1e-12)
+    loss2, pair2 = model.forward_sum(ref, deg)
+    assert torch.equal(pair2, pair) and torch.equal(loss2, loss)
+    d = deg.clone().requires_grad_(True)
+    static = {}
+
+    def step():
+        out, s = model.forward_sum(ref, d)
+        static["pair"] = s
+        return out
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(static["pair"], pair)

@@ -136,6 +136,10 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_size_t)],
     ),
+    "pesq_loss_sum_offset": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_uint32, ctypes.POINTER(ctypes.c_size_t)],
+    ),
     "pesq_forward": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
@@ -242,7 +246,65 @@ def load_ops() -> None:
             import torch
 
             torch.ops.load_library(OPS_PATH)
+            _register_fakes()
             _ops_loaded = True
+
+
+def _register_fakes() -> None:
+    """Shape functions of the ``torch.ops.pesq_cuda`` ops for tracing
+    (``torch.compile``, ``torch.export``, fake tensors): every output shape
+    follows from the input shapes and the plan, through the same host
+    functions of the C ABI that size the real outputs."""
+
+    import torch
+
+    def workspace_floats(plan, batch, n, flags):
+        nbytes = ctypes.c_size_t()
+        check(library().pesq_workspace_size(ctypes.c_void_p(plan), int(batch), int(n), int(flags),
+                                            ctypes.byref(nbytes)), "pesq_workspace_size")
+        return (nbytes.value + 3) // 4
+
+    def input_flag(ref):
+        return INPUT_BF16 if ref.dtype == torch.bfloat16 else INPUT_F16 if ref.dtype == torch.float16 else 0
+
+    @torch.library.register_fake("pesq_cuda::forward")
+    def _forward(plan, ref, deg, flags):
+        torch._check(ref.dim() == 2 and ref.shape == deg.shape, lambda: "ref and deg must be [batch, sample]")
+        batch, n = ref.shape
+        outs = [ref.new_empty((batch,), dtype=torch.float32) for _ in range(4)]
+        ws = ref.new_empty((workspace_floats(plan, batch, n, flags | input_flag(ref)),), dtype=torch.float32)
+        return (*outs, ws)
+
+    @torch.library.register_fake("pesq_cuda::backward")
+    def _backward(plan, ref, deg, flags, workspace, g_loss, g_mos, g_dsymm, g_dasymm):
+        batch, n = ref.shape
+        g_ref = ref.new_empty((batch, n)) if flags & GRAD_REF else ref.new_empty((0,))
+        g_deg = deg.new_empty((batch, n)) if flags & GRAD_DEG else deg.new_empty((0,))
+        return g_ref, g_deg
+
+    @torch.library.register_fake("pesq_cuda::resample")
+    def _resample(resampler, waveform):
+        n_out = ctypes.c_int64()
+        check(library().pesq_resampler_length(ctypes.c_void_p(resampler), int(waveform.shape[1]),
+                                              ctypes.byref(n_out)), "pesq_resampler_length")
+        return waveform.new_empty((waveform.shape[0], n_out.value))
+
+    @torch.library.register_fake("pesq_cuda::resample_adjoint")
+    def _resample_adjoint(resampler, grad, n_in):
+        return grad.new_empty((grad.shape[0], n_in))
+
+    @torch.library.register_fake("pesq_cuda::iir")
+    def _iir(filt, signal, flags):
+        return signal.new_empty(signal.shape)
+
+
+def loss_sum_offset(handle: int, batch: int, n: int, flags: int) -> int:
+    """Byte offset of the [loss sum, batch] float64 pair in a call's workspace."""
+
+    off = ctypes.c_size_t()
+    check(library().pesq_loss_sum_offset(ctypes.c_void_p(handle), int(batch), int(n), int(flags),
+                                         ctypes.byref(off)), "pesq_loss_sum_offset")
+    return int(off.value)
 
 
 def last_error() -> str:

@@ -476,11 +476,32 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   }
   if (q == 0) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
-      const float m = 4.5f - 0.1f * ds - 0.0309f * da;
-      if (p.mos) p.mos[u] = 0.999f + 4.0f / (1.0f + expf(-1.3669f * m + 3.8224f));
-      if (p.loss) p.loss[u] = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
+    if (warp == 0) {
+      uint32_t last = 0;
+      if (lane == 0) {
+        const float ds = sv[p.lay.scal + kDSymm], da = sv[p.lay.scal + kDAsymm];
+        const float m = 4.5f - 0.1f * ds - 0.0309f * da;
+        const float loss = (float)(p.factor * (0.1 * (double)ds + 0.0309 * (double)da));
+        if (p.mos) p.mos[u] = 0.999f + 4.0f / (1.0f + expf(-1.3669f * m + 3.8224f));
+        if (p.loss) p.loss[u] = loss;
+        sv[p.lay.scal + kLoss] = loss;
+        // batch sum of the losses (the global mean of a data-parallel step
+        // reduces it over the ranks): the cluster that arrives last adds the
+        // batch up, in a fixed order whichever cluster that is
+        __threadfence();
+        last = atomicAdd(p.done, 1u) == (uint32_t)(B - 1) ? 1u : 0u;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        double acc = 0.0;
+        for (int i = lane; i < B; i += 32) acc += (double)__ldcg(p.saved + (int64_t)i * p.lay.stride + p.lay.scal + kLoss);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+          p.loss_sum[0] = acc;
+          p.loss_sum[1] = (double)B;
+        }
+      }
     }
   }
   if (cst && threadIdx.x == 0) bulk_wait_all();

@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_CTA_BEGIN(g_cta_front);
   PESQ_STAMP(g_phase_front, 0);
 
+  // the chain forward that follows on the stream counts its clusters here
+  if (blockIdx.x == 0 && tid == 0) *p.done = 0u;
   // constant tables, copied in the background of the span staging
   copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
   copy_async<kThreads>(tw, p.tw64, (int)sizeof(DevTwiddle64));

@@ -95,6 +95,7 @@ struct FrontArgs {
   Cx<float>* spec;   // [rows][T][256]  rfft bins 0..255 of every frame
   float* fpow;       // [rows][n]       f = H x, written for the rows that save the spectrum
   uint32_t* err;
+  uint32_t* done;    // arrival counter of the chain forward's batch sum, zeroed here
   // general frame geometry (n_fft / hop other than 512 / 256): the kernel
   // writes the pre-emphasised rows y here instead of evaluating the frames
   double* y64;       // [rows][n], or nullptr
@@ -172,7 +173,7 @@ struct ChainLayout {
   static ChainLayout make(int T, int nb);
 };
 
-enum ChainScalar { kS2Ref = 0, kS2Deg, kDSymm, kDAsymm, kNumScalars = 8 };
+enum ChainScalar { kS2Ref = 0, kS2Deg, kDSymm, kDAsymm, kLoss, kNumScalars = 8 };
 
 struct ChainFwdArgs {
   int batch;
@@ -189,6 +190,10 @@ struct ChainFwdArgs {
   float* d_asymm;
   float* mos;
   float* loss;
+  // [sum of the batch's losses, batch] (float64), written by the cluster that
+  // finishes last, which `done` (zeroed by the front kernel) identifies
+  double* loss_sum;
+  uint32_t* done;
   int staged;               // Bark slice staged in shared memory
   // per (frame, band) adjoint coefficients for the backward (nullable: no
   // gradient requested), see CellField and cell_block

@@ -15,6 +15,12 @@
 //     loading that happens on the first call of this entry point on the device;
 //   * the first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress; make that first call before any stream capture;
+//   * that address is cached per device ordinal for the primary context, the
+//     one the CUDA runtime uses: after cudaDeviceReset (which tears down that
+//     context, this module and its array with it) the cached address is
+//     stale, and a context created through the driver API has an array of its
+//     own at another address -- do not call this entry point after a device
+//     reset in the same process, nor with a non-primary context current;
 //   * all calls on a device share the one array, which keeps the contents of
 //     the last call: calls whose GPU work overlaps (different streams, or
 //     concurrent host threads without ordering) race on it and must be
@@ -69,8 +75,16 @@ extern "C" int pesq_forward_noalloc(const pesq_plan* plan, void* stream, const f
                                     const float* deg, int64_t ld_deg, int64_t batch, int64_t n_src, float* d_symm,
                                     float* d_asymm, float* mos, float* loss) {
   if (!plan) return pesq::set_error(PESQ_ERR_INVALID_ARGUMENT, "pesq_forward_noalloc: NULL plan");
+  // the plan's device must be current (as pesq_forward requires) before the
+  // scratch lookup, which would otherwise load this module on another device
+  int plan_dev = -1, cur_dev = -1;
+  int rc = pesq_plan_device(plan, &plan_dev);
+  if (rc) return rc;
+  if (cudaGetDevice(&cur_dev) != cudaSuccess || cur_dev != plan_dev)
+    return pesq::set_error(PESQ_ERR_INVALID_ARGUMENT,
+                           "pesq_forward_noalloc: the plan was created on another device than the current one");
   size_t need = 0;
-  int rc = pesq_workspace_size(plan, batch, n_src, 0u, &need);
+  rc = pesq_workspace_size(plan, batch, n_src, 0u, &need);
   if (rc) return rc;
   if (need > kNoAllocScratchBytes)
     return pesq::set_error(PESQ_ERR_WORKSPACE,

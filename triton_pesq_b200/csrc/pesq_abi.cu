@@ -120,7 +120,7 @@ struct Geometry {
   int grad_begin, grad_end;
   ChainLayout lay;
   // byte offsets
-  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, y64, fgrad, err,
+  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, y64, fgrad, err, lsum,
       total;
   int64_t cell_stride;  // floats between the fields of the chain's adjoint coefficients
 };
@@ -155,7 +155,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     return fail(PESQ_ERR_INVALID_ARGUMENT,
                 "The PESQ chain needs at least 20 frames for the overlapping sums, got %d (%lld samples at 16 kHz).",
                 g.T, (long long)g.n16);
-  if (g.n16 > (int64_t)1 << 31 || g.rows > 65535)
+  if (g.n16 > (int64_t)1 << 31 || g.rows > INT32_MAX)
     return fail(PESQ_ERR_INVALID_ARGUMENT, "signal or batch too large (%lld samples, %lld rows)",
                 (long long)g.n16, (long long)g.rows);
   if ((int64_t)g.T * p->nfft > (int64_t)1 << 33)
@@ -189,6 +189,11 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     g.bwd_stage_cells = chain_bwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
     g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
   }
+  // every kernel folds rows x segments (or utterances x cluster CTAs) onto
+  // grid x; the resampler launches at most 65535 rows at a time in grid y
+  if (g.rows * g.nseg > INT32_MAX || g.batch * g.cluster > INT32_MAX)
+    return fail(PESQ_ERR_INVALID_ARGUMENT, "batch too large for one call (%lld rows of %d segments)",
+                (long long)g.rows, g.nseg);
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
   g.grad_begin = (flags & PESQ_GRAD_REF) ? 0 : (int)batch;
   g.grad_end = (flags & PESQ_GRAD_DEG) ? (int)g.rows : (int)batch;
@@ -219,6 +224,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.y64 = take(g.general ? rows * g.n16 * 8 : 0);
   g.fgrad = take(g.grad && g.general ? (size_t)(g.grad_end - g.grad_begin) * g.T * p->nfft * 4 : 0);
   g.err = take(16);
+  g.lsum = take(32);  // double[2] batch loss sum and count, uint32 arrival counter at +16
   g.total = o;
   return PESQ_OK;
 }
@@ -448,6 +454,15 @@ int pesq_workspace_size(const pesq_plan* p, int64_t batch, int64_t n_src, uint32
   return PESQ_OK;
 }
 
+int pesq_loss_sum_offset(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, size_t* offset) {
+  if (!p || !offset) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  Geometry g;
+  const int rc = geometry(p, batch, n_src, flags, g);
+  if (rc) return rc;
+  *offset = g.lsum;
+  return PESQ_OK;
+}
+
 int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int64_t ld_ref, const void* deg_in,
                        int64_t ld_deg, int64_t batch, int64_t n_src, uint32_t flags, void* ws, size_t ws_bytes) {
   // the caller's rows; 16-bit rows are widened to float as the first kernel reads them
@@ -497,6 +512,7 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int
   fa.spec = at<Cx<float>>(ws, g.spec);
   fa.fpow = at<float>(ws, g.fpow);
   fa.err = at<uint32_t>(ws, g.err);
+  fa.done = at<uint32_t>(ws, g.lsum + 16);
   fa.y64 = g.general ? at<double>(ws, g.y64) : nullptr;
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
   if (g.general) {
@@ -542,6 +558,8 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ca.d_asymm = d_asymm;
   ca.mos = mos;
   ca.loss = loss;
+  ca.loss_sum = at<double>(ws, g.lsum);
+  ca.done = at<uint32_t>(ws, g.lsum + 16);
   ca.staged = g.fwd_staged;
   ca.cells = g.grad ? at<float>(ws, g.cells) : nullptr;
   ca.cell_stride = g.cell_stride;

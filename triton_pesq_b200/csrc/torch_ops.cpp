@@ -223,7 +223,7 @@ at::Tensor iir_op(int64_t handle, const at::Tensor& x_in, int64_t flags) {
 TORCH_LIBRARY(pesq_cuda, m) {
   m.def("forward(int plan, Tensor ref, Tensor deg, int flags) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
   m.def(
-      "backward(int plan, Tensor ref, Tensor deg, int flags, Tensor workspace, Tensor? g_loss, Tensor? g_mos, "
+      "backward(int plan, Tensor ref, Tensor deg, int flags, Tensor(a!) workspace, Tensor? g_loss, Tensor? g_mos, "
       "Tensor? g_dsymm, Tensor? g_dasymm) -> (Tensor, Tensor)");
   m.def("resample(int resampler, Tensor waveform) -> Tensor");
   m.def("resample_adjoint(int resampler, Tensor grad, int n_in) -> Tensor");

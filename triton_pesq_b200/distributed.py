@@ -57,6 +57,41 @@ def mean_loss(local: torch.Tensor, group=None, async_op: bool = False):
     return buf[0] / buf[1].clamp_min(1.0)
 
 
+class GlobalMean:
+    """The global mean loss of a data-parallel step, capturable in a CUDA graph.
+
+    ``mean_loss`` builds its ``[sum, count]`` message from a host value, which
+    a CUDA graph cannot record.  This keeps the message in a persistent
+    float64 device buffer instead: every call writes this rank's sum and count
+    into it on the current stream, all-reduces it over the process group (an
+    NCCL all-reduce of 16 bytes; nothing when no group is initialised) and
+    returns the mean as a 0-d device tensor.  The loss gradient does not
+    depend on it, so a caller runs it under ``torch.cuda.stream(side)`` and
+    joins that stream after the backward: the collective then overlaps the
+    backward kernels, in eager mode and inside a captured step alike.  All
+    ranks must call it the same number of times, in the same order.
+    """
+
+    def __init__(self, device, group=None):
+        self.group = group
+        self.buf = torch.zeros(2, dtype=torch.float64, device=device)
+
+    def __call__(self, local: torch.Tensor, loss_sum: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``local``: this rank's ``[b]`` losses; ``loss_sum``: their float64
+        ``[sum, count]`` pair when the loss module produced it already
+        (``PesqLossCuda.forward_sum``: summed inside its chain kernel, so no
+        reduction kernel runs here)."""
+
+        if loss_sum is not None:
+            self.buf.copy_(loss_sum)
+        else:
+            self.buf[0] = local.detach().sum(dtype=torch.float64)
+            self.buf[1].fill_(float(local.numel()))
+        if dist.is_available() and dist.is_initialized():
+            dist.all_reduce(self.buf, group=self.group)
+        return self.buf[0] / self.buf[1]
+
+
 class ShardedPesqLoss(torch.nn.Module):
     """Evaluate a PESQ loss module on this rank's slice of a global batch.
 
@@ -73,5 +108,11 @@ class ShardedPesqLoss(torch.nn.Module):
 
     def forward(self, ref: torch.Tensor, deg: torch.Tensor):
         r, d = shard(ref, deg, self.group)
+        if hasattr(self.loss, "forward_sum"):
+            local, pair = self.loss.forward_sum(r, d)
+            buf = pair.detach().clone()
+            if dist.is_available() and dist.is_initialized():
+                dist.all_reduce(buf, group=self.group)
+            return local, buf[0] / buf[1].clamp_min(1.0)
         local = self.loss(r, d)
         return local, mean_loss(local, self.group)

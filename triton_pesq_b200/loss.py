@@ -22,17 +22,34 @@ import numpy as np
 import torch
 
 from . import _lib
-from .tables import PlanConfig
+from .model import BarkScale, Loudness, PowerSpectrogram, edge_ramp
+from .resample import ResampleCuda
+from .tables import ALIGN_DIV, ALIGN_PAD, ALIGN_TARGET, PlanConfig
 
 __all__ = ["PesqLossCuda"]
 
 
-class _PesqFunction(torch.autograd.Function):
-    """(ref, deg) -> (d_symm, d_asymm, mos, loss), one forward launch sequence.
+_SUM_OFFSETS: Dict[tuple, int] = {}
 
-    The backward takes the upstream gradient of all four outputs at once (the
-    epilogue adjoint runs inside the chain adjoint kernel) and returns the
-    gradients of the inputs that asked for one.
+
+def _loss_sum_view(ws: torch.Tensor, plan: int, ref: torch.Tensor, flags: int) -> torch.Tensor:
+    """The [loss sum, batch] float64 pair the chain forward leaves in the workspace."""
+
+    key = (plan, ref.shape[0], ref.shape[1], flags)
+    off = _SUM_OFFSETS.get(key)
+    if off is None:
+        off = _SUM_OFFSETS[key] = _lib.loss_sum_offset(plan, ref.shape[0], ref.shape[1], flags)
+    return ws[off // 4 : off // 4 + 4].view(torch.float64)
+
+
+class _PesqFunction(torch.autograd.Function):
+    """(ref, deg) -> (d_symm, d_asymm, mos, loss, loss_sum), one forward launch
+    sequence; ``loss_sum`` is the float64 pair [sum of the batch's losses,
+    batch] (not differentiable).
+
+    The backward takes the upstream gradient of the four per-utterance outputs
+    at once (the epilogue adjoint runs inside the chain adjoint kernel) and
+    returns the gradients of the inputs that asked for one.
     """
 
     @staticmethod
@@ -41,20 +58,27 @@ class _PesqFunction(torch.autograd.Function):
             _lib.GRAD_DEG if ctx.needs_input_grad[1] else 0
         )
         d_symm, d_asymm, mos, loss, ws = torch.ops.pesq_cuda.forward(plan, ref, deg, flags)
+        in_flag = (_lib.INPUT_BF16 if ref.dtype == torch.bfloat16 else
+                   _lib.INPUT_F16 if ref.dtype == torch.float16 else 0)
+        if ref.shape[0] > 0:
+            loss_sum = _loss_sum_view(ws, plan, ref, flags | in_flag)
+        else:
+            loss_sum = torch.zeros(2, dtype=torch.float64, device=ref.device)
+        ctx.mark_non_differentiable(loss_sum)
         # outputs nobody differentiates get no (zero-filled) gradient
         ctx.set_materialize_grads(False)
         ctx.plan = plan
         ctx.flags = flags
         if flags:
-            ctx.save_for_backward(ref, deg)
-            ctx.workspace = ws
-        ctx.mark_non_differentiable()
-        return d_symm, d_asymm, mos, loss
+            # the workspace is neither an input nor an output; saving such an
+            # intermediate is fine for a once-differentiable backward
+            ctx.save_for_backward(ref, deg, ws)
+        return d_symm, d_asymm, mos, loss, loss_sum
 
     @staticmethod
     @torch.autograd.function.once_differentiable
-    def backward(ctx, g_dsymm, g_dasymm, g_mos, g_loss):
-        ref, deg = ctx.saved_tensors
+    def backward(ctx, g_dsymm, g_dasymm, g_mos, g_loss, g_sum):
+        ref, deg, ws = ctx.saved_tensors
 
         # broadcast gradients (of a sum or mean over the batch) are passed on
         # as one shared value, without materialising them
@@ -62,7 +86,7 @@ class _PesqFunction(torch.autograd.Function):
             return None if g is None else g.float()
 
         g_ref, g_deg = torch.ops.pesq_cuda.backward(
-            ctx.plan, ref, deg, ctx.flags, ctx.workspace,
+            ctx.plan, ref, deg, ctx.flags, ws,
             prep(g_loss), prep(g_mos), prep(g_dsymm), prep(g_dasymm),
         )
         return (
@@ -117,6 +141,19 @@ class PesqLossCuda(torch.nn.Module):
         the pre-emphasis, as in ``PesqLoss`` (no gradient)
     config : PlanConfig
         The host float64 tables the plans are built from
+    resampler : ResampleCuda
+        Resampler to 16 kHz (returns its input at 16 kHz), as ``PesqLoss.resampler``
+    resample_op : ResampleCuda or None
+        The same, None at 16 kHz, as ``PesqLossTriton.resample_op``
+    power_iir, pre_iir : IIRCuda
+        The level alignment band pass and the pre-emphasis as standalone
+        filters (built on first use), as ``PesqLossTriton.power_iir`` /
+        ``pre_iir``; used by ``align_level`` / ``preemphasize``
+    to_spec, fbank, loudness : torch.nn.Module
+        The constant-holding submodules ``PesqLossTriton`` inherits from
+        ``PesqLoss`` (power spectrogram, Bark filterbank, loudness model; see
+        :mod:`triton_pesq_b200.model`).  The loss itself evaluates them fused
+        in its kernels and never calls them.
     """
 
     def __init__(
@@ -141,7 +178,55 @@ class PesqLossCuda(torch.nn.Module):
             requires_grad=False,
         )
         self._plans: Dict[int, int] = {}
+        self.resampler = ResampleCuda(self.source_sample_rate, 16000)
+        self.resample_op = None if self.source_sample_rate == 16000 else self.resampler
+        self.to_spec = PowerSpectrogram(win_length, n_fft, hop_length)
+        self.fbank = BarkScale(n_fft // 2, nbarks)
+        self.loudness = Loudness(nbarks)
         _lib.load_ops()
+
+    # ------------------------------------------------------------------
+    # the two signal stages of PesqLoss as standalone methods
+    # ------------------------------------------------------------------
+
+    def _filter(self, name: str, coeffs: torch.nn.Parameter):
+        module = self._modules.get(name)
+        if module is None:
+            from .iir import IIRCuda
+
+            module = IIRCuda(coeffs[0].detach().cpu().double().numpy(), coeffs[1].detach().cpu().double().numpy())
+            self.add_module(name, module)
+        return module
+
+    @property
+    def power_iir(self):
+        """The order-10 level alignment band pass as an ``IIRCuda`` filter."""
+
+        return self._filter("_power_iir", self.power_filter)
+
+    @property
+    def pre_iir(self):
+        """The pre-emphasis biquad as an ``IIRCuda`` filter."""
+
+        return self._filter("_pre_iir", self.pre_filter)
+
+    def align_level(self, signal: torch.Tensor) -> torch.Tensor:
+        """Scale each row so that its 325-3250 Hz band power is 1e7
+        (``PesqLoss.align_level``, loss.py:111-141; ``PesqLossTriton``
+        evaluates it with its IIR and a scaling kernel, triton_ops/loss.py:94-97).
+        ``[batch, sample]`` float32 CUDA rows in, the scaled rows out,
+        differentiable w.r.t. the signal.  The band power is summed in float64."""
+
+        filtered = self.power_iir(signal)
+        power = filtered.double().pow(2).sum(dim=-1, keepdim=True) / (filtered.shape[-1] + ALIGN_PAD) / ALIGN_DIV
+        return signal * (ALIGN_TARGET / power).sqrt().to(signal.dtype)
+
+    def preemphasize(self, signal: torch.Tensor) -> torch.Tensor:
+        """The 15-sample edge fades, then the pre-emphasis biquad
+        (``PesqLoss.preemphasize``, loss.py:143-169; triton_ops/loss.py:99-102).
+        Unlike the reference's version the input is not modified in place."""
+
+        return self.pre_iir(edge_ramp(signal))
 
     # ------------------------------------------------------------------
     # plans
@@ -198,7 +283,7 @@ class PesqLossCuda(torch.nn.Module):
     def raw(self, ref: torch.Tensor, deg: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         """Symmetric and asymmetric distance, both ``[batch]`` (loss.py:172-268)."""
 
-        d_symm, d_asymm, _, _ = self._evaluate(ref, deg)
+        d_symm, d_asymm = self._evaluate(ref, deg)[:2]
         return d_symm, d_asymm
 
     def mos(self, ref: torch.Tensor, deg: torch.Tensor) -> torch.Tensor:
@@ -210,6 +295,15 @@ class PesqLossCuda(torch.nn.Module):
         """Loss ``factor * (0.1 d_symm + 0.0309 d_asymm)`` (loss.py:300-322)."""
 
         return self._evaluate(ref, deg)[3]
+
+    def forward_sum(self, ref: torch.Tensor, deg: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``forward`` plus the float64 pair [sum of the batch's losses, batch],
+        summed by the chain kernel itself (no extra launch): the numerator and
+        denominator of the global mean a data-parallel step all-reduces
+        (``distributed.GlobalMean``).  The pair is not differentiable."""
+
+        out = self._evaluate(ref, deg)
+        return out[3], out[4]
 
     def graphed(self, ref: torch.Tensor, deg: torch.Tensor):
         """Capture forward (and backward) in a CUDA graph for one input shape.
