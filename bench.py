@@ -682,7 +682,8 @@ def capture_step(model, ref, deg, global_batch: int, group=None):
     from triton_pesq_b200.distributed import GlobalMean
 
     dev = ref.device
-    deg_p = deg.detach().clone().requires_grad_(True)
+    # (a leaf that requires grad is used as it is: its caller refills it in place)
+    deg_p = deg if (deg.requires_grad and deg.is_leaf) else deg.detach().clone().requires_grad_(True)
     mean_op = GlobalMean(dev, group)
     side = torch.cuda.Stream(dev)
     # d(global mean)/d(loss_u) = 1 / global batch for every utterance: the
@@ -837,43 +838,37 @@ def run_cuda(args):
         eager.append(time.perf_counter() - t0)
 
     # ---- end to end through the public API with host buffers
-    # Every step copies its inputs from pinned host memory and reads its loss
-    # (and the global mean) back.  The loop is double buffered as a training
-    # input pipeline is: the copy of step k + 1 (on a copy stream, into the
-    # second of two graphed input sets) overlaps the compute of step k; a set
-    # is overwritten only after the step that used it has finished.  The
-    # serial variant (copy, compute, read back, wait) is reported beside it.
-    # With several ranks per box each process first moves to the cores of its
-    # GPU's NUMA node (numa_local_cores), so that its pinned buffers are local.
+    # Every step copies its inputs from pinned host memory and reads its
+    # losses and the global mean back.  The step itself is the captured
+    # training step a user builds from the public API (PesqLossCuda.forward_sum,
+    # autograd, distributed.GlobalMean; capture_step), on two input sets: the
+    # copy of step k + 1 (on copy streams, into the other set) overlaps the
+    # compute of step k, and a set is overwritten only after the step that
+    # used it has finished.  Beside it: the serial variant (copy, compute,
+    # read back, wait), and the same loop through PesqLossCuda.graphed (the
+    # reference's graphed API: forward and backward graphs replayed from
+    # Python autograd).  With several ranks per box each process first moves
+    # to the cores of its GPU's NUMA node (numa_local_cores), so that its
+    # pinned buffers are local.
     ref_h = ref_cpu.pin_memory()
     deg_h = deg_cpu.pin_memory()
     loss_h = [torch.empty(BATCH + 1, dtype=torch.float64, pin_memory=True) for _ in range(2)]
-    # (graphed() rebinds the module's forward, as PesqLossTriton.graphed does,
-    # so each input set gets its own module instance)
+    stream = torch.cuda.current_stream(dev)
     sets = []
     for _ in range(2):
-        ref_d = torch.empty_like(ref)
-        deg_d = torch.empty_like(deg).requires_grad_(True)
-        with torch.no_grad():
-            ref_d.copy_(ref)
-            deg_d.copy_(deg)
-        sets.append((ref_d, deg_d, PesqLossCuda(1.0, sample_rate=RATE).graphed(ref_d, deg_d),
-                     torch.empty(BATCH + 1, dtype=torch.float64, device=dev)))
-    stream = torch.cuda.current_stream(dev)
-    side = torch.cuda.Stream(dev)
-    mean_op = GlobalMean(dev)
-    upstream = torch.full((1,), 1.0 / global_batch, device=dev).expand(BATCH)
-    # the reference and the degraded signal are copied on two copy streams
-    # (two DMA engines in flight) when `split`, else one after the other
+        ref_d = ref.clone()
+        deg_d = deg.clone().requires_grad_(True)
+        g_step, (loss_s, _, mean_s) = capture_step(PesqLossCuda(1.0, sample_rate=RATE), ref_d, deg_d, global_batch)
+        result = torch.empty(BATCH + 1, dtype=torch.float64, device=dev)
+        sets.append((ref_d, deg_d, g_step, loss_s, mean_s, result))
     copy_streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
     copied = [[torch.cuda.Event(), torch.cuda.Event()] for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     split = [True]
 
     def issue_copy(k):
-        ref_d, deg_d, _, _ = sets[k % 2]
-        pairs = ((ref_d, ref_h), (deg_d, deg_h))
-        for i, (dst, src) in enumerate(pairs):
+        ref_d, deg_d = sets[k % 2][:2]
+        for i, (dst, src) in enumerate(((ref_d, ref_h), (deg_d, deg_h))):
             cs = copy_streams[i] if split[0] else copy_streams[0]
             with torch.cuda.stream(cs):
                 cs.wait_event(consumed[k % 2])
@@ -882,19 +877,14 @@ def run_cuda(args):
                 copied[k % 2][i].record(cs)
 
     def run_step(k):
-        ref_d, deg_d, graphed, result = sets[k % 2]
+        _, _, g_step, loss_s, mean_s, result = sets[k % 2]
         stream.wait_event(copied[k % 2][0])
         stream.wait_event(copied[k % 2][1])
-        out = graphed(ref_d, deg_d)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            mean = mean_op(out)
-        torch.autograd.grad(out, [deg_d], grad_outputs=upstream)
+        g_step.replay()
         consumed[k % 2].record(stream)
-        stream.wait_stream(side)
         with torch.no_grad():
-            result[:BATCH].copy_(out.detach())
-            result[BATCH:].copy_(mean.reshape(1))
+            result[:BATCH].copy_(loss_s.detach())
+            result[BATCH:].copy_(mean_s.reshape(1))
         loss_h[k % 2].copy_(result, non_blocking=True)
 
     def pipelined(n):
@@ -940,27 +930,62 @@ def run_cuda(args):
     serial_ms = []
     for k in range(max(5, args.steps // 5)):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ref_d, deg_d, graphed, result = sets[0]
+        ref_d, deg_d, g_step, loss_s, mean_s, result = sets[0]
         a.record(stream)
         with torch.no_grad():
             ref_d.copy_(ref_h, non_blocking=True)
             deg_d.copy_(deg_h, non_blocking=True)
-        out = graphed(ref_d, deg_d)
-        mean = mean_op(out)
-        torch.autograd.grad(out, [deg_d], grad_outputs=upstream)
+        g_step.replay()
         with torch.no_grad():
-            result[:BATCH].copy_(out.detach())
-            result[BATCH:].copy_(mean.reshape(1))
+            result[:BATCH].copy_(loss_s.detach())
+            result[BATCH:].copy_(mean_s.reshape(1))
         loss_h[0].copy_(result, non_blocking=True)
         b.record(stream)
         b.synchronize()
         serial_ms.append(a.elapsed_time(b))
+
+    # the same loop through the module's graphed callables (forward and
+    # backward CUDA graphs of PesqLossCuda.graphed, autograd in Python)
+    mod_sets = []
+    for _ in range(2):
+        ref_d = ref.clone()
+        deg_d = deg.clone().requires_grad_(True)
+        mod_sets.append((ref_d, deg_d, PesqLossCuda(1.0, sample_rate=RATE).graphed(ref_d, deg_d)))
+    side = torch.cuda.Stream(dev)
+    mean_op = GlobalMean(dev)
+    upstream = torch.full((1,), 1.0 / global_batch, device=dev).expand(BATCH)
+
+    def module_loop(n):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for k in range(n):
+            ref_d, deg_d, graphed = mod_sets[k % 2]
+            with torch.no_grad():
+                ref_d.copy_(ref_h, non_blocking=True)
+                deg_d.copy_(deg_h, non_blocking=True)
+            out = graphed(ref_d, deg_d)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                mean = mean_op(out)
+            torch.autograd.grad(out, [deg_d], grad_outputs=upstream)
+            stream.wait_stream(side)
+            loss_h[k % 2][:BATCH].copy_(out.detach(), non_blocking=True)
+            loss_h[k % 2][BATCH:].copy_(mean.reshape(1), non_blocking=True)
+        stop.record(stream)
+        stop.synchronize()
+        return start.elapsed_time(stop)
+
+    module_loop(3)
+    module_ms = torch.tensor([module_loop(args.steps)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
         dist.all_reduce(one_stream, op=dist.ReduceOp.MAX)
+        dist.all_reduce(module_ms, op=dist.ReduceOp.MAX)
     e2e_ms_total = float(e2e_total.item())
     e2e_value = utt_per_step * args.steps / (e2e_ms_total / 1e3)
     one_stream_ms = float(one_stream.item()) / args.steps
+    module_ms_per_step = float(module_ms.item()) / args.steps
+    del mod_sets
 
     # ---- the north star's scaling configuration: 512 x 3 s at 16 kHz as one
     # global batch sharded over the ranks, and the 64 x 10 s at 48 kHz batch
@@ -989,7 +1014,8 @@ def run_cuda(args):
     geometries = measure_geometries(dev, flush) if single else None
 
     if world > 1:
-        del graph
+        # graphs that hold NCCL calls are released before the process group
+        del graph, sets
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -1024,12 +1050,14 @@ def run_cuda(args):
             "unit": UNIT,
             "h2d_bytes_per_step": int(ref.numel() * 4 * 2),
             "d2h_bytes_per_step": int((BATCH + 1) * 8),
-            "api": "PesqLossCuda.graphed (two instances, one per input set), inputs copied from pinned host memory "
-                   "every step (reference and degraded signal on two copy streams) overlapping the previous "
-                   "step's compute, global mean all-reduced, losses and mean read back every step",
+            "api": "the captured training step (PesqLossCuda.forward_sum, autograd backward of the global mean, "
+                   "distributed.GlobalMean) on two input sets, inputs copied from pinned host memory every step "
+                   "(reference and degraded signal on two copy streams) overlapping the previous step's compute, "
+                   "losses and global mean read back every step",
             "ms_per_step": e2e_ms_total / args.steps,
             "one_copy_stream_ms_per_step": one_stream_ms,
             "serial_ms_per_step": statistics.median(serial_ms),
+            "graphed_module_ms_per_step": module_ms_per_step,
             "h2d_gbs_alone": h2d_gbs,
             "numa_local_cores": f"{len(cores)} cores" if cores else None,
         },

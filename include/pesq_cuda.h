@@ -124,6 +124,14 @@ int pesq_plan_create(const pesq_plan_desc* desc, pesq_plan** plan);
 
 int pesq_plan_destroy(pesq_plan* plan);
 
+/* Synchronises `stream`, then reads and clears the plan's device error word:
+ * nonzero (PESQ_DEVICE_* flags) when a kernel of an earlier call gave up a
+ * bounded wait (a bulk copy into shared memory that did not complete in
+ * time) -- the outputs of that call are then not valid.  The reference has
+ * no device-side waits; its errors are Python exceptions on bad input. */
+int pesq_plan_check(const pesq_plan* plan, void* stream, uint32_t* flags);
+#define PESQ_DEVICE_BULK_TIMEOUT 1u
+
 /* CUDA device ordinal the plan lives on. */
 int pesq_plan_device(const pesq_plan* plan, int* device);
 
@@ -307,6 +315,14 @@ size_t pesq_iir_workspace_bytes(const pesq_iir* filter, int64_t rows, int64_t n)
  * _IIRFunction, iir.py:1232-1263). */
 int pesq_iir_filter(const pesq_iir* filter, void* stream, const float* x, int64_t ld_x, int64_t rows, int64_t n,
                     float* y, int64_t ld_y, uint32_t flags, void* workspace, size_t workspace_bytes);
+/* Polls a tile of a chained row makes while it waits for a predecessor's
+ * published state before it gives up (its error word then reads nonzero and
+ * the predecessor counts as zero).  Default 2^21 (about 0.1 s with the 64 ns
+ * back-off); small values make the waits run out on purpose, e.g. to test
+ * that a caller notices.  The reference's IIR has no device-side waits: it
+ * chains its tiles with a separate sequential carry kernel
+ * (triton_ops/iir.py:766-796). */
+int pesq_iir_set_spin_limit(pesq_iir* filter, uint32_t polls);
 /* Synchronises `stream`, then reads and clears the filter's error word:
  * nonzero when a tile of an earlier call stopped waiting for its predecessor
  * (a bounded wait that ran out; its rows are then wrong). */

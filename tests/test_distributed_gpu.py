@@ -84,9 +84,9 @@ def _worker(rank, world, port, out):
         for _ in range(2):
             graph.replay()
             torch.cuda.synchronize()
-            replays.append((g_loss.clone().cpu(), g_grad.clone().cpu(), float(g_mean)))
+            replays.append((g_loss.detach().cpu(), g_grad.detach().cpu(), float(g_mean)))
         out[rank] = {
-            "local": local.detach().cpu(), "grad": grad[lo:hi].cpu(), "mean": float(mean),
+            "local": local.detach().cpu(), "grad": grad[lo:hi].detach().cpu(), "mean": float(mean),
             "untouched_zero": bool(torch.all(untouched == 0)), "replays": replays,
         }
     finally:

@@ -131,6 +131,7 @@ SIGNATURES = {
     "pesq_plan_create": (ctypes.c_int, [ctypes.POINTER(PlanDesc), ctypes.POINTER(ctypes.c_void_p)]),
     "pesq_plan_destroy": (ctypes.c_int, [ctypes.c_void_p]),
     "pesq_plan_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "pesq_plan_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "pesq_query_shape": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(Shape)]),
     "pesq_workspace_size": (
         ctypes.c_int,
@@ -201,6 +202,7 @@ SIGNATURES = {
          ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t],
     ),
     "pesq_iir_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "pesq_iir_set_spin_limit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
     "pesq_forward_noalloc": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
@@ -296,6 +298,15 @@ def _register_fakes() -> None:
     @torch.library.register_fake("pesq_cuda::iir")
     def _iir(filt, signal, flags):
         return signal.new_empty(signal.shape)
+
+
+def plan_check(handle: int, stream: int = 0) -> int:
+    """Synchronise ``stream`` and return (and clear) the plan's device error word."""
+
+    flags = ctypes.c_uint32(0)
+    check(library().pesq_plan_check(ctypes.c_void_p(handle), ctypes.c_void_p(stream), ctypes.byref(flags)),
+          "pesq_plan_check")
+    return int(flags.value)
 
 
 def loss_sum_offset(handle: int, batch: int, n: int, flags: int) -> int:

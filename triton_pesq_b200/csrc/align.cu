@@ -15,9 +15,10 @@
 //     after the chain adjoint, which releases it as soon as its own CTAs are
 //     resident, so its CTAs fill the SMs the chain leaves idle;
 //   * it reads nothing the chain adjoint writes, and it waits for the chain
-//     adjoint's grid to complete (pdl_wait) only after its own work, so the
-//     next kernel on the stream (the back kernel, launched normally) starts
-//     after both.
+//     adjoint's grid to complete (pdl_wait) only after its own work, so its
+//     completion implies the chain adjoint's; the back kernel that follows
+//     (launched the same way, released at the end of this kernel's CTAs)
+//     waits for this kernel's completion before reading.
 //
 // The adjoint filter runs backwards in time: the CTA stages f on
 // [a, send + kHorizon) (zero past the row end, where f is not part of the
@@ -90,7 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_CTA_END(g_cta_align);
   PESQ_SPAN_END(g_span_align, 0);
 
-  // complete only after the kernel this one was released early from
+  // the back kernel may be scheduled once every CTA is here; this kernel
+  // completes only after the kernel it was released early from
+  pdl_trigger();
   pdl_wait();
 }
 

@@ -14,8 +14,8 @@
 //
 // The CTA overlap-adds the per-frame gradients around its segment in a fixed
 // order (even frames, then odd frames: no atomics, bitwise reproducible) and
-// runs the pre-emphasis adjoint backwards in time with kHorizon samples of
-// look-ahead.
+// runs the pre-emphasis adjoint backwards in time with kBackHorizon samples
+// of look-ahead.
 #include "kernels.cuh"
 
 namespace pesq {
@@ -26,11 +26,12 @@ PESQ_CTA_TABLE(g_cta_back)
 
 namespace {
 
-constexpr int kSegMax = kSpan - kHorizon - 3 * kHop;  // samples of the longest segment
-// frames a CTA processes: one before its segment, the segment (<= 57 frames)
-// and those reaching kHorizon past its end
-constexpr int kBackFrames = 64;
-static_assert((kSpan - 2 * kHorizon) / kHop + 6 <= kBackFrames, "frames of the longest segment");
+constexpr int kSegMax = kBackSegFrames * kHop;  // samples of the longest segment
+// frames a CTA processes: one before its segment, the segment and those
+// reaching kBackHorizon past its end (one per warp and parity pass)
+constexpr int kBackFrames = 2 * kWarps;
+static_assert(kBackSegFrames + 1 + kBackHorizon / kHop <= kBackFrames, "frames of the longest segment");
+static_assert(kHop + kSegMax + kBackHorizon <= kSpan, "back kernel span");
 constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * FftLayout<float>::kSlots * 8 +
                                kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4 +
                                kBackFrames * kMaxBands * 4;
@@ -62,13 +63,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_STAMP(g_phase_back, 0);
 
   if constexpr (kGather) {
-    // dL/dy on [a, send + kHorizon): sum over the frames covering each sample
+    pdl_wait();
+    // dL/dy on [a, send + kBackHorizon): sum over the frames covering each sample
     // (frame order), z staged in the background
     const float* zr = p.z + (int64_t)row * n_row;
     for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
     cp_async_commit();
     const float* fg = p.frame_grad + (int64_t)(row - p.row_begin) * p.frames * p.nfft;
-    const int top_g = kHop + kHorizon + (int)(send - a);
+    const int top_g = kHop + kBackHorizon + (int)(send - a);
     for (int i = tid; i < kSpan; i += kThreads) {
       const int64_t n = base + i;
       float acc = 0.0f;
@@ -83,16 +85,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
   } else {
-  // frames that touch [a, send + kHorizon)
+  // frames that touch [a, send + kBackHorizon)
   const int nb = p.nb;
   const int t0 = seg * p.seg_frames;
   const int t_lo = max(0, t0 - 1);
-  const int t_hi = min(p.frames - 1, (int)((send + kHorizon - 1) / kHop));
+  const int t_hi = min(p.frames - 1, (int)((send + kBackHorizon - 1) / kHop));
 
   // first copy group: constant tables and dL/dB of the CTA's frames; second
   // group: z = H^T H x of the segment, only needed at the very end, copied in
   // the background of the frame loop
   copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
+  // launched with programmatic serialisation: what follows reads the output
+  // of the kernels before this one
+  pdl_wait();
   {
     const float* src = p.g_bark + ((int64_t)row * p.frames + t_lo) * nb;
     const int cnt = (t_hi - t_lo + 1) * nb;
@@ -158,9 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float kappa = p.kappa[row];
   PESQ_STAMP(g_phase_back, 2);
 
-  // pre-emphasis adjoint on [a, send): backwards in time from send + kHorizon;
+  // pre-emphasis adjoint on [a, send): backwards in time from send + kBackHorizon;
   // the gradient of the zero padding after the row end is dropped
-  const int top = kHop + kHorizon + (int)(send - a) - 1;
+  const int top = kHop + kBackHorizon + (int)(send - a) - 1;
   chunk_scan<2, true, float>(
       pre, es,
       [&](int q) {
@@ -194,7 +199,9 @@ size_t back_smem_bytes() { return (size_t)kBackSmemBytes; }
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
-  LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(), s, false);
+  // programmatic serialisation: the CTAs may be scheduled while the align
+  // kernel finishes and wait (pdl_wait) before reading its output
+  LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(), s, true);
   if (a.frame_grad) return cudaLaunchKernelEx(&l.cfg, back_kernel<true>, a, pre);
   return cudaLaunchKernelEx(&l.cfg, back_kernel<false>, a, pre);
 }

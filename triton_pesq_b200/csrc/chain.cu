@@ -225,8 +225,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   PESQ_STAMP(g_phase_chain_fwd, 0);
 
   // tables and the slice's spectra are copied asynchronously while warps 0-1
-  // reduce the level alignment power
+  // reduce the level alignment power; the tables do not depend on the front
+  // kernel, everything after pdl_wait does
   copy_async<kChainThreads>(&tab, p.tab, (int)sizeof(DevTables));
+  pdl_wait();
   const float* Fr = p.bark + (int64_t)u * T * p.lay.nb;
   const float* Fd = p.bark + (int64_t)(B + u) * T * p.lay.nb;
   const int nb = p.lay.nb;
@@ -507,6 +509,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   if (cst && threadIdx.x == 0) bulk_wait_all();
   PESQ_STAMP(g_phase_chain_fwd, 5);
   PESQ_SPAN_END(g_span_chain, 0);
+  pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------
@@ -534,6 +537,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   // kernel writes) may start on the SMs the clusters leave free
   pdl_trigger();
   copy_async<kChainThreads>(&tab, p.tab, (int)sizeof(DevTables));
+  // everything below reads what the forward (or the caller's upstream
+  // gradient) wrote
+  pdl_wait();
   const float* sv = p.saved + (int64_t)u * p.lay.stride;
   float* gf = p.scratch + (int64_t)u * 2 * T;  // [g_fpr | g_h] per frame
   const float* Fr = p.bark + (int64_t)u * T * nb;
@@ -822,10 +828,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   PESQ_SPAN_END(g_span_chain, 1);
 }
 
+// Both chain kernels are launched with programmatic stream serialisation:
+// their CTAs may be scheduled once the preceding kernel's CTAs have all
+// signalled (front / chain forward: at their end), copy their constant
+// tables, and wait for that kernel's completion (pdl_wait) before reading
+// anything it wrote.
 template <class Kernel, class Args>
 cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, size_t smem, cudaStream_t s) {
   if (batch <= 0) return cudaSuccess;
-  LaunchShape l((unsigned)(batch * cluster), kChainThreads, smem, s, false, cluster);
+  LaunchShape l((unsigned)(batch * cluster), kChainThreads, smem, s, true, cluster);
   return cudaLaunchKernelEx(&l.cfg, k, a);
 }
 

@@ -224,10 +224,12 @@ __device__ __forceinline__ float log2f_fast(float x) {
 // kernel following this one to start (once every CTA of this grid has called
 // it or exited); pdl_wait() blocks until the preceding kernel has completed and
 // its memory is visible, and is a no-op in a kernel launched normally.  The
-// one kernel of this library launched this way (the align kernel, released by
-// the chain adjoint) calls pdl_wait() before it exits, so its completion
-// implies the completion of the chain adjoint.  (Releasing the other kernels
-// early as well was measured to slow the captured step down.)
+// chain kernels and the back kernel are launched this way and released at
+// the end of their predecessors' CTAs (their table copies overlap the
+// predecessor's tail; everything else waits in pdl_wait); the align kernel is
+// released at the start of the chain adjoint and runs beside it.  Every
+// kernel launched this way calls pdl_wait() before it exits, so its
+// completion implies the completion of everything before it on the stream.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
@@ -360,9 +362,63 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // the issuing thread's bulk copies have completed (their writes are done)
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Device-side error flags, OR-ed into a word the host reads back on demand.
+// ---------------------------------------------------------------------------
+// bulk copy (TMA, no multicast) global -> shared, completed on an mbarrier
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// One thread initialises the barrier (one arrival per phase); a CTA barrier
+// must follow before other threads wait on it.
+__device__ __forceinline__ void mbar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// The issuing thread's arrival, announcing `bytes` of bulk copies that
+// complete the current phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
+// GPU's global memory into this CTA's shared memory, signalled on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Tries (each a hardware-bounded suspend) before a wait on a bulk copy gives
+// up; a copy of this GPU's memory lands within microseconds.
+constexpr uint32_t kMbarTries = 1u << 16;
+
+// Waits for phase `parity` of `bar` with a bounded number of tries; false if
+// it did not complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMbarTries; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Device-side error flags, OR-ed into the plan's error word, which the host
+// reads back (and clears) with pesq_plan_check.
 enum : uint32_t {
-  kErrBulkTimeout = 1u << 0,
+  kErrBulkTimeout = 1u << 0,  // a bulk copy into shared memory did not complete in time
   kErrBadGeometry = 1u << 1,
 };
 

@@ -39,7 +39,9 @@ constexpr int kFftFloats = kWarps * FftLayout<double>::kSlots * 4;
 constexpr int kFrontScratchFloats =
     kFftFloats > scan_scratch_floats<10>() ? kFftFloats : scan_scratch_floats<10>();
 constexpr int kFrontSmemBytes = 2 * kSpan * 4 + kFrontScratchFloats * 4 + (int)sizeof(DevTables) +
-                                (int)sizeof(DevTwiddle64) + kWarps * 8;
+                                (int)sizeof(DevTwiddle64) + kWarps * 8 + 16;
+static_assert(sizeof(DevTables) % 16 == 0 && sizeof(DevTwiddle64) % 16 == 0, "bulk copies of the tables");
+static_assert((2 * kSpan * 4 + kFrontScratchFloats * 4) % 16 == 0, "16-byte aligned tables in shared memory");
 
 // kSignal: general frame geometry, y is written to p.y64 and the frames are
 // left to the spectrum kernel (spectrum.cu)
@@ -55,6 +57,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
   DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
   double* red = reinterpret_cast<double*>(tw + 1);  // kWarps
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + kWarps);  // completion of the bulk copies
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.x / p.nseg;
@@ -71,17 +74,45 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // the chain forward that follows on the stream counts its clusters here
   if (blockIdx.x == 0 && tid == 0) *p.done = 0u;
-  // constant tables, copied in the background of the span staging
-  copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
-  copy_async<kThreads>(tw, p.tw64, (int)sizeof(DevTwiddle64));
-  cp_async_commit();
-  // stage the span; zeros outside the row reproduce the zero initial state.
+  // Stage the span (zeros outside the row reproduce the zero initial state)
+  // and the constant tables.  The tables, and the part of a float32 row's
+  // span that starts on a 16-byte boundary in both memories, arrive by bulk
+  // copies (TMA, this GPU's memory, no multicast) signalled on one mbarrier;
+  // the ragged tail, the zeros and other rows (16-bit, misaligned) are staged
+  // by the threads meanwhile.
+  const float* xf = static_cast<const float*>(xr);
+  const int64_t lo = base > 0 ? base : 0;
+  const int64_t hi = min(base + (int64_t)kSpan, n_row);
+  const int64_t cnt4 = hi > lo ? ((hi - lo) & ~(int64_t)3) : 0;
+  const bool bulk_span = p.src.type == kInF32 && cnt4 > 0 && ((lo - base) & 3) == 0 &&
+                         (reinterpret_cast<uintptr_t>(xf + lo) & 15) == 0;
+  if (tid == 0) mbar_init(bar);
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t span_bytes = bulk_span ? (uint32_t)(cnt4 * 4) : 0u;
+    mbar_arrive_expect_tx(bar, (uint32_t)(sizeof(DevTables) + sizeof(DevTwiddle64)) + span_bytes);
+    bulk_g2s(tab, p.tab, (uint32_t)sizeof(DevTables), bar);
+    bulk_g2s(tw, p.tw64, (uint32_t)sizeof(DevTwiddle64), bar);
+    if (bulk_span) bulk_g2s(xs + (lo - base), xf + lo, span_bytes, bar);
+  }
+  if (bulk_span) {
+    for (int i = tid; i < kSpan; i += kThreads) {
+      const int64_t q = base + i;
+      if (q < lo || q >= lo + cnt4) xs[i] = q >= lo && q < hi ? __ldg(xf + q) : 0.0f;
+    }
+  } else {
+    stage_span_any(xs, xr, base, n_row, p.src.type);
+  }
   // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
   // On gradient rows fb first holds f = H x (below), the low part only after.
   const bool has_lo = p.src_lo.ref != nullptr;
-  stage_span_any(xs, xr, base, n_row, p.src.type);
   if (has_lo && !grad_row) stage_span(fb, p.src_lo.row(row), base, n_row);
-  cp_async_wait_all();
+  if (!mbar_wait(bar, 0)) {
+    // the copies did not land in time: flag it, give them one more bounded
+    // wait (they write into this CTA's shared memory) and carry on
+    if (tid == 0) atomicOr(p.err, kErrBulkTimeout);
+    mbar_wait(bar, 0);
+  }
   __syncthreads();
   PESQ_STAMP(g_phase_front, 1);
 
@@ -182,8 +213,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     float* out = p.bark + ((int64_t)row * p.frames + t) * nb;
     for (int b = lane; b < nb; b += 32) {
+      // the band's bins in order, eight loads in flight at a time (the
+      // padding past the band's end adds exact zeros)
+      const int f1 = tab->band_end[b];
       double acc = 0.0;
-      for (int f = tab->band_start[b]; f < tab->band_end[b]; ++f) acc += pw[f];
+#pragma unroll 1
+      for (int f = tab->band_start[b]; f < f1; f += 8) {
+        double v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = f + i < f1 ? pw[f + i] : 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc += v[i];
+      }
       out[b] = (float)(acc * (double)tab->band_corr[b]);
     }
     __syncwarp();
@@ -192,6 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   PESQ_STAMP(g_phase_front, 6);
   PESQ_CTA_END(g_cta_front);
   PESQ_SPAN_END(g_span_front, 0);
+  // the chain forward (launched with programmatic serialisation) may be
+  // scheduled once every CTA of this grid is here
+  pdl_trigger();
 }
 
 }  // namespace

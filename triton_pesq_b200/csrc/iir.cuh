@@ -36,7 +36,8 @@
 // inclusive end state, and publishes its own inclusive state.  Published
 // states are self-validating tagged words (no memory fences, see publish).  Nothing is
 // truncated: the result is exact for any stable or unstable filter.  Every
-// wait is bounded (kSpinLimit polls); a wait that gives up records an error
+// wait is bounded (Args::spin_limit polls, kSpinLimit unless the caller set
+// another with pesq_iir_set_spin_limit); a wait that gives up records an error
 // in the filter's error word and treats the predecessor as zero.
 //
 // Every warp-collective operation (shuffle, ballot) is executed by all 32
@@ -98,6 +99,7 @@ struct Args {
   uint32_t* ticket;        // tile counter (zero before the launch)
   unsigned long long* slots;  // [tiles][2][P][2]: aggregate / inclusive state, zero before the launch
   uint32_t* err;
+  uint32_t spin_limit;     // polls a look-back wait makes before it gives up (normally kSpinLimit)
 };
 
 constexpr int kNearPowers = 4;  // A^(k kTile), k < 4, staged for the look-back
@@ -210,7 +212,7 @@ __device__ double lookback(const Args& a, int64_t tile, int64_t tin, const doubl
           st = 1u;
           break;
         }
-        if (++it > kSpinLimit) {
+        if (++it > a.spin_limit) {
           atomicOr(a.err, 1u);
           st = 3u;  // give up: the predecessor counts as a zero inclusive state
           break;

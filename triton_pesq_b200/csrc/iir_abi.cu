@@ -53,6 +53,7 @@ struct pesq_iir {
   float* wpow = nullptr;
   double* look = nullptr;
   uint32_t* err = nullptr;
+  uint32_t spin_limit = pesq::iir::kSpinLimit;
   double largest32 = 0.0, largest64 = 0.0;
 };
 
@@ -369,6 +370,7 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   a.wpow = f->wpow;
   a.look = f->look;
   a.err = f->err;
+  a.spin_limit = f->spin_limit;
   if (g.chained()) {
     char* w = static_cast<char*>(workspace);
     a.ticket = reinterpret_cast<uint32_t*>(w);
@@ -392,6 +394,12 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
     default: break;
   }
   if (e != cudaSuccess) return set_error(PESQ_ERR_CUDA, cudaGetErrorString(e));
+  return PESQ_OK;
+}
+
+int pesq_iir_set_spin_limit(pesq_iir* f, uint32_t polls) {
+  if (!f) return set_error(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  f->spin_limit = polls;
   return PESQ_OK;
 }
 

@@ -141,6 +141,16 @@ struct AlignArgs {
   float* z;          // [rows][n]  H^T f
 };
 
+// Segmentation of the back kernel: at most kBackSegFrames hops of output per
+// CTA (with the frame before the segment and the kBackHorizon samples after
+// it, whose frames' gradients run back into the segment through the
+// pre-emphasis adjoint: 32 frames, one per warp in each of the two parity
+// passes of its overlap-add).  The gradient beyond the horizon reaches the
+// segment through A_pre^768 (norm below 1e-9 for the pre-emphasis biquad,
+// checked at plan creation), far below float32 rounding.
+constexpr int kBackSegFrames = 28;
+constexpr int kBackHorizon = 3 * kHop;
+
 struct BackArgs {
   int row_begin;     // rows [row_begin, row_end) get a gradient
   int nb;            // Bark bands

@@ -37,6 +37,7 @@ struct pesq_plan {
   PreTab64 pre64;    // float64 tables: pre-emphasis of the front kernel
   DevTables* dtab;   // device copy
   DevTwiddle64* tw64;
+  uint32_t* err;     // device error word (kErr* flags), read and cleared by pesq_plan_check
   // frame geometry; `general` when it is not n_fft 512 / hop 256 (the
   // spectrum kernels with the tables in `gen_buf`)
   int nfft, hop;
@@ -72,6 +73,35 @@ int cuda_fail(cudaError_t e, const char* what) {
     cudaError_t _e = (expr);                  \
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
+
+// Max-abs-row-sum norm of A^k for the P x P row-major float64 matrix a.
+double power_norm(const double* a, int P, int k) {
+  std::vector<double> r((size_t)P * P, 0.0), b(a, a + (size_t)P * P), t((size_t)P * P);
+  for (int i = 0; i < P; ++i) r[(size_t)i * P + i] = 1.0;
+  auto mul = [&](const std::vector<double>& x, const std::vector<double>& y, std::vector<double>& z) {
+    for (int i = 0; i < P; ++i)
+      for (int j = 0; j < P; ++j) {
+        double acc = 0.0;
+        for (int l = 0; l < P; ++l) acc += x[(size_t)i * P + l] * y[(size_t)l * P + j];
+        z[(size_t)i * P + j] = acc;
+      }
+  };
+  for (; k > 0; k >>= 1) {
+    if (k & 1) {
+      mul(r, b, t);
+      r.swap(t);
+    }
+    mul(b, b, t);
+    b.swap(t);
+  }
+  double norm = 0.0;
+  for (int i = 0; i < P; ++i) {
+    double row = 0.0;
+    for (int j = 0; j < P; ++j) row += fabs(r[(size_t)i * P + j]);
+    norm = std::max(norm, row);
+  }
+  return norm;
+}
 
 template <int P, class R>
 int fill_scan(ScanTab<P, R>& t, const pesq_scan_desc& d, const char* name) {
@@ -112,7 +142,8 @@ static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel 
 struct Geometry {
   int64_t batch, rows, n_src, n16;
   int T, L, nb;
-  int seg, nseg;  // segmentation of a row
+  int seg, nseg;      // segmentation of a row (front, align)
+  int seg_b, nseg_b;  // segmentation of a row for the back kernel
   int cluster;
   bool fwd_staged, fwd_stage_cells, bwd_staged, bwd_stage_cells;
   bool resample, grad, general;
@@ -120,7 +151,7 @@ struct Geometry {
   int grad_begin, grad_end;
   ChainLayout lay;
   // byte offsets
-  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, y64, fgrad, err, lsum,
+  size_t x16, x16lo, partial, sumsq, bark, fpow, z, spec, saved, cells, gbark, kappa, cscratch, gx16, y64, fgrad, lsum,
       total;
   int64_t cell_stride;  // floats between the fields of the chain's adjoint coefficients
 };
@@ -165,6 +196,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.general = p->general;
   g.nfreq = p->general ? p->gen.nfreq : kBins;
   balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
+  balance(g.n16, kBackSegFrames, g.seg_b, g.nseg_b);
   // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
   // a long utterance whose 8-CTA slices do not fit the chain backward's
@@ -191,7 +223,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   }
   // every kernel folds rows x segments (or utterances x cluster CTAs) onto
   // grid x; the resampler launches at most 65535 rows at a time in grid y
-  if (g.rows * g.nseg > INT32_MAX || g.batch * g.cluster > INT32_MAX)
+  if (g.rows * g.nseg_b > INT32_MAX || g.batch * g.cluster > INT32_MAX)
     return fail(PESQ_ERR_INVALID_ARGUMENT, "batch too large for one call (%lld rows of %d segments)",
                 (long long)g.rows, g.nseg);
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
@@ -223,7 +255,6 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.gx16 = take(g.grad && g.resample ? rows * g.n16 * 4 : 0);
   g.y64 = take(g.general ? rows * g.n16 * 8 : 0);
   g.fgrad = take(g.grad && g.general ? (size_t)(g.grad_end - g.grad_begin) * g.T * p->nfft * 4 : 0);
-  g.err = take(16);
   g.lsum = take(32);  // double[2] batch loss sum and count, uint32 arrival counter at +16
   g.total = o;
   return PESQ_OK;
@@ -304,6 +335,11 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   if (rc) return bail(rc);
   rc = fill_scan(p->pre64, d->pre_filter, "pre-emphasis filter");
   if (rc) return bail(rc);
+  // the back kernel folds in kBackHorizon samples of look-ahead of the
+  // pre-emphasis adjoint and drops the rest, which A^kBackHorizon bounds
+  if (!(power_norm(d->pre_filter.trans, 2, kBackHorizon) < 1e-9))
+    return bail(fail(PESQ_ERR_UNSUPPORTED, "pre-emphasis filter: its impulse response decays too slowly for the "
+                                           "%d-sample look-ahead of the backward", kBackHorizon));
 
   // constant tables
   DevTables h;
@@ -395,6 +431,9 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
     p->gen.bin_band = reinterpret_cast<const int*>(dev + tw_bytes + win_bytes);
   }
 
+  if (cudaMalloc(&p->err, 16) != cudaSuccess || cudaMemset(p->err, 0, 16) != cudaSuccess)
+    return bail(fail(PESQ_ERR_CUDA, "allocating the error word"));
+
   // resampler tables
   p->resample = d->sample_rate != 16000;
   if (p->resample) {
@@ -423,8 +462,21 @@ int pesq_plan_destroy(pesq_plan* p) {
   cudaFree(p->dtab);
   cudaFree(p->tw64);
   cudaFree(p->gen_buf);
+  cudaFree(p->err);
   free_resample_tables(p->rs);
   delete p;
+  return PESQ_OK;
+}
+
+int pesq_plan_check(const pesq_plan* p, void* stream, uint32_t* flags) {
+  if (!p || !flags) return fail(PESQ_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, p->err, 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p->err, 0, 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "pesq_plan_check");
+  *flags = v;
   return PESQ_OK;
 }
 
@@ -511,7 +563,7 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int
   fa.partial = at<double>(ws, g.partial);
   fa.spec = at<Cx<float>>(ws, g.spec);
   fa.fpow = at<float>(ws, g.fpow);
-  fa.err = at<uint32_t>(ws, g.err);
+  fa.err = p->err;
   fa.done = at<uint32_t>(ws, g.lsum + 16);
   fa.y64 = g.general ? at<double>(ws, g.y64) : nullptr;
   PESQ_CUDA_TRY(launch_front(fa, p->pow, p->pre64, (int)g.rows, s), "front kernel");
@@ -657,8 +709,8 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ba.nb = g.nb;
   ba.n = g.n16;
   ba.frames = g.T;
-  ba.seg_frames = g.seg;
-  ba.nseg = g.nseg;
+  ba.seg_frames = g.seg_b;
+  ba.nseg = g.nseg_b;
   ba.tab = p->dtab;
   ba.g_bark = at<float>(ws, g.gbark);
   ba.kappa = at<float>(ws, g.kappa);
@@ -666,7 +718,7 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ba.spec = at<Cx<float>>(ws, g.spec);
   ba.out = g.resample ? RowSink{gx16, gx16 + batch * g.n16, g.n16, g.n16, (int)batch}
                       : RowSink{g_ref, g_deg, ld_gref, ld_gdeg, (int)batch};
-  ba.err = at<uint32_t>(ws, g.err);
+  ba.err = p->err;
   if (g.general) {
     SpecArgs sa{};
     sa.g = p->gen;
