@@ -798,7 +798,7 @@ def run_cuda(args):
     sys.stdout.flush()
     stdout_fd = os.dup(1)
     os.dup2(2, 1)
-    cores = numa_local_cores(local) if world > 1 else None
+    cores = numa_local_cores(local)
     if world > 1:
         import datetime
 

@@ -340,7 +340,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   PESQ_STAMP(g_phase_chain_fwd, 2);
 
   // pass B: frame power ratio, loudness, disturbance and the weighted norms
-  // (loss.py:217-255)
+  // (loss.py:217-255).  A warp takes its frames in chunks of up to 32: the
+  // band sums of every frame first, then the per-frame scalars (frame power
+  // ratio and its smoothing, h) one frame per lane, then the bands of each
+  // frame, and the frame distances again one frame per lane -- the same
+  // operations in the same order per frame as one frame at a time, with the
+  // divisions and transcendentals of the frames side by side.
   {
     const float bpr0 = b0.ok ? bpr_s[b0.k] : 0.0f, bpr1 = b1.ok ? bpr_s[b1.k] : 0.0f;
     const float sqW = tab.sqrt_total_width;
@@ -351,73 +356,97 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       taer = warp_sum((er0 > b0.th ? er0 : 0.0f) + (er1 > b1.th ? er1 : 0.0f));
       tad = warp_sum((D0 > b0.th ? D0 : 0.0f) + (D1 > b1.th ? D1 : 0.0f));
     };
-    float fpr0_prev = 0.0f;
+    // fpr0 of the frame before the warp's first (its smoothing partner)
+    float fpr0_carry = 0.0f;
     if (sl.w_lo < sl.w_hi && sl.w_lo > 0) {
       float ta, td;
       audible(sl.w_lo - 1, ta, td);
-      fpr0_prev = (ta + 5e3f) / (td + 5e3f);
+      fpr0_carry = (ta + 5e3f) / (td + 5e3f);
     }
-    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-      const float R0 = b0.ok ? s2r * fr[at(t, b0.k)] : 0.0f, R1 = b1.ok ? s2r * fr[at(t, b1.k)] : 0.0f;
-      const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
-      float taer, tad;
-      audible(t, taer, tad);
-      const float fpr0 = (taer + 5e3f) / (tad + 5e3f);
-      const float fpr1 = t == 0 ? fpr0 : fpr0 * 0.8f + fpr0_prev * 0.2f;
-      const float fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
-      const float h = exp2f_fast(0.04f * log2f_fast((taer + 1e5f) * 1e-7f));
-      Cell c0, c1;
-      c0.eval(b0, R0, D0, bpr0, fpr);
-      c1.eval(b1, R1, D1, bpr1, fpr);
-      if (p.cells) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const Band& b = half == 0 ? b0 : b1;
-          const Cell& c = half == 0 ? c0 : c1;
-          if (!b.ok) continue;
-          float co[4];
-          c.adjoint(b, co);
-          const int i = (t - sl.c_lo) * nb + b.k;
-          // shared memory block (bulk-stored after the pass) or straight to global
-          float* dst = cst ? cst + i : p.cells + ((int64_t)u * C + q) * cblk + i;
-          const int64_t fs = cst ? cblk : p.cell_stride;
-          dst[kCellDist * fs] = c.dist;
-          dst[kCellAsc * fs] = c.asc;
-          dst[kCellEdDist * fs] = co[0];
-          dst[kCellEdAsc * fs] = co[1];
-          dst[kCellErDist * fs] = co[2];
-          dst[kCellErAsc * fs] = co[3];
+    for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
+      const int nf = min(32, sl.w_hi - t_base);
+      // 1. total audible energies of each frame (lane j keeps frame j's)
+      float my_taer = 0.0f, my_tad = 0.0f;
+      for (int j = 0; j < nf; ++j) {
+        float taer, tad;
+        audible(t_base + j, taer, tad);
+        if (lane == j) {
+          my_taer = taer;
+          my_tad = tad;
         }
       }
-      float qs = 0.0f, qa = 0.0f;
-      if (b0.norm) {
-        const float v = b0.w * c0.dist;
-        qs = v * v;
-        qa = fabsf(b0.w * (c0.dist * c0.asc));
+      // 2. frame power ratio, its two-tap smoothing and clamp, h
+      const int tl = t_base + lane;
+      const float fpr0 = (my_taer + 5e3f) / (my_tad + 5e3f);
+      const float prev = __shfl_up_sync(0xffffffffu, fpr0, 1);
+      const float fpr0_prev = lane == 0 ? fpr0_carry : prev;
+      const float fpr1 = tl == 0 ? fpr0 : fpr0 * 0.8f + fpr0_prev * 0.2f;
+      const float my_fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
+      const float my_h = exp2f_fast(0.04f * log2f_fast((my_taer + 1e5f) * 1e-7f));
+      fpr0_carry = __shfl_sync(0xffffffffu, fpr0, nf - 1);
+      // 3. bands of each frame: loudness, disturbance, asymmetry, adjoint
+      //    coefficients, and the two norms (lane j keeps frame j's)
+      float my_qs = 0.0f, my_qa = 0.0f;
+      for (int j = 0; j < nf; ++j) {
+        const int t = t_base + j;
+        const float fpr = __shfl_sync(0xffffffffu, my_fpr, j);
+        const float R0 = b0.ok ? s2r * fr[at(t, b0.k)] : 0.0f, R1 = b1.ok ? s2r * fr[at(t, b1.k)] : 0.0f;
+        const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
+        Cell c0, c1;
+        c0.eval(b0, R0, D0, bpr0, fpr);
+        c1.eval(b1, R1, D1, bpr1, fpr);
+        if (p.cells) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const Band& b = half == 0 ? b0 : b1;
+            const Cell& c = half == 0 ? c0 : c1;
+            if (!b.ok) continue;
+            float co[4];
+            c.adjoint(b, co);
+            const int i = (t - sl.c_lo) * nb + b.k;
+            // shared memory block (bulk-stored after the pass) or straight to global
+            float* dst = cst ? cst + i : p.cells + ((int64_t)u * C + q) * cblk + i;
+            const int64_t fs = cst ? cblk : p.cell_stride;
+            dst[kCellDist * fs] = c.dist;
+            dst[kCellAsc * fs] = c.asc;
+            dst[kCellEdDist * fs] = co[0];
+            dst[kCellEdAsc * fs] = co[1];
+            dst[kCellErDist * fs] = co[2];
+            dst[kCellErAsc * fs] = co[3];
+          }
+        }
+        float qs = 0.0f, qa = 0.0f;
+        if (b0.norm) {
+          const float v = b0.w * c0.dist;
+          qs = v * v;
+          qa = fabsf(b0.w * (c0.dist * c0.asc));
+        }
+        if (b1.norm) {
+          const float v = b1.w * c1.dist;
+          qs = fmaf(v, v, qs);
+          qa += fabsf(b1.w * (c1.dist * c1.asc));
+        }
+        qs = warp_sum(qs);
+        qa = warp_sum(qa);
+        if (lane == j) {
+          my_qs = qs;
+          my_qa = qa;
+        }
       }
-      if (b1.norm) {
-        const float v = b1.w * c1.dist;
-        qs = fmaf(v, v, qs);
-        qa += fabsf(b1.w * (c1.dist * c1.asc));
+      // 4. frame distances, and the frame's saved state
+      if (lane < nf) {
+        const float sraw = sqW * sqrtf(my_qs);
+        const float araw = my_qa;
+        sv[p.lay.taer + tl] = my_taer;
+        sv[p.lay.tad + tl] = my_tad;
+        sv[p.lay.fpr0 + tl] = fpr0;
+        sv[p.lay.fpr1 + tl] = fpr1;
+        sv[p.lay.h + tl] = my_h;
+        sv[p.lay.sraw + tl] = sraw;
+        sv[p.lay.araw + tl] = araw;
+        sv[p.lay.sp + tl] = fminf(fmaxf(sraw, 1e-20f) / my_h, 45.0f);
+        sv[p.lay.ap + tl] = fminf(fmaxf(araw, 1e-20f) / my_h, 45.0f);
       }
-      qs = warp_sum(qs);
-      qa = warp_sum(qa);
-      const float sraw = sqW * sqrtf(qs);
-      const float araw = qa;
-      const float sp = fminf(fmaxf(sraw, 1e-20f) / h, 45.0f);
-      const float ap = fminf(fmaxf(araw, 1e-20f) / h, 45.0f);
-      if (lane == 0) {
-        sv[p.lay.taer + t] = taer;
-        sv[p.lay.tad + t] = tad;
-        sv[p.lay.fpr0 + t] = fpr0;
-        sv[p.lay.fpr1 + t] = fpr1;
-        sv[p.lay.h + t] = h;
-        sv[p.lay.sraw + t] = sraw;
-        sv[p.lay.araw + t] = araw;
-        sv[p.lay.sp + t] = sp;
-        sv[p.lay.ap + t] = ap;
-      }
-      fpr0_prev = fpr0;
     }
   }
   if (cst) {
@@ -673,41 +702,54 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   };
 
   // pass 1: norm / disturbance / loudness adjoint per band from the forward's
-  // coefficients; per-frame dL/dfpr
-  for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-    const float sraw = FS(kSraw, t);
-    float g_sraw, g_araw, g_h;
-    frame_grads(t, g_sraw, g_araw, g_h);
-    const float coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
-
-    float gfpr = 0.0f;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const Band& b = half == 0 ? b0 : b1;
-      if (!b.ok) continue;
-      const int64_t o = at(t, b.k);
-      const float D = s2d * fd[o];
-      float g_dist = 0.0f, g_asc = 0.0f;
-      if (b.norm) {
-        const float dist = CELL(kCellDist, t, b.k), asc = CELL(kCellAsc, t, b.k);
-        g_dist = coef * (b.w * b.w) * dist;
-        const float g_y = g_araw * b.w * sgnf(dist * asc);
-        g_dist += g_y * asc;
-        g_asc = g_y * dist;
-      }
-      const float g_ed = g_dist * CELL(kCellEdDist, t, b.k) + g_asc * CELL(kCellEdAsc, t, b.k);
-      const float g_er = g_dist * CELL(kCellErDist, t, b.k) + g_asc * CELL(kCellErAsc, t, b.k);
-      gfpr = fmaf(g_ed, D, gfpr);
-      gd[o] = g_ed;
-      gr[o] = g_er;
+  // coefficients; per-frame dL/dfpr.  The per-frame scalars are evaluated one
+  // frame per lane for up to 32 frames at a time, then each frame's bands.
+  for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
+    const int nf = min(32, sl.w_hi - t_base);
+    float l_coef = 0.0f, l_garaw = 0.0f, l_gh = 0.0f, l_gfpr = 0.0f;
+    if (lane < nf) {
+      const int t = t_base + lane;
+      const float sraw = FS(kSraw, t);
+      float g_sraw;
+      frame_grads(t, g_sraw, l_garaw, l_gh);
+      l_coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
     }
-    gfpr = warp_sum(gfpr);
-    if (lane == 0) {
-      gf[t] = gfpr;
-      gf[T + t] = g_h;
+    for (int j = 0; j < nf; ++j) {
+      const int t = t_base + j;
+      const float coef = __shfl_sync(0xffffffffu, l_coef, j);
+      const float g_araw = __shfl_sync(0xffffffffu, l_garaw, j);
+
+      float gfpr = 0.0f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const Band& b = half == 0 ? b0 : b1;
+        if (!b.ok) continue;
+        const int64_t o = at(t, b.k);
+        const float D = s2d * fd[o];
+        float g_dist = 0.0f, g_asc = 0.0f;
+        if (b.norm) {
+          const float dist = CELL(kCellDist, t, b.k), asc = CELL(kCellAsc, t, b.k);
+          g_dist = coef * (b.w * b.w) * dist;
+          const float g_y = g_araw * b.w * sgnf(dist * asc);
+          g_dist += g_y * asc;
+          g_asc = g_y * dist;
+        }
+        const float g_ed = g_dist * CELL(kCellEdDist, t, b.k) + g_asc * CELL(kCellEdAsc, t, b.k);
+        const float g_er = g_dist * CELL(kCellErDist, t, b.k) + g_asc * CELL(kCellErAsc, t, b.k);
+        gfpr = fmaf(g_ed, D, gfpr);
+        gd[o] = g_ed;
+        gr[o] = g_er;
+      }
+      gfpr = warp_sum(gfpr);
+      if (lane == j) l_gfpr = gfpr;
+    }
+    if (lane < nf) {
+      const int t = t_base + lane;
+      gf[t] = l_gfpr;
+      gf[T + t] = l_gh;
       if (p.staged) {
-        gfs[t - sl.c_lo] = gfpr;
-        gfs[fpitch + t - sl.c_lo] = g_h;
+        gfs[t - sl.c_lo] = l_gfpr;
+        gfs[fpitch + t - sl.c_lo] = l_gh;
       }
     }
   }
@@ -725,32 +767,44 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       const float g = (p.staged && tt < sl.c_hi) ? gfs[tt - sl.c_lo] : __ldcg(gf + tt);
       return (f1 >= 3e-4f && f1 <= 5.0f) ? g : 0.0f;
     };
-    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-      const float g1 = clamp_pass(t);
-      const float g1n = t + 1 < T ? clamp_pass(t + 1) : 0.0f;
-      const float g_fpr0 = (t == 0 ? g1 : 0.8f * g1) + 0.2f * g1n;
-      const float taer = FS(kTaer, t), tad = FS(kTad, t);
-      const float fpr0 = FS(kFpr0, t), h = FS(kH, t);
-      const float fpr = fminf(fmaxf(FS(kFpr1, t), 3e-4f), 5.0f);
-      const float g_h = p.staged ? gfs[fpitch + t - sl.c_lo] : __ldcg(gf + T + t);
-      const float g_taer = g_fpr0 / (tad + 5e3f) + g_h * 0.04f * h / (taer + 1e5f);
-      const float g_tad = -g_fpr0 * fpr0 / (tad + 5e3f);
+    for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
+      const int nf = min(32, sl.w_hi - t_base);
+      // per-frame scalars, one frame per lane
+      float l_gtaer = 0.0f, l_gtad = 0.0f, l_fpr = 0.0f;
+      if (lane < nf) {
+        const int t = t_base + lane;
+        const float g1 = clamp_pass(t);
+        const float g1n = t + 1 < T ? clamp_pass(t + 1) : 0.0f;
+        const float g_fpr0 = (t == 0 ? g1 : 0.8f * g1) + 0.2f * g1n;
+        const float taer = FS(kTaer, t), tad = FS(kTad, t);
+        const float fpr0 = FS(kFpr0, t), h = FS(kH, t);
+        l_fpr = fminf(fmaxf(FS(kFpr1, t), 3e-4f), 5.0f);
+        const float g_h = p.staged ? gfs[fpitch + t - sl.c_lo] : __ldcg(gf + T + t);
+        l_gtaer = g_fpr0 / (tad + 5e3f) + g_h * 0.04f * h / (taer + 1e5f);
+        l_gtad = -g_fpr0 * fpr0 / (tad + 5e3f);
+      }
+      for (int j = 0; j < nf; ++j) {
+        const int t = t_base + j;
+        const float fpr = __shfl_sync(0xffffffffu, l_fpr, j);
+        const float g_taer = __shfl_sync(0xffffffffu, l_gtaer, j);
+        const float g_tad = __shfl_sync(0xffffffffu, l_gtad, j);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const Band& b = half == 0 ? b0 : b1;
-        if (!b.ok) continue;
-        const int64_t o = at(t, b.k);
-        const float R = s2r * fr[o], D = s2d * fd[o];
-        const float bpr = half == 0 ? bpr0 : bpr1;
-        const float er = bpr * R;
-        const float g_er = gr[o] + (er > b.th ? g_taer : 0.0f);
-        gr[o] = g_er * bpr;
-        const double contrib = (double)g_er * (double)R;
-        if (half == 0)
-          acc0 += contrib;
-        else
-          acc1 += contrib;
-        gd[o] = gd[o] * fpr + (D > b.th ? g_tad : 0.0f);
+        for (int half = 0; half < 2; ++half) {
+          const Band& b = half == 0 ? b0 : b1;
+          if (!b.ok) continue;
+          const int64_t o = at(t, b.k);
+          const float R = s2r * fr[o], D = s2d * fd[o];
+          const float bpr = half == 0 ? bpr0 : bpr1;
+          const float er = bpr * R;
+          const float g_er = gr[o] + (er > b.th ? g_taer : 0.0f);
+          gr[o] = g_er * bpr;
+          const double contrib = (double)g_er * (double)R;
+          if (half == 0)
+            acc0 += contrib;
+          else
+            acc1 += contrib;
+          gd[o] = gd[o] * fpr + (D > b.th ? g_tad : 0.0f);
+        }
       }
     }
     wpart[warp][lane] = acc0;
