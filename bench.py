@@ -65,8 +65,9 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2 (8 x 8 s, the headline) or cfg5 (512 x 3 s, larger than L2)")
     ap.add_argument("--skip-cpu", action="store_true", help="leave out the CPU baseline leg")
-    ap.add_argument("--op", choices=["iir", "resample", "geometry", "triton-reference"], default=None,
-                    help="time only a standalone op on its large case (one JSON line; for profiling)")
+    ap.add_argument("--op", choices=["iir", "resample", "geometry", "triton-reference", "step"], default=None,
+                    help="time only a standalone op on its large case, or (step) the workload's eager "
+                         "fwd+bwd W + K times (one JSON line; the target of single-kernel profiler captures)")
     args = ap.parse_args()
     global BATCH, SECONDS
     BATCH, SECONDS = WORKLOADS[args.workload]
@@ -496,13 +497,45 @@ def measure_configs(dev, flush, steps=10):
     from triton_pesq_b200 import PesqLossCuda
     from triton_pesq_b200.signals import workload
 
+    import torch
+
+    from triton_pesq_b200 import ResampleCuda
+
     out = {}
     for name, keep, secs in (("cfg1", 1, 1.0), ("cfg3", 16, 4.0), ("cfg4_per_gpu", 8, 10.0), ("cfg5", 512, 3.0)):
-        ref_c, deg_c, sr = workload(name.split("_")[0], seed=0)
-        ms = _graphed_step_ms(PesqLossCuda(1.0, sample_rate=sr), ref_c[:keep].to(dev), deg_c[:keep].to(dev), flush,
-                              steps)
+        ref_c, deg_c, sr = workload(name.split("_")[0], seed=0, rows=range(keep))
+        model = PesqLossCuda(1.0, sample_rate=sr)
+        ref, deg = ref_c.to(dev), deg_c.to(dev)
+        ms = _graphed_step_ms(model, ref, deg, flush, steps)
         out[name] = {"batch": keep, "seconds": secs, "sample_rate": sr, "ms_per_step": ms,
                      "utterance_seconds_per_s": keep * secs / (ms * 1e-3)}
+        if sr != 16000:
+            # the stages of the resampled step (front and back include the
+            # resampler and its adjoint), and the resampler alone on the
+            # same rows (2B forward, B gradient rows for the adjoint)
+            out[name]["stages_us"] = stage_times(model, ref, deg, dev)
+            rs = ResampleCuda(sr, 16000).to(dev)
+            handle = rs._handle(dev)
+            both = torch.cat([ref, deg])
+            y = torch.ops.pesq_cuda.resample(handle, both)
+            g = torch.randn_like(y[:keep])
+            stream = torch.cuda.current_stream(dev)
+
+            def timed(fn, n=20):
+                for _ in range(3):
+                    fn()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(n):
+                    fn()
+                b.record(stream)
+                torch.cuda.synchronize()
+                return 1e3 * a.elapsed_time(b) / n
+
+            out[name]["resample_us"] = {
+                "forward_2B_rows": timed(lambda: torch.ops.pesq_cuda.resample(handle, both)),
+                "adjoint_B_rows": timed(lambda: torch.ops.pesq_cuda.resample_adjoint(handle, g, ref.shape[1])),
+            }
     return out
 
 
@@ -1274,6 +1307,27 @@ def run_op(args):
 
     dev = torch.device("cuda", 0)
     peak, _ = measured_peaks()
+    if args.op == "step":
+        from triton_pesq_b200 import PesqLossCuda
+        from triton_pesq_b200.signals import workload
+
+        ref_c, deg_c, sr = workload(args.workload, seed=0)
+        ref, deg = ref_c.to(dev), deg_c.to(dev).requires_grad_(True)
+        model = PesqLossCuda(1.0, sample_rate=sr)
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        times = []
+        for k in range(args.warmup + args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            loss = model(ref, deg)
+            torch.autograd.grad(loss.sum(), [deg])
+            b.record()
+            b.synchronize()
+            if k >= args.warmup:
+                times.append(a.elapsed_time(b))
+        print(json.dumps({"op": "step", "workload": args.workload, "eager_ms_per_step": statistics.median(times)}))
+        return
     if args.op == "triton-reference":
         flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
         try:

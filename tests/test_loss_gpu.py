@@ -321,3 +321,26 @@ def test_loss_sum_of_the_chain_kernel(cuda_device, batch):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(static["pair"], pair)
+
+
+def test_second_device_from_the_autograd_thread(cuda_device):
+    """A plan on cuda:1 while cuda:0 is current: the forward and the backward
+    (run by autograd's worker thread for that device) use the plan's device,
+    and the results equal those of cuda:0 bit for bit (the reference binds
+    the context for its autograd thread, triton_ops/iir.py:945-963)."""
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ref = speech_like(2, 16000, 16000, seed=97)
+    deg = add_noise(ref, 6.0, seed=98)
+    model = PesqLossCuda(1.0, sample_rate=16000)
+    out = {}
+    for index in (0, 1):
+        dev = torch.device("cuda", index)
+        r, d = ref.to(dev), deg.to(dev).requires_grad_(True)
+        with torch.cuda.device(0):  # the current device stays cuda:0
+            loss = model(r, d)
+            loss.sum().backward()
+        out[index] = (loss.detach().cpu(), d.grad.cpu())
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])

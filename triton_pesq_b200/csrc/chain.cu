@@ -281,19 +281,42 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   // pass A: silent frames (loss.py:206) and band sums of audible power over
   // the non-silent frames (loudness.py:297-320)
   {
+    // four frames at a time: their band sums go through the warp's shuffle
+    // tree side by side (the same tree per frame as warp_sum), then the
+    // frames are accumulated in order
+    constexpr int kG = 4;
     double ar0 = 0.0, ar1 = 0.0, ad0 = 0.0, ad1 = 0.0;
-    for (int t = sl.w_lo; t < sl.w_hi; ++t) {
-      const float R0 = b0.ok ? s2r * fr[at(t, b0.k)] : 0.0f, R1 = b1.ok ? s2r * fr[at(t, b1.k)] : 0.0f;
-      const float D0 = b0.ok ? s2d * fd[at(t, b0.k)] : 0.0f, D1 = b1.ok ? s2d * fd[at(t, b1.k)] : 0.0f;
-      const float a0 = R0 > b0.th100 ? R0 : 0.0f, a1 = R1 > b1.th100 ? R1 : 0.0f;
-      const float tot = warp_sum(a0 + a1);
-      const bool keep = !(tot < 1e7f);
-      if (lane == 0) sv[p.lay.keep + t] = keep ? 1.0f : 0.0f;
-      if (keep) {
-        ar0 += a0;
-        ar1 += a1;
-        ad0 += D0 > b0.th100 ? D0 : 0.0f;
-        ad1 += D1 > b1.th100 ? D1 : 0.0f;
+    for (int t = sl.w_lo; t < sl.w_hi; t += kG) {
+      float a0[kG], a1[kG], e0[kG], e1[kG], tot[kG];
+#pragma unroll
+      for (int i = 0; i < kG; ++i) {
+        const bool v = t + i < sl.w_hi;
+        const float R0 = v && b0.ok ? s2r * fr[at(t + i, b0.k)] : 0.0f;
+        const float R1 = v && b1.ok ? s2r * fr[at(t + i, b1.k)] : 0.0f;
+        const float D0 = v && b0.ok ? s2d * fd[at(t + i, b0.k)] : 0.0f;
+        const float D1 = v && b1.ok ? s2d * fd[at(t + i, b1.k)] : 0.0f;
+        a0[i] = R0 > b0.th100 ? R0 : 0.0f;
+        a1[i] = R1 > b1.th100 ? R1 : 0.0f;
+        e0[i] = D0 > b0.th100 ? D0 : 0.0f;
+        e1[i] = D1 > b1.th100 ? D1 : 0.0f;
+        tot[i] = a0[i] + a1[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int i = 0; i < kG; ++i) tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], o);
+      }
+#pragma unroll
+      for (int i = 0; i < kG; ++i) {
+        if (t + i >= sl.w_hi) break;
+        const bool keep = !(tot[i] < 1e7f);
+        if (lane == 0) sv[p.lay.keep + t + i] = keep ? 1.0f : 0.0f;
+        if (keep) {
+          ar0 += a0[i];
+          ar1 += a1[i];
+          ad0 += e0[i];
+          ad1 += e1[i];
+        }
       }
     }
     wpr[warp][lane] = ar0;
@@ -488,13 +511,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   // RMS over the windows (rank 0), then MOS and loss (loss.py:289-297, 320-322)
   if (q == 0 && warp < 2) {
     const int64_t src = warp == 0 ? p.lay.psqm_s : p.lay.psqm_a;
-    float mx = 0.0f;
-    for (int l = lane; l < L; l += 32) mx = fmaxf(mx, __ldcg(sv + src + l));
+    // the windows of two strides of the warp stay in registers between the
+    // maximum and the sum (one memory round trip for up to 64 windows)
+    const float w0 = lane < L ? __ldcg(sv + src + lane) : 0.0f;
+    const float w1 = lane + 32 < L ? __ldcg(sv + src + lane + 32) : 0.0f;
+    float mx = fmaxf(w0, w1);
+    for (int l = lane + 64; l < L; l += 32) mx = fmaxf(mx, __ldcg(sv + src + l));
     mx = warp_max(mx);
     const float sc = mx > 0.0f ? mx : 1.0f;
     float acc = 0.0f;
     for (int l = lane; l < L; l += 32) {
-      const float v = __ldcg(sv + src + l) / sc;
+      const float v = (l < lane + 64 ? (l < 32 ? w0 : w1) : __ldcg(sv + src + l)) / sc;
       acc = fmaf(v, v, acc);
     }
     acc = warp_sum(acc);
