@@ -23,6 +23,8 @@ namespace pesq {
 
 constexpr int kChainThreads = 512;
 constexpr int kChainWarps = kChainThreads / 32;
+// Largest slice (frames of a CTA) whose pass B runs cell by cell.
+constexpr int kCellSlice = 128;
 // Dynamic shared memory the staged kernels may use.
 constexpr size_t kChainSmemLimit = 180 * 1024;
 
@@ -215,6 +217,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
   __shared__ double band_tot[2][kMaxBands];
   __shared__ float bpr_s[kMaxBands];
   __shared__ float s2s[2];
+  __shared__ float fpr_s[kCellSlice], h_s[kCellSlice];  // per frame of the slice (cell-wise pass B)
 
   const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
   const int u = blockIdx.x / C;
@@ -386,6 +389,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       audible(sl.w_lo - 1, ta, td);
       fpr0_carry = (ta + 5e3f) / (td + 5e3f);
     }
+    // With the adjoint coefficients staged in shared memory, the bands of the
+    // slice are spread over all threads of the CTA, a (frame, band) cell at a
+    // time, between a per-frame pass that sets the frame power ratios and one
+    // that forms the norms from the staged disturbances; each cell and each
+    // norm is evaluated exactly as below, so the results are the same.
+    const bool by_cell = cst != nullptr && sl.c_hi - sl.c_lo <= kCellSlice;
     for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
       const int nf = min(32, sl.w_hi - t_base);
       // 1. total audible energies of each frame (lane j keeps frame j's)
@@ -407,6 +416,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
       const float my_fpr = fminf(fmaxf(fpr1, 3e-4f), 5.0f);
       const float my_h = exp2f_fast(0.04f * log2f_fast((my_taer + 1e5f) * 1e-7f));
       fpr0_carry = __shfl_sync(0xffffffffu, fpr0, nf - 1);
+      if (by_cell) {
+        if (lane < nf) {
+          fpr_s[tl - sl.c_lo] = my_fpr;
+          h_s[tl - sl.c_lo] = my_h;
+          sv[p.lay.taer + tl] = my_taer;
+          sv[p.lay.tad + tl] = my_tad;
+          sv[p.lay.fpr0 + tl] = fpr0;
+          sv[p.lay.fpr1 + tl] = fpr1;
+          sv[p.lay.h + tl] = my_h;
+        }
+        continue;
+      }
       // 3. bands of each frame: loudness, disturbance, asymmetry, adjoint
       //    coefficients, and the two norms (lane j keeps frame j's)
       float my_qs = 0.0f, my_qa = 0.0f;
@@ -469,6 +490,75 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
         sv[p.lay.araw + tl] = araw;
         sv[p.lay.sp + tl] = fminf(fmaxf(sraw, 1e-20f) / my_h, 45.0f);
         sv[p.lay.ap + tl] = fminf(fmaxf(araw, 1e-20f) / my_h, 45.0f);
+      }
+    }
+    if (by_cell) {
+      __syncthreads();
+      // cells (t, k) of the slice, k fastest, over all threads
+      const int ncell = (sl.c_hi - sl.c_lo) * nb;
+      int ct = threadIdx.x / nb, ck = threadIdx.x - ct * nb;
+      const int dt = kChainThreads / nb, dk = kChainThreads - dt * nb;
+      for (int c = threadIdx.x; c < ncell; c += kChainThreads) {
+        Band b;
+        b.load(tab, ck);
+        const int t = sl.c_lo + ct;
+        const float R = s2r * fr[at(t, ck)], D = s2d * fd[at(t, ck)];
+        Cell cl;
+        cl.eval(b, R, D, bpr_s[ck], fpr_s[ct]);
+        float co[4];
+        cl.adjoint(b, co);
+        float* dst = cst + c;
+        dst[kCellDist * cblk] = cl.dist;
+        dst[kCellAsc * cblk] = cl.asc;
+        dst[kCellEdDist * cblk] = co[0];
+        dst[kCellEdAsc * cblk] = co[1];
+        dst[kCellErDist * cblk] = co[2];
+        dst[kCellErAsc * cblk] = co[3];
+        ct += dt;
+        ck += dk;
+        if (ck >= nb) {
+          ck -= nb;
+          ++ct;
+        }
+      }
+      __syncthreads();
+      // the two norms of each frame from the staged disturbances (lane j
+      // keeps frame j's), then the frame distances
+      for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
+        const int nf = min(32, sl.w_hi - t_base);
+        float my_qs = 0.0f, my_qa = 0.0f;
+        for (int j = 0; j < nf; ++j) {
+          const int i = (t_base + j - sl.c_lo) * nb;
+          float qs = 0.0f, qa = 0.0f;
+          if (b0.norm) {
+            const float dist = cst[kCellDist * cblk + i + b0.k], asc = cst[kCellAsc * cblk + i + b0.k];
+            const float v = b0.w * dist;
+            qs = v * v;
+            qa = fabsf(b0.w * (dist * asc));
+          }
+          if (b1.norm) {
+            const float dist = cst[kCellDist * cblk + i + b1.k], asc = cst[kCellAsc * cblk + i + b1.k];
+            const float v = b1.w * dist;
+            qs = fmaf(v, v, qs);
+            qa += fabsf(b1.w * (dist * asc));
+          }
+          qs = warp_sum(qs);
+          qa = warp_sum(qa);
+          if (lane == j) {
+            my_qs = qs;
+            my_qa = qa;
+          }
+        }
+        const int tl = t_base + lane;
+        if (lane < nf) {
+          const float h = h_s[tl - sl.c_lo];
+          const float sraw = sqW * sqrtf(my_qs);
+          const float araw = my_qa;
+          sv[p.lay.sraw + tl] = sraw;
+          sv[p.lay.araw + tl] = araw;
+          sv[p.lay.sp + tl] = fminf(fmaxf(sraw, 1e-20f) / h, 45.0f);
+          sv[p.lay.ap + tl] = fminf(fmaxf(araw, 1e-20f) / h, 45.0f);
+        }
       }
     }
   }
@@ -580,6 +670,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   __shared__ float gm_r[kMaxBands], gm_d[kMaxBands];
   __shared__ double kap[kChainWarps][2];
   __shared__ double kpart[2];
+  __shared__ float coef_s[kCellSlice], garaw_s[kCellSlice];  // per frame of the slice (cell-wise pass 1)
 
   const int C = (int)cluster_nctarank(), q = (int)cluster_ctarank();
   const int u = blockIdx.x / C;
@@ -730,7 +821,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
 
   // pass 1: norm / disturbance / loudness adjoint per band from the forward's
   // coefficients; per-frame dL/dfpr.  The per-frame scalars are evaluated one
-  // frame per lane for up to 32 frames at a time, then each frame's bands.
+  // frame per lane for up to 32 frames at a time, then each frame's bands --
+  // or, with the slice staged, the cells (frame, band) of the slice over all
+  // threads, and the per-frame sums after them (the same operations, so the
+  // same results).
+  const bool by_cell = cells_staged && sl.c_hi - sl.c_lo <= kCellSlice;
   for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
     const int nf = min(32, sl.w_hi - t_base);
     float l_coef = 0.0f, l_garaw = 0.0f, l_gh = 0.0f, l_gfpr = 0.0f;
@@ -740,6 +835,16 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       float g_sraw;
       frame_grads(t, g_sraw, l_garaw, l_gh);
       l_coef = sraw > 0.0f ? g_sraw * W / sraw : 0.0f;
+    }
+    if (by_cell) {
+      if (lane < nf) {
+        const int t = t_base + lane;
+        coef_s[t - sl.c_lo] = l_coef;
+        garaw_s[t - sl.c_lo] = l_garaw;
+        gf[T + t] = l_gh;
+        gfs[fpitch + t - sl.c_lo] = l_gh;
+      }
+      continue;
     }
     for (int j = 0; j < nf; ++j) {
       const int t = t_base + j;
@@ -777,6 +882,58 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
       if (p.staged) {
         gfs[t - sl.c_lo] = l_gfpr;
         gfs[fpitch + t - sl.c_lo] = l_gh;
+      }
+    }
+  }
+  if (by_cell) {
+    __syncthreads();
+    const int ncell = (sl.c_hi - sl.c_lo) * nb;
+    int ct = threadIdx.x / nb, ck = threadIdx.x - ct * nb;
+    const int dt = kChainThreads / nb, dk = kChainThreads - dt * nb;
+    for (int c = threadIdx.x; c < ncell; c += kChainThreads) {
+      const int t = sl.c_lo + ct;
+      const int64_t o = at(t, ck);
+      const float w = tab.width[ck];
+      float g_dist = 0.0f, g_asc = 0.0f;
+      if (ck >= 1) {
+        const float coef = coef_s[ct], g_araw = garaw_s[ct];
+        const float dist = CELL(kCellDist, t, ck), asc = CELL(kCellAsc, t, ck);
+        g_dist = coef * (w * w) * dist;
+        const float g_y = g_araw * w * sgnf(dist * asc);
+        g_dist += g_y * asc;
+        g_asc = g_y * dist;
+      }
+      gd[o] = g_dist * CELL(kCellEdDist, t, ck) + g_asc * CELL(kCellEdAsc, t, ck);
+      gr[o] = g_dist * CELL(kCellErDist, t, ck) + g_asc * CELL(kCellErAsc, t, ck);
+      ct += dt;
+      ck += dk;
+      if (ck >= nb) {
+        ck -= nb;
+        ++ct;
+      }
+    }
+    __syncthreads();
+    // dL/dfpr of each frame: sum over bands of g_ed * D (lane j keeps frame j's)
+    for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
+      const int nf = min(32, sl.w_hi - t_base);
+      float l_gfpr = 0.0f;
+      for (int j = 0; j < nf; ++j) {
+        const int t = t_base + j;
+        float gfpr = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const Band& b = half == 0 ? b0 : b1;
+          if (!b.ok) continue;
+          const int64_t o = at(t, b.k);
+          gfpr = fmaf(gd[o], s2d * fd[o], gfpr);
+        }
+        gfpr = warp_sum(gfpr);
+        if (lane == j) l_gfpr = gfpr;
+      }
+      if (lane < nf) {
+        const int t = t_base + lane;
+        gf[t] = l_gfpr;
+        gfs[t - sl.c_lo] = l_gfpr;
       }
     }
   }
