@@ -33,6 +33,7 @@ reference is not installed) on this host's cores instead.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -959,6 +960,23 @@ def run_cuda(args):
         b.synchronize()
         h2d.append(a.elapsed_time(b))
     h2d_gbs = 2 * ref.numel() * 4 / (statistics.median(h2d) * 1e-3) / 1e9
+    # the same copies on every rank at once: the box's host-to-device ceiling
+    # for this many GPUs (aggregate over the ranks, max-over-ranks time)
+    h2d_all = None
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(10):
+            with torch.no_grad():
+                sets[0][0].copy_(ref_h, non_blocking=True)
+                sets[0][1].copy_(deg_h, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        t_all = torch.tensor([a.elapsed_time(b)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+        h2d_all = world * 10 * 2 * ref.numel() * 4 / (float(t_all.item()) * 1e-3) / 1e9
 
     serial_ms = []
     for k in range(max(5, args.steps // 5)):
@@ -1047,8 +1065,12 @@ def run_cuda(args):
     geometries = measure_geometries(dev, flush) if single else None
 
     if world > 1:
-        # graphs that hold NCCL calls are released before the process group
-        del graph, sets
+        # every graph that holds an NCCL call is released before the process
+        # group (its teardown waits for them): the headline step, both e2e
+        # input sets, and the loop variable that still names one of them
+        del graph, sets, g_step
+        gc.collect()
+        torch.cuda.synchronize()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -1092,6 +1114,7 @@ def run_cuda(args):
             "serial_ms_per_step": statistics.median(serial_ms),
             "graphed_module_ms_per_step": module_ms_per_step,
             "h2d_gbs_alone": h2d_gbs,
+            "h2d_gbs_all_ranks_aggregate": h2d_all,
             "numa_local_cores": f"{len(cores)} cores" if cores else None,
         },
         # front + chain forward, chain adjoint + align + back per step

@@ -86,3 +86,45 @@ def test_signal_stages_need_a_gpu():
     loss = PesqLossCuda(1.0, sample_rate=16000)
     with pytest.raises(RuntimeError):
         loss.align_level(torch.randn(1, 4000))
+
+
+def test_native_handles_are_released_after_the_last_reference():
+    """A plan / resampler handle lives while its module or an autograd node
+    holds its owner, and is released once; a released plan's cached
+    workspace offsets go with it (a later plan may reuse the address)."""
+    import gc
+
+    from triton_pesq_b200 import _lib
+    from triton_pesq_b200 import loss as loss_mod
+
+    released = []
+    owner = _lib.Owned(1234, released.append)
+    holders = [owner]
+    del owner
+    gc.collect()
+    assert released == []
+    holders.clear()
+    gc.collect()
+    assert released == [1234]
+
+    calls = []
+    keys = [(77, 8, 16000, 2), (78, 8, 16000, 2)]
+    saved_destroy = _lib.destroy_plan
+    try:
+        _lib.destroy_plan = calls.append
+        for k, key in enumerate(keys):
+            loss_mod._SUM_OFFSETS[key] = 256 * (k + 1)
+        loss_mod._release_plan(77)
+        assert calls == [77]
+        assert keys[0] not in loss_mod._SUM_OFFSETS
+        assert loss_mod._SUM_OFFSETS[keys[1]] == 512
+    finally:
+        _lib.destroy_plan = saved_destroy
+        loss_mod._SUM_OFFSETS.pop(keys[1], None)
+
+    model = PesqLossCuda(1.0, sample_rate=44100)
+    model._plans[0], model._plan_owners[5] = 5, _lib.Owned(5, lambda h: None)
+    state = model.__getstate__()
+    assert state["_plans"] == {} and state["_plan_owners"] == {}
+    rs = ResampleCuda(44100, 16000)
+    assert rs.__getstate__()["_owners"] == {}

@@ -344,3 +344,37 @@ def test_second_device_from_the_autograd_thread(cuda_device):
         out[index] = (loss.detach().cpu(), d.grad.cpu())
     assert torch.equal(out[0][0], out[1][0])
     assert torch.equal(out[0][1], out[1][1])
+
+
+def test_backward_after_the_module_is_dropped(cuda_device):
+    """The autograd graph keeps the plan alive: a module evaluated once and
+    dropped (its plan released with it otherwise) still runs its backward,
+    and so does a dropped resampler's double backward."""
+    import gc
+
+    from triton_pesq_b200 import ResampleCuda
+
+    ref = speech_like(2, 16000, 16000, seed=91).to(cuda_device)
+    deg = add_noise(ref.cpu(), 5.0, seed=92).to(cuda_device).requires_grad_(True)
+    keep = PesqLossCuda(1.0, sample_rate=16000)
+    want = keep(ref, deg)
+    (g_want,) = torch.autograd.grad(want.sum(), [deg])
+    loss = PesqLossCuda(1.0, sample_rate=16000)(ref, deg)
+    gc.collect()
+    (g,) = torch.autograd.grad(loss.sum(), [deg])
+    assert torch.equal(loss, want)
+    assert torch.equal(g, g_want)
+
+    x = torch.randn(2, 4410, device=cuda_device, requires_grad=True)
+    rs = ResampleCuda(44100, 16000)
+    y_want = rs(x)
+    (gx_want,) = torch.autograd.grad(y_want.square().sum(), [x], create_graph=True)
+    (ggx_want,) = torch.autograd.grad(gx_want.sum(), [x])
+    y = ResampleCuda(44100, 16000)(x)
+    gc.collect()
+    (gx,) = torch.autograd.grad(y.square().sum(), [x], create_graph=True)
+    gc.collect()
+    (ggx,) = torch.autograd.grad(gx.sum(), [x])
+    assert torch.equal(y, y_want)
+    assert torch.equal(gx, gx_want)
+    assert torch.equal(ggx, ggx_want)

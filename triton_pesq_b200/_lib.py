@@ -409,6 +409,33 @@ def destroy_plan(handle: int) -> None:
         _lib.pesq_plan_destroy(ctypes.c_void_p(handle))
 
 
+def destroy_resampler(handle: int) -> None:
+    if handle and _lib is not None:
+        _lib.pesq_resampler_destroy(ctypes.c_void_p(handle))
+
+
+class Owned:
+    """A native handle (plan, resampler) owned from Python.
+
+    The handle is released when the last reference goes: the module's table of
+    per-device handles holds one, and every autograd node that may still run a
+    backward with the handle holds another, so a module that is dropped right
+    after its forward (``PesqLossCuda(...)(ref, deg).sum().backward()``) keeps
+    its plan until the backward is done.  ``release(handle)`` runs once."""
+
+    def __init__(self, handle: int, release):
+        self.handle = int(handle)
+        self._release = release
+
+    def __del__(self):
+        handle, self.handle = self.handle, 0
+        if handle:
+            try:
+                self._release(handle)
+            except Exception:  # pragma: no cover - interpreter shutdown
+                pass
+
+
 def query_shape(handle: int, n_src: int):
     shape = Shape()
     check(library().pesq_query_shape(ctypes.c_void_p(handle), int(n_src), ctypes.byref(shape)), "pesq_query_shape")

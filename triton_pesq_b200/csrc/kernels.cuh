@@ -273,6 +273,21 @@ struct ResampleArgs {
   int fwd_staged, adj_staged;  // shared memory kernels (the tables fit)
   int tpitch;                  // odd row pitch of the staged taps
   uint32_t inv_os, inv_ns;     // ceil(2^32 / orig_step), ceil(2^32 / new_step): 32-bit divisions
+  // float64 tensor-core forward (ResampleMma): 8 x 8 output tiles of
+  // super-frames x consecutive super-phases
+  const double* mma_b;  // B fragments [blocks][ksteps][32 lanes]
+  const int* mma_s;     // first sample of each block's tap span in a super-frame window [blocks]
+  int fwd_mma;          // 0, or the tile k-steps (taps / 4) of the kernel to run
+  int mma_os, mma_ns;   // input samples / outputs per super-frame
+  int mma_blocks;       // super-phases / 8
+  int mma_span, mma_pitch, mma_frames, mma_warps;  // staged window: samples per super-frame, row pitch, rows; warps
+  // float64 tensor-core adjoint: 8 x 8 tiles of super-frames x consecutive
+  // residues, K = the block's (super-frame offset, super-phase) entries
+  const double* amma_b;  // B fragments [k-steps of all blocks][32 lanes]
+  const int* amma_a;     // A offsets in the staged window [k-steps][4]: -offset * pitch + super-phase
+  const int* amma_off;   // first k-step of each block [blocks + 1]
+  int adj_mma;           // tensor-core adjoint available
+  int amma_os, amma_ns, amma_blocks, amma_pitch, amma_frames, amma_warps, amma_maxdl;
 };
 
 // Device tables of one polyphase resampler: the compact nonzero taps of every
@@ -289,6 +304,23 @@ struct ResampleTables {
   float* adj_tap = nullptr;     // [max_entries][orig_step]
   int max_entries = 0, max_dl = 0;
   bool fwd_staged = false, adj_staged = false;
+  // float64 tensor-core forward: G = 8 / gcd(new_step, 8) frames form a
+  // super-frame of G * new_step outputs (a multiple of 8), whose super-phases
+  // go in blocks of 8; each block's taps, shifted to a common first sample,
+  // are the B operand of an m8n8k4 tile (zero outside each phase's span)
+  double* mma_b = nullptr;  // [mma_blocks][fwd_mma][32]
+  int* mma_s = nullptr;     // [mma_blocks]
+  int fwd_mma = 0, mma_os = 0, mma_ns = 0, mma_blocks = 0;
+  int mma_span = 0, mma_pitch = 0, mma_frames = 0, mma_warps = 0;
+  // float64 tensor-core adjoint: G' frames (G' = 1 for orig_step >= 64, else
+  // 8 / gcd(orig_step, 8)) form a super-frame of G' * orig_step input samples
+  // (residues), taken in blocks of 8; a block's K operand lists the
+  // (super-frame offset, super-phase) pairs whose taps reach any of its residues
+  double* amma_b = nullptr;  // [k-steps][32]
+  int* amma_a = nullptr;     // [k-steps][4]
+  int* amma_off = nullptr;   // [amma_blocks + 1]
+  bool adj_mma = false;
+  int amma_os = 0, amma_ns = 0, amma_blocks = 0, amma_pitch = 0, amma_frames = 0, amma_warps = 0, amma_maxdl = 0;
 };
 // Allows the staged resampler kernels their shared memory (once per process).
 cudaError_t configure_resample();

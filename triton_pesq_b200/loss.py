@@ -29,7 +29,16 @@ from .tables import ALIGN_DIV, ALIGN_PAD, ALIGN_TARGET, PlanConfig
 __all__ = ["PesqLossCuda"]
 
 
+# (plan handle, batch, samples, flags) -> byte offset of the loss sum pair;
+# a plan's entries go when the plan is released (a later plan may reuse the
+# address)
 _SUM_OFFSETS: Dict[tuple, int] = {}
+
+
+def _release_plan(handle: int) -> None:
+    for key in [k for k in _SUM_OFFSETS if k[0] == handle]:
+        del _SUM_OFFSETS[key]
+    _lib.destroy_plan(handle)
 
 
 def _loss_sum_view(ws: torch.Tensor, plan: int, ref: torch.Tensor, flags: int) -> torch.Tensor:
@@ -53,7 +62,7 @@ class _PesqFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, ref, deg, plan):
+    def forward(ctx, ref, deg, plan, owner):
         flags = (_lib.GRAD_REF if ctx.needs_input_grad[0] else 0) | (
             _lib.GRAD_DEG if ctx.needs_input_grad[1] else 0
         )
@@ -68,6 +77,8 @@ class _PesqFunction(torch.autograd.Function):
         # outputs nobody differentiates get no (zero-filled) gradient
         ctx.set_materialize_grads(False)
         ctx.plan = plan
+        # the plan's owner (None while tracing) lives as long as this node
+        ctx.owner = owner
         ctx.flags = flags
         if flags:
             # the workspace is neither an input nor an output; saving such an
@@ -92,6 +103,7 @@ class _PesqFunction(torch.autograd.Function):
         return (
             g_ref if ctx.flags & _lib.GRAD_REF else None,
             g_deg if ctx.flags & _lib.GRAD_DEG else None,
+            None,
             None,
         )
 
@@ -177,7 +189,9 @@ class PesqLossCuda(torch.nn.Module):
             torch.tensor(np.stack([self.config.pre_b, self.config.pre_a]), dtype=torch.float32),
             requires_grad=False,
         )
+        # device index -> plan handle, and handle -> its owner (_lib.Owned)
         self._plans: Dict[int, int] = {}
+        self._plan_owners: Dict[int, _lib.Owned] = {}
         self.resampler = ResampleCuda(self.source_sample_rate, 16000)
         self.resample_op = None if self.source_sample_rate == 16000 else self.resampler
         self.to_spec = PowerSpectrogram(win_length, n_fft, hop_length)
@@ -238,22 +252,14 @@ class PesqLossCuda(torch.nn.Module):
         if plan is None:
             with torch.cuda.device(index):
                 plan = _lib.create_plan(self.config)
+            self._plan_owners[plan] = _lib.Owned(plan, _release_plan)
             self._plans[index] = plan
         return plan
-
-    def __del__(self):
-        plans = getattr(self, "_plans", None)
-        if plans:
-            for handle in plans.values():
-                try:
-                    _lib.destroy_plan(handle)
-                except Exception:  # pragma: no cover - interpreter shutdown
-                    pass
-            plans.clear()
 
     def __getstate__(self):
         state = self.__dict__.copy()
         state["_plans"] = {}
+        state["_plan_owners"] = {}
         return state
 
     # ------------------------------------------------------------------
@@ -278,7 +284,10 @@ class PesqLossCuda(torch.nn.Module):
         if deg.stride(-1) != 1:
             deg = deg.contiguous()
         plan = self._plan(ref.device)
-        return _PesqFunction.apply(ref, deg, plan)
+        # eager autograd nodes keep the plan alive (a traced graph holds the
+        # handle as a constant and its caller the module)
+        owner = None if torch.compiler.is_compiling() else self._plan_owners[plan]
+        return _PesqFunction.apply(ref, deg, plan, owner)
 
     def raw(self, ref: torch.Tensor, deg: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         """Symmetric and asymmetric distance, both ``[batch]`` (loss.py:172-268)."""

@@ -29,31 +29,33 @@ class _ResampleAdjoint(torch.autograd.Function):
     """gx = A^T gy, differentiable: its derivative w.r.t. gy is A."""
 
     @staticmethod
-    def forward(ctx, grad_out, handle, n_in):
+    def forward(ctx, grad_out, handle, n_in, owner):
         ctx.handle = handle
+        ctx.owner = owner  # keeps the resampler alive while this node may run
         return torch.ops.pesq_cuda.resample_adjoint(handle, grad_out, n_in)
 
     @staticmethod
     def backward(ctx, grad_grad_x):
         if not ctx.needs_input_grad[0]:
-            return None, None, None
-        return torch.ops.pesq_cuda.resample(ctx.handle, grad_grad_x), None, None
+            return None, None, None, None
+        return torch.ops.pesq_cuda.resample(ctx.handle, grad_grad_x), None, None, None
 
 
 class _ResampleFunction(torch.autograd.Function):
     """y = A x over the rows of x."""
 
     @staticmethod
-    def forward(ctx, waveform, handle):
+    def forward(ctx, waveform, handle, owner):
         ctx.handle = handle
+        ctx.owner = owner  # keeps the resampler alive while this node may run
         ctx.n_in = waveform.shape[1]
         return torch.ops.pesq_cuda.resample(handle, waveform)
 
     @staticmethod
     def backward(ctx, grad_out):
         if not ctx.needs_input_grad[0]:
-            return None, None
-        return _ResampleAdjoint.apply(grad_out, ctx.handle, ctx.n_in), None
+            return None, None, None
+        return _ResampleAdjoint.apply(grad_out, ctx.handle, ctx.n_in, ctx.owner), None, None
 
 
 class ResampleCuda(torch.nn.Module):
@@ -103,7 +105,9 @@ class ResampleCuda(torch.nn.Module):
         self.beta = beta
         self.orig_step = int(orig_freq) // self.gcd
         self.new_step = int(new_freq) // self.gcd
+        # device index -> resampler handle, and handle -> its owner (_lib.Owned)
         self._handles: Dict[int, int] = {}
+        self._owners: Dict[int, _lib.Owned] = {}
         if self.orig_freq != self.new_freq:
             self.design = sinc_resample_kernel(
                 orig_freq, new_freq, lowpass_filter_width, rolloff, resampling_method, beta
@@ -121,8 +125,15 @@ class ResampleCuda(torch.nn.Module):
         if handle is None:
             with torch.cuda.device(index):
                 handle = _lib.create_resampler(self.design)
+            self._owners[handle] = _lib.Owned(handle, _lib.destroy_resampler)
             self._handles[index] = handle
         return handle
+
+    def __getstate__(self):
+        state = self.__dict__.copy()
+        state["_handles"] = {}
+        state["_owners"] = {}
+        return state
 
     def output_length(self, samples: int) -> int:
         """Number of output samples for ``samples`` input samples."""
@@ -149,7 +160,11 @@ class ResampleCuda(torch.nn.Module):
         shape = waveform.shape
         rows = math.prod(shape[:-1])
         packed = waveform.reshape(rows, shape[-1])
-        out = _ResampleFunction.apply(packed, self._handle(waveform.device))
+        handle = self._handle(waveform.device)
+        # eager autograd nodes keep the resampler alive (a traced graph holds
+        # the handle as a constant and its caller the module)
+        owner = None if torch.compiler.is_compiling() else self._owners[handle]
+        out = _ResampleFunction.apply(packed, handle, owner)
         return out.reshape(shape[:-1] + out.shape[-1:])
 
     def extra_repr(self) -> str:
