@@ -441,7 +441,7 @@ def measure_iir(dev, peak, launches=20, large_only=False):
 
     import torch
 
-    from triton_pesq_b200 import IIRCuda
+    from triton_pesq_b200 import IIRCuda, _lib
     from triton_pesq_b200.tables import power_filter, pre_filter
 
     stream = torch.cuda.current_stream(dev)
@@ -479,7 +479,12 @@ def measure_iir(dev, peak, launches=20, large_only=False):
             "forward_gbs": alg / (fwd * 1e-6) / 1e9, "reverse_gbs": alg / (rev * 1e-6) / 1e9,
             "forward_frac_of_measured_hbm": alg / (fwd * 1e-6) / 1e9 / peak,
             "gsamples_per_s": rows * n / (fwd * 1e-6) / 1e9,
+            "tiles": "overlapped" if module.overlap and n > 8448 else ("chained" if n > 8448 else "packed rows"),
         }
+        if module.overlap and n > 8448:
+            # the same rows with the tiles chained by the look-back instead
+            out[f"{label}_{rows}x{n}"]["forward_lookback_us"] = timed(
+                lambda: torch.ops.pesq_cuda.iir(handle, x, module._flags(False) | _lib.IIR_CHAINED))
     out["note"] = ("per call, eager (allocation and launch included) for the reference's shapes; "
                    "the reference quotes 83 / 153 us forward and 387 us forward plus backward on a GTX 1080 Ti")
     errors = band.check_errors()

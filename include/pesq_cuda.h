@@ -292,7 +292,9 @@ typedef struct pesq_iir_info {
   int32_t block_lower;    /* A is block lower triangular in 2 x 2 blocks (zero blocks skipped) */
   int32_t chunk;          /* samples per thread chunk */
   int32_t tile;           /* samples per tile of a long row */
-  int32_t reserved0;
+  int32_t overlap;        /* warm-up samples of the overlapped tiles long rows run when the
+                             filter's state dies out within them (||A^overlap|| < 1e-11);
+                             0: long rows chain their tiles by the look-back */
   double largest32;       /* largest entry of the float32 tables */
   double largest64;       /* largest entry of the float64 tile chaining tables */
 } pesq_iir_info;
@@ -301,6 +303,9 @@ typedef struct pesq_iir_info {
 #define PESQ_IIR_REVERSE 1u /* filter each row back to front: the adjoint (iir.py:1232-1258) */
 #define PESQ_IIR_RERUN 2u   /* chunk outputs by re-running the recursion ("scan") instead of the
                                impulse response product ("matmul", the default) */
+#define PESQ_IIR_CHAINED 4u /* long rows chain their tiles by the decoupled look-back even where
+                               the filter allows overlapped tiles (pesq_iir_info.overlap > 0):
+                               exact for any filter, at the cost of the waits */
 
 /* Builds the kernel tables (float64, then float32) on the current device
  * (replaces TritonIIR.__init__'s table build, iir.py:602-667 and 1343-1397). */
@@ -308,7 +313,8 @@ int pesq_iir_create(const pesq_iir_desc* desc, pesq_iir** out);
 int pesq_iir_destroy(pesq_iir* filter);
 int pesq_iir_query(const pesq_iir* filter, pesq_iir_info* info);
 /* Device workspace of one pesq_iir_filter call (0 when no row spans more than
- * one tile); a workspace serves one call in flight at a time. */
+ * one tile; sized for the look-back, which overlapped tiles do not use); a
+ * workspace serves one call in flight at a time. */
 size_t pesq_iir_workspace_bytes(const pesq_iir* filter, int64_t rows, int64_t n);
 /* y = filter(x) over `rows` rows of n samples, row strides in elements; x and
  * y must not overlap (replaces _launch, iir.py:1016-1161, and

@@ -23,7 +23,11 @@ pytestmark = pytest.mark.gpu
 
 def test_iir_lookback_wait_runs_out_and_recovers(cuda_device):
     iir = IIRCuda(*power_filter())
-    # one row of 600 tiles: every tile but the first waits for a predecessor
+    # one row of 600 tiles chained by the look-back (this filter's state dies
+    # out within a tile's warm-up, so its long rows would otherwise run
+    # overlapped tiles that never wait): every tile but the first waits for a
+    # predecessor
+    iir.force_lookback = True
     x = torch.randn(1, 600 * 8448, device=cuda_device, generator=torch.Generator(cuda_device).manual_seed(5))
     good = iir(x)
     assert iir.check_errors() == 0

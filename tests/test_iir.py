@@ -186,3 +186,22 @@ def test_module_attributes():
     with warnings.catch_warnings():
         warnings.simplefilter("error")
         IIRCuda(*FILTERS["order2"], chunk_size=128)
+
+
+def test_overlapped_tiles_only_where_the_state_dies_out():
+    """Long rows run overlapped tiles (a 1056-sample warm-up, no waits) when
+    ||A^1056|| < 1e-11 in the chosen realisation -- the PESQ filters and the
+    usual designs -- and chain their tiles by the look-back for poles close
+    to the unit circle."""
+
+    from iir_cases import resonator
+    from triton_pesq_b200.tables import power_filter, pre_filter
+
+    for b, a in [power_filter(), pre_filter(), *FILTERS.values(), *DEGENERATE.values()]:
+        module = IIRCuda(b, a)
+        assert module.overlap == D.IIR_LANES * D.IIR_CHUNK
+        assert module.force_lookback is False
+    for radius in (0.99, 0.9999):
+        tabs = D.design(*resonator(radius)).tables()
+        assert tabs.overlap == 0
+        assert float(np.abs(tabs.warp_powers[1]).sum(axis=1).max()) >= D.IIR_OVERLAP_TOL

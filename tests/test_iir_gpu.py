@@ -101,12 +101,16 @@ def test_batch_sweep(modules, batch):
     assert (out.abs().amax(dim=1) > 0).all()
 
 
-def test_many_tiles_on_a_single_row(modules):
-    """480000 samples are 57 chained tiles of one row (test_triton_iir.py:916)."""
+@pytest.mark.parametrize("lookback", [False, True])
+def test_many_tiles_on_a_single_row(cuda_device, lookback):
+    """480000 samples are 57 chained tiles of one row (test_triton_iir.py:916),
+    or 65 overlapped ones."""
 
     b, a = FILTERS["order10"]
+    module = IIRCuda(b, a)
+    module.force_lookback = lookback
     signal = noise(2, 480000, seed=102)
-    out = modules[("order10", "matmul")](signal)
+    out = module(signal)
     assert torch.isfinite(out).all()
     assert peak_error(out, exact(signal, b, a)) < TOL
 
@@ -117,12 +121,15 @@ def test_very_long_row_deep_lookback(modules):
     aggregate; the result must not depend on it."""
 
     b, a = FILTERS["order2"]
+    module = IIRCuda(b, a)
+    module.force_lookback = True  # (this filter would run overlapped tiles)
     signal = noise(1, 8448 * 600 + 77, seed=5)
-    out = modules[("order2", "matmul")](signal)
+    out = module(signal)
     truth = exact(signal, b, a)
     assert peak_error(out, truth) < TOL
-    again = modules[("order2", "matmul")](signal)
+    again = module(signal)
     assert peak_error(again, truth) < TOL
+    assert module.check_errors() == 0
 
 
 def test_batch_beyond_the_grid_y_limit(modules):
@@ -326,6 +333,7 @@ def test_c_abi_tables_match_the_host_design(cuda_device):
         assert info.states == m.states and info.kernel_states == tabs.states
         assert bool(info.block_lower) == tabs.lower
         assert info.chunk == D.IIR_CHUNK and info.tile == D.IIR_TILE
+        assert info.overlap == tabs.overlap == m.overlap
         assert math.isclose(info.largest32, tabs.largest32, rel_tol=1e-9)
         assert math.isclose(info.largest64, tabs.largest64, rel_tol=1e-9)
 
@@ -471,12 +479,13 @@ def test_subnormal_input_does_not_produce_nan(cuda_device):
     assert torch.isfinite(out).all()
 
 
-@pytest.mark.parametrize("shape", [(3, 20000), (40, 700)])
-def test_cuda_graph_replay(modules, shape):
+@pytest.mark.parametrize("shape,lookback", [((3, 20000), False), ((3, 20000), True), ((40, 700), False)])
+def test_cuda_graph_replay(cuda_device, shape, lookback):
     """Captured in a CUDA graph (chained tiles: the workspace reset is a memset
     node of the graph), replayed on new inputs, bitwise equal to eager calls."""
 
-    module = modules[("order10", "matmul")]
+    module = IIRCuda(*FILTERS["order10"])
+    module.force_lookback = lookback
     static = noise(*shape, seed=7)
     module(static)  # plan and kernel set-up outside the capture
     torch.cuda.synchronize()
@@ -553,3 +562,28 @@ def test_widest_kernels(cuda_device, name, dense, method):
         _lib.destroy_iir(handle)
     assert peak_error(out, exact(signal, b, a)) < bound
     assert peak_error(grad, exact_vjp(signal, upstream, b, a)) < bound
+
+
+@pytest.mark.parametrize("method", ["matmul", "scan"])
+def test_overlapped_tiles_agree_with_the_lookback(cuda_device, method):
+    """Long rows of a filter whose state dies out within a tile's warm-up run
+    overlapped tiles (no waits); they agree with the look-back chaining and
+    with float64 lfilter, forward and reversed, at lengths that end inside
+    the first, a middle and the last warm-up."""
+
+    b, a = FILTERS["order10"]
+    module = IIRCuda(b, a, method=method)
+    assert module.overlap == 32 * D.IIR_CHUNK  # the overlapped path runs (not vacuous)
+    step = D.IIR_TILE - module.overlap
+    for n in (D.IIR_TILE + 1, 3 * step + 17, 7 * step + module.overlap - 3):
+        x = noise(3, n, seed=n)
+        truth = exact(x, b, a)
+        for reverse in (False, True):
+            module.force_lookback = False
+            ovl = module._launch(x, reverse)
+            module.force_lookback = True
+            chained = module._launch(x, reverse)
+            want = exact(x.flip(-1), b, a).flip(-1) if reverse else truth
+            assert peak_error(ovl, want) < TOL
+            assert peak_error(ovl, chained) < FLOOR
+    module.force_lookback = False

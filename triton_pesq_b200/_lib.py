@@ -109,7 +109,7 @@ class IirInfo(ctypes.Structure):
         ("block_lower", ctypes.c_int32),
         ("chunk", ctypes.c_int32),
         ("tile", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("overlap", ctypes.c_int32),
         ("largest32", ctypes.c_double),
         ("largest64", ctypes.c_double),
     ]
@@ -118,6 +118,7 @@ class IirInfo(ctypes.Structure):
 #: pesq_iir_filter flags
 IIR_REVERSE = 1
 IIR_RERUN = 2
+IIR_CHAINED = 4
 
 
 class Shape(ctypes.Structure):

@@ -27,7 +27,12 @@
 //
 // Tile geometry.  Rows of at most kThreads chunks are packed whole, several to
 // a tile (segments of cpr chunks, a head at each segment start): nothing
-// crosses a tile.  Longer rows are cut into tiles of kTile samples that are
+// crosses a tile.  Longer rows of a filter whose state dies out within one
+// warp's span (||A^kOverlap|| < 1e-11, checked on the host, as for the loss
+// path's level-alignment scan) run overlapped tiles: tile k stages the kOverlap
+// samples before its kTile - kOverlap outputs as well and starts from zero
+// state there (warp 0's chunks are the warm-up and store nothing), so no tile
+// waits for another.  Otherwise the tiles of kTile samples are
 // chained by a decoupled look-back (single pass, 8 bytes of HBM traffic per
 // sample): a CTA takes its tile from a ticket counter (so every tile it waits
 // for belongs to a CTA that is already running), publishes its zero-start
@@ -58,6 +63,8 @@ constexpr int kLook = 32;               // predecessors per look-back window (a 
 constexpr int kFar = 256;               // predecessors the look-back reaches (8 windows)
 constexpr int kMaxStates = 24;
 constexpr unsigned kSpinLimit = 1u << 21;
+constexpr int kOverlap = 32 * kL;       // warm-up of an overlapped tile: warp 0's chunks (1056 samples)
+static_assert(kOverlap % 4 == 0 && (kTile - kOverlap) % 4 == 0, "overlapped tiles store in 16-byte pieces");
 
 // Per-filter constants in float32, passed as a kernel parameter (constant
 // bank operands of the FMAs).
@@ -100,20 +107,13 @@ struct Args {
   unsigned long long* slots;  // [tiles][2][P][2]: aggregate / inclusive state, zero before the launch
   uint32_t* err;
   uint32_t spin_limit;     // polls a look-back wait makes before it gives up (normally kSpinLimit)
+  int overlap;             // > 0: overlapped tiles (below) instead of chained ones
 };
 
 constexpr int kNearPowers = 4;  // A^(k kTile), k < 4, staged for the look-back
 __host__ __device__ constexpr size_t smem_bytes(int P) {
   return (size_t)kTile * 4 + (size_t)kNearPowers * P * P * 8 + (size_t)lane_floats(P) * 4 +
          (size_t)wpow_floats(P) * 4 + (size_t)kWarps * P * 4 + (size_t)P * 4 + 16;
-}
-
-// 4-byte asynchronous copy global -> shared that writes zero (and reads
-// nothing) when `valid` is false; `src` must still be a valid address.
-__device__ __forceinline__ void cp_async4_zfill(float* dst, const float* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-               "l"(src), "r"(valid ? 4 : 0)
-               : "memory");
 }
 
 #ifdef PESQ_PHASE_PROBE
@@ -298,10 +298,12 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool chained = a.tiles_per_row > 1;
-  if (tid == 0) s_tile = chained ? (int64_t)atomicAdd(a.ticket, 1u) : (int64_t)blockIdx.x;
+  const bool ovl = chained && a.overlap > 0;  // overlapped tiles: no look-back
+  const bool looks = chained && !ovl;
+  if (tid == 0) s_tile = looks ? (int64_t)atomicAdd(a.ticket, 1u) : (int64_t)blockIdx.x;
   copy_async<kThreads>(lanes, a.lanes, lane_floats(P) * 4);
   copy_async<kThreads>(wpow, a.wpow, wpow_floats(P) * 4);
-  if (chained) copy_async<kThreads>(near, a.look, kNearPowers * P * P * 8);
+  if (looks) copy_async<kThreads>(near, a.look, kNearPowers * P * P * 8);
   __syncthreads();
 
   // tile geometry: rows [row0, row0 + nrows), memory span [m0, m0 + seg) of each
@@ -310,7 +312,15 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
   const int seg = a.seg;
   int64_t row0, tin, m0;
   int nrows;
-  if (chained) {
+  if (ovl) {
+    // outputs [tin E, (tin + 1) E) after a warm-up of the kOverlap samples
+    // before them (E = kTile - kOverlap); reversed, the warm-up lies above
+    const int64_t E = kTile - kOverlap;
+    row0 = tile / a.tiles_per_row;
+    tin = tile - row0 * a.tiles_per_row;
+    nrows = 1;
+    m0 = kRev ? a.n - (tin + 1) * E : tin * E - kOverlap;
+  } else if (chained) {
     row0 = tile / a.tiles_per_row;
     tin = tile - row0 * a.tiles_per_row;
     nrows = 1;
@@ -325,8 +335,11 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
   const float* xrow = a.x + row0 * a.ld_x;
   float* yrow = a.y + row0 * a.ld_y;
   const bool full = chained && m0 >= 0 && m0 + kTile <= a.n;
+  // staged samples [qa, qb) of the tile are outputs (all but the warm-up)
+  const int qa = ovl && !kRev ? kOverlap : 0;
+  const int qb = ovl && kRev ? kTile - kOverlap : kTile;
   const bool vec_in = full && ((reinterpret_cast<uintptr_t>(xrow + m0) & 15) == 0);
-  const bool vec_out = full && ((reinterpret_cast<uintptr_t>(yrow + m0) & 15) == 0);
+  const bool vec_out = full && ((reinterpret_cast<uintptr_t>(yrow + m0 + qa) & 15) == 0);
 
   // stage the tile in memory order (zeros outside the rows)
   if (vec_in) {
@@ -368,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
   const int r = chained ? 0 : tid / a.cpr;
   const int lc = chained ? tid : tid - r * a.cpr;
   const bool used = chained || r < nrows;
-  const bool head = chained ? (tin == 0 && tid == 0) : (!used || lc == 0);
+  const bool head = ovl ? tid == 0 : chained ? (tin == 0 && tid == 0) : (!used || lc == 0);
   constexpr int dir = kRev ? -1 : 1;
   const int base = kRev ? r * seg + seg - 1 - lc * kL : r * seg + lc * kL;
 
@@ -454,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
     if (s_whead[v]) h = v;
   const int ci = lane < P ? lane : 0;
   float xw = warp_sum<P, kLower>(wpow, tot, h < 0 ? 0 : h, warp, ci);
-  if (chained) {
+  if (looks) {
     const bool successor = tin + 1 < a.tiles_per_row;
     if (tin == 0) {
       if (warp == 0 && successor)
@@ -545,15 +558,16 @@ __global__ void __launch_bounds__(kThreads, P <= 2 ? 4 : (P <= 10 ? 3 : 1)) scan
 
   PESQ_IIR_STAMP(tile, 4);
   if (vec_out) {
-    float4* dst = reinterpret_cast<float4*>(yrow + m0);
-    const float4* src = reinterpret_cast<const float4*>(xs);
-    for (int i = tid; i < kTile / 4; i += kThreads) dst[i] = src[i];
+    // (qa and qb - qa are multiples of 4)
+    float4* dst = reinterpret_cast<float4*>(yrow + m0 + qa);
+    const float4* src = reinterpret_cast<const float4*>(xs + qa);
+    for (int i = tid; i < (qb - qa) / 4; i += kThreads) dst[i] = src[i];
   } else if (chained) {
 #pragma unroll 11
     for (int k = 0; k < kL; ++k) {
       const int q = tid + k * kThreads;
       const int64_t m = m0 + q;
-      if (m >= 0 && m < a.n) yrow[m] = xs[q];
+      if (q >= qa && q < qb && m >= 0 && m < a.n) yrow[m] = xs[q];
     }
   } else {
     const int n = (int)a.n;

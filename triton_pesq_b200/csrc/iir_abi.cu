@@ -55,11 +55,16 @@ struct pesq_iir {
   uint32_t* err = nullptr;
   uint32_t spin_limit = pesq::iir::kSpinLimit;
   double largest32 = 0.0, largest64 = 0.0;
+  // ||A^kOverlap|| (max row sum) < kOverlapTol: long rows may run overlapped tiles
+  bool overlap_ok = false;
 };
 
 namespace {
 
 constexpr int kKernelStates[] = {2, 4, 6, 8, 10, 12, 14, 16, 20, 24};
+// state an overlapped tile may drop after its kOverlap-sample warm-up, relative
+// (the same bound as the loss path's level-alignment horizon)
+constexpr double kOverlapTol = 1e-11;
 
 using Mat = std::vector<double>;  // row-major P x P
 
@@ -127,10 +132,14 @@ void free_tables(pesq_iir* f) {
 struct Geometry {
   int cpr, rows_per_tile, seg;
   int64_t tiles_per_row, tiles;
+  bool overlap;  // overlapped tiles of long rows (no look-back, no workspace)
   bool chained() const { return tiles_per_row > 1; }
+  bool lookback() const { return chained() && !overlap; }
 };
 
-Geometry geometry(int64_t rows, int64_t n) {
+// overlap: the filter allows overlapped tiles and the caller did not ask for
+// the look-back
+Geometry geometry(int64_t rows, int64_t n, bool overlap = false) {
   Geometry g{};
   const int64_t cpr = (n + kL - 1) / kL;
   if (cpr <= kThreads) {
@@ -143,7 +152,9 @@ Geometry geometry(int64_t rows, int64_t n) {
     g.cpr = kThreads;
     g.rows_per_tile = 1;
     g.seg = kTile;
-    g.tiles_per_row = (n + kTile - 1) / kTile;
+    g.overlap = overlap;
+    const int64_t out = overlap ? kTile - kOverlap : kTile;  // outputs per tile
+    g.tiles_per_row = (n + out - 1) / out;
     g.tiles = rows * g.tiles_per_row;
   }
   return g;
@@ -152,7 +163,7 @@ Geometry geometry(int64_t rows, int64_t n) {
 // chained rows: the tile ticket (16 bytes) and two published states of P
 // components per tile, two tagged 64-bit words each; all zero before a launch
 size_t workspace_bytes(const pesq_iir* f, const Geometry& g) {
-  if (!g.chained()) return 0;
+  if (!g.lookback()) return 0;
   return 16 + (size_t)g.tiles * 2 * f->kstates * 2 * 8;
 }
 
@@ -237,7 +248,13 @@ int pesq_iir_create(const pesq_iir_desc* d, pesq_iir** out) {
     lanes[l] = cur;
     cur = mul(chunk_step, cur, P);
   }
-  const Mat wstep = cur;  // A^(32 L)
+  const Mat wstep = cur;  // A^(32 L) = A^kOverlap
+  double wnorm = 0.0;
+  for (int i = 0; i < P; ++i) {
+    double row = 0.0;
+    for (int j = 0; j < P; ++j) row += std::fabs(wstep[(size_t)i * P + j]);
+    wnorm = std::fmax(wnorm, row);
+  }
   std::vector<Mat> wp(kWarps + 1);  // A^(32 L k), k = 0..kWarps
   wp[0] = eye(P);
   for (int w = 1; w <= kWarps; ++w) wp[w] = mul(wstep, wp[w - 1], P);
@@ -288,6 +305,7 @@ int pesq_iir_create(const pesq_iir_desc* d, pesq_iir** out) {
   }
   f->largest32 = big32;
   f->largest64 = absmax(look);
+  f->overlap_ok = std::isfinite(wnorm) && wnorm < kOverlapTol;
   if (!std::isfinite(f->largest32) || !std::isfinite(f->largest64)) {
     delete f;
     return set_error(PESQ_ERR_INVALID_ARGUMENT, "the realisation's tables overflow");
@@ -326,11 +344,14 @@ int pesq_iir_query(const pesq_iir* f, pesq_iir_info* info) {
   info->tile = kTile;
   info->largest32 = f->largest32;
   info->largest64 = f->largest64;
+  info->overlap = f->overlap_ok ? kOverlap : 0;
   return PESQ_OK;
 }
 
 size_t pesq_iir_workspace_bytes(const pesq_iir* f, int64_t rows, int64_t n) {
   if (!f || rows <= 0 || n <= 0) return 0;
+  // enough for either tiling (the look-back one needs it; PESQ_IIR_CHAINED
+  // is a per-call flag)
   return workspace_bytes(f, geometry(rows, n));
 }
 
@@ -338,7 +359,7 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
                     float* y, int64_t ld_y, uint32_t flags, void* workspace, size_t workspace_bytes_) {
   if (!f) return set_error(PESQ_ERR_INVALID_ARGUMENT, "NULL filter");
   if (rows < 0 || n < 0) return set_error(PESQ_ERR_INVALID_ARGUMENT, "negative rows or samples");
-  if (flags & ~(uint32_t)(PESQ_IIR_REVERSE | PESQ_IIR_RERUN))
+  if (flags & ~(uint32_t)(PESQ_IIR_REVERSE | PESQ_IIR_RERUN | PESQ_IIR_CHAINED))
     return set_error(PESQ_ERR_INVALID_ARGUMENT, "unknown flags");
   if (rows == 0 || n == 0) return PESQ_OK;
   if (!x || !y) return set_error(PESQ_ERR_INVALID_ARGUMENT, "NULL signal");
@@ -346,7 +367,7 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   int dev = -1;
   cudaGetDevice(&dev);
   if (dev != f->device) return set_error(PESQ_ERR_INVALID_ARGUMENT, "the filter lives on another device");
-  const Geometry g = geometry(rows, n);
+  const Geometry g = geometry(rows, n, f->overlap_ok && !(flags & PESQ_IIR_CHAINED));
   if (g.tiles > ((int64_t)1 << 31) - 1) return set_error(PESQ_ERR_INVALID_ARGUMENT, "more than 2^31 - 1 tiles");
   const size_t need = workspace_bytes(f, g);
   if (need > 0 && (!workspace || workspace_bytes_ < need))
@@ -371,7 +392,8 @@ int pesq_iir_filter(const pesq_iir* f, void* stream, const float* x, int64_t ld_
   a.look = f->look;
   a.err = f->err;
   a.spin_limit = f->spin_limit;
-  if (g.chained()) {
+  a.overlap = g.overlap ? kOverlap : 0;
+  if (g.lookback()) {
     char* w = static_cast<char*>(workspace);
     a.ticket = reinterpret_cast<uint32_t*>(w);
     a.slots = reinterpret_cast<unsigned long long*>(w + 16);

@@ -92,6 +92,14 @@ class IIRCuda(torch.nn.Module):
         State count of the kernel instantiation (the realisation zero padded)
     feed : float
         Direct feed-through ``D``
+    overlap : int
+        Warm-up samples of the overlapped tiles rows longer than one tile run
+        (each tile re-runs that much of the row before it from zero state, no
+        waits between tiles), or 0 when the filter's state does not die out
+        within them and the tiles are chained by the look-back
+    force_lookback : bool
+        Chain the tiles of long rows by the look-back even where overlapped
+        tiles would do (False by default)
     """
 
     def __init__(self, b_coeffs, a_coeffs, chunk_size: Optional[Union[int, str]] = None, method: str = "auto"):
@@ -118,6 +126,8 @@ class IIRCuda(torch.nn.Module):
         self.order = max(numerator.size, denominator.size) - 1
         self.states = self.design.states
         self.basis = self.design.basis
+        self.overlap = self.design.tables().overlap
+        self.force_lookback = False
         self.feed = self.design.feed
         self.padded = self.design.tables().states
         self.score = self.design.score
@@ -139,7 +149,8 @@ class IIRCuda(torch.nn.Module):
         return handle
 
     def _flags(self, reverse: bool) -> int:
-        return (_lib.IIR_REVERSE if reverse else 0) | (_lib.IIR_RERUN if self.method == "scan" else 0)
+        return ((_lib.IIR_REVERSE if reverse else 0) | (_lib.IIR_RERUN if self.method == "scan" else 0)
+                | (_lib.IIR_CHAINED if self.force_lookback else 0))
 
     def _launch(self, signal: torch.Tensor, reverse: bool) -> torch.Tensor:
         return torch.ops.pesq_cuda.iir(self._handle(signal.device), signal, self._flags(reverse))

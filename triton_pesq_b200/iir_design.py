@@ -49,6 +49,7 @@ __all__ = [
     "IIR_THREADS",
     "IIR_TILE",
     "IIR_LOOKBACK",
+    "IIR_OVERLAP_TOL",
     "as_coeffs",
     "companion",
     "modal",
@@ -94,6 +95,8 @@ KERNEL_STATES = (2, 4, 6, 8, 10, 12, 14, 16, 20, 24)
 #: Kernel geometry (csrc/iir.cuh): samples per thread chunk, threads per CTA,
 #: lanes per warp, warp scan levels, samples per tile, look-back window.
 IIR_CHUNK = 33
+#: state an overlapped tile may drop after its warm-up of 32 chunks, relative
+IIR_OVERLAP_TOL = 1e-11
 IIR_THREADS = 256
 IIR_LANES = 32
 IIR_LEVELS = 5
@@ -318,6 +321,16 @@ class KernelTables:
         """Largest entry of the float64 tables (tile chaining)."""
 
         return float(np.abs(self.lookback).max())
+
+    @property
+    def overlap(self) -> int:
+        """Warm-up samples of the overlapped tiles long rows run (one warp's
+        chunks, ``32 L``) when the state dies out within them --
+        ``||A^(32 L)||`` (max row sum) below ``IIR_OVERLAP_TOL`` -- else 0 (the
+        tiles are chained by the look-back)."""
+
+        norm = float(np.abs(self.warp_powers[1]).sum(axis=1).max())
+        return IIR_LANES * IIR_CHUNK if np.isfinite(norm) and norm < IIR_OVERLAP_TOL else 0
 
 
 def kernel_tables(trans, drive, read, feed, order: Optional[int] = None) -> KernelTables:
