@@ -213,24 +213,47 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32)
   const int64_t L0 = (int64_t)blockIdx.x * F;
   const int nf = (int)min((int64_t)F, frames - L0);
 
-  // stage: row f holds samples [0, S) of super-frame L0 + f's window
+  // stage: row f holds samples [0, S) of super-frame L0 + f's window, rows
+  // P apart: padded rows (P >= S), or with P = mma_os the window itself,
+  // each sample once (rows overlap), where padding would copy samples
+  // several times over.  float32 rows go by asynchronous copies (every load
+  // of the window in flight at once), others through registers.
   const void* x = p.src.row_any(r);
   const int xtype = p.src.type;
   const int64_t base = L0 * p.mma_os - p.width;
-  for (int f = warp; f < nf; f += nw) {
-    const int64_t g0 = base + (int64_t)f * p.mma_os;
-    float* row = win + f * P;
-    if (g0 >= 0 && g0 + S <= p.n_in) {
-      if (xtype == kInF32) {
-        const float* xf = static_cast<const float*>(x) + g0;
-        for (int t = lane; t < S; t += 32) row[t] = __ldg(xf + t);
-      } else {
-        for (int t = lane; t < S; t += 32) row[t] = load_elem(x, g0 + t, xtype);
+  const bool contiguous = P == p.mma_os;
+  const int span = contiguous ? (nf - 1) * P + S : 0;
+  if (xtype == kInF32) {
+    const float* xf = static_cast<const float*>(x);
+    if (contiguous) {
+      for (int i = threadIdx.x; i < span; i += blockDim.x) {
+        const int64_t g = base + i;
+        const bool valid = g >= 0 && g < p.n_in;
+        cp_async4_zfill(win + i, valid ? xf + g : xf, valid);
       }
     } else {
+      for (int f = warp; f < nf; f += nw) {
+        const int64_t g0 = base + (int64_t)f * p.mma_os;
+        for (int t = lane; t < S; t += 32) {
+          const int64_t g = g0 + t;
+          const bool valid = g >= 0 && g < p.n_in;
+          cp_async4_zfill(win + f * P + t, valid ? xf + g : xf, valid);
+        }
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+  } else if (contiguous) {
+    for (int i = threadIdx.x; i < span; i += blockDim.x) {
+      const int64_t g = base + i;
+      win[i] = (g >= 0 && g < p.n_in) ? load_elem(x, g, xtype) : 0.0f;
+    }
+  } else {
+    for (int f = warp; f < nf; f += nw) {
+      const int64_t g0 = base + (int64_t)f * p.mma_os;
       for (int t = lane; t < S; t += 32) {
         const int64_t g = g0 + t;
-        row[t] = (g >= 0 && g < p.n_in) ? load_elem(x, g, xtype) : 0.0f;
+        win[f * P + t] = (g >= 0 && g < p.n_in) ? load_elem(x, g, xtype) : 0.0f;
       }
     }
   }
@@ -328,16 +351,21 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32)
   const int64_t L0 = (int64_t)blockIdx.x * F;
   const int nf = (int)min((int64_t)F, frames - L0);
 
-  // stage gradient rows L0 - D .. L0 + nf - 1 (row f holds super-frame L0 - D + f)
+  // stage gradient rows L0 - D .. L0 + nf - 1 (row f holds super-frame L0 - D
+  // + f; column ns2 is the zero the padding entries read), by asynchronous
+  // copies: every load of the window in flight at once
   const float* g = p.src.row(r);
   for (int f = warp; f < nf + D; f += nw) {
     const int64_t m0 = (L0 - D + f) * ns2;
     float* row = gw + f * P;
     for (int t = lane; t <= ns2; t += 32) {
       const int64_t m = m0 + t;
-      row[t] = (t < ns2 && m >= 0 && m < p.n_out) ? __ldg(g + m) : 0.0f;
+      const bool valid = t < ns2 && m >= 0 && m < p.n_out;
+      cp_async4_zfill(row + t, valid ? g + m : g, valid);
     }
   }
+  cp_async_commit();
+  cp_async_wait_all();
   __syncthreads();
 
   const int chunks = F / (8 * kMmaGroups);
@@ -463,7 +491,8 @@ cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s) {
     if (a.fwd_mma) {
       const int64_t frames = ceil_div(a.n_out, (int64_t)a.mma_ns);
       dim3 grid((unsigned)ceil_div(frames, (int64_t)a.mma_frames), (unsigned)c.rows);
-      const size_t smem = (size_t)a.mma_frames * a.mma_pitch * 4;
+      // rows of mma_pitch floats, the last one mma_span long
+      const size_t smem = ((size_t)a.mma_frames * a.mma_pitch + (size_t)std::max(0, a.mma_span - a.mma_pitch)) * 4;
       const cudaError_t e = launch_fwd_mma(a.fwd_mma, grid, a.mma_warps * 32, smem, s, c);
       if (e != cudaSuccess) return e;
     } else if (a.fwd_staged) {
@@ -577,8 +606,13 @@ void plan_fwd_mma(int os, int ns, const std::vector<int>& first, const std::vect
   ks += ks & 1;
   if (ks > kMmaMaxKSteps) return;
   const int S = smax + 4 * ks;
-  const int P = S + ((36 - S % 32) % 32);  // >= S, 4 mod 32
-  const int F = std::min(256, (int)(kMmaWindowBytes / ((size_t)P * 4)) / 32 * 32);
+  // padded rows (pitch >= S, 4 mod 32: the 8 rows of an A fragment hit
+  // distinct banks), or the contiguous window (pitch os2, rows overlapping,
+  // some A fragments 2-way bank conflicted) where padded rows would stage
+  // every sample more than 1.25 times
+  const int P = 4 * S > 5 * os2 ? os2 : S + ((36 - S % 32) % 32);
+  const size_t row_bytes = (size_t)P * 4;
+  int F = std::min(256, (int)((kMmaWindowBytes - (size_t)(S - std::min(S, P)) * 4) / row_bytes) / 32 * 32);
   if (F < 8 * kMmaGroups) return;
   const int units = nb * (F / (8 * kMmaGroups));
   int warps = std::min(units, 8);
