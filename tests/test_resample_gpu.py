@@ -14,7 +14,10 @@ from triton_pesq_b200 import ResampleCuda
 
 pytestmark = pytest.mark.gpu
 
-RATES = [(44100, 16000), (48000, 16000), (8000, 16000), (22050, 16000), (16000, 48000), (16000, 44100)]
+# the usual rates (float64 tensor-core kernels), upsampling, and 96 kHz, whose
+# 8-phase tap spans are too long for the tensor-core tiles (staged kernels)
+RATES = [(44100, 16000), (48000, 16000), (8000, 16000), (22050, 16000), (16000, 48000), (16000, 44100),
+         (24000, 16000), (32000, 16000), (11025, 16000), (16000, 8000), (96000, 16000)]
 
 
 def _reference64(x, module):
@@ -44,6 +47,23 @@ def test_forward_matches_torchaudio(cuda_device, orig, new, method):
     # and the float32 torchaudio module itself
     ta = torchaudio.transforms.Resample(orig, new, resampling_method=method)(x)
     assert _peak_err(y, ta.double()) < 1e-5
+
+
+@pytest.mark.parametrize("orig,new", RATES)
+def test_adjoint_matches_torchaudio(cuda_device, orig, new):
+    """The adjoint (the gradient of the forward) against the gradient of
+    torchaudio's float64 convolution with the same taps, at every rate pair."""
+
+    g = torch.Generator().manual_seed(3 * orig + new)
+    x = torch.randn(3, orig // 4 + 53, generator=g, dtype=torch.float64)
+    module = ResampleCuda(orig, new).to(cuda_device)
+    xd = x.float().to(cuda_device).requires_grad_(True)
+    y = module(xd)
+    gy = torch.randn(y.shape, generator=g, dtype=torch.float64)
+    (gx,) = torch.autograd.grad(y, xd, gy.float().to(cuda_device))
+    xr = x.clone().requires_grad_(True)
+    (want,) = torch.autograd.grad(_reference64(xr, module), xr, gy.float().double())
+    assert _peak_err(gx, want) < 1e-6
 
 
 def test_adjoint_and_double_backward(cuda_device):
@@ -128,3 +148,27 @@ def test_cuda_graph_replay(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(y, torch.ops.pesq_cuda.resample(handle, fx))
         assert torch.equal(gx, torch.ops.pesq_cuda.resample_adjoint(handle, fg, n_in))
+
+
+@pytest.mark.parametrize("orig", [44100, 48000, 8000])
+@pytest.mark.parametrize("samples", [1, 2, 3, 7, 23, 24, 25, 440, 441, 442, 7055, 14112])
+def test_short_and_ragged_lengths(cuda_device, orig, samples):
+    """Lengths that end inside the first super-frame, on and around a
+    super-frame boundary, and on a staged window's edge (partial windows,
+    tiles with rows past the row end): forward and adjoint against float64."""
+
+    g = torch.Generator().manual_seed(orig + samples)
+    x = torch.randn(2, samples, generator=g, dtype=torch.float64)
+    module = ResampleCuda(orig, 16000).to(cuda_device)
+    xd = x.float().to(cuda_device).requires_grad_(True)
+    y = module(xd)
+    want = _reference64(x.float().double(), module)
+    assert y.shape == want.shape
+    if want.numel() == 0:
+        return
+    assert _peak_err(y, want) < 1e-6
+    gy = torch.randn(y.shape, generator=g, dtype=torch.float64)
+    (gx,) = torch.autograd.grad(y, xd, gy.float().to(cuda_device))
+    xr = x.float().double().requires_grad_(True)
+    (gwant,) = torch.autograd.grad(_reference64(xr, module), xr, gy.float().double())
+    assert _peak_err(gx, gwant) < 1e-6

@@ -381,6 +381,8 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32)
     double acc[kMmaGroups][2];
 #pragma unroll
     for (int gi = 0; gi < kMmaGroups; ++gi) acc[gi][0] = acc[gi][1] = 0.0;
+    // (loading a few k-steps' operands ahead of their MMAs cut the load
+    // stalls but cost a CTA per SM in registers: no faster)
 #pragma unroll 2
     for (int k = k0; k < k1; ++k) {
       const double b = __ldg(p.amma_b + (size_t)k * 32 + lane);
