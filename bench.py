@@ -500,12 +500,8 @@ def measure_configs(dev, flush, steps=10):
 
     import torch
 
-    from triton_pesq_b200 import PesqLossCuda
+    from triton_pesq_b200 import PesqLossCuda, ResampleCuda
     from triton_pesq_b200.signals import workload
-
-    import torch
-
-    from triton_pesq_b200 import ResampleCuda
 
     out = {}
     for name, keep, secs in (("cfg1", 1, 1.0), ("cfg3", 16, 4.0), ("cfg4_per_gpu", 8, 10.0), ("cfg5", 512, 3.0)):
@@ -515,6 +511,9 @@ def measure_configs(dev, flush, steps=10):
         ms = _graphed_step_ms(model, ref, deg, flush, steps)
         out[name] = {"batch": keep, "seconds": secs, "sample_rate": sr, "ms_per_step": ms,
                      "utterance_seconds_per_s": keep * secs / (ms * 1e-3)}
+        if name == "cfg5":
+            # the stages of the scaling configuration's whole batch on one GPU
+            out[name]["stages_us"] = stage_times(model, ref, deg, dev)
         if sr != 16000:
             # the stages of the resampled step (front and back include the
             # resampler and its adjoint), and the resampler alone on the

@@ -239,40 +239,42 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 static_assert(kSpan % kThreads == 0, "a span is a whole number of rows of the CTA");
 
-// dst[i] = src[base + i] for i in [0, kSpan), 0 where base + i lies outside
-// [0, n).  Every thread issues all of its loads before its first shared
-// store, so the whole span is in flight at once instead of one DRAM round
-// trip per loop iteration.  Must be called by all kThreads threads.
+// dst[i] = src[base + i] for i in [0, NT * kChunk), 0 where base + i lies
+// outside [0, n).  Every thread issues all of its loads before its first
+// shared store, so the whole span is in flight at once instead of one DRAM
+// round trip per loop iteration.  Must be called by all NT threads of the CTA.
+template <int NT = kThreads>
 __device__ __forceinline__ void stage_span(float* dst, const float* src, int64_t base, int64_t n) {
-  constexpr int kPer = kSpan / kThreads;
+  constexpr int kPer = kChunk;
   float v[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    const int64_t g = base + threadIdx.x + k * kThreads;
+    const int64_t g = base + threadIdx.x + k * NT;
     v[k] = (g >= 0 && g < n) ? __ldg(src + g) : 0.0f;
   }
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) dst[threadIdx.x + k * kThreads] = v[k];
+  for (int k = 0; k < kPer; ++k) dst[threadIdx.x + k * NT] = v[k];
 }
 
 // stage_span over a row of 16-bit elements (type 1: bf16, 2: fp16), widened
 // to float; type 0 is stage_span itself.
+template <int NT = kThreads>
 __device__ __forceinline__ void stage_span_any(float* dst, const void* src, int64_t base, int64_t n, int type) {
   if (type == 0) {
-    stage_span(dst, static_cast<const float*>(src), base, n);
+    stage_span<NT>(dst, static_cast<const float*>(src), base, n);
     return;
   }
-  constexpr int kPer = kSpan / kThreads;
+  constexpr int kPer = kChunk;
   const unsigned short* s = static_cast<const unsigned short*>(src);
   unsigned short v[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    const int64_t g = base + threadIdx.x + k * kThreads;
+    const int64_t g = base + threadIdx.x + k * NT;
     v[k] = (g >= 0 && g < n) ? __ldg(s + g) : (unsigned short)0;
   }
 #pragma unroll
   for (int k = 0; k < kPer; ++k)
-    dst[threadIdx.x + k * kThreads] =
+    dst[threadIdx.x + k * NT] =
         type == 1 ? __uint_as_float((unsigned)v[k] << 16) : __half2float(__ushort_as_half(v[k]));
 }
 

@@ -35,28 +35,43 @@ PESQ_CTA_TABLE(g_cta_front)
 
 namespace {
 
-constexpr int kFftFloats = kWarps * FftLayout<double>::kSlots * 4;
-constexpr int kFrontScratchFloats =
-    kFftFloats > scan_scratch_floats<10>() ? kFftFloats : scan_scratch_floats<10>();
-constexpr int kFrontSmemBytes = 2 * kSpan * 4 + kFrontScratchFloats * 4 + (int)sizeof(DevTables) +
-                                (int)sizeof(DevTwiddle64) + kWarps * 8 + 16;
+// Shared-memory geometry of a front CTA of NT threads: NT chunks of kChunk
+// samples, NT / 32 warps.  The 512-thread CTA holds the forward twiddles in
+// shared memory too (one CTA per SM); the 256-thread one, which runs two
+// CTAs per SM, reads them through L1.
+template <int NT>
+struct FrontGeom {
+  static constexpr int kSpanT = NT * kChunk;
+  static constexpr int kWarpsT = NT / 32;
+  static constexpr bool kTwInSmem = NT == kThreads;
+  static constexpr int kFftFloats = kWarpsT * FftLayout<double>::kSlots * 4;
+  static constexpr int kScratchFloats =
+      kFftFloats > scan_scratch_floats<10, float, NT>() ? kFftFloats : scan_scratch_floats<10, float, NT>();
+  static constexpr int kSmemBytes = 2 * kSpanT * 4 + kScratchFloats * 4 + (int)sizeof(DevTables) +
+                                    (kTwInSmem ? (int)sizeof(DevTwiddle64) : 0) + kWarpsT * 8 + 16;
+  static_assert((2 * kSpanT * 4 + kScratchFloats * 4) % 16 == 0, "16-byte aligned tables in shared memory");
+};
 static_assert(sizeof(DevTables) % 16 == 0 && sizeof(DevTwiddle64) % 16 == 0, "bulk copies of the tables");
-static_assert((2 * kSpan * 4 + kFrontScratchFloats * 4) % 16 == 0, "16-byte aligned tables in shared memory");
+static_assert(2 * (FrontGeom<kThreads / 2>::kSmemBytes + 1024) <= 228 * 1024, "two half-size CTAs per SM");
 
 // kSignal: general frame geometry, y is written to p.y64 and the frames are
 // left to the spectrum kernel (spectrum.cu)
-template <bool kSignal>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kSignal, int NT>
+__global__ void __launch_bounds__(NT, kThreads / NT)
     front_kernel(const __grid_constant__ FrontArgs p, const __grid_constant__ PowTab pow,
                  const __grid_constant__ PreTab64 pre) {
+  using G = FrontGeom<NT>;
+  constexpr int kSpan = G::kSpanT;    // (shadow the 512-thread constants)
+  constexpr int kWarps = G::kWarpsT;
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;                 // kSpan: input (hi part)
   float* fb = xs + kSpan;           // kSpan: [f = H x,] low part of a resampled x
                                     // (xs, fb) then hold y as kSpan doubles
   float* scratch = fb + kSpan;      // scan scratch, later the per-warp FFT scratch
-  DevTables* tab = reinterpret_cast<DevTables*>(scratch + kFrontScratchFloats);
-  DevTwiddle64* tw = reinterpret_cast<DevTwiddle64*>(tab + 1);
-  double* red = reinterpret_cast<double*>(tw + 1);  // kWarps
+  DevTables* tab = reinterpret_cast<DevTables*>(scratch + G::kScratchFloats);
+  DevTwiddle64* tw_s = reinterpret_cast<DevTwiddle64*>(tab + 1);
+  const DevTwiddle64* tw = G::kTwInSmem ? tw_s : p.tw64;
+  double* red = reinterpret_cast<double*>(reinterpret_cast<char*>(tab + 1) + (G::kTwInSmem ? sizeof(DevTwiddle64) : 0));
   uint64_t* bar = reinterpret_cast<uint64_t*>(red + kWarps);  // completion of the bulk copies
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -90,23 +105,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (tid == 0) {
     const uint32_t span_bytes = bulk_span ? (uint32_t)(cnt4 * 4) : 0u;
-    mbar_arrive_expect_tx(bar, (uint32_t)(sizeof(DevTables) + sizeof(DevTwiddle64)) + span_bytes);
+    const uint32_t tw_bytes = G::kTwInSmem ? (uint32_t)sizeof(DevTwiddle64) : 0u;
+    mbar_arrive_expect_tx(bar, (uint32_t)sizeof(DevTables) + tw_bytes + span_bytes);
     bulk_g2s(tab, p.tab, (uint32_t)sizeof(DevTables), bar);
-    bulk_g2s(tw, p.tw64, (uint32_t)sizeof(DevTwiddle64), bar);
+    if (G::kTwInSmem) bulk_g2s(tw_s, p.tw64, tw_bytes, bar);
     if (bulk_span) bulk_g2s(xs + (lo - base), xf + lo, span_bytes, bar);
   }
   if (bulk_span) {
-    for (int i = tid; i < kSpan; i += kThreads) {
+    for (int i = tid; i < kSpan; i += NT) {
       const int64_t q = base + i;
       if (q < lo || q >= lo + cnt4) xs[i] = q >= lo && q < hi ? __ldg(xf + q) : 0.0f;
     }
   } else {
-    stage_span_any(xs, xr, base, n_row, p.src.type);
+    stage_span_any<NT>(xs, xr, base, n_row, p.src.type);
   }
   // The low part of a resampled input (x = hi + lo) joins the pre-emphasis.
   // On gradient rows fb first holds f = H x (below), the low part only after.
   const bool has_lo = p.src_lo.ref != nullptr;
-  if (has_lo && !grad_row) stage_span(fb, p.src_lo.row(row), base, n_row);
+  if (has_lo && !grad_row) stage_span<NT>(fb, p.src_lo.row(row), base, n_row);
   if (!mbar_wait(bar, 0)) {
     // the copies did not land in time: flag it, give them one more bounded
     // wait (they write into this CTA's shared memory) and carry on
@@ -120,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   //    on gradient rows f itself on [a, send), from which the align kernel of
   //    the backward evaluates the adjoint term H^T f
   double ssq = 0.0;
-  chunk_scan<10, false, float, true>(
+  chunk_scan<10, false, float, true, NT>(
       pow, scratch, [&](int q) { return xs[q]; },
       [&](int q, float y) {
         const int64_t n = base + q;
@@ -138,14 +154,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (grad_row) {
     float* fr = p.fpow + (int64_t)row * n_row;
-    for (int i = tid; i < (int)(send - a); i += kThreads) fr[a + i] = fb[kHorizon + i];
+    for (int i = tid; i < (int)(send - a); i += NT) fr[a + i] = fb[kHorizon + i];
     __syncthreads();
-    if (has_lo) stage_span(fb, p.src_lo.row(row), base, n_row);
+    if (has_lo) stage_span<NT>(fb, p.src_lo.row(row), base, n_row);
   }
   PESQ_STAMP(g_phase_front, 3);
   // x = xs + fb from here on (fb = 0 for a 16 kHz input)
   if (!has_lo)
-    for (int i = tid; i < kSpan; i += kThreads) fb[i] = 0.0f;
+    for (int i = tid; i < kSpan; i += NT) fb[i] = 0.0f;
   __syncthreads();
   // 2. edge fade (15 samples at each end of the row), in place: the product
   //    of x with the ramp value k/16 is exact in double and splits exactly
@@ -173,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   //    padding after the row end is 0
   double* yd = reinterpret_cast<double*>(xs);
   const int q_end = (int)min((int64_t)kSpan, n_row - base);
-  chunk_scan<2, true, double>(
+  chunk_scan<2, true, double, false, NT>(
       pre, reinterpret_cast<double*>(scratch), [&](int q) { return (double)xs[q] + (double)fb[q]; },
       [&](int q, double y) { yd[q] = q < q_end ? y : 0.0; });
   __syncthreads();
@@ -181,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if constexpr (kSignal) {
     double* yo = p.y64 + (int64_t)row * n_row;
-    for (int i = tid; i < (int)(send - a); i += kThreads) yo[a + i] = yd[kHorizon + i];
+    for (int i = tid; i < (int)(send - a); i += NT) yo[a + i] = yd[kHorizon + i];
   } else {
   // 4. frames starting in this segment: window, rfft, power, Bark segment sums
   const int nb = tab->nb;
@@ -240,21 +256,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t front_smem_bytes() { return (size_t)kFrontSmemBytes; }
+size_t front_smem_bytes(int threads) {
+  return (size_t)(threads == kThreads ? FrontGeom<kThreads>::kSmemBytes : FrontGeom<kThreads / 2>::kSmemBytes);
+}
 
 cudaError_t configure_front() {
-  const cudaError_t e =
-      cudaFuncSetAttribute(front_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
+  cudaError_t e = cudaFuncSetAttribute(front_kernel<false, kThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)front_smem_bytes(kThreads));
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(front_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)front_smem_bytes());
+  e = cudaFuncSetAttribute(front_kernel<true, kThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)front_smem_bytes(kThreads));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(front_kernel<false, kThreads / 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)front_smem_bytes(kThreads / 2));
 }
 
 cudaError_t launch_front(const FrontArgs& a, const PowTab& pow, const PreTab64& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
-  LaunchShape l((unsigned)blocks, kThreads, front_smem_bytes(), s, false);
-  if (a.y64) return cudaLaunchKernelEx(&l.cfg, front_kernel<true>, a, pow, pre);
-  return cudaLaunchKernelEx(&l.cfg, front_kernel<false>, a, pow, pre);
+  if (a.threads == kThreads / 2 && !a.y64) {
+    LaunchShape l((unsigned)blocks, kThreads / 2, front_smem_bytes(kThreads / 2), s, false);
+    return cudaLaunchKernelEx(&l.cfg, front_kernel<false, kThreads / 2>, a, pow, pre);
+  }
+  LaunchShape l((unsigned)blocks, kThreads, front_smem_bytes(kThreads), s, false);
+  if (a.y64) return cudaLaunchKernelEx(&l.cfg, front_kernel<true, kThreads>, a, pow, pre);
+  return cudaLaunchKernelEx(&l.cfg, front_kernel<false, kThreads>, a, pow, pre);
 }
 
 }  // namespace pesq

@@ -86,6 +86,7 @@ struct FrontArgs {
   int frames;        // T
   int seg_frames;    // frames per segment
   int nseg;          // segments per row
+  int threads;       // CTA size: kThreads, or kThreads / 2 (half spans, two CTAs per SM)
   int spec_begin;    // rows [spec_begin, spec_end) also save the spectrum X
   int spec_end;      // for the backward
   const DevTables* tab;
@@ -386,7 +387,7 @@ size_t chain_smem_limit();
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
 
-size_t front_smem_bytes();
+size_t front_smem_bytes(int threads);
 size_t back_smem_bytes();
 size_t align_smem_bytes();
 

@@ -44,6 +44,7 @@ struct pesq_plan {
   bool general;
   void* gen_buf;
   int active_clusters[17];  // [c]: chain clusters of c CTAs the plan's device runs at once (c = 8..16)
+  int sms;                  // streaming multiprocessors of the plan's device
   GenTables gen;
   // resampler to 16 kHz (sample_rate != 16000)
   bool resample;
@@ -138,11 +139,20 @@ int fill_scan(ScanTab<P, R>& t, const pesq_scan_desc& d, const char* name) {
 // segment, the back kernel one hop before and kHorizon + 3 hops after it.
 constexpr int kMaxSegFrames = (kSpan - 2 * kHorizon) / kHop;  // 57
 static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel span");
+// Frames per segment of a half-size front CTA (kThreads / 2 threads, two per
+// SM): its span holds the warm-up and the frames that start in the segment.
+constexpr int kMaxSegFramesHalf = ((kThreads / 2) * kChunk - kHorizon - kHop) / kHop;  // 27
+// Front CTAs of the full size beyond which the half-size ones run instead:
+// from three waves of one CTA per SM on, two CTAs per SM overlap each
+// other's float32 scan and float64 transform phases.
+constexpr int kHalfFrontWaves = 2;
 
 struct Geometry {
   int64_t batch, rows, n_src, n16;
   int T, L, nb;
-  int seg, nseg;      // segmentation of a row (front, align)
+  int seg, nseg;      // segmentation of a row (align; the front unless half-size)
+  int seg_f, nseg_f;  // segmentation of a row for the front kernel and its partial sums
+  int front_threads;  // kThreads or kThreads / 2
   int seg_b, nseg_b;  // segmentation of a row for the back kernel
   int cluster;
   bool fwd_staged, fwd_stage_cells, bwd_staged, bwd_stage_cells;
@@ -197,6 +207,13 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.nfreq = p->general ? p->gen.nfreq : kBins;
   balance(g.n16, kMaxSegFrames, g.seg, g.nseg);
   balance(g.n16, kBackSegFrames, g.seg_b, g.nseg_b);
+  g.seg_f = g.seg;
+  g.nseg_f = g.nseg;
+  g.front_threads = kThreads;
+  if (!p->general && g.rows * g.nseg > (int64_t)kHalfFrontWaves * std::max(1, p->sms)) {
+    balance(g.n16, kMaxSegFramesHalf, g.seg_f, g.nseg_f);
+    g.front_threads = kThreads / 2;
+  }
   // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
   g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
   // a long utterance whose 8-CTA slices do not fit the chain backward's
@@ -223,7 +240,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   }
   // every kernel folds rows x segments (or utterances x cluster CTAs) onto
   // grid x; the resampler launches at most 65535 rows at a time in grid y
-  if (g.rows * g.nseg_b > INT32_MAX || g.batch * g.cluster > INT32_MAX)
+  if (g.rows * g.nseg_b > INT32_MAX || g.rows * g.nseg_f > INT32_MAX || g.batch * g.cluster > INT32_MAX)
     return fail(PESQ_ERR_INVALID_ARGUMENT, "batch too large for one call (%lld rows of %d segments)",
                 (long long)g.rows, g.nseg);
   g.grad = (flags & (PESQ_GRAD_REF | PESQ_GRAD_DEG)) != 0;
@@ -240,7 +257,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   const size_t rows = (size_t)g.rows;
   g.x16 = take(g.resample ? rows * g.n16 * 4 : 0);
   g.x16lo = take(g.resample ? rows * g.n16 * 4 : 0);
-  g.partial = take(rows * g.nseg * 8);
+  g.partial = take(rows * g.nseg_f * 8);
   g.sumsq = take(rows * 8);
   g.bark = take(rows * (size_t)g.T * g.nb * 4);
   g.fpow = take(g.grad ? rows * g.n16 * 4 : 0);
@@ -449,6 +466,7 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
   e = configure_chain();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the chain kernels"));
   for (int c = 8; c <= 16; ++c) p->active_clusters[c] = chain_active_clusters(c);
+  if (cudaDeviceGetAttribute(&p->sms, cudaDevAttrMultiProcessorCount, p->device) != cudaSuccess) p->sms = 1;
   e = configure_align();
   if (e != cudaSuccess) return bail(cuda_fail(e, "configuring the align kernel"));
   e = configure_spectrum();
@@ -553,8 +571,9 @@ int pesq_forward_front(const pesq_plan* p, void* stream, const void* ref_in, int
   fa.src_lo = lo16;
   fa.n = g.n16;
   fa.frames = g.T;
-  fa.seg_frames = g.seg;
-  fa.nseg = g.nseg;
+  fa.seg_frames = g.seg_f;
+  fa.nseg = g.nseg_f;
+  fa.threads = g.front_threads;
   fa.spec_begin = g.grad ? g.grad_begin : 0;
   fa.spec_end = g.grad ? g.grad_end : 0;
   fa.tab = p->dtab;
@@ -597,7 +616,7 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   if (rc) return rc;
   ChainFwdArgs ca{};
   ca.batch = (int)batch;
-  ca.nseg = g.nseg;
+  ca.nseg = g.nseg_f;
   ca.n = g.n16;
   ca.tab = p->dtab;
   ca.bark = at<float>(ws, g.bark);

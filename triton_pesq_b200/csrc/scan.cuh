@@ -42,19 +42,21 @@ struct ScanTab {
   R D;
 };
 
-// Shared memory floats the scan needs as scratch.
-template <int P, class R = float>
+// Shared memory floats the scan needs as scratch (CTAs of NT threads).
+template <int P, class R = float, int NT = kThreads>
 __host__ __device__ constexpr int scan_scratch_floats() {
-  return P * kThreads * (int)(sizeof(R) / sizeof(float));
+  return P * NT * (int)(sizeof(R) / sizeof(float));
 }
 
-// `load(p)` returns the input at logical position p (0 <= p < kSpan) and
-// `store(p, y)` consumes the output there.  `es` is scan scratch of
-// scan_scratch_floats<P, R>() floats.  Must be called by all kThreads threads.
+// `load(p)` returns the input at logical position p (0 <= p < NT * kChunk)
+// and `store(p, y)` consumes the output there.  `es` is scan scratch of
+// scan_scratch_floats<P, R, NT>() floats.  Must be called by all NT threads
+// of the CTA (a span of NT chunks; the horizon is kHorizonChunks chunks
+// whatever NT).
 // kBlockLower: A (hence every doubling matrix M) is block lower triangular in
 // 2 x 2 blocks, as for a series of second order sections; the structurally
 // zero entries above the block diagonal are skipped (the host checks them).
-template <int P, bool kRerun, class R, bool kBlockLower = false, class Load, class Store>
+template <int P, bool kRerun, class R, bool kBlockLower = false, int NT = kThreads, class Load, class Store>
 __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load&& load, Store&& store) {
   const int c = threadIdx.x;
   const int p0 = c * kChunk;
@@ -75,14 +77,14 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load
 
   // 2. Kogge-Stone over the chunks of the span
 #pragma unroll
-  for (int j = 0; j < P; ++j) es[j * kThreads + c] = e[j];
+  for (int j = 0; j < P; ++j) es[j * NT + c] = e[j];
   __syncthreads();
 #pragma unroll
   for (int lv = 0; lv < kLevels; ++lv) {
     const int d = 1 << lv;
     R prev[P];
 #pragma unroll
-    for (int j = 0; j < P; ++j) prev[j] = c >= d ? es[j * kThreads + c - d] : R(0);
+    for (int j = 0; j < P; ++j) prev[j] = c >= d ? es[j * NT + c - d] : R(0);
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < P; ++i) {
@@ -95,13 +97,13 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load
       e[i] = acc;
     }
 #pragma unroll
-    for (int j = 0; j < P; ++j) es[j * kThreads + c] = e[j];
+    for (int j = 0; j < P; ++j) es[j * NT + c] = e[j];
     __syncthreads();
   }
 
   R s[P];
 #pragma unroll
-  for (int j = 0; j < P; ++j) s[j] = c >= 1 ? es[j * kThreads + c - 1] : R(0);
+  for (int j = 0; j < P; ++j) s[j] = c >= 1 ? es[j * NT + c - 1] : R(0);
   // the scratch is free again once every thread holds its start state
   __syncthreads();
 
