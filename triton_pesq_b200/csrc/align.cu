@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kAlignSmemBytes = kSpan * 4 + scan_scratch_floats<10>() * 4;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     align_adjoint_kernel(const __grid_constant__ AlignArgs p, const __grid_constant__ PowTab pow) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;  // kSpan: f, then z = H^T f in place

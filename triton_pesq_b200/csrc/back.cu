@@ -28,23 +28,36 @@ namespace {
 
 constexpr int kSegMax = kBackSegFrames * kHop;  // samples of the longest segment
 // frames a CTA processes: one before its segment, the segment and those
-// reaching kBackHorizon past its end (one per warp and parity pass)
-constexpr int kBackFrames = 2 * kWarps;
-static_assert(kBackSegFrames + 1 + kBackHorizon / kHop <= kBackFrames, "frames of the longest segment");
-static_assert(kHop + kSegMax + kBackHorizon <= kSpan, "back kernel span");
-constexpr int kBackSmemBytes = kSpan * 4 + scan_scratch_floats<2>() * 4 + kWarps * FftLayout<float>::kSlots * 8 +
-                               kWarps * kMaxBands * 4 + (int)sizeof(DevTables) + kSegMax * 4 +
-                               kBackFrames * kMaxBands * 4;
+// reaching kBackHorizon past its end
+constexpr int kBackFrames = kBackSegFrames + 1 + kBackHorizon / kHop;
+
+// Shared-memory geometry of a back CTA of NT threads.  A full-size CTA (one
+// per SM) processes one frame per warp and parity pass; a half-size one (two
+// per SM, for batches of many waves) two.  Both stage the same segment: the
+// span of a half-size CTA (8448 samples) still covers the hop before it, the
+// segment and the look-ahead, so the results are the same bit for bit.
+template <int NT>
+struct BackGeom {
+  static constexpr int kSpanT = NT * kChunk;
+  static constexpr int kWarpsT = NT / 32;
+  static constexpr int kSmemBytes = kSpanT * 4 + scan_scratch_floats<2, float, NT>() * 4 +
+                                    kWarpsT * FftLayout<float>::kSlots * 8 + kWarpsT * kMaxBands * 4 +
+                                    (int)sizeof(DevTables) + kSegMax * 4 + kBackFrames * kMaxBands * 4;
+  static_assert(kHop + kSegMax + kBackHorizon <= kSpanT, "back kernel span");
+};
+static_assert(2 * (BackGeom<kThreads / 2>::kSmemBytes + 1024) <= 228 * 1024, "two half-size CTAs per SM");
 
 // kGather: general frame geometry, dL/dy is gathered from the frame gradients
 // of the spectrum kernel (spectrum.cu) instead of the fused transforms
-template <bool kGather>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kGather, int NT>
+__global__ void __launch_bounds__(NT, kThreads / NT)
     back_kernel(const __grid_constant__ BackArgs p, const __grid_constant__ PreTab pre) {
+  constexpr int kSpan = BackGeom<NT>::kSpanT;  // (shadow the 512-thread constants)
+  constexpr int kWarps = BackGeom<NT>::kWarpsT;
   extern __shared__ __align__(16) float smem[];
   float* gy = smem;  // kSpan: dL/dy, then dL/d(ramped x) in place
   float* es = gy + kSpan;
-  Cx<float>* fft = reinterpret_cast<Cx<float>*>(es + scan_scratch_floats<2>());
+  Cx<float>* fft = reinterpret_cast<Cx<float>*>(es + scan_scratch_floats<2, float, NT>());
   float* gb = reinterpret_cast<float*>(fft + kWarps * FftLayout<float>::kSlots);  // per warp kMaxBands
   DevTables* tab = reinterpret_cast<DevTables*>(gb + kWarps * kMaxBands);
   float* zs = reinterpret_cast<float*>(tab + 1);  // z on [a, send), staged asynchronously
@@ -67,11 +80,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // dL/dy on [a, send + kBackHorizon): sum over the frames covering each sample
     // (frame order), z staged in the background
     const float* zr = p.z + (int64_t)row * n_row;
-    for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
+    for (int i = tid; i < (int)(send - a); i += NT) cp_async4(zs + i, zr + a + i);
     cp_async_commit();
     const float* fg = p.frame_grad + (int64_t)(row - p.row_begin) * p.frames * p.nfft;
     const int top_g = kHop + kBackHorizon + (int)(send - a);
-    for (int i = tid; i < kSpan; i += kThreads) {
+    for (int i = tid; i < kSpan; i += NT) {
       const int64_t n = base + i;
       float acc = 0.0f;
       if (i >= kHop && i < top_g && n < n_row) {
@@ -94,19 +107,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first copy group: constant tables and dL/dB of the CTA's frames; second
   // group: z = H^T H x of the segment, only needed at the very end, copied in
   // the background of the frame loop
-  copy_async<kThreads>(tab, p.tab, (int)sizeof(DevTables));
+  copy_async<NT>(tab, p.tab, (int)sizeof(DevTables));
   // launched with programmatic serialisation: what follows reads the output
   // of the kernels before this one
   pdl_wait();
   {
     const float* src = p.g_bark + ((int64_t)row * p.frames + t_lo) * nb;
     const int cnt = (t_hi - t_lo + 1) * nb;
-    for (int i = tid; i < cnt; i += kThreads) cp_async4(gs + i, src + i);
+    for (int i = tid; i < cnt; i += NT) cp_async4(gs + i, src + i);
   }
   cp_async_commit();
-  for (int i = tid; i < kSpan; i += kThreads) gy[i] = 0.0f;
+  for (int i = tid; i < kSpan; i += NT) gy[i] = 0.0f;
   const float* zr = p.z + (int64_t)row * n_row;
-  for (int i = tid; i < (int)(send - a); i += kThreads) cp_async4(zs + i, zr + a + i);
+  for (int i = tid; i < (int)(send - a); i += NT) cp_async4(zs + i, zr + a + i);
   cp_async_commit();
   cp_async_wait_group<1>();
   __syncthreads();
@@ -166,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // pre-emphasis adjoint on [a, send): backwards in time from send + kBackHorizon;
   // the gradient of the zero padding after the row end is dropped
   const int top = kHop + kBackHorizon + (int)(send - a) - 1;
-  chunk_scan<2, true, float>(
+  chunk_scan<2, true, float, false, NT>(
       pre, es,
       [&](int q) {
         const int idx = top - q;
@@ -182,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   PESQ_STAMP(g_phase_back, 3);
   float* outr = p.out.row(row);
-  for (int i = tid; i < (int)(send - a); i += kThreads) {
+  for (int i = tid; i < (int)(send - a); i += NT) {
     const int64_t n = a + i;
     const float g = edge_ramp(gy[kHop + i], n, n_row);
     outr[n] = fmaf(-kappa, zs[i], g);
@@ -194,23 +207,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t back_smem_bytes() { return (size_t)kBackSmemBytes; }
+size_t back_smem_bytes(int threads) {
+  return (size_t)(threads == kThreads ? BackGeom<kThreads>::kSmemBytes : BackGeom<kThreads / 2>::kSmemBytes);
+}
 
 cudaError_t launch_back(const BackArgs& a, const PreTab& pre, int rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)rows * a.nseg;
   if (blocks <= 0) return cudaSuccess;
   // programmatic serialisation: the CTAs may be scheduled while the align
   // kernel finishes and wait (pdl_wait) before reading its output
-  LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(), s, true);
-  if (a.frame_grad) return cudaLaunchKernelEx(&l.cfg, back_kernel<true>, a, pre);
-  return cudaLaunchKernelEx(&l.cfg, back_kernel<false>, a, pre);
+  if (a.threads == kThreads / 2 && !a.frame_grad) {
+    LaunchShape l((unsigned)blocks, kThreads / 2, back_smem_bytes(kThreads / 2), s, true);
+    return cudaLaunchKernelEx(&l.cfg, back_kernel<false, kThreads / 2>, a, pre);
+  }
+  LaunchShape l((unsigned)blocks, kThreads, back_smem_bytes(kThreads), s, true);
+  if (a.frame_grad) return cudaLaunchKernelEx(&l.cfg, back_kernel<true, kThreads>, a, pre);
+  return cudaLaunchKernelEx(&l.cfg, back_kernel<false, kThreads>, a, pre);
 }
 
 cudaError_t configure_back() {
-  const cudaError_t e =
-      cudaFuncSetAttribute(back_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)back_smem_bytes());
+  cudaError_t e = cudaFuncSetAttribute(back_kernel<false, kThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)back_smem_bytes(kThreads));
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(back_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)back_smem_bytes());
+  e = cudaFuncSetAttribute(back_kernel<true, kThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)back_smem_bytes(kThreads));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(back_kernel<false, kThreads / 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)back_smem_bytes(kThreads / 2));
 }
 
 }  // namespace pesq

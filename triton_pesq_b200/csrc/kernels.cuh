@@ -159,6 +159,7 @@ struct BackArgs {
   int frames;
   int seg_frames;
   int nseg;
+  int threads;          // CTA size: kThreads, or kThreads / 2 (two CTAs per SM)
   const DevTables* tab;
   const float* g_bark;  // [rows][T][nb]  dL/d(unscaled Bark)
   const float* kappa;   // [rows]
@@ -388,7 +389,7 @@ cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
 
 size_t front_smem_bytes(int threads);
-size_t back_smem_bytes();
+size_t back_smem_bytes(int threads);
 size_t align_smem_bytes();
 
 }  // namespace pesq

@@ -142,9 +142,9 @@ static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel 
 // Frames per segment of a half-size front CTA (kThreads / 2 threads, two per
 // SM): its span holds the warm-up and the frames that start in the segment.
 constexpr int kMaxSegFramesHalf = ((kThreads / 2) * kChunk - kHorizon - kHop) / kHop;  // 27
-// Front CTAs of the full size beyond which the half-size ones run instead:
-// from three waves of one CTA per SM on, two CTAs per SM overlap each
-// other's float32 scan and float64 transform phases.
+// Front (back) CTAs of the full size beyond which the half-size ones run
+// instead: from three waves of one CTA per SM on, two CTAs per SM overlap
+// each other's phases (the front's float32 scan and float64 transforms).
 constexpr int kHalfFrontWaves = 2;
 
 struct Geometry {
@@ -730,6 +730,11 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ba.frames = g.T;
   ba.seg_frames = g.seg_b;
   ba.nseg = g.nseg_b;
+  // half-size CTAs (two per SM, the same results) from three waves of
+  // full-size ones on
+  ba.threads = (int64_t)(g.grad_end - g.grad_begin) * g.nseg_b > (int64_t)kHalfFrontWaves * std::max(1, p->sms)
+                   ? kThreads / 2
+                   : kThreads;
   ba.tab = p->dtab;
   ba.g_bark = at<float>(ws, g.gbark);
   ba.kappa = at<float>(ws, g.kappa);
