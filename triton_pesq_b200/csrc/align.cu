@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // z = H^T f on [a, send): logical position q at physical index top - q
   const int top = 2 * kHorizon + (int)(send - a) - 1;
-  chunk_scan<10, false, float, true>(
+  chunk_scan<10, false, float, true, kThreads, true>(
       pow, scratch,
       [&](int q) {
         const int idx = top - q;

@@ -56,7 +56,10 @@ __host__ __device__ constexpr int scan_scratch_floats() {
 // kBlockLower: A (hence every doubling matrix M) is block lower triangular in
 // 2 x 2 blocks, as for a series of second order sections; the structurally
 // zero entries above the block diagonal are skipped (the host checks them).
-template <int P, bool kRerun, class R, bool kBlockLower = false, int NT = kThreads, class Load, class Store>
+// kSkipWarmup: the caller uses no output of the warm-up chunks (the first
+// kHorizonChunks, warp 0), which then skip step 3.
+template <int P, bool kRerun, class R, bool kBlockLower = false, int NT = kThreads, bool kSkipWarmup = false,
+          class Load, class Store>
 __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load&& load, Store&& store) {
   const int c = threadIdx.x;
   const int p0 = c * kChunk;
@@ -108,7 +111,10 @@ __device__ __forceinline__ void chunk_scan(const ScanTab<P, R>& tab, R* es, Load
   __syncthreads();
 
   // 3. outputs of the chunk
-  if constexpr (kRerun) {
+  static_assert(kHorizonChunks == 32, "the warm-up chunks are warp 0");
+  if (kSkipWarmup && c < kHorizonChunks) {
+    // warm-up chunk: no output needed
+  } else if constexpr (kRerun) {
 #pragma unroll
     for (int t = 0; t < kChunk; ++t) {
       R y = tab.D * x[t];
