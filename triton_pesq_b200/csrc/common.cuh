@@ -113,7 +113,6 @@ constexpr int kNfft = 512;
 constexpr int kHop = 256;
 constexpr int kBins = 256;
 constexpr int kMaxBands = 64;
-constexpr int kMaxPieces = 96;  // band pieces of at most 8 bins (three per lane)
 
 // Largest state size of a filter handled by the chunked scan.
 constexpr int kMaxStates = 16;

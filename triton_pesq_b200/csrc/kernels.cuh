@@ -20,13 +20,6 @@ struct alignas(16) DevTables {
   int bin_band[kBins];         // band owning bin f, -1 if none (bin 0 never has one)
   int band_start[kMaxBands];
   int band_end[kMaxBands];
-  // the bands cut into pieces of at most 8 bins (in bin order) for the
-  // front kernel's band sums; band b's pieces are [band_piece[b],
-  // band_piece[b + 1]); npieces 0: sum the bands bin by bin
-  int piece_start[kMaxPieces];
-  int piece_len[kMaxPieces];
-  int band_piece[kMaxBands + 1];
-  int npieces;
   float band_corr[kMaxBands];  // power density correction
   float thresh[kMaxBands];     // hearing threshold
   float inv2th[kMaxBands];     // 0.5 / threshold

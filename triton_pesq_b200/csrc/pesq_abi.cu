@@ -404,26 +404,6 @@ int pesq_plan_create(const pesq_plan_desc* d, pesq_plan** out) {
     h.width_sq[b] = (float)(d->width[b] * d->width[b]);
   }
   h.nb = d->nbarks;
-  // pieces of at most 8 bins per band (the fused 512-point path only)
-  h.npieces = 0;
-  if (!p->general) {
-    int q = 0;
-    bool fits = true;
-    for (int b = 0; b < d->nbarks && fits; ++b) {
-      h.band_piece[b] = q;
-      for (int f = d->band_start[b]; f < d->band_end[b]; f += 8) {
-        if (q == kMaxPieces) {
-          fits = false;
-          break;
-        }
-        h.piece_start[q] = f;
-        h.piece_len[q] = std::min(8, d->band_end[b] - f);
-        ++q;
-      }
-    }
-    h.band_piece[d->nbarks] = q;
-    if (fits) h.npieces = q;
-  }
   h.total_width = (float)d->total_width;
   h.sqrt_total_width = (float)sqrt(d->total_width);
 
