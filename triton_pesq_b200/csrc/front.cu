@@ -52,7 +52,6 @@ struct FrontGeom {
   static_assert((2 * kSpanT * 4 + kScratchFloats * 4) % 16 == 0, "16-byte aligned tables in shared memory");
 };
 static_assert(sizeof(DevTables) % 16 == 0 && sizeof(DevTwiddle64) % 16 == 0, "bulk copies of the tables");
-static_assert(kBins + kMaxPieces <= 2 * FftLayout<double>::kSlots, "power and piece sums in a warp's scratch");
 static_assert(2 * (FrontGeom<kThreads / 2>::kSmemBytes + 1024) <= 228 * 1024, "two half-size CTAs per SM");
 
 // kSignal: general frame geometry, y is written to p.y64 and the frames are
@@ -229,40 +228,20 @@ __global__ void __launch_bounds__(NT, kThreads / NT)
     }
     __syncwarp();
     float* out = p.bark + ((int64_t)row * p.frames + t) * nb;
-    const int npieces = tab->npieces;
-    if (npieces > 0) {
-      // every lane sums whole pieces of at most 8 bins as a tree (the
-      // padding adds exact zeros), then every band its pieces in bin order
-      double* ps = pw + kBins;  // piece sums (the transform scratch is free)
-      for (int q = lane; q < npieces; q += 32) {
-        const int f0 = tab->piece_start[q], len = tab->piece_len[q];
+    for (int b = lane; b < nb; b += 32) {
+      // the band's bins in order, eight loads in flight at a time (the
+      // padding past the band's end adds exact zeros)
+      const int f1 = tab->band_end[b];
+      double acc = 0.0;
+#pragma unroll 1
+      for (int f = tab->band_start[b]; f < f1; f += 8) {
         double v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = i < len ? pw[f0 + i] : 0.0;
-        ps[q] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-      }
-      __syncwarp();
-      for (int b = lane; b < nb; b += 32) {
-        double acc = 0.0;
-        for (int q = tab->band_piece[b]; q < tab->band_piece[b + 1]; ++q) acc += ps[q];
-        out[b] = (float)(acc * (double)tab->band_corr[b]);
-      }
-    } else {
-      for (int b = lane; b < nb; b += 32) {
-        // the band's bins in order, eight loads in flight at a time (the
-        // padding past the band's end adds exact zeros)
-        const int f1 = tab->band_end[b];
-        double acc = 0.0;
-#pragma unroll 1
-        for (int f = tab->band_start[b]; f < f1; f += 8) {
-          double v[8];
+        for (int i = 0; i < 8; ++i) v[i] = f + i < f1 ? pw[f + i] : 0.0;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = f + i < f1 ? pw[f + i] : 0.0;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc += v[i];
-        }
-        out[b] = (float)(acc * (double)tab->band_corr[b]);
+        for (int i = 0; i < 8; ++i) acc += v[i];
       }
+      out[b] = (float)(acc * (double)tab->band_corr[b]);
     }
     __syncwarp();
   }
