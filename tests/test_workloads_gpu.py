@@ -112,26 +112,28 @@ def test_saturated_fixtures_are_covered():
     assert {"sr16k_sat_b2_n16000.npz", "sr48k_sat_b1_n24000.npz", "sr16k_clamp_b2_n16000.npz"} <= names
 
 
-def test_half_size_front_ctas_on_a_large_batch(cuda_device):
+@pytest.mark.parametrize("name,batch,segments", [("cfg5", 160, 4), ("cfg4", 40, 11)])
+def test_half_size_front_ctas_on_a_large_batch(cuda_device, name, batch, segments):
     """A batch whose front kernel would need three or more waves of one
     512-thread CTA per SM runs half-size CTAs (two per SM, 27-frame
-    segments): its utterances match float64 and the same utterances
+    segments; at 48 kHz behind the resampler, with the float residual of the
+    resampled rows): its utterances match float64 and the same utterances
     evaluated in a batch of their own (full-size CTAs, 57-frame segments)."""
 
-    batch = 160  # 320 rows x 4 segments of 3 s: far beyond two waves of 148 SMs
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
-    assert 2 * batch * 4 > 2 * sms  # (the half-size path runs)
-    ref, deg, sr = workload("cfg5", seed=0, rows=range(batch))
+    assert 2 * batch * segments > 2 * sms  # (the half-size path runs)
+    ref, deg, sr = workload(name, seed=0, rows=range(batch))
     model = PesqLossCuda(1.0, sample_rate=sr)
     loss, g_ref, g_deg = _both_grads(model, ref.to(cuda_device), deg.to(cuda_device))
-    few = [0, 1, 77, batch - 1]
+    few = [0, 1, batch // 2 - 3, batch - 1]
     alone, a_ref, a_deg = _both_grads(model, ref[few].to(cuda_device), deg[few].to(cuda_device))
     assert rel_err(loss[few].detach().cpu(), alone.detach().cpu()) < 1e-6
     assert peak_rel_err(g_deg[few].cpu(), a_deg.cpu()) < 1e-5
     assert peak_rel_err(g_ref[few].cpu(), a_ref.cpu()) < 1e-5
-    ds64, da64, gr64, gd64 = oracle_grads(ref[few], deg[few], 1.0, sr)
+    check = few[:2] if name == "cfg4" else few  # (10-s rows at 48 kHz: two of them in float64)
+    ds64, da64, gr64, gd64 = oracle_grads(ref[check], deg[check], 1.0, sr)
     ds, da = model.raw(ref.to(cuda_device), deg.to(cuda_device))
-    assert rel_err(ds[few].cpu(), ds64) < F64_RTOL
-    assert rel_err(da[few].cpu(), da64) < F64_RTOL
-    assert peak_rel_err(g_ref[few].cpu(), gr64) < GRAD_RTOL
-    assert peak_rel_err(g_deg[few].cpu(), gd64) < GRAD_RTOL
+    assert rel_err(ds[check].cpu(), ds64) < F64_RTOL
+    assert rel_err(da[check].cpu(), da64) < F64_RTOL
+    assert peak_rel_err(g_ref[check].cpu(), gr64) < GRAD_RTOL
+    assert peak_rel_err(g_deg[check].cpu(), gd64) < GRAD_RTOL
