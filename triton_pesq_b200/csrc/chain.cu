@@ -17,6 +17,8 @@
 // enters as s^2 = 1e7 / P with P = sum (H x)^2 / (N + 5120) / 1.04684.
 #include <math.h>
 
+#include <stdint.h>
+
 #include "kernels.cuh"
 
 namespace pesq {
@@ -209,7 +211,11 @@ __device__ __forceinline__ double warp_row_sumsq(const double* partial, int nseg
 // forward
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __grid_constant__ ChainFwdArgs p) {
+// kMinBlocks 2: the many-waves variant (64 registers, two CTAs per SM; its
+// shared-memory layout leaves the adjoint coefficients unstaged and its cell
+// passes run on their global copy, so both variants give the same results)
+template <int kMinBlocks>
+__global__ void __launch_bounds__(kChainThreads, kMinBlocks) chain_fwd_kernel(const __grid_constant__ ChainFwdArgs p) {
   extern __shared__ __align__(16) float dsm[];
   __shared__ DevTables tab;
   __shared__ double wpr[kChainWarps][kMaxBands], wpd[kChainWarps][kMaxBands];
@@ -394,7 +400,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
     // time, between a per-frame pass that sets the frame power ratios and one
     // that forms the norms from the staged disturbances; each cell and each
     // norm is evaluated exactly as below, so the results are the same.
-    const bool by_cell = cst != nullptr && sl.c_hi - sl.c_lo <= kCellSlice;
+    // the cell pass works on the staged coefficients, or (many-waves variant)
+    // on their global copy: a compile-time choice of shared or global accesses
+    constexpr bool kDual = kMinBlocks == 2;
+    float* const cb = kDual ? (p.cells ? p.cells + ((int64_t)u * C + q) * cblk : nullptr) : cst;
+    const int64_t cbs = kDual ? p.cell_stride : cblk;  // floats between the fields of cb
+    const bool by_cell = cb != nullptr && sl.c_hi - sl.c_lo <= kCellSlice;
     for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
       const int nf = min(32, sl.w_hi - t_base);
       // 1. total audible energies of each frame (lane j keeps frame j's)
@@ -507,13 +518,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
         cl.eval(b, R, D, bpr_s[ck], fpr_s[ct]);
         float co[4];
         cl.adjoint(b, co);
-        float* dst = cst + c;
-        dst[kCellDist * cblk] = cl.dist;
-        dst[kCellAsc * cblk] = cl.asc;
-        dst[kCellEdDist * cblk] = co[0];
-        dst[kCellEdAsc * cblk] = co[1];
-        dst[kCellErDist * cblk] = co[2];
-        dst[kCellErAsc * cblk] = co[3];
+        float* dst = cb + c;
+        dst[kCellDist * cbs] = cl.dist;
+        dst[kCellAsc * cbs] = cl.asc;
+        dst[kCellEdDist * cbs] = co[0];
+        dst[kCellEdAsc * cbs] = co[1];
+        dst[kCellErDist * cbs] = co[2];
+        dst[kCellErAsc * cbs] = co[3];
         ct += dt;
         ck += dk;
         if (ck >= nb) {
@@ -531,13 +542,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
           const int i = (t_base + j - sl.c_lo) * nb;
           float qs = 0.0f, qa = 0.0f;
           if (b0.norm) {
-            const float dist = cst[kCellDist * cblk + i + b0.k], asc = cst[kCellAsc * cblk + i + b0.k];
+            const float dist = cb[kCellDist * cbs + i + b0.k], asc = cb[kCellAsc * cbs + i + b0.k];
             const float v = b0.w * dist;
             qs = v * v;
             qa = fabsf(b0.w * (dist * asc));
           }
           if (b1.norm) {
-            const float dist = cst[kCellDist * cblk + i + b1.k], asc = cst[kCellAsc * cblk + i + b1.k];
+            const float dist = cb[kCellDist * cbs + i + b1.k], asc = cb[kCellAsc * cbs + i + b1.k];
             const float v = b1.w * dist;
             qs = fmaf(v, v, qs);
             qa += fabsf(b1.w * (dist * asc));
@@ -662,7 +673,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_fwd_kernel(const __gri
 // adjoint
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __grid_constant__ ChainBwdArgs p) {
+template <int kMinBlocks>
+__global__ void __launch_bounds__(kChainThreads, kMinBlocks) chain_bwd_kernel(const __grid_constant__ ChainBwdArgs p) {
   extern __shared__ __align__(16) float dsm[];
   __shared__ DevTables tab;
   __shared__ double wpart[kChainWarps][kMaxBands];
@@ -825,7 +837,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_bwd_kernel(const __gri
   // or, with the slice staged, the cells (frame, band) of the slice over all
   // threads, and the per-frame sums after them (the same operations, so the
   // same results).
-  const bool by_cell = cells_staged && sl.c_hi - sl.c_lo <= kCellSlice;
+  // (the many-waves variant reads its unstaged coefficients in the same cell
+  // pass: the same results as the staged variant)
+  const bool by_cell = (kMinBlocks == 2 ? p.staged : cells_staged) && sl.c_hi - sl.c_lo <= kCellSlice;
   for (int t_base = sl.w_lo; t_base < sl.w_hi; t_base += 32) {
     const int nf = min(32, sl.w_hi - t_base);
     float l_coef = 0.0f, l_garaw = 0.0f, l_gh = 0.0f, l_gfpr = 0.0f;
@@ -1081,22 +1095,26 @@ cudaError_t launch_cluster(Kernel k, const Args& a, int batch, int cluster, size
 }  // namespace
 
 cudaError_t configure_chain() {
-  cudaError_t e = cudaFuncSetAttribute(chain_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kChainSmemLimit);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmemLimit);
-  if (e != cudaSuccess) return e;
-  // clusters of up to 16 CTAs (beyond the portable 8) for long utterances
-  e = cudaFuncSetAttribute(chain_fwd_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(chain_bwd_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  const void* kernels[] = {reinterpret_cast<const void*>(chain_fwd_kernel<1>),
+                           reinterpret_cast<const void*>(chain_bwd_kernel<1>),
+                           reinterpret_cast<const void*>(chain_fwd_kernel<2>),
+                           reinterpret_cast<const void*>(chain_bwd_kernel<2>)};
+  for (const void* k : kernels) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmemLimit);
+    if (e != cudaSuccess) return e;
+    // clusters of up to 16 CTAs (beyond the portable 8) for long utterances
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 int chain_active_clusters(int cluster) {
   // clusters of `cluster` CTAs of both chain kernels that the current device
   // runs at once with the full shared memory allocation (0: none)
   int fewest = 1 << 30;
-  for (const void* k : {reinterpret_cast<const void*>(chain_fwd_kernel), reinterpret_cast<const void*>(chain_bwd_kernel)}) {
+  for (const void* k : {reinterpret_cast<const void*>(chain_fwd_kernel<1>),
+                        reinterpret_cast<const void*>(chain_bwd_kernel<1>)}) {
     LaunchShape l((unsigned)cluster, kChainThreads, kChainSmemLimit, nullptr, false, cluster);
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, k, &l.cfg) != cudaSuccess) {
@@ -1108,16 +1126,42 @@ int chain_active_clusters(int cluster) {
   return fewest;
 }
 
+namespace {
+// static shared memory of a many-waves chain kernel (queried once), or
+// SIZE_MAX when the query fails
+size_t dual_static_smem(const void* k) {
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) {
+    cudaGetLastError();
+    return SIZE_MAX;
+  }
+  return fa.sharedSizeBytes;
+}
+}  // namespace
+
+bool chain_dual_fits(int slice, int nb) {
+  // both kernels' static and dynamic shared memory (coefficients unstaged)
+  // within half an SM's, with the 1 KB the system reserves per CTA
+  static const size_t fwd_static = dual_static_smem(reinterpret_cast<const void*>(chain_fwd_kernel<2>));
+  static const size_t bwd_static = dual_static_smem(reinterpret_cast<const void*>(chain_bwd_kernel<2>));
+  const size_t half = 228 * 1024 / 2 - 1024;
+  return fwd_static <= half && bwd_static <= half &&
+         fwd_static + chain_fwd_smem_bytes(slice, nb, false) <= half &&
+         bwd_static + chain_bwd_smem_bytes(slice, nb, false) <= half;
+}
+
 cudaError_t launch_chain_fwd(const ChainFwdArgs& a, int cluster, cudaStream_t s) {
   const int slice = chain_slice_frames(a.lay.T, cluster);
   const size_t smem = a.staged ? chain_fwd_smem_bytes(slice, a.lay.nb, a.cells && a.stage_cells) : 0;
-  return launch_cluster(chain_fwd_kernel, a, a.batch, cluster, smem, s);
+  if (a.dual) return launch_cluster(chain_fwd_kernel<2>, a, a.batch, cluster, smem, s);
+  return launch_cluster(chain_fwd_kernel<1>, a, a.batch, cluster, smem, s);
 }
 
 cudaError_t launch_chain_bwd(const ChainBwdArgs& a, int cluster, cudaStream_t s) {
   const int slice = chain_slice_frames(a.lay.T, cluster);
   const size_t smem = a.staged ? chain_bwd_smem_bytes(slice, a.lay.nb, a.stage_cells != 0) : 0;
-  return launch_cluster(chain_bwd_kernel, a, a.batch, cluster, smem, s);
+  if (a.dual) return launch_cluster(chain_bwd_kernel<2>, a, a.batch, cluster, smem, s);
+  return launch_cluster(chain_bwd_kernel<1>, a, a.batch, cluster, smem, s);
 }
 
 }  // namespace pesq

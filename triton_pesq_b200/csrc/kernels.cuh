@@ -212,6 +212,7 @@ struct ChainFwdArgs {
   float* cells;
   int64_t cell_stride;
   int stage_cells;          // write them to shared memory first (when staged and they fit)
+  int dual;                 // many-waves variant: two CTAs per SM (64 registers, cells unstaged)
 };
 
 // Layout of the adjoint coefficients: field f of frame t, band k of utterance
@@ -249,6 +250,7 @@ struct ChainBwdArgs {
   const float* cells;       // the forward's adjoint coefficients (see CellField)
   int64_t cell_stride;
   int stage_cells;          // (staged) the slice's coefficients are staged too, else read from L2
+  int dual;                 // many-waves variant: two CTAs per SM (64 registers, cells unstaged)
 };
 
 struct ResampleArgs {
@@ -385,6 +387,9 @@ int chain_slice_frames(int T, int cluster);
 size_t chain_fwd_smem_bytes(int slice, int nb, bool cells);
 size_t chain_bwd_smem_bytes(int slice, int nb, bool cells = true);
 size_t chain_smem_limit();
+// The many-waves chain variant (two CTAs per SM, coefficients unstaged) fits
+// slices of `slice` frames.
+bool chain_dual_fits(int slice, int nb);
 cudaError_t launch_resample_fwd(const ResampleArgs& a, cudaStream_t s);
 cudaError_t launch_resample_adj(const ResampleArgs& a, cudaStream_t s);
 

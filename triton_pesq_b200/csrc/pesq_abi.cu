@@ -156,6 +156,7 @@ struct Geometry {
   int seg_b, nseg_b;  // segmentation of a row for the back kernel
   int cluster;
   bool fwd_staged, fwd_stage_cells, bwd_staged, bwd_stage_cells;
+  bool chain_dual;  // chain kernels two CTAs per SM (many waves of clusters)
   bool resample, grad, general;
   int nfreq;  // spectrum bins saved per frame
   int grad_begin, grad_end;
@@ -237,6 +238,10 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     g.fwd_stage_cells = chain_fwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
     g.bwd_stage_cells = chain_bwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
     g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
+    // many waves of clusters: two CTAs per SM, the coefficients through L2
+    g.chain_dual = !p->general && g.batch * g.cluster > (int64_t)kHalfFrontWaves * std::max(1, p->sms) &&
+                   g.fwd_staged && g.bwd_staged && chain_dual_fits(slice, p->nb);
+    if (g.chain_dual) g.fwd_stage_cells = g.bwd_stage_cells = false;
   }
   // every kernel folds rows x segments (or utterances x cluster CTAs) onto
   // grid x; the resampler launches at most 65535 rows at a time in grid y
@@ -632,6 +637,7 @@ int pesq_forward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ca.loss_sum = at<double>(ws, g.lsum);
   ca.done = at<uint32_t>(ws, g.lsum + 16);
   ca.staged = g.fwd_staged;
+  ca.dual = g.chain_dual;
   ca.cells = g.grad ? at<float>(ws, g.cells) : nullptr;
   ca.cell_stride = g.cell_stride;
   ca.stage_cells = g.fwd_stage_cells;
@@ -677,6 +683,7 @@ int pesq_backward_chain(const pesq_plan* p, void* stream, int64_t batch, int64_t
   cb.g_bark = at<float>(ws, g.gbark);
   cb.kappa = at<float>(ws, g.kappa);
   cb.staged = g.bwd_staged;
+  cb.dual = g.chain_dual;
   cb.stage_cells = g.bwd_stage_cells;
   cb.cells = at<float>(ws, g.cells);
   cb.cell_stride = g.cell_stride;
