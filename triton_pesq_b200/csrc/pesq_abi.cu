@@ -142,10 +142,14 @@ static_assert(kMaxSegFrames * kHop + kHorizon + 3 * kHop <= kSpan, "back kernel 
 // Frames per segment of a half-size front CTA (kThreads / 2 threads, two per
 // SM): its span holds the warm-up and the frames that start in the segment.
 constexpr int kMaxSegFramesHalf = ((kThreads / 2) * kChunk - kHorizon - kHop) / kHop;  // 27
-// Front (back) CTAs of the full size beyond which the half-size ones run
-// instead: from three waves of one CTA per SM on, two CTAs per SM overlap
-// each other's phases (the front's float32 scan and float64 transforms).
-constexpr int kHalfFrontWaves = 2;
+// Waves of full-size CTAs (one per SM) beyond which the front and back
+// kernels launch half-size CTAs and the chain kernels their two-CTAs-per-SM
+// variant: from two waves on, two CTAs per SM overlap each other's phases
+// (the front's float32 scan and float64 transforms) and fill the second
+// wave's idle SMs.  Measured graph-replayed steps, one wave -> two-wave
+// threshold: 16 x 4 s @44.1 kHz 0.160 -> 0.150 ms, 8 x 10 s @48 kHz 0.183 ->
+// 0.170 ms, 64 x 3 s @16 kHz 0.220 -> 0.205 ms.
+constexpr int kManyWaves = 1;
 
 struct Geometry {
   int64_t batch, rows, n_src, n16;
@@ -211,7 +215,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.seg_f = g.seg;
   g.nseg_f = g.nseg;
   g.front_threads = kThreads;
-  if (!p->general && g.rows * g.nseg > (int64_t)kHalfFrontWaves * std::max(1, p->sms)) {
+  if (!p->general && g.rows * g.nseg > (int64_t)kManyWaves * std::max(1, p->sms)) {
     balance(g.n16, kMaxSegFramesHalf, g.seg_f, g.nseg_f);
     g.front_threads = kThreads / 2;
   }
@@ -239,7 +243,7 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     g.bwd_stage_cells = chain_bwd_smem_bytes(slice, p->nb, true) <= chain_smem_limit();
     g.bwd_staged = chain_bwd_smem_bytes(slice, p->nb, false) <= chain_smem_limit();
     // many waves of clusters: two CTAs per SM, the coefficients through L2
-    g.chain_dual = !p->general && g.batch * g.cluster > (int64_t)kHalfFrontWaves * std::max(1, p->sms) &&
+    g.chain_dual = !p->general && g.batch * g.cluster > (int64_t)kManyWaves * std::max(1, p->sms) &&
                    g.fwd_staged && g.bwd_staged && chain_dual_fits(slice, p->nb);
     if (g.chain_dual) g.fwd_stage_cells = g.bwd_stage_cells = false;
   }
@@ -737,9 +741,9 @@ int pesq_backward_back(const pesq_plan* p, void* stream, int64_t batch, int64_t 
   ba.frames = g.T;
   ba.seg_frames = g.seg_b;
   ba.nseg = g.nseg_b;
-  // half-size CTAs (two per SM, the same results) from three waves of
+  // half-size CTAs (two per SM, the same results) from two waves of
   // full-size ones on
-  ba.threads = (int64_t)(g.grad_end - g.grad_begin) * g.nseg_b > (int64_t)kHalfFrontWaves * std::max(1, p->sms)
+  ba.threads = (int64_t)(g.grad_end - g.grad_begin) * g.nseg_b > (int64_t)kManyWaves * std::max(1, p->sms)
                    ? kThreads / 2
                    : kThreads;
   ba.tab = p->dtab;
