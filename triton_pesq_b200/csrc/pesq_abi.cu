@@ -150,6 +150,10 @@ constexpr int kMaxSegFramesHalf = ((kThreads / 2) * kChunk - kHorizon - kHop) / 
 // threshold: 16 x 4 s @44.1 kHz 0.160 -> 0.150 ms, 8 x 10 s @48 kHz 0.183 ->
 // 0.170 ms, 64 x 3 s @16 kHz 0.220 -> 0.205 ms.
 constexpr int kManyWaves = 1;
+// chain cluster sizing (frames per CTA slice, CTAs of a small batch)
+constexpr int kChainSliceMax = 104;
+constexpr int kChainSliceMin = 32;
+constexpr int kChainFillCtas = 64;
 
 struct Geometry {
   int64_t batch, rows, n_src, n16;
@@ -219,8 +223,21 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
     balance(g.n16, kMaxSegFramesHalf, g.seg_f, g.nseg_f);
     g.front_threads = kThreads / 2;
   }
-  // ~64 frames per CTA (4 per warp), at most 8 CTAs (a portable cluster)
-  g.cluster = (int)std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(g.T, 64)));
+  // Chain cluster size (CTAs per utterance; the results do not depend on it):
+  // slices of at most kChainSliceMax frames, and for small batches enough
+  // CTAs per utterance to reach kChainFillCtas in all -- the rest of the SMs
+  // run the align kernel beside the chain adjoint -- with slices of at least
+  // kChainSliceMin frames and at most 8 CTAs (a portable cluster).  Larger
+  // slices amortise each CTA's fixed cost (its cluster reductions and the
+  // staging of the tables) once the batch fills the GPU.  Measured steps
+  // (graph replay, fwd+bwd): 512 x 3 s 1.196 -> 1.133 ms with 2 CTAs
+  // instead of 3, 64 x 3 s 0.205 -> 0.199 ms, 4 x 3 s 0.088 -> 0.082 ms
+  // with 6, 1 x 1 s 0.086-0.090 -> 0.082-0.084 ms with 2; 128 x 6 s best
+  // with 4 (0.596 ms; 0.610 with 2, 0.627 with 3), 64 x 10 s at 48 kHz
+  // with 6 or 8 (0.797 ms; odd sizes 5 and 7 measured slower there).
+  g.cluster = (int)std::max<int64_t>(ceil_div(g.T, kChainSliceMax), ceil_div(kChainFillCtas, std::max<int64_t>(batch, 1)));
+  g.cluster = (int)std::min<int64_t>({(int64_t)g.cluster, 8, std::max<int64_t>(1, ceil_div(g.T, kChainSliceMin))});
+  g.cluster = std::max(g.cluster, 1);
   // a long utterance whose 8-CTA slices do not fit the chain backward's
   // shared memory layout takes the smallest larger cluster (up to 16) whose
   // slices fit, unless the device runs fewer of those at once than it
