@@ -137,3 +137,19 @@ def test_half_size_front_ctas_on_a_large_batch(cuda_device, name, batch, segment
     assert rel_err(da[check].cpu(), da64) < F64_RTOL
     assert peak_rel_err(g_ref[check].cpu(), gr64) < GRAD_RTOL
     assert peak_rel_err(g_deg[check].cpu(), gd64) < GRAD_RTOL
+
+
+def test_chain_cluster_size_leaves_results_unchanged(cuda_device):
+    """The plan sizes the chain clusters from the batch (8 utterances of 3 s:
+    6 CTAs each; 16: 4 each) while the front and back kernels keep the same
+    segments (one wave of full-size front CTAs in both): the utterances of
+    the smaller batch come out the same bit for bit inside the larger one."""
+
+    ref, deg, sr = workload("cfg5", seed=0, rows=range(16))
+    model = PesqLossCuda(1.0, sample_rate=sr)
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    assert 2 * 16 * 4 <= sms  # (both batches: one wave of full-size front CTAs)
+    big = _both_grads(model, ref.to(cuda_device), deg.to(cuda_device))
+    small = _both_grads(model, ref[:8].to(cuda_device), deg[:8].to(cuda_device))
+    for b, s in zip(big, small):
+        assert torch.equal(b[:8], s)
