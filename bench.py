@@ -108,6 +108,19 @@ def profiled_traffic():
     return None
 
 
+def device_identity(index: int):
+    """Name and driver version of the GPU (nvidia-smi): step times of the same
+    code were seen to differ between boxes with different drivers."""
+
+    try:
+        out = subprocess.run(["nvidia-smi", f"--id={index}", "--query-gpu=name,driver_version",
+                              "--format=csv,noheader"], capture_output=True, text=True, timeout=20).stdout
+        name, driver = [p.strip() for p in out.strip().splitlines()[0].split(",")[:2]]
+        return {"name": name, "driver": driver}
+    except (OSError, IndexError, ValueError, subprocess.TimeoutExpired):
+        return None
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
@@ -1104,6 +1117,7 @@ def run_cuda(args):
             "l2": "flushed between steps (256 MiB write, outside the step events)",
         },
         "clocks": clocks.summary(),
+        "device": device_identity(local),
         "e2e": {
             "value": e2e_value,
             "unit": UNIT,
