@@ -108,6 +108,45 @@ def profiled_traffic():
     return None
 
 
+def profiled_flops():
+    """Float64 and float32 FLOPs per front-kernel launch on the headline
+    workload, from the ncu instruction counters of the committed summary
+    (a fixed count of the workload: DFMA counts two, DADD and DMUL one)."""
+
+    path = os.path.join(ROOT, "profiles", "front_kernel_cfg2.txt")
+    out = {}
+    if os.path.exists(path):
+        for line in open(path):
+            for key in ("fp64_flops_per_launch", "fp32_flops_per_launch"):
+                if line.startswith(key + ":"):
+                    out[key] = float(line.split(":")[1])
+    return out if len(out) == 2 else None
+
+
+def front_compute(flops, launch_us, dev, clocks):
+    """The front kernel against its arithmetic pipes: it reads its inputs once
+    and is bound by instruction issue and the float64 pipe (the FFTs and the
+    pre-emphasis), not by HBM.  Achieved = the profiled FLOPs per launch over
+    the live launch time; peaks are nominal, 64 float64 and 128 float32 FMA
+    lanes per SM per clock at the sampled maximum SM clock."""
+
+    import torch
+
+    if not flops or not launch_us:
+        return None
+    mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak64 = sms * 64 * 2 * mhz * 1e6 / 1e12
+    peak32 = sms * 128 * 2 * mhz * 1e6 / 1e12
+    f64 = flops["fp64_flops_per_launch"] / (launch_us * 1e-6) / 1e12
+    f32 = flops["fp32_flops_per_launch"] / (launch_us * 1e-6) / 1e12
+    return {"fp64_flops_per_launch": flops["fp64_flops_per_launch"], "fp64_tflops": f64,
+            "fp64_peak_tflops_nominal": peak64, "fp64_frac": f64 / peak64,
+            "fp32_flops_per_launch": flops["fp32_flops_per_launch"], "fp32_tflops": f32,
+            "fp32_peak_tflops_nominal": peak32, "fp32_frac": f32 / peak32,
+            "source": "ncu sass op counters of profiles/front_kernel_cfg2.txt; nominal peaks"}
+
+
 def device_identity(index: int):
     """Name and driver version of the GPU (nvidia-smi): step times of the same
     code were seen to differ between boxes with different drivers."""
@@ -868,6 +907,7 @@ def run_cuda(args):
     graph, (loss_g, grad_g, mean_g) = capture_step(model, ref, deg, global_batch)
     with ClockSampler(local) as clocks:
         step_ms, total_s, wall = timed_replays(graph, args.steps, args.warmup, flush, world)
+    clock_summary = clocks.summary()
     utt_per_step = BATCH * SECONDS * world
     value = utt_per_step * args.steps / total_s
     # the all-reduced mean agrees with the losses of every rank
@@ -1075,6 +1115,7 @@ def run_cuda(args):
     front_us = stages["front"]
     achieved = alg["front"] / (front_us * 1e-6) / 1e9
     traffic = profiled_traffic()
+    flops = profiled_flops()
     single = world == 1 and not args.skip_configs
     ops = {"resample_44k1_to_16k": measure_resampler(dev, peak), "iir": measure_iir(dev, peak)} if world == 1 else None
     configs = measure_configs(dev, flush) if single else None
@@ -1116,7 +1157,7 @@ def run_cuda(args):
                           "stream overlapping the backward" if world > 1 else "none (one rank)",
             "l2": "flushed between steps (256 MiB write, outside the step events)",
         },
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
         "device": device_identity(local),
         "e2e": {
             "value": e2e_value,
@@ -1149,6 +1190,7 @@ def run_cuda(args):
             "traffic": traffic,
             "algorithmic_bytes_per_launch": alg["front"],
             "launch_us": front_us,
+            "compute": front_compute(flops, front_us, dev, clock_summary),
         },
         "stages_us": stages,
         **sharded,
