@@ -118,7 +118,7 @@ def test_half_size_front_ctas_on_a_large_batch(cuda_device, name, batch, segment
     512-thread CTA per SM runs half-size CTAs (two per SM, 27-frame
     segments; at 48 kHz behind the resampler, with the float residual of the
     resampled rows): its utterances match float64 and the same utterances
-    evaluated in a batch of their own (full-size CTAs, 57-frame segments)."""
+    evaluated in a batch of their own."""
 
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
     assert 2 * batch * segments > sms  # (the half-size path runs)
@@ -142,14 +142,32 @@ def test_half_size_front_ctas_on_a_large_batch(cuda_device, name, batch, segment
 def test_chain_cluster_size_leaves_results_unchanged(cuda_device):
     """The plan sizes the chain clusters from the batch (8 utterances of 3 s:
     6 CTAs each; 16: 4 each) while the front and back kernels keep the same
-    segments (one wave of full-size front CTAs in both): the utterances of
-    the smaller batch come out the same bit for bit inside the larger one."""
+    segments (half-size front CTAs, 27-frame segments, in both): the
+    utterances of the smaller batch come out the same bit for bit inside the
+    larger one."""
 
     ref, deg, sr = workload("cfg5", seed=0, rows=range(16))
     model = PesqLossCuda(1.0, sample_rate=sr)
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
-    assert 2 * 16 * 4 <= sms  # (both batches: one wave of full-size front CTAs)
+    assert 2 * 16 * 7 <= 2 * sms  # (both batches: one wave of half-size front CTAs)
     big = _both_grads(model, ref.to(cuda_device), deg.to(cuda_device))
     small = _both_grads(model, ref[:8].to(cuda_device), deg[:8].to(cuda_device))
     for b, s in zip(big, small):
         assert torch.equal(b[:8], s)
+
+
+def test_full_and_half_size_front_ctas_agree(cuda_device):
+    """8 utterances of 8 s are the one shape class that keeps full-size front
+    CTAs (144 of them fit one wave, their 304 half-size ones would not); a
+    ninth utterance moves the batch to half-size CTAs (19 segments of 27
+    frames per row instead of 9 of 56).  The eight utterances agree across
+    the two layouts within 1e-6 (the segments' warm-up boundaries differ)."""
+
+    ref, deg, sr = workload("cfg2", seed=0)
+    model = PesqLossCuda(1.0, sample_rate=sr)
+    full = _both_grads(model, ref.to(cuda_device), deg.to(cuda_device))
+    ref9, deg9 = torch.cat([ref, ref[:1]]), torch.cat([deg, deg[:1]])
+    half = _both_grads(model, ref9.to(cuda_device), deg9.to(cuda_device))
+    assert rel_err(half[0][:8].detach().cpu(), full[0].detach().cpu()) < 1e-6
+    assert peak_rel_err(half[1][:8].cpu(), full[1].cpu()) < 1e-5
+    assert peak_rel_err(half[2][:8].cpu(), full[2].cpu()) < 1e-5

@@ -219,9 +219,23 @@ int geometry(const pesq_plan* p, int64_t batch, int64_t n_src, uint32_t flags, G
   g.seg_f = g.seg;
   g.nseg_f = g.nseg;
   g.front_threads = kThreads;
-  if (!p->general && g.rows * g.nseg > (int64_t)kManyWaves * std::max(1, p->sms)) {
-    balance(g.n16, kMaxSegFramesHalf, g.seg_f, g.nseg_f);
-    g.front_threads = kThreads / 2;
+  if (!p->general) {
+    // Half-size front CTAs (two per SM, segments of at most kMaxSegFramesHalf
+    // frames) unless the full-size ones fit one wave and the half-size ones
+    // do not (the 8 x 8 s batch: 144 full-size CTAs in 32.8 us against 304
+    // half-size ones in 42.8 us).  A small batch gains from the shorter
+    // segments' extra CTAs (8 x 3 s: 29.4 -> 22.6 us, 1 x 1 s: 26.7 -> 20.6
+    // us), a large one from two CTAs per SM overlapping their phases.
+    int seg_h = 0, nseg_h = 0;
+    balance(g.n16, kMaxSegFramesHalf, seg_h, nseg_h);
+    const int64_t sms = std::max(1, p->sms);
+    const bool full_one_wave = g.rows * g.nseg <= (int64_t)kManyWaves * sms;
+    const bool half_one_wave = g.rows * nseg_h <= 2 * (int64_t)kManyWaves * sms;
+    if (!full_one_wave || half_one_wave) {
+      g.seg_f = seg_h;
+      g.nseg_f = nseg_h;
+      g.front_threads = kThreads / 2;
+    }
   }
   // Chain cluster size (CTAs per utterance; the results do not depend on it):
   // slices of at most kChainSliceMax frames, and for small batches enough
