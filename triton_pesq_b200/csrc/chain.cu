@@ -902,28 +902,60 @@ __global__ void __launch_bounds__(kChainThreads, kMinBlocks) chain_bwd_kernel(co
   if (by_cell) {
     __syncthreads();
     const int ncell = (sl.c_hi - sl.c_lo) * nb;
-    int ct = threadIdx.x / nb, ck = threadIdx.x - ct * nb;
-    const int dt = kChainThreads / nb, dk = kChainThreads - dt * nb;
-    for (int c = threadIdx.x; c < ncell; c += kChainThreads) {
-      const int t = sl.c_lo + ct;
-      const int64_t o = at(t, ck);
+    // the adjoint of cell (frame sl.c_lo + ct, band ck) from its coefficients
+    // v[kCell...] (v[kCellDist] and v[kCellAsc] are used for bands >= 1 only)
+    auto cell_adjoint = [&](int ct, int ck, const float* v) {
+      const int64_t o = at(sl.c_lo + ct, ck);
       const float w = tab.width[ck];
       float g_dist = 0.0f, g_asc = 0.0f;
       if (ck >= 1) {
         const float coef = coef_s[ct], g_araw = garaw_s[ct];
-        const float dist = CELL(kCellDist, t, ck), asc = CELL(kCellAsc, t, ck);
+        const float dist = v[kCellDist], asc = v[kCellAsc];
         g_dist = coef * (w * w) * dist;
         const float g_y = g_araw * w * sgnf(dist * asc);
         g_dist += g_y * asc;
         g_asc = g_y * dist;
       }
-      gd[o] = g_dist * CELL(kCellEdDist, t, ck) + g_asc * CELL(kCellEdAsc, t, ck);
-      gr[o] = g_dist * CELL(kCellErDist, t, ck) + g_asc * CELL(kCellErAsc, t, ck);
-      ct += dt;
-      ck += dk;
-      if (ck >= nb) {
-        ck -= nb;
-        ++ct;
+      gd[o] = g_dist * v[kCellEdDist] + g_asc * v[kCellEdAsc];
+      gr[o] = g_dist * v[kCellErDist] + g_asc * v[kCellErAsc];
+    };
+    if constexpr (kMinBlocks == 2) {
+      // The coefficients come from global memory (L2, or DRAM once a large
+      // batch's no longer fit): each thread issues the loads of kAhead of its
+      // cells before it uses the first, instead of waiting on every cell's.
+      constexpr int kAhead = 3;
+      for (int c0 = threadIdx.x; c0 < ncell; c0 += kAhead * kChainThreads) {
+        float v[kAhead][kCellFields];
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) {
+          const int c = c0 + a * kChainThreads;
+#pragma unroll
+          for (int f = 0; f < kCellFields; ++f) v[a][f] = c < ncell ? __ldg(cells + f * p.cell_stride + c) : 0.0f;
+        }
+#pragma unroll
+        for (int a = 0; a < kAhead; ++a) {
+          const int c = c0 + a * kChainThreads;
+          if (c < ncell) {
+            const int ct = c / nb;
+            cell_adjoint(ct, c - ct * nb, v[a]);
+          }
+        }
+      }
+    } else {
+      int ct = threadIdx.x / nb, ck = threadIdx.x - ct * nb;
+      const int dt = kChainThreads / nb, dk = kChainThreads - dt * nb;
+      for (int c = threadIdx.x; c < ncell; c += kChainThreads) {
+        const int t = sl.c_lo + ct;
+        float v[kCellFields];
+#pragma unroll
+        for (int f = 0; f < kCellFields; ++f) v[f] = (ck >= 1 || f >= kCellEdDist) ? CELL(f, t, ck) : 0.0f;
+        cell_adjoint(ct, ck, v);
+        ct += dt;
+        ck += dk;
+        if (ck >= nb) {
+          ck -= nb;
+          ++ct;
+        }
       }
     }
     __syncthreads();
